@@ -1,0 +1,468 @@
+"""Benchmark of the B200 HiF8 static W8A8 decode hot path.
+
+One step = the decode projection sweep of configs[1]: for every token count
+M in {1, 2, 4, 8, 16} and every projection shape (N, K) in
+{(24576, 4096) gate/up, (4096, 12288) down, (6144, 4096) qkv}, one W8A8HIF8
+static linear call ``y = linear(x)`` exactly as the quant scheme issues it
+(static activation quant with the fixed input_scale + HiF8 linear; rows <= 4
+take the fused quant+linear kernel).  Every call has its own weight, so a step
+streams 15 distinct weights (880 MB, larger than the 126 MB L2) and no weight
+is re-read from L2 between steps.
+
+Metric: HiF8 GEMV HBM GB/s = algorithmic bytes / device time, algorithmic
+bytes per call = N*K weight bytes + 4N channel scales + 2MK BF16 activation
++ 2MN BF16 output + 4 (input scale).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (torchrun, one rank per GPU, NCCL) the projections are split
+tensor-parallel: gate/up and qkv by output channel (column parallel), down by
+input channel (row parallel, followed by an NCCL all-reduce of the [M, 4096]
+output).  Total work is fixed, so scaling is "strong".
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG_ROOT = ROOT / "gcc-hif8-quantized-from-qwen3.5-9b_b200"
+for _p in (str(ROOT), str(PKG_ROOT)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+M_VALUES = (1, 2, 4, 8, 16)
+SHAPES = (("gate_up", 24576, 4096), ("down", 4096, 12288), ("qkv", 6144, 4096))
+METRIC = "HiF8 GEMV HBM GB/s vs peak (M=1-16); W8A8KV8 decode tok/s at 1/2/4/8 B200"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def call_bytes(m: int, n: int, k: int) -> int:
+    return n * k + 4 * n + 2 * m * k + 2 * m * n + 4
+
+
+def step_bytes() -> int:
+    return sum(call_bytes(m, n, k) for m in M_VALUES for _, n, k in SHAPES)
+
+
+def workload_config(world: int) -> dict:
+    return {
+        "workload": "configs[1] decode GEMV sweep: M in {1,2,4,8,16} x (N,K) in {(24576,4096) gate_up, "
+                    "(4096,12288) down, (6144,4096) qkv}; one static-quant + HiF8 linear call each",
+        "calls_per_step": len(M_VALUES) * len(SHAPES),
+        "algorithmic_bytes_per_step": step_bytes(),
+        "weights": "N(0,0.02) BF16 -> HiF8 u8, per-channel scale = row amax / 32768; seeded",
+        "activations": "N(0,1) BF16, fixed input_scale = calibration absmax / 32768",
+        "l2": "inputs larger than L2: 15 distinct weights (880 MB) streamed per step",
+        "parallelism": "single GPU" if world == 1 else f"tp{world} (column: gate_up, qkv; row: down + NCCL all-reduce)",
+        "graph": "one step captured as a CUDA graph, replayed per timed step",
+    }
+
+
+# ------------------------------------------------------------- utilities ---
+
+def load_peak_hbm() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_profile_traffic() -> dict | None:
+    path = ROOT / "profiles" / "gemv_traffic.json"
+    try:
+        return json.loads(path.read_text())
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], [], set()
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
+                                  parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------- CPU baseline ---
+
+def time_cpu_baseline(budget_s: float = 20.0) -> dict:
+    """Time the oracle port (the reference's CPU path restated: static quant
+    in C, decode LUT + FP32 matmul in numpy/BLAS) on a bounded sample of the
+    sweep: each projection shape at M = 1 and M = 16."""
+    import numpy as np
+
+    from oracle import oracle
+
+    rng = np.random.default_rng(0)
+    sample = [(m, name, n, k) for name, n, k in SHAPES for m in (1, 16)]
+    done_bytes, spent = 0, 0.0
+    runs = 0
+    weights = {}
+    for name, n, k in SHAPES:
+        w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+        weights[name] = oracle.quantize_rows_amax(w)
+    start_all = time.perf_counter()
+    while spent < budget_s and runs < 4:
+        for m, name, n, k in sample:
+            wq, ws = weights[name]
+            x = oracle.f32_to_bf16_bits(rng.standard_normal((m, k), dtype=np.float32))
+            scale = np.array([4.5 / 32768.0], np.float32)
+            t0 = time.perf_counter()
+            a, a_s = oracle.static_quant(x, scale)
+            y = oracle.linear_f32(a, wq, a_s, ws)
+            oracle.f32_to_bf16_bits(y)
+            spent += time.perf_counter() - t0
+            done_bytes += call_bytes(m, n, k)
+        runs += 1
+        if time.perf_counter() - start_all > 3 * budget_s:
+            break
+    return {"value": done_bytes / spent / 1e9, "unit": UNIT, "cores": oracle.cpu_threads(), "kind": "port",
+            "sample": f"{runs} pass(es) over M in {{1,16}} x the 3 projection shapes (static quant + decode + "
+                      f"FP32 matmul, numpy BLAS threads); {spent:.1f} s"}
+
+
+def run_reference(args) -> None:
+    """--impl reference: the reference's CPU path (oracle port) on the host
+    cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import oracle
+
+    rng = np.random.default_rng(0)
+    # one step = the whole sweep on CPU is ~minutes; each step times a bounded
+    # sample (every shape at M = 1 and 16) and reports GB/s over it
+    weights = {name: oracle.quantize_rows_amax(rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+               for name, n, k in SHAPES}
+    xs = {(m, name): oracle.f32_to_bf16_bits(rng.standard_normal((m, k), dtype=np.float32))
+          for name, n, k in SHAPES for m in (1, 16)}
+    scale = np.array([4.5 / 32768.0], np.float32)
+
+    def one_step() -> tuple[float, int]:
+        t0 = time.perf_counter()
+        nbytes = 0
+        for name, n, k in SHAPES:
+            wq, ws = weights[name]
+            for m in (1, 16):
+                a, a_s = oracle.static_quant(xs[(m, name)], scale)
+                oracle.f32_to_bf16_bits(oracle.linear_f32(a, wq, a_s, ws))
+                nbytes += call_bytes(m, n, k)
+        return time.perf_counter() - t0, nbytes
+
+    for _ in range(args.warmup):
+        one_step()
+    total_t, total_b = 0.0, 0
+    for _ in range(args.steps):
+        t, b = one_step()
+        total_t += t
+        total_b += b
+    value = total_b / total_t / 1e9
+    cores = oracle.cpu_threads()
+    sample = "per step: static quant + decode + FP32 matmul for every shape at M in {1,16} (oracle port)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total_t / max(args.steps, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(1) | {"reference_sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- our arm ---
+
+def build_layers(world: int, rank: int, device):
+    """Seeded weights and activations for every call of the sweep; this rank's
+    tensor-parallel shard when world > 1."""
+    import torch
+
+    from hif8_b200 import scheme
+
+    calls = []
+    for m in M_VALUES:
+        for idx, (name, n, k) in enumerate(SHAPES):
+            row_parallel = name == "down"
+            # column shards differ per rank; row shards are slices of one seeded weight
+            seed = 1000 * m + idx + (0 if row_parallel else 7919 * rank)
+            g = torch.Generator(device=device).manual_seed(seed)
+            n_loc = n if (world == 1 or row_parallel) else n // world
+            k_loc = k // world if (world > 1 and row_parallel) else k
+            w_full_rows = torch.randn(n_loc, k, device=device, generator=g, dtype=torch.float32).mul_(0.02)
+            w = w_full_rows[:, rank * k_loc:(rank + 1) * k_loc] if k_loc != k else w_full_rows
+            w = w.to(torch.bfloat16).contiguous()
+            calib = torch.randn(16, k, device=device, generator=g).to(torch.bfloat16)
+            input_scale = (calib.float().abs().amax() / 32768.0).reshape(1).to(torch.float32)
+            layer = scheme.Hif8StaticLinear.from_float(w, input_scale)
+            x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
+            x = x[:, rank * k_loc:(rank + 1) * k_loc].contiguous() if k_loc != k else x
+            calls.append({"m": m, "name": name, "n": n, "k": k, "layer": layer, "x": x, "row_parallel": row_parallel,
+                          "n_loc": n_loc, "k_loc": k_loc})
+            del w_full_rows, w
+    torch.cuda.synchronize()
+    return calls
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
+    from hif8_b200 import native, scheme
+
+    native.load_extension()
+    calls = build_layers(world, rank, device)
+
+    def step():
+        outs = []
+        for c in calls:
+            y = scheme.apply(c["layer"], c["x"])
+            if c["row_parallel"] and world > 1:
+                dist.all_reduce(y)
+            outs.append(y)
+        return outs
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        step()  # warm the private pool on the capture stream
+        torch.cuda.synchronize(device)
+        with torch.cuda.graph(graph, stream=stream):
+            graph_outs = step()
+    torch.cuda.current_stream(device).wait_stream(stream)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # ------------------------------------------------ timed region ------
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        start.record(cur)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(cur)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    total_bytes = step_bytes() * args.steps
+    value = total_bytes / (elapsed_ms * 1e-3) / 1e9
+    launches_per_step = sum(1 if c["m"] <= 4 else 2 for c in calls)
+
+    # -------------------------- dominant kernel: the GEMV, timed alone ---
+    roofline = gemv_roofline(calls, device, world)
+
+    # -------------------------------------------- e2e: public API, host I/O
+    e2e = measure_e2e(calls, args, device, world)
+
+    del graph, graph_outs
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(world),
+        "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(), "roofline": roofline,
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = time_cpu_baseline(args.cpu_budget)
+    print(json.dumps(line), flush=True)
+
+
+def gemv_roofline(calls, device, world) -> dict:
+    """Time every GEMV launch of the sweep alone (L2 flushed before each
+    launch, CUDA events on the launching stream) and report algorithmic GB/s
+    of the GEMV kernel against the measured HBM copy peak."""
+    import torch
+
+    from hif8_b200 import native
+
+    ext = native.load_extension()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    cur = torch.cuda.current_stream(device)
+    per = []
+    total_b, total_ms = 0, 0.0
+    reps = 5
+    for c in calls:
+        layer = c["layer"]
+        data, row_scale = native.static_quant(c["x"], layer.input_scale)
+        m, n_loc, k_loc = c["m"], c["n_loc"], c["k_loc"]
+        b = n_loc * k_loc + 4 * n_loc + m * k_loc + 4 * m + 2 * m * n_loc
+        times = []
+        for _ in range(reps):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(cur)
+            ext.soft_hif8_gemm(data, layer.weight, row_scale, layer.weight_scale, None, torch.bfloat16)
+            e.record(cur)
+            e.synchronize()
+            times.append(s.elapsed_time(e))
+        t = statistics.median(times)
+        per.append({"m": m, "shape": c["name"], "us": round(t * 1e3, 2), "gbs": round(b / (t * 1e-3) / 1e9, 1)})
+        total_b += b
+        total_ms += t
+    peak, kind = load_peak_hbm()
+    achieved = total_b / (total_ms * 1e-3) / 1e9
+    prof = load_profile_traffic()
+    traffic = None
+    if prof and prof.get("world") == world:
+        traffic = prof.get("traffic_bytes_per_launch")
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": traffic, "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs, copy)" if kind == "measured"
+            else "fallback 6650 GB/s", "kernel": "gemv_hif8_kernel (split-K tcgen-free mma.sync, LUT decode)",
+            "algorithmic_bytes_per_launch": "N*K + 4N + M*K + 4M + 2MN (u8 activation in, BF16 out)",
+            "per_launch": per, "timing": "median of 5 cold-L2 launches per config, CUDA events"}
+
+
+def measure_e2e(calls, args, device, world) -> dict:
+    """The same sweep through the public API (hif8_b200.scheme / native ops,
+    eager) with every step's activations copied from pinned host memory and
+    every output read back to pinned host memory inside the timed region."""
+    import torch
+    import torch.distributed as dist
+
+    from hif8_b200 import scheme
+
+    host_x = [c["x"].cpu().pin_memory() for c in calls]
+    host_y = [torch.empty(c["m"], c["n_loc"] if not c["row_parallel"] else c["n"], dtype=torch.bfloat16).pin_memory()
+              for c in calls]
+    dev_x = [torch.empty_like(c["x"]) for c in calls]
+    cur = torch.cuda.current_stream(device)
+
+    def step():
+        for i, c in enumerate(calls):
+            dev_x[i].copy_(host_x[i], non_blocking=True)
+            y = scheme.apply(c["layer"], dev_x[i])
+            if c["row_parallel"] and world > 1:
+                dist.all_reduce(y)
+            host_y[i].copy_(y, non_blocking=True)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(cur)
+    for _ in range(args.steps):
+        step()
+    end.record(cur)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    h2d = sum(x.numel() * 2 for x in host_x)
+    d2h = sum(y.numel() * 2 for y in host_y)
+    return {"value": step_bytes() * args.steps / (ms * 1e-3) / 1e9, "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms / args.steps,
+            "path": "hif8_b200.scheme.apply (eager PyTorch ops -> C ABI), pinned host buffers"}
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline work")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be >= 3")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.gpus:
+        parser.error(f"--gpus {args.gpus} does not match WORLD_SIZE {world}; launch N>1 under torchrun")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

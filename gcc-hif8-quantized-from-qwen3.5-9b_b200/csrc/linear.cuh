@@ -1,0 +1,27 @@
+// Shared declarations of the HiF8 linear kernels (split-K GEMV and the
+// tcgen05 prefill GEMM).
+#pragma once
+
+#include "hif8_common.cuh"
+
+namespace hif8 {
+
+struct GemvArgs {
+  const void *a;          // [M, K]: HiF8 bytes, or FP16/BF16 for the fused quant path
+  const uint8_t *w;       // [N, K]
+  const float *ts;        // [M] (or [1] with ts_stride 0)
+  const float *cs;        // [N]
+  const void *bias;       // [N] or null
+  void *out;              // [M, N]
+  int m, n, k;
+  int kc;                 // K range per CTA (multiple of 64)
+  int bias_dtype;
+  int ts_stride;          // 1: one token scale per row; 0: one shared fixed scale
+};
+
+bool hif8_gemm_tc_supported(int64_t m, int64_t n, int64_t k);
+size_t hif8_gemm_tc_workspace(int64_t m, int64_t n, int64_t k);
+int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t workspace_bytes,
+                 cudaStream_t stream);
+
+}  // namespace hif8

@@ -1,0 +1,406 @@
+// PyTorch operator registrations over the hif8_b200 C ABI.
+//
+// Namespace vllm_ascend_hif8 carries the reference plugin's operators with
+// their exact schemas (reference csrc/extension/pybind.cpp:6-14), a CUDA
+// implementation and Meta (shape) implementations, so `native.py`-style
+// callers that look up torch.ops.vllm_ascend_hif8.<op> reach these kernels
+// unchanged.  The argument checks and their messages follow the reference
+// bridge (csrc/extension/hif8_native.cpp:131-316), with "NPU" read as "CUDA".
+// Namespace hif8_b200 carries the fused KV operators that have no single
+// reference operator (they replace Python sequences in kv_runtime.py).
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <cstdint>
+#include <limits>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/hif8_b200.h"
+
+namespace {
+
+void CheckStatus(int status, const char *operation) {
+  TORCH_CHECK(status == HIF8_OK, operation, " failed: ", hif8_status_string(status),
+              status == HIF8_ERR_CUDA ? std::string(" (") + hif8_last_error() + ")" : std::string());
+}
+
+void CheckCudaTensor(const at::Tensor &tensor, const char *name) {
+  TORCH_CHECK(tensor.defined(), name, " must be defined");
+  TORCH_CHECK(tensor.is_cuda(), name, " must be a CUDA tensor, got ", tensor.device());
+  TORCH_CHECK(tensor.is_contiguous(), name, " must be contiguous");
+  TORCH_CHECK(tensor.storage_offset() == 0, name, " must have storage_offset == 0");
+}
+
+void CheckSameDevice(const at::Tensor &tensor, const at::Device &device, const char *name) {
+  TORCH_CHECK(tensor.device() == device, name, " must be on ", device, ", got ", tensor.device());
+}
+
+void CheckPositiveDimensions(const at::Tensor &tensor, const char *name) {
+  for (int64_t dim = 0; dim < tensor.dim(); ++dim)
+    TORCH_CHECK(tensor.size(dim) > 0, name, " dimensions must be positive, got ", tensor.sizes());
+}
+
+void CheckFitsUint32(int64_t value, const char *name) {
+  TORCH_CHECK(value > 0 && static_cast<uint64_t>(value) <= std::numeric_limits<uint32_t>::max(), name,
+              " must fit a positive uint32, got ", value);
+}
+
+int DtypeCode(at::ScalarType t) {
+  return t == at::ScalarType::BFloat16 ? HIF8_DTYPE_BF16 : HIF8_DTYPE_F16;
+}
+
+void *Stream(const at::Tensor &t) {
+  return static_cast<void *>(at::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+void ValidateSoftLinear(const at::Tensor &activation, const at::Tensor &weight, const at::Tensor &token_scale,
+                        const at::Tensor &channel_scale, const std::optional<at::Tensor> &bias,
+                        at::ScalarType output_type, bool gemv) {
+  CheckCudaTensor(activation, "activation");
+  CheckCudaTensor(weight, "weight");
+  CheckCudaTensor(token_scale, "token_scale");
+  CheckCudaTensor(channel_scale, "channel_scale");
+  TORCH_CHECK(activation.scalar_type() == at::ScalarType::Byte, "activation must have dtype torch.uint8");
+  TORCH_CHECK(weight.scalar_type() == at::ScalarType::Byte, "weight must have dtype torch.uint8");
+  TORCH_CHECK(token_scale.scalar_type() == at::ScalarType::Float, "token_scale must have dtype torch.float32");
+  TORCH_CHECK(channel_scale.scalar_type() == at::ScalarType::Float, "channel_scale must have dtype torch.float32");
+  TORCH_CHECK(activation.dim() == 2, "activation must have shape [M, K]");
+  TORCH_CHECK(weight.dim() == 2, "weight must have shape [N, K]");
+  TORCH_CHECK(token_scale.dim() == 1, "token_scale must have shape [M]");
+  TORCH_CHECK(channel_scale.dim() == 1, "channel_scale must have shape [N]");
+  CheckPositiveDimensions(activation, "activation");
+  CheckPositiveDimensions(weight, "weight");
+  const int64_t m = activation.size(0), k = activation.size(1), n = weight.size(0);
+  TORCH_CHECK(weight.size(1) == k, "activation and weight K dimensions differ: ", k, " != ", weight.size(1));
+  TORCH_CHECK(token_scale.numel() == m, "token_scale must contain one value per activation row");
+  TORCH_CHECK(channel_scale.numel() == n, "channel_scale must contain one value per output channel");
+  TORCH_CHECK(gemv ? m <= 2 : m > 0, gemv ? "soft_hif8_gemv requires M <= 2" : "soft_hif8_gemm requires M > 0");
+  CheckFitsUint32(m, "M");
+  CheckFitsUint32(n, "N");
+  CheckFitsUint32(k, "K");
+  const auto device = activation.device();
+  CheckSameDevice(weight, device, "weight");
+  CheckSameDevice(token_scale, device, "token_scale");
+  CheckSameDevice(channel_scale, device, "channel_scale");
+  if (bias.has_value()) {
+    CheckCudaTensor(*bias, "bias");
+    CheckSameDevice(*bias, device, "bias");
+    TORCH_CHECK(bias->dim() == 1, "bias must have shape [N]");
+    TORCH_CHECK(bias->numel() == n, "bias must contain N values");
+    TORCH_CHECK(bias->scalar_type() == at::ScalarType::Half || bias->scalar_type() == at::ScalarType::BFloat16,
+                "bias must have dtype torch.float16 or torch.bfloat16");
+  }
+  TORCH_CHECK(output_type == at::ScalarType::Half || output_type == at::ScalarType::BFloat16,
+              "output_dtype must be torch.float16 or torch.bfloat16");
+}
+
+std::tuple<at::Tensor, at::Tensor> Hif8StaticQuant(const at::Tensor &x, const at::Tensor &fixed_scale) {
+  CheckCudaTensor(x, "x");
+  CheckCudaTensor(fixed_scale, "fixed_scale");
+  TORCH_CHECK(x.scalar_type() == at::ScalarType::Half || x.scalar_type() == at::ScalarType::BFloat16,
+              "x must have dtype torch.float16 or torch.bfloat16");
+  TORCH_CHECK(fixed_scale.scalar_type() == at::ScalarType::Float, "fixed_scale must have dtype torch.float32");
+  TORCH_CHECK(x.dim() >= 1, "x must have at least one dimension");
+  TORCH_CHECK(fixed_scale.dim() == 1, "fixed_scale must have shape [scale_count]");
+  CheckPositiveDimensions(x, "x");
+  CheckPositiveDimensions(fixed_scale, "fixed_scale");
+  const int64_t rows = x.numel() / x.size(-1);
+  TORCH_CHECK(rows % fixed_scale.numel() == 0, "fixed_scale count must divide the activation row count");
+  CheckFitsUint32(rows, "activation row count");
+  CheckFitsUint32(x.size(-1), "K");
+  CheckFitsUint32(fixed_scale.numel(), "fixed scale count");
+  CheckSameDevice(fixed_scale, x.device(), "fixed_scale");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto data = at::empty(x.sizes(), x.options().dtype(at::kByte));
+  auto row_scale = at::empty({rows}, x.options().dtype(at::kFloat));
+  CheckStatus(hif8_static_quant(x.data_ptr(), DtypeCode(x.scalar_type()), rows, x.size(-1),
+                                fixed_scale.data_ptr<float>(), fixed_scale.numel(), data.data_ptr<uint8_t>(),
+                                row_scale.data_ptr<float>(), Stream(x)),
+              "hif8_static_quant");
+  return {data, row_scale};
+}
+
+at::Tensor Hif8ScaledDecode(const at::Tensor &data, const at::Tensor &scale) {
+  CheckCudaTensor(data, "data");
+  CheckCudaTensor(scale, "scale");
+  TORCH_CHECK(data.scalar_type() == at::ScalarType::Byte, "data must have dtype torch.uint8");
+  TORCH_CHECK(scale.scalar_type() == at::ScalarType::Float, "scale must have dtype torch.float32");
+  TORCH_CHECK(data.dim() == 2, "data must have shape [rows, K]");
+  TORCH_CHECK(scale.dim() == 1, "scale must have shape [rows]");
+  CheckPositiveDimensions(data, "data");
+  TORCH_CHECK(scale.numel() == data.size(0), "scale must contain one value per data row");
+  CheckFitsUint32(data.size(0), "row count");
+  CheckFitsUint32(data.size(1), "K");
+  CheckSameDevice(scale, data.device(), "scale");
+  c10::cuda::CUDAGuard guard(data.device());
+  auto out = at::empty(data.sizes(), data.options().dtype(at::kBFloat16));
+  CheckStatus(hif8_scaled_decode(data.data_ptr<uint8_t>(), data.size(0), data.size(1), data.size(1),
+                                 scale.data_ptr<float>(), reinterpret_cast<uint16_t *>(out.data_ptr()), Stream(data)),
+              "hif8_scaled_decode");
+  return out;
+}
+
+at::Tensor SoftHif8Linear(const at::Tensor &activation, const at::Tensor &weight, const at::Tensor &token_scale,
+                          const at::Tensor &channel_scale, const std::optional<at::Tensor> &bias,
+                          at::ScalarType output_type, bool gemv) {
+  ValidateSoftLinear(activation, weight, token_scale, channel_scale, bias, output_type, gemv);
+  c10::cuda::CUDAGuard guard(activation.device());
+  const int64_t m = activation.size(0), k = activation.size(1), n = weight.size(0);
+  auto out = at::empty({m, n}, activation.options().dtype(output_type));
+  const void *bias_ptr = bias.has_value() ? bias->data_ptr() : nullptr;
+  const int bias_dtype = bias.has_value() ? DtypeCode(bias->scalar_type()) : HIF8_DTYPE_NONE;
+  if (gemv) {
+    CheckStatus(soft_hif8_gemv(activation.data_ptr<uint8_t>(), weight.data_ptr<uint8_t>(),
+                               token_scale.data_ptr<float>(), channel_scale.data_ptr<float>(), bias_ptr, bias_dtype,
+                               DtypeCode(output_type), m, n, k, out.data_ptr(), Stream(activation)),
+                "soft_hif8_gemv");
+  } else {
+    const size_t ws_bytes = soft_hif8_gemm_workspace_size(m, n, k);
+    at::Tensor ws;
+    if (ws_bytes > 0) ws = at::empty({(int64_t)ws_bytes}, activation.options().dtype(at::kByte));
+    CheckStatus(soft_hif8_gemm(activation.data_ptr<uint8_t>(), weight.data_ptr<uint8_t>(),
+                               token_scale.data_ptr<float>(), channel_scale.data_ptr<float>(), bias_ptr, bias_dtype,
+                               DtypeCode(output_type), m, n, k, out.data_ptr(), ws_bytes ? ws.data_ptr() : nullptr,
+                               ws_bytes, Stream(activation)),
+                "soft_hif8_gemm");
+  }
+  return out;
+}
+
+at::Tensor SoftHif8Gemv(const at::Tensor &activation, const at::Tensor &weight, const at::Tensor &token_scale,
+                        const at::Tensor &channel_scale, const std::optional<at::Tensor> &bias,
+                        at::ScalarType output_type) {
+  return SoftHif8Linear(activation, weight, token_scale, channel_scale, bias, output_type, true);
+}
+
+at::Tensor SoftHif8Gemm(const at::Tensor &activation, const at::Tensor &weight, const at::Tensor &token_scale,
+                        const at::Tensor &channel_scale, const std::optional<at::Tensor> &bias,
+                        at::ScalarType output_type) {
+  return SoftHif8Linear(activation, weight, token_scale, channel_scale, bias, output_type, false);
+}
+
+at::Tensor SoftHif8StaticFusedGemm(const at::Tensor &activation, const at::Tensor &weight,
+                                   const at::Tensor &fixed_scale, const at::Tensor &channel_scale,
+                                   const std::optional<at::Tensor> &bias, at::ScalarType output_type) {
+  CheckCudaTensor(activation, "activation");
+  CheckCudaTensor(weight, "weight");
+  CheckCudaTensor(fixed_scale, "fixed_scale");
+  CheckCudaTensor(channel_scale, "channel_scale");
+  TORCH_CHECK(activation.scalar_type() == at::ScalarType::Half || activation.scalar_type() == at::ScalarType::BFloat16,
+              "activation must have dtype torch.float16 or torch.bfloat16");
+  TORCH_CHECK(weight.scalar_type() == at::ScalarType::Byte, "weight must have dtype torch.uint8");
+  TORCH_CHECK(fixed_scale.scalar_type() == at::ScalarType::Float, "fixed_scale must have dtype torch.float32");
+  TORCH_CHECK(channel_scale.scalar_type() == at::ScalarType::Float, "channel_scale must have dtype torch.float32");
+  TORCH_CHECK(activation.dim() == 2, "activation must have shape [M, K]");
+  TORCH_CHECK(weight.dim() == 2, "weight must have shape [N, K]");
+  TORCH_CHECK(fixed_scale.dim() == 1 && fixed_scale.numel() == 1, "fixed_scale must have shape [1]");
+  TORCH_CHECK(channel_scale.dim() == 1, "channel_scale must have shape [N]");
+  CheckPositiveDimensions(activation, "activation");
+  CheckPositiveDimensions(weight, "weight");
+  TORCH_CHECK(activation.size(0) <= 4, "soft_hif8_static_fused_gemm requires M <= 4");
+  TORCH_CHECK(activation.size(1) == weight.size(1), "activation and weight K dimensions differ: ", activation.size(1),
+              " != ", weight.size(1));
+  TORCH_CHECK(channel_scale.numel() == weight.size(0), "channel_scale must contain one value per output channel");
+  CheckFitsUint32(activation.size(0), "M");
+  CheckFitsUint32(weight.size(0), "N");
+  CheckFitsUint32(activation.size(1), "K");
+  CheckSameDevice(weight, activation.device(), "weight");
+  CheckSameDevice(fixed_scale, activation.device(), "fixed_scale");
+  CheckSameDevice(channel_scale, activation.device(), "channel_scale");
+  if (bias.has_value()) {
+    CheckCudaTensor(*bias, "bias");
+    CheckSameDevice(*bias, activation.device(), "bias");
+    TORCH_CHECK(bias->dim() == 1, "bias must have shape [N]");
+    TORCH_CHECK(bias->numel() == weight.size(0), "bias must contain N values");
+    TORCH_CHECK(bias->scalar_type() == at::ScalarType::Half || bias->scalar_type() == at::ScalarType::BFloat16,
+                "bias must have dtype torch.float16 or torch.bfloat16");
+  }
+  TORCH_CHECK(output_type == at::ScalarType::Half || output_type == at::ScalarType::BFloat16,
+              "output_dtype must be torch.float16 or torch.bfloat16");
+  c10::cuda::CUDAGuard guard(activation.device());
+  const int64_t m = activation.size(0), k = activation.size(1), n = weight.size(0);
+  auto out = at::empty({m, n}, activation.options().dtype(output_type));
+  CheckStatus(soft_hif8_static_fused_gemm(activation.data_ptr(), DtypeCode(activation.scalar_type()),
+                                          weight.data_ptr<uint8_t>(), fixed_scale.data_ptr<float>(),
+                                          channel_scale.data_ptr<float>(), bias.has_value() ? bias->data_ptr() : nullptr,
+                                          bias.has_value() ? DtypeCode(bias->scalar_type()) : HIF8_DTYPE_NONE,
+                                          DtypeCode(output_type), m, n, k, out.data_ptr(), Stream(activation)),
+              "soft_hif8_static_fused_gemm");
+  return out;
+}
+
+std::tuple<at::Tensor, at::Tensor> Hif8DynamicQuant(const at::Tensor &) {
+  TORCH_CHECK(false, "hif8_dynamic_quant is not provided by the B200 build: only the static "
+                     "W8A8HIF8_STATIC path (fixed input_scale) is implemented");
+}
+
+at::Tensor SoftHif8FusedGemm(const at::Tensor &, const at::Tensor &, const at::Tensor &,
+                             const std::optional<at::Tensor> &, at::ScalarType) {
+  TORCH_CHECK(false, "soft_hif8_fused_gemm (dynamic activation quant) is not provided by the B200 build; "
+                     "use soft_hif8_static_fused_gemm with a fixed input_scale");
+}
+
+// --------------------------------------------------------------- KV ops --
+
+void Hif8KvCacheWrite(const at::Tensor &key, const at::Tensor &value, const at::Tensor &key_scale,
+                      const at::Tensor &value_scale, const at::Tensor &slot_mapping, at::Tensor key_cache,
+                      at::Tensor value_cache, const std::optional<at::Tensor> &bad_slots) {
+  TORCH_CHECK(key.is_cuda() && value.is_cuda(), "key/value must be CUDA tensors");
+  TORCH_CHECK(key.dim() == 3 && value.sizes() == key.sizes(), "key/value must have shape [tokens, heads, head_size]");
+  TORCH_CHECK(key.scalar_type() == value.scalar_type() &&
+                  (key.scalar_type() == at::kBFloat16 || key.scalar_type() == at::kHalf),
+              "key/value must be float16 or bfloat16");
+  TORCH_CHECK(key.stride(2) == 1 && key.stride(1) == key.size(2) && value.stride(2) == 1 &&
+                  value.stride(1) == value.size(2) && key.stride(0) == value.stride(0),
+              "key/value rows must be contiguous [heads, head_size] blocks with a shared token stride");
+  CheckCudaTensor(key_scale, "key_scale");
+  CheckCudaTensor(value_scale, "value_scale");
+  CheckCudaTensor(slot_mapping, "slot_mapping");
+  CheckCudaTensor(key_cache, "key_cache");
+  CheckCudaTensor(value_cache, "value_cache");
+  TORCH_CHECK(slot_mapping.scalar_type() == at::kLong && slot_mapping.dim() == 1 &&
+                  slot_mapping.numel() >= key.size(0),
+              "slot_mapping must be int64 with one slot per token");
+  TORCH_CHECK(key_scale.scalar_type() == at::kFloat && key_scale.numel() == key.size(1) &&
+                  value_scale.scalar_type() == at::kFloat && value_scale.numel() == key.size(1),
+              "key_scale/value_scale must be float32 with one value per KV head");
+  TORCH_CHECK(key_cache.scalar_type() == at::kByte && key_cache.dim() == 4 && key_cache.size(2) == key.size(1) &&
+                  key_cache.size(3) == key.size(2) + 4 && value_cache.sizes() == key_cache.sizes() &&
+                  value_cache.scalar_type() == at::kByte,
+              "caches must be uint8 [num_blocks, block_size, heads, head_size + 4]");
+  int32_t *bad = nullptr;
+  if (bad_slots.has_value()) {
+    CheckCudaTensor(*bad_slots, "bad_slots");
+    TORCH_CHECK(bad_slots->scalar_type() == at::kInt && bad_slots->numel() >= 1, "bad_slots must be int32");
+    bad = bad_slots->data_ptr<int32_t>();
+  }
+  c10::cuda::CUDAGuard guard(key.device());
+  CheckStatus(hif8_kv_cache_write(key.data_ptr(), value.data_ptr(), DtypeCode(key.scalar_type()), key.size(0),
+                                  key.size(1), key.size(2), key.stride(0), key_scale.data_ptr<float>(),
+                                  value_scale.data_ptr<float>(), slot_mapping.data_ptr<int64_t>(),
+                                  key_cache.data_ptr<uint8_t>(), value_cache.data_ptr<uint8_t>(), key_cache.size(0),
+                                  key_cache.size(1), bad, Stream(key)),
+              "hif8_kv_cache_write");
+}
+
+at::Tensor Hif8PagedAttention(const at::Tensor &query, const at::Tensor &key_cache, const at::Tensor &value_cache,
+                              const at::Tensor &block_tables, const at::Tensor &seq_lens,
+                              const at::Tensor &query_start, int64_t max_seq_len, double softmax_scale,
+                              bool causal) {
+  CheckCudaTensor(query, "query");
+  CheckCudaTensor(key_cache, "key_cache");
+  CheckCudaTensor(value_cache, "value_cache");
+  CheckCudaTensor(block_tables, "block_tables");
+  CheckCudaTensor(seq_lens, "seq_lens");
+  CheckCudaTensor(query_start, "query_start");
+  TORCH_CHECK(query.scalar_type() == at::kBFloat16 && query.dim() == 3, "query must be bfloat16 [tokens, heads, D]");
+  TORCH_CHECK(key_cache.scalar_type() == at::kByte && key_cache.dim() == 4 && value_cache.sizes() == key_cache.sizes(),
+              "caches must be uint8 [num_blocks, block_size, kv_heads, D + 4]");
+  TORCH_CHECK(key_cache.size(3) == query.size(2) + 4, "cache row width must be head_size + 4");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2, "block_tables must be int32 [B, max_blocks]");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt && seq_lens.numel() == block_tables.size(0), "seq_lens must be int32 [B]");
+  TORCH_CHECK(query_start.scalar_type() == at::kInt && query_start.numel() == block_tables.size(0) + 1,
+              "query_start must be int32 [B + 1]");
+  c10::cuda::CUDAGuard guard(query.device());
+  auto out = at::empty_like(query);
+  const int64_t tokens = query.size(0), heads = query.size(1), d = query.size(2);
+  const size_t ws_bytes = hif8_paged_attention_workspace_size(tokens, heads, d, max_seq_len);
+  at::Tensor ws;
+  if (ws_bytes > 0) ws = at::empty({(int64_t)ws_bytes}, query.options().dtype(at::kByte));
+  CheckStatus(hif8_paged_attention(reinterpret_cast<const uint16_t *>(query.data_ptr()), key_cache.data_ptr<uint8_t>(),
+                                   value_cache.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(),
+                                   seq_lens.data_ptr<int32_t>(), query_start.data_ptr<int32_t>(),
+                                   block_tables.size(0), tokens, heads, key_cache.size(2), d, key_cache.size(0),
+                                   key_cache.size(1), block_tables.size(1), max_seq_len, (float)softmax_scale, causal ? 1 : 0,
+                                   reinterpret_cast<uint16_t *>(out.data_ptr()), ws_bytes ? ws.data_ptr() : nullptr,
+                                   ws_bytes, Stream(query)),
+              "hif8_paged_attention");
+  return out;
+}
+
+at::Tensor Hif8KvGatherDecode(const at::Tensor &cache, const at::Tensor &block_tables, const at::Tensor &seq_lens,
+                              const at::Tensor &out_start, int64_t total_rows, int64_t max_seq_len) {
+  CheckCudaTensor(cache, "cache");
+  CheckCudaTensor(block_tables, "block_tables");
+  CheckCudaTensor(seq_lens, "seq_lens");
+  CheckCudaTensor(out_start, "out_start");
+  TORCH_CHECK(cache.scalar_type() == at::kByte && cache.dim() == 4, "cache must be uint8 [blocks, block_size, heads, D + 4]");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  out_start.scalar_type() == at::kInt,
+              "block_tables/seq_lens/out_start must be int32");
+  c10::cuda::CUDAGuard guard(cache.device());
+  const int64_t heads = cache.size(2), d = cache.size(3) - 4;
+  auto out = at::empty({total_rows, heads, d}, cache.options().dtype(at::kBFloat16));
+  if (total_rows == 0) return out;
+  CheckStatus(hif8_kv_gather_decode(cache.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(),
+                                    seq_lens.data_ptr<int32_t>(), out_start.data_ptr<int32_t>(), block_tables.size(0),
+                                    heads, d, cache.size(0), cache.size(1), block_tables.size(1), max_seq_len,
+                                    reinterpret_cast<uint16_t *>(out.data_ptr()), Stream(cache)),
+              "hif8_kv_gather_decode");
+  return out;
+}
+
+std::vector<int64_t> RowScaleShape(const at::Tensor &x) {
+  return {x.dim() >= 1 && x.size(-1) > 0 ? x.numel() / x.size(-1) : 1};
+}
+
+}  // namespace
+
+TORCH_LIBRARY(vllm_ascend_hif8, m) {
+  m.def("hif8_dynamic_quant(Tensor x) -> (Tensor, Tensor)");
+  m.def("hif8_static_quant(Tensor x, Tensor fixed_scale) -> (Tensor, Tensor)");
+  m.def("hif8_scaled_decode(Tensor data, Tensor scale) -> Tensor");
+  m.def("soft_hif8_gemv(Tensor activation, Tensor weight, Tensor token_scale, Tensor channel_scale, Tensor? bias, "
+        "ScalarType output_dtype) -> Tensor");
+  m.def("soft_hif8_gemm(Tensor activation, Tensor weight, Tensor token_scale, Tensor channel_scale, Tensor? bias, "
+        "ScalarType output_dtype) -> Tensor");
+  m.def("soft_hif8_fused_gemm(Tensor activation, Tensor weight, Tensor channel_scale, Tensor? bias, "
+        "ScalarType output_dtype) -> Tensor");
+  m.def("soft_hif8_static_fused_gemm(Tensor activation, Tensor weight, Tensor fixed_scale, Tensor channel_scale, "
+        "Tensor? bias, ScalarType output_dtype) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(vllm_ascend_hif8, CUDA, m) {
+  m.impl("hif8_dynamic_quant", &Hif8DynamicQuant);
+  m.impl("hif8_static_quant", &Hif8StaticQuant);
+  m.impl("hif8_scaled_decode", &Hif8ScaledDecode);
+  m.impl("soft_hif8_gemv", &SoftHif8Gemv);
+  m.impl("soft_hif8_gemm", &SoftHif8Gemm);
+  m.impl("soft_hif8_fused_gemm", &SoftHif8FusedGemm);
+  m.impl("soft_hif8_static_fused_gemm", &SoftHif8StaticFusedGemm);
+}
+
+TORCH_LIBRARY_IMPL(vllm_ascend_hif8, Meta, m) {
+  m.impl("hif8_static_quant", [](const at::Tensor &x, const at::Tensor &) -> std::tuple<at::Tensor, at::Tensor> {
+    return {at::empty_like(x, x.options().dtype(at::kByte)), at::empty(RowScaleShape(x), x.options().dtype(at::kFloat))};
+  });
+  m.impl("hif8_scaled_decode", [](const at::Tensor &data, const at::Tensor &) -> at::Tensor {
+    return at::empty_like(data, data.options().dtype(at::kBFloat16));
+  });
+  auto linear_meta = [](const at::Tensor &activation, const at::Tensor &weight, const at::Tensor &, const at::Tensor &,
+                        const std::optional<at::Tensor> &, at::ScalarType output_dtype) -> at::Tensor {
+    return at::empty({activation.size(0), weight.size(0)}, activation.options().dtype(output_dtype));
+  };
+  m.impl("soft_hif8_gemv", linear_meta);
+  m.impl("soft_hif8_gemm", linear_meta);
+  m.impl("soft_hif8_static_fused_gemm", linear_meta);
+}
+
+TORCH_LIBRARY(hif8_b200, m) {
+  m.def("kv_cache_write(Tensor key, Tensor value, Tensor key_scale, Tensor value_scale, Tensor slot_mapping, "
+        "Tensor(a!) key_cache, Tensor(b!) value_cache, Tensor(c!)? bad_slots=None) -> ()");
+  m.def("paged_attention(Tensor query, Tensor key_cache, Tensor value_cache, Tensor block_tables, Tensor seq_lens, "
+        "Tensor query_start, int max_seq_len, float softmax_scale, bool causal=True) -> Tensor");
+  m.def("kv_gather_decode(Tensor cache, Tensor block_tables, Tensor seq_lens, Tensor out_start, int total_rows, "
+        "int max_seq_len) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(hif8_b200, CUDA, m) {
+  m.impl("kv_cache_write", &Hif8KvCacheWrite);
+  m.impl("paged_attention", &Hif8PagedAttention);
+  m.impl("kv_gather_decode", &Hif8KvGatherDecode);
+}

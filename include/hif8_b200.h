@@ -1,0 +1,174 @@
+/*
+ * hif8_b200 -- C ABI of the B200 (sm_100a) HiFloat8 static W8A8KV8 hot path.
+ *
+ * Plain pointers, sizes and a CUDA stream (passed as void*, i.e. a
+ * cudaStream_t; NULL = legacy default stream).  Every entry point enqueues
+ * its kernels asynchronously on that stream and returns a status code
+ * (HIF8_OK on success).  No entry point allocates device memory: outputs and
+ * (where a workspace is named) the scratch buffer are owned by the caller.
+ * Device pointers must be on the current CUDA device.
+ *
+ * Each entry point replaces one operator of the reference plugin; the cited
+ * lines are in the reference project (csrc/extension/ is its ACLNN bridge,
+ * src/vllm_ascend_hif8/ its Python layer).
+ */
+#ifndef HIF8_B200_H
+#define HIF8_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------- */
+#define HIF8_OK 0
+#define HIF8_ERR_INVALID_ARGUMENT 1 /* shape/dtype/pointer contract violated */
+#define HIF8_ERR_CUDA 2             /* a CUDA runtime call or launch failed */
+#define HIF8_ERR_WORKSPACE 3        /* workspace missing or too small */
+
+/* ---- dtype codes (match the reference bridge: kFp16Output = 0,
+ *      kBf16Output = 1, csrc/extension/hif8_native.cpp:32-33) ---------- */
+#define HIF8_DTYPE_F16 0
+#define HIF8_DTYPE_BF16 1
+#define HIF8_DTYPE_NONE -1 /* "no bias" */
+
+/* Human-readable text for a status code. */
+const char *hif8_status_string(int status);
+
+/* Text of the last CUDA error seen by this library on the calling thread
+ * (valid after HIF8_ERR_CUDA). */
+const char *hif8_last_error(void);
+
+/* Library version, e.g. "0.1.0". */
+const char *hif8_version(void);
+
+/* ---- codec tables (host-side, no device work) ---------------------- */
+
+/* 256 BF16 payloads of the HiF8 decode; NaN byte -> 0x7FC0.
+ * Replaces the generated decode tables of src/vllm_ascend_hif8/tablegen.py:63-82. */
+void hif8_decode_table_bf16(uint16_t out[256]);
+
+/* 4096-entry magnitude encode LUT indexed by (fp32 exponent << 4) | top-4
+ * mantissa bits.  Same contents as torch_codec.FLOAT32_ENCODE_LUT
+ * (src/vllm_ascend_hif8/torch_codec.py:19-29). */
+void hif8_encode_table(uint8_t out[4096]);
+
+/* ---- activation static quantisation --------------------------------
+ * Replaces op hif8_static_quant (csrc/extension/pybind.cpp:8,
+ * csrc/extension/hif8_native.cpp:487-554, kernel
+ * csrc/opp/op_kernel/hif8_static_quant.cpp).
+ *   data[r, k]   = enc_sat( fp32(x[r, k]) / fixed_scale[r % scale_count] )
+ *   row_scale[r] = fixed_scale[r % scale_count]        (row_scale may be NULL)
+ * x: [rows, k] contiguous FP16/BF16 (x_dtype); data: [rows, k] bytes.
+ * IEEE division, finite values saturate to +-32768, NaN -> 0x80, +-Inf ->
+ * 0x6F/0xEF: bit-exact with calibration.static_quantize_tensor. */
+int hif8_static_quant(const void *x, int x_dtype, int64_t rows, int64_t k,
+                      const float *fixed_scale, int64_t scale_count, uint8_t *data,
+                      float *row_scale, void *stream);
+
+/* ---- scaled decode ----------------------------------------------------
+ * Replaces op hif8_scaled_decode (csrc/extension/pybind.cpp:9,
+ * csrc/extension/hif8_native.cpp:556-611).
+ *   out[r, k] = bf16_rne( decode(data[r * data_row_stride + k]) * scale[r] ),
+ * NaN -> 0x7FC0.  out: [rows, k] contiguous BF16 bits.  data_row_stride is in
+ * bytes (>= k), so KV page rows with their 4-byte sidecar decode in place. */
+int hif8_scaled_decode(const uint8_t *data, int64_t rows, int64_t k, int64_t data_row_stride,
+                       const float *scale, uint16_t *out, void *stream);
+
+/* ---- linear -------------------------------------------------------------
+ * y[m, n] = cast( (acc[m, n] * channel_scale[n]) * token_scale[m] + bias[n] ),
+ * acc = sum_k decode(activation[m, k]) * decode(weight[n, k]) in FP32.
+ * activation: [m, k] bytes, weight: [n, k] bytes (row-major, K contiguous),
+ * bias: [n] FP16/BF16 or NULL (bias_dtype HIF8_DTYPE_NONE), out: [m, n] in
+ * output_dtype.
+ *
+ * soft_hif8_gemv replaces op soft_hif8_gemv (csrc/extension/pybind.cpp:10,
+ * hif8_native.cpp:613-631) and keeps its contract m <= 2.
+ * soft_hif8_gemm replaces ops soft_hif8_gemm / soft_hif8_prefill_gemm
+ * (csrc/extension/pybind.cpp:11, hif8_native.cpp:633-669), any m >= 1; small
+ * m runs the split-K tensor-core GEMV, large m the tcgen05 GEMM.
+ * workspace: soft_hif8_gemm_workspace_size() bytes of device memory (may be
+ * NULL when that size is 0). */
+int soft_hif8_gemv(const uint8_t *activation, const uint8_t *weight, const float *token_scale,
+                   const float *channel_scale, const void *bias, int bias_dtype,
+                   int output_dtype, int64_t m, int64_t n, int64_t k, void *out, void *stream);
+
+size_t soft_hif8_gemm_workspace_size(int64_t m, int64_t n, int64_t k);
+
+int soft_hif8_gemm(const uint8_t *activation, const uint8_t *weight, const float *token_scale,
+                   const float *channel_scale, const void *bias, int bias_dtype,
+                   int output_dtype, int64_t m, int64_t n, int64_t k, void *out,
+                   void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---- fused static quant + linear ---------------------------------------
+ * Replaces op soft_hif8_static_fused_gemm (csrc/extension/pybind.cpp:13,
+ * hif8_native.cpp:784-...): x FP16/BF16 [m, k] is encoded with the single
+ * fixed_scale[0] (bytes identical to hif8_static_quant), decoded, and fed to
+ * the linear above with token_scale = fixed_scale[0].  Contract m <= 4. */
+int soft_hif8_static_fused_gemm(const void *x, int x_dtype, const uint8_t *weight,
+                                const float *fixed_scale, const float *channel_scale,
+                                const void *bias, int bias_dtype, int output_dtype,
+                                int64_t m, int64_t n, int64_t k, void *out, void *stream);
+
+/* ---- paged HiF8 KV cache -----------------------------------------------
+ * Page layout (src/vllm_ascend_hif8/kv_cache.py:26-88): K and V caches are
+ * separate byte tensors [num_blocks, block_size, kv_heads, head_size + 4];
+ * each row is head_size HiF8 bytes followed by its little-endian FP32 scale.
+ *
+ * hif8_kv_cache_write replaces the static write path
+ * kv_runtime._write_hif8_cache (src/vllm_ascend_hif8/kv_runtime.py:1222-1339):
+ * static quant with per-head scales (S = kv_heads), pack_kv_rows
+ * (kv_cache.py:151-170) and the slot_mapping index_copy_, fused in one
+ * kernel.  key/value: [tokens, kv_heads, head_size] FP16/BF16 (src_dtype),
+ * row stride src_token_stride elements between tokens (>= kv_heads*head_size);
+ * slot_mapping: [tokens] int64, negative = skip.  Rows whose block is outside
+ * [0, num_blocks) are skipped and counted into *bad_slots (device int32, may
+ * be NULL). value/value_cache/value_scale may be NULL to write K only. */
+int hif8_kv_cache_write(const void *key, const void *value, int src_dtype, int64_t tokens,
+                        int64_t kv_heads, int64_t head_size, int64_t src_token_stride,
+                        const float *key_scale, const float *value_scale,
+                        const int64_t *slot_mapping, uint8_t *key_cache, uint8_t *value_cache,
+                        int64_t num_blocks, int64_t block_size, int32_t *bad_slots,
+                        void *stream);
+
+/* Paged attention over HiF8 pages; replaces _gather_dense_hif8 + scaled
+ * decode + the fused-infer-attention call of kv_runtime.py:1375-1563 (and the
+ * oracle kv_cache.paged_attention_reference, kv_cache.py:314-372).  Only the
+ * pages a request touches are read; K/V are decoded in registers (value
+ * rounded to BF16, as the reference materialises them), softmax in FP32.
+ *   query: [num_tokens, num_heads, head_size] BF16, tokens of request b are
+ *          rows [query_start[b], query_start[b+1]) and sit at the last
+ *          positions of that request's context (right-aligned causal mask);
+ *   block_tables: [batch, max_blocks] int32; seq_lens: [batch] int32, each
+ *          <= max_seq_len; table entries outside [0, num_blocks) are skipped;
+ *   query_start: [batch + 1] int32 (cumulative); out: like query.
+ * workspace: hif8_paged_attention_workspace_size() bytes (split-KV partials). */
+size_t hif8_paged_attention_workspace_size(int64_t num_tokens, int64_t num_heads,
+                                           int64_t head_size, int64_t max_seq_len);
+
+int hif8_paged_attention(const uint16_t *query, const uint8_t *key_cache,
+                         const uint8_t *value_cache, const int32_t *block_tables,
+                         const int32_t *seq_lens, const int32_t *query_start, int64_t batch,
+                         int64_t num_tokens, int64_t num_heads, int64_t kv_heads,
+                         int64_t head_size, int64_t num_blocks, int64_t block_size,
+                         int64_t max_blocks, int64_t max_seq_len, float softmax_scale, int causal,
+                         uint16_t *out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Gather + decode the rows of every request into a dense BF16 tensor, the
+ * output of kv_runtime._gather_dense_hif8 (kv_runtime.py:1375-1468):
+ * out[sum_b seq_lens[b], kv_heads, head_size] with out_start[b] the first
+ * row of request b (cumulative, [batch + 1]).  Positions whose block-table
+ * entry is outside [0, num_blocks) decode to zeros. */
+int hif8_kv_gather_decode(const uint8_t *cache, const int32_t *block_tables,
+                          const int32_t *seq_lens, const int32_t *out_start, int64_t batch,
+                          int64_t kv_heads, int64_t head_size, int64_t num_blocks,
+                          int64_t block_size, int64_t max_blocks, int64_t max_seq_len,
+                          uint16_t *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HIF8_B200_H */

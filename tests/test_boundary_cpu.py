@@ -1,0 +1,250 @@
+"""CPU checks of the drop-in boundary: the C-ABI library loads and exports
+every declared symbol, its host-side codec tables match the oracle, argument
+contracts are enforced before any device work, and the PyTorch operators are
+registered with the reference's exact schemas (no compute without a GPU)."""
+
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+
+ROOT = Path(__file__).resolve().parents[1]
+
+REFERENCE_SCHEMAS = {
+    # reference csrc/extension/pybind.cpp:7-13
+    "hif8_dynamic_quant": "vllm_ascend_hif8::hif8_dynamic_quant(Tensor x) -> (Tensor, Tensor)",
+    "hif8_static_quant": "vllm_ascend_hif8::hif8_static_quant(Tensor x, Tensor fixed_scale) -> (Tensor, Tensor)",
+    "hif8_scaled_decode": "vllm_ascend_hif8::hif8_scaled_decode(Tensor data, Tensor scale) -> Tensor",
+    "soft_hif8_gemv": "vllm_ascend_hif8::soft_hif8_gemv(Tensor activation, Tensor weight, Tensor token_scale, "
+                      "Tensor channel_scale, Tensor? bias, ScalarType output_dtype) -> Tensor",
+    "soft_hif8_gemm": "vllm_ascend_hif8::soft_hif8_gemm(Tensor activation, Tensor weight, Tensor token_scale, "
+                      "Tensor channel_scale, Tensor? bias, ScalarType output_dtype) -> Tensor",
+    "soft_hif8_fused_gemm": "vllm_ascend_hif8::soft_hif8_fused_gemm(Tensor activation, Tensor weight, "
+                            "Tensor channel_scale, Tensor? bias, ScalarType output_dtype) -> Tensor",
+    "soft_hif8_static_fused_gemm": "vllm_ascend_hif8::soft_hif8_static_fused_gemm(Tensor activation, Tensor weight, "
+                                   "Tensor fixed_scale, Tensor channel_scale, Tensor? bias, "
+                                   "ScalarType output_dtype) -> Tensor",
+}
+
+
+def _declared_functions() -> list[str]:
+    text = (ROOT / "include" / "hif8_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return re.findall(r"^\s*(?:const\s+)?(?:char|int|void|size_t)\s*\*?\s*(\w+)\s*\(", text, flags=re.M)
+
+
+def test_cabi_exports_every_declared_symbol():
+    from hif8_b200 import cabi
+
+    names = _declared_functions()
+    assert len(names) >= 14
+    lib = cabi.library()
+    for name in names:
+        assert hasattr(lib, name), f"{name} is declared in include/hif8_b200.h but not exported"
+        assert name in cabi.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(cabi.SIGNATURES) == set(names)
+
+
+def test_cabi_codec_tables_match_oracle():
+    from hif8_b200 import cabi
+
+    lib = cabi.library()
+    dec = np.zeros(256, dtype=np.uint16)
+    lib.hif8_decode_table_bf16(dec.ctypes.data)
+    np.testing.assert_array_equal(dec, oracle.decode_bf16_table())
+    enc = np.zeros(4096, dtype=np.uint8)
+    lib.hif8_encode_table(enc.ctypes.data)
+    np.testing.assert_array_equal(enc, oracle.encode_lut4096())
+
+
+def test_cabi_rejects_contract_violations_without_device_work():
+    from hif8_b200 import cabi
+
+    lib = cabi.library()
+    fake = 256  # never dereferenced: every case fails validation first
+    # soft_hif8_gemv keeps the reference's M <= 2 contract
+    assert lib.soft_hif8_gemv(fake, fake, fake, fake, None, -1, 1, 3, 8, 64, fake, None) == cabi.HIF8_ERR_INVALID_ARGUMENT
+    # null activation
+    assert lib.soft_hif8_gemm(None, fake, fake, fake, None, -1, 1, 1, 8, 64, fake, None, 0, None) == 1
+    # bad output dtype / bias dtype
+    assert lib.soft_hif8_gemm(fake, fake, fake, fake, None, -1, 7, 1, 8, 64, fake, None, 0, None) == 1
+    assert lib.soft_hif8_gemm(fake, fake, fake, fake, fake, 5, 1, 1, 8, 64, fake, None, 0, None) == 1
+    # scale count must divide the rows
+    assert lib.hif8_static_quant(fake, 1, 6, 16, fake, 4, fake, None, None) == 1
+    assert lib.hif8_static_quant(fake, 3, 4, 16, fake, 1, fake, None, None) == 1
+    # static fused: M <= 4
+    assert lib.soft_hif8_static_fused_gemm(fake, 1, fake, fake, fake, None, -1, 1, 5, 8, 64, fake, None) == 1
+    # KV: head_size must keep the FP32 sidecar aligned
+    assert lib.hif8_kv_cache_write(fake, fake, 1, 1, 1, 6, 6, fake, fake, fake, fake, fake, 1, 1, None, None) == 1
+    # attention: heads must be a multiple of kv heads
+    assert lib.hif8_paged_attention(fake, fake, fake, fake, fake, fake, 1, 1, 6, 4, 256, 8, 128, 1, 1, 1.0, 1,
+                                    fake, None, 0, None) == 1
+    assert lib.hif8_status_string(3) == b"workspace missing or too small"
+
+
+def test_paged_attention_workspace_sizes():
+    from hif8_b200 import cabi
+
+    lib = cabi.library()
+    assert lib.hif8_paged_attention_workspace_size(4, 16, 256, 256) == 0  # one chunk: no partials
+    assert lib.hif8_paged_attention_workspace_size(4, 16, 256, 4096) == 4 * 16 * 16 * (256 + 2) * 4
+
+
+def test_torch_ops_have_reference_schemas():
+    from hif8_b200 import native
+
+    native.load_extension()
+    for name, schema in REFERENCE_SCHEMAS.items():
+        assert str(getattr(torch.ops.vllm_ascend_hif8, name).default._schema) == schema
+
+
+def test_ops_have_no_cpu_fallback():
+    from hif8_b200 import native
+
+    native.load_extension()
+    x = torch.zeros(2, 16, dtype=torch.bfloat16)
+    with pytest.raises(NotImplementedError):
+        torch.ops.vllm_ascend_hif8.hif8_static_quant(x, torch.ones(1))
+
+
+def test_meta_shapes():
+    from hif8_b200 import native
+
+    native.load_extension()
+    x = torch.empty(2, 3, 64, dtype=torch.bfloat16, device="meta")
+    data, row_scale = torch.ops.vllm_ascend_hif8.hif8_static_quant(x, torch.empty(1, device="meta"))
+    assert data.shape == x.shape and data.dtype == torch.uint8
+    assert row_scale.shape == (6,) and row_scale.dtype == torch.float32
+    a = torch.empty(5, 64, dtype=torch.uint8, device="meta")
+    w = torch.empty(7, 64, dtype=torch.uint8, device="meta")
+    out = torch.ops.vllm_ascend_hif8.soft_hif8_gemm(a, w, torch.empty(5, device="meta"), torch.empty(7, device="meta"),
+                                                    None, torch.bfloat16)
+    assert out.shape == (5, 7) and out.dtype == torch.bfloat16
+    dec = torch.ops.vllm_ascend_hif8.hif8_scaled_decode(a, torch.empty(5, device="meta"))
+    assert dec.shape == a.shape and dec.dtype == torch.bfloat16
+
+
+def test_native_wrapper_contracts_raise_before_dispatch():
+    from hif8_b200 import native
+
+    with pytest.raises(TypeError):
+        native.static_quant(torch.zeros(2, 4), torch.ones(1))
+    with pytest.raises(TypeError):
+        native.static_quant(torch.zeros(2, 4, dtype=torch.bfloat16), torch.ones(1, dtype=torch.float64))
+    with pytest.raises(ValueError, match="must divide"):
+        native.static_quant(torch.zeros(3, 4, dtype=torch.bfloat16), torch.ones(2))
+    with pytest.raises(TypeError):
+        native.soft_linear(torch.zeros(1, 4), torch.zeros(2, 4, dtype=torch.uint8), torch.ones(1), torch.ones(2),
+                           output_dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="incompatible K"):
+        native.soft_linear(torch.zeros(1, 4, dtype=torch.uint8), torch.zeros(2, 5, dtype=torch.uint8),
+                           torch.ones(1), torch.ones(2), output_dtype=torch.bfloat16)
+    with pytest.raises(TypeError):
+        native.scaled_decode(torch.zeros(2, 4), torch.ones(2))
+    with pytest.raises(ValueError):
+        native.scaled_decode(torch.zeros(2, 2, 4, dtype=torch.uint8), torch.ones(2))
+    with pytest.raises(native.NativeExtensionUnavailable):
+        native.dynamic_quant(torch.zeros(2, 4, dtype=torch.bfloat16))
+    with pytest.raises(TypeError):
+        native.soft_static_fused_linear(torch.zeros(1, 4, dtype=torch.bfloat16), torch.zeros(2, 4, dtype=torch.uint8),
+                                        torch.ones(2), torch.ones(2), output_dtype=torch.bfloat16)
+
+
+def test_missing_extension_is_fatal(monkeypatch, tmp_path):
+    from hif8_b200 import _loader, native
+
+    monkeypatch.setattr(_loader, "_ops_loaded", False)
+    monkeypatch.setattr(_loader, "_ops_error", None)
+    monkeypatch.setattr(_loader, "OPS_PATH", tmp_path / "missing.so")
+    native.reset_extension_cache()
+    try:
+        assert not native.is_available()
+        with pytest.raises(native.NativeExtensionUnavailable, match="no decoded-weight or floating-point fallback"):
+            native.load_extension()
+    finally:
+        native.reset_extension_cache()
+
+
+def test_kv_layout_contract():
+    from hif8_b200.kv_cache import HIF8_SCALE_BYTES, Hif8KVCacheLayout
+
+    layout = Hif8KVCacheLayout(3, 8, 2, 16, 24)
+    assert layout.key_width == 16 + HIF8_SCALE_BYTES
+    assert layout.value_width == 24 + HIF8_SCALE_BYTES
+    assert layout.page_size_bytes == 8 * 2 * ((16 + 4) + (24 + 4))
+    assert layout.key_shape() == (3, 8, 2, 20)
+    assert layout.value_shape() == (3, 8, 2, 28)
+    qwen = Hif8KVCacheLayout(1, 128, 4, 256)
+    assert qwen.key_width == 260 and qwen.page_size_bytes == 128 * 4 * 520
+    with pytest.raises(ValueError):
+        Hif8KVCacheLayout(1, 4, 1, 6)
+    with pytest.raises(ValueError):
+        Hif8KVCacheLayout(1, 4, 1, 8, 6)
+
+
+def test_static_kv_scale_metadata(tmp_path):
+    import json
+
+    from hif8_b200.kv_cache import load_static_kv_scales
+
+    good = tmp_path / "good"
+    good.mkdir()
+    (good / "hif8_metadata.json").write_text(json.dumps({
+        "format": "W8A8HIF8_STATIC",
+        "kv_cache": {"mode": "static_per_layer_per_head",
+                     "layers": {"3": {"key_scales": [0.5, 0.75], "value_scales": [0.25, 1.0]}}}}))
+    assert load_static_kv_scales(str(good)) == {3: ((0.5, 0.75), (0.25, 1.0))}
+    bad = tmp_path / "bad"
+    bad.mkdir()
+    (bad / "hif8_metadata.json").write_text(json.dumps({
+        "format": "W8A8HIF8_STATIC",
+        "kv_cache": {"mode": "static_per_layer_per_head",
+                     "layers": {"3": {"key_scales": [0.5, -1.0], "value_scales": [0.25, 1.0]}}}}))
+    with pytest.raises(ValueError, match="invalid key_scales"):
+        load_static_kv_scales(str(bad))
+    missing = tmp_path / "missing"
+    missing.mkdir()
+    (missing / "hif8_metadata.json").write_text(json.dumps({"format": "W8A8HIF8_STATIC"}))
+    with pytest.raises(ValueError, match="missing kv_cache"):
+        load_static_kv_scales(str(missing))
+    assert load_static_kv_scales(str(tmp_path)) is None
+
+
+def test_static_scheme_parameter_contract():
+    from types import SimpleNamespace
+
+    from hif8_b200 import scheme
+
+    def layer(scale):
+        return SimpleNamespace(weight=torch.nn.Parameter(torch.zeros(4, 8, dtype=torch.uint8), requires_grad=False),
+                               weight_scale=torch.nn.Parameter(torch.ones(4, 1), requires_grad=False),
+                               input_scale=torch.nn.Parameter(scale, requires_grad=False))
+
+    ok = layer(torch.tensor([0.5]))
+    scheme.process_weights_after_loading(ok)
+    assert ok.weight_scale.shape == (4,) and ok.input_scale.shape == (1,)
+    for bad in (torch.tensor([0.0]), torch.tensor([float("inf")]), torch.tensor([-1.0]), torch.tensor([1.0, 2.0])):
+        with pytest.raises(ValueError):
+            scheme.process_weights_after_loading(layer(bad))
+    no_scale = SimpleNamespace(weight=ok.weight, weight_scale=ok.weight_scale)
+    with pytest.raises(ValueError, match="missing input_scale"):
+        scheme.process_weights_after_loading(no_scale)
+
+
+def test_static_scale_factor_env(monkeypatch):
+    from hif8_b200 import scheme
+
+    monkeypatch.setenv("HIF8_STATIC_SCALE_FACTOR", "2.0")
+    assert scheme.static_scale_factor() == 2.0
+    monkeypatch.setenv("HIF8_STATIC_SCALE_FACTOR", "-1")
+    with pytest.raises(ValueError):
+        scheme.static_scale_factor()
+    monkeypatch.setenv("HIF8_COMPUTE_BACKEND", "other")
+    with pytest.raises(ValueError):
+        scheme._check_backend()
