@@ -89,26 +89,35 @@ def load_profile_traffic() -> dict | None:
 class ClockSampler:
     """Samples nvidia-smi clocks and throttle reasons during the timed region."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.proc = None
+        self.lines: list[str] = []
+        self.window = (0.0, 0.0)
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.5)  # the sampler is producing lines before the timed region starts
         except Exception:
             self.proc = None
         return self
 
+    def mark_start(self):
+        self.window = (time.time(), self.window[1])
+
+    def mark_end(self):
+        self.window = (self.window[0], time.time())
+
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
+            time.sleep(0.1)
             self.proc.terminate()
             try:
                 out, _ = self.proc.communicate(timeout=5)
@@ -118,18 +127,25 @@ class ClockSampler:
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self) -> dict:
+        from datetime import datetime
+
         sm, smax, reasons = [], [], set()
-        for line in getattr(self, "lines", []):
+        start, end = self.window
+        for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
+                stamp = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                sm_mhz, max_mhz = float(parts[2]), float(parts[3])
             except ValueError:
                 continue
+            if start and not (start - 0.02 <= stamp <= end + 0.02):
+                continue
+            sm.append(sm_mhz)
+            smax.append(max_mhz)
             for name, flag in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
-                                  parts[5:9]):
+                                  parts[6:10]):
                 if flag.lower() == "active":
                     reasons.add(name)
         if not sm:
@@ -313,11 +329,13 @@ def run_ours(args) -> None:
     cur = torch.cuda.current_stream(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        clocks.mark_start()
         start.record(cur)
         for _ in range(args.steps):
             graph.replay()
         end.record(cur)
         torch.cuda.synchronize()
+        clocks.mark_end()
     if world > 1:
         dist.barrier()
     elapsed_ms = start.elapsed_time(end)
@@ -362,7 +380,9 @@ def gemv_roofline(calls, device, world) -> dict:
     from hif8_b200 import native
 
     ext = native.load_extension()
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    # L2 is evicted by READING a 512 MB buffer: writing one would leave dirty
+    # lines whose write-back competes with the timed launch.
+    flush = torch.ones(128 * 1024 * 1024, dtype=torch.float32, device=device)
     cur = torch.cuda.current_stream(device)
     per = []
     total_b, total_ms = 0, 0.0
@@ -374,7 +394,7 @@ def gemv_roofline(calls, device, world) -> dict:
         b = n_loc * k_loc + 4 * n_loc + m * k_loc + 4 * m + 2 * m * n_loc
         times = []
         for _ in range(reps):
-            flush.fill_(1)
+            flush.sum()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(cur)
             ext.soft_hif8_gemm(data, layer.weight, row_scale, layer.weight_scale, None, torch.bfloat16)
@@ -395,7 +415,7 @@ def gemv_roofline(calls, device, world) -> dict:
             "traffic": traffic, "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs, copy)" if kind == "measured"
             else "fallback 6650 GB/s", "kernel": "gemv_hif8_kernel (split-K tcgen-free mma.sync, LUT decode)",
             "algorithmic_bytes_per_launch": "N*K + 4N + M*K + 4M + 2MN (u8 activation in, BF16 out)",
-            "per_launch": per, "timing": "median of 5 cold-L2 launches per config, CUDA events"}
+            "per_launch": per, "timing": "median of 5 launches per config, each after a read-based L2 eviction, CUDA events"}
 
 
 def measure_e2e(calls, args, device, world) -> dict:
@@ -444,15 +464,48 @@ def measure_e2e(calls, args, device, world) -> dict:
             "path": "hif8_b200.scheme.apply (eager PyTorch ops -> C ABI), pinned host buffers"}
 
 
+def run_profile_case(spec: str, launches: int) -> None:
+    """Small single-kernel case for ncu captures: ``gemv:<shape>:<m>`` runs
+    the linear kernel of one sweep call ``launches`` times (two warm-up
+    launches first), nothing else of the bench."""
+    import torch
+
+    from hif8_b200 import native, scheme
+
+    kind, shape, m = spec.split(":")
+    if kind != "gemv":
+        raise SystemExit(f"unknown profile case {spec!r}")
+    n, k = {name: (n, k) for name, n, k in SHAPES}[shape]
+    m = int(m)
+    dev = torch.device("cuda", 0)
+    ext = native.load_extension()
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    wq, ws = scheme.quantize_weight_rows(w)
+    del w
+    x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+    a, ts = native.static_quant(x, torch.tensor([4.5 / 32768.0], device=dev))
+    for _ in range(2 + launches):
+        ext.soft_hif8_gemm(a, wq, ts, ws, None, torch.bfloat16)
+    torch.cuda.synchronize()
+    print(f"profile case {spec}: {2 + launches} launches ok")
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline work")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--profile-case", default=None,
+                        help="run one small kernel case for ncu (e.g. gemv:gate_up:1) and exit")
+    parser.add_argument("--profile-launches", type=int, default=3)
     args = parser.parse_args()
+    if args.profile_case:
+        run_profile_case(args.profile_case, args.profile_launches)
+        return
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -1,25 +1,36 @@
-// Split-K tensor-core GEMV for HiF8 W8A8 decode shapes (M <= 16).
+// Persistent split-K tensor-core GEMV for HiF8 W8A8 decode shapes (M <= 16).
 //
 //   y[m, n] = cast((acc[m, n] * cs[n]) * ts[m] + bias[n]),
 //   acc = sum_k decode(a[m, k]) * decode(w[n, k])          (FP32 accumulate)
 //
-// The weight stream (N x K bytes) is the whole cost, so the kernel is built
-// to keep HBM busy:
-//   * each warp owns 16 weight rows and streams them with 16-byte
-//     L1-bypassing loads, several 64-byte K blocks ahead in registers;
-//   * a weight byte becomes BF16 with one shared-memory lookup: a 256-entry
-//     table replicated per lane (entry b of lane l at byte (b << 8) | (l << 2)),
-//     so every lane always hits its own bank; one PRMT builds that address
-//     from the weight word and the lane offset;
-//   * the decoded 16 x 16 tile feeds mma.sync m16n8k16 (BF16 in, FP32
-//     accumulate) against the activation tile (8 or 16 tokens, decoded once
-//     per CTA into shared memory).  Lane (g, t) takes K bytes t*16 .. t*16+15
-//     of a 64-byte block, so the MMA's logical K order is a fixed
-//     permutation of memory order -- applied identically to the activations;
-//   * K is split over a thread-block cluster (1..8 CTAs); partial tiles are
-//     reduced through distributed shared memory in a fixed order, so results
-//     are deterministic and no global scratch is needed.
+// The weight stream (N x K bytes) is the whole cost; the kernel is shaped to
+// keep HBM busy from every SM for the whole launch:
+//   * one persistent CTA of 16 warps per SM (grid = SMs, rounded to whole
+//     clusters), so the 64 KB lane-replicated decode table and the activation
+//     tile are built once per SM;
+//   * K is split over a thread-block cluster of S CTAs (rank = K slice); each
+//     cluster walks row blocks ("items") round-robin, so every CTA keeps one
+//     K slice of the activation decoded in shared memory for the whole launch;
+//   * inside a CTA the 16 warps split the item as WR row groups x WK K parts;
+//     every warp always owns exactly four 64-byte K blocks per item, so its
+//     4-deep register ring of 16-byte weight loads is indexed at compile time
+//     and runs straight across item boundaries (the next item's blocks are in
+//     flight while the current one is reduced);
+//   * a weight byte becomes BF16 with one shared-memory lookup: entry b of
+//     lane l sits at byte (b << 8) | (l << 2), so a lane always hits its own
+//     bank, and one PRMT builds the address from the weight word;
+//   * decoded 16 x 16 weight tiles feed mma.sync m16n8k16 (BF16, FP32
+//     accumulate) against the activation fragments.  Lane (g, t) takes bytes
+//     t*16 .. t*16+15 of a 64-byte block, so the MMA's K order is a fixed
+//     permutation of memory order, applied identically to the activations;
+//   * partial sums are reduced in a fixed order: the warps of an item after
+//     every item, the cluster ranks once for all items at the end, through
+//     distributed shared memory -- deterministic, no global scratch.
 #include <cooperative_groups.h>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
 
 #include "linear.cuh"
 
@@ -27,10 +38,16 @@ namespace cg = cooperative_groups;
 
 namespace hif8 {
 
-constexpr int kGemvWarps = 8;
-constexpr int kGemvRows = kGemvWarps * 16;  // weight rows per CTA
+constexpr int kWarps = 16;                  // warps per CTA
+constexpr int kThreads = kWarps * 32;
 constexpr int kLutBytes = 256 * 256;        // lane-replicated table, 256 B per entry
-constexpr int kPrefetch = 4;                // 64-byte K blocks in flight per lane
+constexpr int kRing = 4;                    // 64-byte K blocks per warp per item (= ring depth)
+constexpr int kWarpK = kRing * 64;          // K per warp per item
+
+// Activation source of the linear kernels.
+constexpr int kActCodes = 0;  // HiF8 bytes
+constexpr int kActBf16 = 1;   // BF16, quantised in the prologue with ts[0]
+constexpr int kActF16 = 2;    // FP16, idem
 
 __device__ __forceinline__ uint4 ldg_stream(const uint8_t *p) {
   uint4 v;
@@ -40,36 +57,27 @@ __device__ __forceinline__ uint4 ldg_stream(const uint8_t *p) {
   return v;
 }
 
-__device__ __forceinline__ uint32_t lut_lookup(uint32_t lut_base, uint32_t word, uint32_t lane4, uint32_t sel) {
-  const uint32_t off = __byte_perm(word, lane4, sel);
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(lut_base + off));
-  return v;
+__device__ __forceinline__ uint32_t lut_lookup(const uint8_t *lut, uint32_t word, uint32_t lane4, uint32_t sel) {
+  return *reinterpret_cast<const uint32_t *>(lut + __byte_perm(word, lane4, sel));
 }
 
 // Decode the 4 bytes of `word` into two BF16x2 registers (bytes 0,1 and 2,3).
-__device__ __forceinline__ void decode4(uint32_t lut_base, uint32_t word, uint32_t lane4, uint32_t &lo,
+__device__ __forceinline__ void decode4(const uint8_t *lut, uint32_t word, uint32_t lane4, uint32_t &lo,
                                         uint32_t &hi) {
-  const uint32_t e0 = lut_lookup(lut_base, word, lane4, 0x5504u);
-  const uint32_t e1 = lut_lookup(lut_base, word, lane4, 0x5514u);
-  const uint32_t e2 = lut_lookup(lut_base, word, lane4, 0x5524u);
-  const uint32_t e3 = lut_lookup(lut_base, word, lane4, 0x5534u);
+  const uint32_t e0 = lut_lookup(lut, word, lane4, 0x5504u);
+  const uint32_t e1 = lut_lookup(lut, word, lane4, 0x5514u);
+  const uint32_t e2 = lut_lookup(lut, word, lane4, 0x5524u);
+  const uint32_t e3 = lut_lookup(lut, word, lane4, 0x5534u);
   lo = __byte_perm(e0, e1, 0x5410u);
   hi = __byte_perm(e2, e3, 0x5410u);
 }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-
-// Activation source of the linear kernels.
-constexpr int kActCodes = 0;  // HiF8 bytes
-constexpr int kActBf16 = 1;   // BF16, quantised in the prologue with ts[0]
-constexpr int kActF16 = 2;    // FP16, idem
 
 // Static-quantise one FP16/BF16 value with fixed scale s and decode it back:
 // the BF16 payload of decode(enc_sat(x / s)), bit-identical to running
@@ -91,20 +99,6 @@ __device__ __forceinline__ uint32_t fake_quant_bf16(uint32_t h, float s, float r
   return g_decode_f32.v[code] >> 16;
 }
 
-template <int NT>
-__host__ __device__ constexpr int gemv_act_stride(int kc) {
-  return kc * 2 + 16;  // bytes; the 16-byte pad spreads token rows over banks
-}
-
-// The activation tile is reused for the cluster reduction after the main
-// loop ([kGemvRows][8 * NT] FP32), so the region is the larger of the two.
-template <int NT>
-__host__ __device__ constexpr size_t gemv_smem_bytes(int kc) {
-  const size_t act = (size_t)(8 * NT) * gemv_act_stride<NT>(kc);
-  const size_t red = (size_t)kGemvRows * 8 * NT * sizeof(float);
-  return (size_t)kLutBytes + (act > red ? act : red);
-}
-
 template <int OUT>
 __device__ __forceinline__ void store_out(void *out, int64_t idx, float v) {
   if constexpr (OUT == HIF8_DTYPE_BF16) static_cast<uint16_t *>(out)[idx] = (uint16_t)f32_to_bf16_bits(v);
@@ -116,24 +110,48 @@ __device__ __forceinline__ float load_bias(const void *bias, int dtype, int n) {
   return dtype == HIF8_DTYPE_BF16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
 }
 
-template <int NT, int OUT, int ASRC>
-__global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_hif8_kernel(const GemvArgs p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t *act = smem + kLutBytes;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ks = gridDim.y, kr = blockIdx.y;  // cluster spans the K splits
-  const int k0 = kr * p.kc;
-  const int act_stride = gemv_act_stride<NT>(p.kc);
+// Launch geometry of one call (host-computed).
+struct GemvPlan {
+  int s = 0;        // cluster size = number of K slices (0: not applicable)
+  int kc = 0;       // K slice per CTA
+  int wk = 0;       // warps splitting an item's K slice (kc = wk * kWarpK)
+  int wr = 0;       // row groups of 16 per item (wr * wk == kWarps)
+  int nt = 1;       // 8-token MMA tiles (1: M <= 8, 2: M <= 16)
+  int clusters = 0;
+  int max_items = 0;  // row blocks per cluster (upper bound)
+};
 
-  // ---- prologue: lane-replicated decode table + decoded activation tile ----
+__host__ __device__ constexpr int act_stride_bytes(int kc) { return kc * 2 + 16; }
+
+// shared memory: table | activation tile | warp partials x2 | CTA partials
+// of every item of this cluster (reduced across the cluster once, at the end)
+__host__ __device__ constexpr size_t gemv_smem_bytes(int nt, int kc, int wr, int max_items) {
+  return (size_t)kLutBytes + (size_t)(8 * nt) * act_stride_bytes(kc) +
+         2 * (size_t)kWarps * 128 * nt * sizeof(float) + (size_t)max_items * (16 * wr) * 8 * nt * sizeof(float);
+}
+
+template <int NT, int OUT, int ASRC>
+__global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p, const GemvPlan plan) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int kTok = 8 * NT;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int S = plan.s, kc = plan.kc, WK = plan.wk, WR = plan.wr;
+  const int rank = (int)(blockIdx.x % S), cluster_id = (int)(blockIdx.x / S);
+  const int k0 = rank * kc;
+  const int act_stride = act_stride_bytes(kc);
+  uint8_t *act = smem + kLutBytes;
+  float *red = reinterpret_cast<float *>(act + (size_t)kTok * act_stride);  // [2][kWarps][16][kTok]
+  float *part = red + 2 * kWarps * 16 * kTok;                               // [items][16 * WR][kTok]
+
+  // ---- prologue: lane-replicated decode table + this rank's activation slice
   {
     uint32_t *lut = reinterpret_cast<uint32_t *>(smem);
-    for (int i = tid; i < 256 * 32; i += blockDim.x) {
+    for (int i = tid; i < 256 * 32; i += kThreads) {
       const int b = i >> 5, l = i & 31;
       lut[b * 64 + l] = g_decode_f32.v[b] >> 16;
     }
-    const int chunks_per_tok = p.kc >> 4;  // 16-byte chunks
-    for (int i = tid; i < 8 * NT * chunks_per_tok; i += blockDim.x) {
+    const int chunks_per_tok = kc >> 4;  // 16 K values per chunk
+    for (int i = tid; i < kTok * chunks_per_tok; i += kThreads) {
       const int tok = i / chunks_per_tok, ch = i - tok * chunks_per_tok;
       uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
       if (ASRC != kActCodes && tok < p.m) {
@@ -160,8 +178,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_hif8_kernel(const Gem
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint32_t w = w4[j];
-          r[2 * j] = (g_decode_f32.v[w & 0xFF] >> 16) | (g_decode_f32.v[(w >> 8) & 0xFF] & 0xFFFF0000u);
-          r[2 * j + 1] = (g_decode_f32.v[(w >> 16) & 0xFF] >> 16) | (g_decode_f32.v[w >> 24] & 0xFFFF0000u);
+          r[2 * j] = __byte_perm(g_decode_f32.v[w & 0xFF], g_decode_f32.v[(w >> 8) & 0xFF], 0x7632u);
+          r[2 * j + 1] = __byte_perm(g_decode_f32.v[(w >> 16) & 0xFF], g_decode_f32.v[w >> 24], 0x7632u);
         }
         o0 = make_uint4(r[0], r[1], r[2], r[3]);
         o1 = make_uint4(r[4], r[5], r[6], r[7]);
@@ -173,116 +191,122 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_hif8_kernel(const Gem
   }
   __syncthreads();
 
-  // ---- main loop --------------------------------------------------------
+  // ---- work assignment -----------------------------------------------------
   const int g = lane >> 2, t = lane & 3;
-  const int row0 = blockIdx.x * kGemvRows + warp * 16 + g;
-  const int r0 = min(row0, p.n - 1), r1 = min(row0 + 8, p.n - 1);
-  const uint8_t *w0 = p.w + (int64_t)r0 * p.k + k0 + t * 16;
-  const uint8_t *w1 = p.w + (int64_t)r1 * p.k + k0 + t * 16;
-  const uint32_t lut_base = (uint32_t)__cvta_generic_to_shared(smem);
+  const int wr = warp / WK, wk = warp - wr * WK;  // row group / K part of this warp
+  const int rows_per_item = 16 * WR;
+  const int n_items = (p.n + rows_per_item - 1) / rows_per_item;
+  const int my_items = n_items > cluster_id ? (n_items - cluster_id + plan.clusters - 1) / plan.clusters : 0;
+  const int kw0 = k0 + wk * kWarpK;  // this warp's K offset inside every item
+  const uint8_t *lut = smem;
   const uint32_t lane4 = (uint32_t)lane << 2;
-  const uint32_t act_base = (uint32_t)__cvta_generic_to_shared(act) + g * act_stride + t * 32;
-  const int nkb = p.kc >> 6;
+  const uint8_t *act_lane = act + g * act_stride + (wk * kWarpK / 64) * 128 + t * 32;
 
-  float acc[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  auto weight_ptrs = [&](int item, const uint8_t *&w0, const uint8_t *&w1) {
+    const int row = (cluster_id + item * plan.clusters) * rows_per_item + wr * 16 + g;
+    const int r0 = min(row, p.n - 1), r1 = min(row + 8, p.n - 1);
+    w0 = p.w + (int64_t)r0 * p.k + kw0 + t * 16;
+    w1 = p.w + (int64_t)r1 * p.k + kw0 + t * 16;
+  };
 
-  uint4 ring[kPrefetch][2];
+  uint4 ring[kRing][2];
+  if (my_items > 0) {
+    const uint8_t *w0, *w1;
+    weight_ptrs(0, w0, w1);
 #pragma unroll
-  for (int s = 0; s < kPrefetch; ++s) {
-    if (s < nkb) {
+    for (int s = 0; s < kRing; ++s) {
       ring[s][0] = ldg_stream(w0 + s * 64);
       ring[s][1] = ldg_stream(w1 + s * 64);
     }
   }
 
-  for (int kb0 = 0; kb0 < nkb; kb0 += kPrefetch) {
+  cg::cluster_group cluster = cg::this_cluster();
+  for (int item = 0; item < my_items; ++item) {
+    const uint8_t *n0 = nullptr, *n1 = nullptr;
+    const bool has_next = item + 1 < my_items;
+    if (has_next) weight_ptrs(item + 1, n0, n1);
+
+    float acc[2][NT][4];
 #pragma unroll
-    for (int s = 0; s < kPrefetch; ++s) {
-      const int kb = kb0 + s;
-      if (kb < nkb) {
-        const uint4 x0 = ring[s][0], x1 = ring[s][1];
-        if (kb + kPrefetch < nkb) {
-          ring[s][0] = ldg_stream(w0 + (kb + kPrefetch) * 64);
-          ring[s][1] = ldg_stream(w1 + (kb + kPrefetch) * 64);
-        }
-        // activation fragments of this 64-byte block: 16 BF16 per token row
-        uint4 bf[NT][2];
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) acc[h][nt][0] = acc[h][nt][1] = acc[h][nt][2] = acc[h][nt][3] = 0.f;
+
+#pragma unroll
+    for (int s = 0; s < kRing; ++s) {
+      const uint4 x0 = ring[s][0], x1 = ring[s][1];
+      if (has_next) {  // the next item's block s goes into the freed slot
+        ring[s][0] = ldg_stream(n0 + s * 64);
+        ring[s][1] = ldg_stream(n1 + s * 64);
+      }
+      uint4 bf[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(act_lane + nt * 8 * act_stride + s * 128);
+        bf[nt][0] = src[0];
+        bf[nt][1] = src[1];
+      }
+      const uint32_t wa[4] = {x0.x, x0.y, x0.z, x0.w};
+      const uint32_t wb[4] = {x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t a[4];
+        decode4(lut, wa[j], lane4, a[0], a[2]);
+        decode4(lut, wb[j], lane4, a[1], a[3]);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const uint32_t addr = act_base + nt * 8 * act_stride + kb * 128;
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(bf[nt][0].x), "=r"(bf[nt][0].y), "=r"(bf[nt][0].z), "=r"(bf[nt][0].w)
-                       : "r"(addr));
-          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                       : "=r"(bf[nt][1].x), "=r"(bf[nt][1].y), "=r"(bf[nt][1].z), "=r"(bf[nt][1].w)
-                       : "r"(addr + 16));
-        }
-        const uint32_t wa[4] = {x0.x, x0.y, x0.z, x0.w};
-        const uint32_t wb[4] = {x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t a[4];
-          decode4(lut_base, wa[j], lane4, a[0], a[2]);
-          decode4(lut_base, wb[j], lane4, a[1], a[3]);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            const uint4 &q = bf[nt][j >> 1];
-            const uint32_t b0 = (j & 1) ? q.z : q.x;
-            const uint32_t b1 = (j & 1) ? q.w : q.y;
-            mma_bf16_16816(acc[nt], a, b0, b1);
-          }
+          const uint4 &q = bf[nt][j >> 1];
+          mma_bf16_16816(acc[j & 1][nt], a, (j & 1) ? q.z : q.x, (j & 1) ? q.w : q.y);
         }
       }
     }
-  }
 
-  // ---- reduction over the K split + epilogue -----------------------------
-  const int n_a = row0, n_b = row0 + 8;
-  if (ks == 1) {
+    // ---- reduce the item: warps (fixed order), then cluster ranks ---------
+    const int buf = item & 1;
+    float *wred = red + ((size_t)buf * kWarps + warp) * 16 * kTok;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int m = nt * 8 + 2 * t + (q & 1);
-        const int n = (q < 2) ? n_a : n_b;
+        const int rl = g + ((q < 2) ? 0 : 8);
+        wred[rl * kTok + m] = acc[0][nt][q] + acc[1][nt][q];
+      }
+    }
+    __syncthreads();
+    const int row_base = (cluster_id + item * plan.clusters) * rows_per_item;
+    float *cpart = part + (size_t)item * rows_per_item * kTok;
+    for (int e = tid; e < rows_per_item * kTok; e += kThreads) {
+      const int rl = e / kTok, m = e - rl * kTok;  // row within the item, token
+      const int grp = rl >> 4, r16 = rl & 15;
+      const float *src = red + ((size_t)buf * kWarps + grp * WK) * 16 * kTok + r16 * kTok + m;
+      float v = 0.f;
+      for (int w = 0; w < WK; ++w) v += src[(size_t)w * 16 * kTok];
+      if (S == 1) {
+        const int n = row_base + rl;
         if (m < p.m && n < p.n) {
-          float v = acc[nt][q] * __ldg(p.cs + n);
+          v = v * __ldg(p.cs + n);
           v = v * __ldg(p.ts + m * p.ts_stride);
           if (p.bias) v += load_bias(p.bias, p.bias_dtype, n);
           store_out<OUT>(p.out, (int64_t)m * p.n + n, v);
         }
+      } else {
+        cpart[e] = v;
       }
     }
-    return;
   }
+  if (S == 1) return;
 
-  cg::cluster_group cluster = cg::this_cluster();
-  float *red = reinterpret_cast<float *>(act);  // [kGemvRows][8 * NT]
-  __syncthreads();                              // activation tile is dead now
-  constexpr int kTok = 8 * NT;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int m = nt * 8 + 2 * t + (q & 1);
-      const int rl = warp * 16 + g + ((q < 2) ? 0 : 8);
-      red[rl * kTok + m] = acc[nt][q];
-    }
-  }
+  // ---- cross-rank reduction of every item, once: rank r owns the elements
+  // e with e % S == r; partials are summed in rank order (deterministic).
   cluster.sync();
-  // CTA `kr` of the cluster reduces rows [kr * rows_per, (kr + 1) * rows_per)
-  const int rows_per = kGemvRows / ks;
-  const int elems = rows_per * kTok;
-  for (int i = tid; i < elems; i += blockDim.x) {
-    const int m = i / rows_per, rl = kr * rows_per + (i - m * rows_per);
+  const int per_item = rows_per_item * kTok;
+  for (int e = rank + S * tid; e < my_items * per_item; e += S * kThreads) {
     float v = 0.f;
-    for (int r = 0; r < ks; ++r) {
-      const float *remote = cluster.map_shared_rank(red, r);
-      v += remote[rl * kTok + m];
-    }
-    const int n = blockIdx.x * kGemvRows + rl;
+    for (int r = 0; r < S; ++r) v += cluster.map_shared_rank(part, r)[e];
+    const int item = e / per_item, rem = e - item * per_item;
+    const int rl = rem / kTok, m = rem - rl * kTok;
+    const int n = (cluster_id + item * plan.clusters) * rows_per_item + rl;
     if (m < p.m && n < p.n) {
       v = v * __ldg(p.cs + n);
       v = v * __ldg(p.ts + m * p.ts_stride);
@@ -290,7 +314,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_hif8_kernel(const Gem
       store_out<OUT>(p.out, (int64_t)m * p.n + n, v);
     }
   }
-  cluster.sync();  // keep this CTA's partials alive until every reader is done
+  cluster.sync();  // no CTA may leave while a peer could still read its partials
 }
 
 // Any shape, any alignment: one warp per (m, n) output, FP32 accumulation in
@@ -333,52 +357,113 @@ __global__ void __launch_bounds__(256) linear_hif8_generic(const GemvArgs p) {
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-struct GemvPlan {
-  int ks = 0;   // cluster size over K (0 = fast path not applicable)
-  int kc = 0;
-  int nt = 1;
-};
+constexpr size_t kMaxSmem = 227 * 1024;
 
-static GemvPlan plan_gemv(int64_t m, int64_t n, int64_t k) {
-  GemvPlan plan;
-  if (m < 1 || m > 16 || k % 64 != 0) return plan;
-  plan.nt = m > 8 ? 2 : 1;
-  const int64_t row_blocks = (n + kGemvRows - 1) / kGemvRows;
-  const int64_t target = 2LL * num_sms();  // two co-resident CTAs per SM
-  for (int ks = 1; ks <= 8; ks *= 2) {
-    if (k % (64LL * ks) != 0) break;
-    const int64_t kc = k / ks;
-    const size_t smem = plan.nt == 2 ? gemv_smem_bytes<2>((int)kc) : gemv_smem_bytes<1>((int)kc);
-    if (smem > 200 * 1024) continue;  // this split does not fit; try a finer one
-    plan.ks = ks;
-    plan.kc = (int)kc;
-    if (row_blocks * ks >= target) break;
+// Clusters of `s` CTAs of `kernel` that can be resident at once (cached per
+// device, kernel, cluster size and shared-memory size).
+static int max_active_clusters(const void *kernel, int s, size_t smem) {
+  struct Entry {
+    const void *kernel;
+    int device, s;
+    size_t smem;
+    int clusters;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry &e : cache)
+      if (e.kernel == kernel && e.device == dev && e.s == s && e.smem == smem) return e.clusters;
   }
-  return plan;
+  const int sms = num_sms();
+  int clusters = sms / s;
+  if (ensure_smem_limit(kernel, smem) == HIF8_OK) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(s * (sms / s)), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)s;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) == cudaSuccess && n > 0) clusters = n < clusters ? n : clusters;
+    else cudaGetLastError();
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache.push_back({kernel, dev, s, smem, clusters});
+  return clusters;
+}
+
+// Pick the K split S (cluster size) and the warp arrangement that balance the
+// rounds of row blocks over the co-resident persistent clusters best.
+static GemvPlan plan_gemv(int64_t m, int64_t n, int64_t k, const void *kernel) {
+  GemvPlan best;
+  if (m < 1 || m > 16 || n < 1 || k % kWarpK != 0) return best;
+  const int nt = m > 8 ? 2 : 1;
+  const int sms = num_sms();
+  double best_eff = -1.0;
+  for (int s = 1; s <= 8; ++s) {
+    if (k % ((int64_t)s * kWarpK) != 0) continue;
+    const int64_t kc = k / s;
+    if (kc % kWarpK != 0) continue;
+    const int64_t wk = kc / kWarpK;
+    if (wk > kWarps || kWarps % wk != 0) continue;
+    const int wr = (int)(kWarps / wk);
+    const int64_t items = (n + 16 * wr - 1) / (16 * wr);
+    // shared memory is sized for the worst case of sms / s clusters
+    const int64_t rounds_max = (items + (sms / s) - 1) / (sms / s);
+    const size_t smem = gemv_smem_bytes(nt, (int)kc, wr, s > 1 ? (int)std::max<int64_t>(rounds_max, items) : 0);
+    if (gemv_smem_bytes(nt, (int)kc, wr, 0) > kMaxSmem) continue;
+    const int clusters = max_active_clusters(kernel, s, std::min(smem, kMaxSmem));
+    if (clusters < 1) continue;
+    const int64_t rounds = (items + clusters - 1) / clusters;
+    if (gemv_smem_bytes(nt, (int)kc, wr, s > 1 ? (int)rounds : 0) > kMaxSmem) continue;
+    // fraction of the machine's CTA-rounds doing useful work
+    const double eff = (double)items / (double)(rounds * clusters) * (double)(clusters * s) / (double)sms;
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best.s = s;
+      best.kc = (int)kc;
+      best.wk = (int)wk;
+      best.wr = wr;
+      best.nt = nt;
+      best.clusters = clusters;
+      best.max_items = s > 1 ? (int)rounds : 0;
+    }
+  }
+  return best;
+}
+
+template <int NT, int OUT, int ASRC>
+static const void *gemv_kernel_ptr() {
+  return reinterpret_cast<const void *>(gemv_hif8_kernel<NT, OUT, ASRC>);
 }
 
 template <int NT, int OUT, int ASRC>
 static int launch_gemv(const GemvArgs &args, const GemvPlan &plan, cudaStream_t stream) {
-  const size_t smem = gemv_smem_bytes<NT>(plan.kc);
+  const size_t smem = gemv_smem_bytes(NT, plan.kc, plan.wr, plan.max_items);
   auto kernel = gemv_hif8_kernel<NT, OUT, ASRC>;
   const int st = ensure_smem_limit(reinterpret_cast<const void *>(kernel), smem);
   if (st != HIF8_OK) return st;
-  cudaError_t err;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((args.n + kGemvRows - 1) / kGemvRows), (unsigned)plan.ks, 1);
-  cfg.blockDim = dim3(kGemvWarps * 32, 1, 1);
+  cfg.gridDim = dim3((unsigned)(plan.clusters * plan.s), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = (unsigned)plan.ks;
+  attr[0].val.clusterDim.x = (unsigned)plan.s;
+  attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  GemvArgs a = args;
-  a.kc = plan.kc;
-  err = cudaLaunchKernelEx(&cfg, kernel, a);
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, args, plan);
   if (err != cudaSuccess) {
     set_last_error(err);
     return HIF8_ERR_CUDA;
@@ -396,7 +481,7 @@ static int launch_generic(const GemvArgs &args, cudaStream_t stream) {
   return check_launch();
 }
 
-// y = a @ w^T for any m: the split-K tensor-core kernel on 16-token slices
+// y = a @ w^T for any m: the persistent split-K kernel on 16-token slices
 // when the shape allows it, otherwise the generic kernel.
 int run_linear(GemvArgs args, int output_dtype, cudaStream_t stream) {
   const bool vec_ok = aligned16(args.a) && aligned16(args.w) && args.k % 64 == 0;
@@ -407,9 +492,13 @@ int run_linear(GemvArgs args, int output_dtype, cudaStream_t stream) {
     s.a = static_cast<const uint8_t *>(args.a) + (int64_t)m0 * args.k;
     s.ts = args.ts + m0;
     s.out = static_cast<uint8_t *>(args.out) + (int64_t)m0 * args.n * 2;
-    const GemvPlan plan = vec_ok ? plan_gemv(s.m, s.n, s.k) : GemvPlan{};
+    const void *kptr = s.m > 8 ? (bf16_out ? gemv_kernel_ptr<2, HIF8_DTYPE_BF16, kActCodes>()
+                                           : gemv_kernel_ptr<2, HIF8_DTYPE_F16, kActCodes>())
+                               : (bf16_out ? gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActCodes>()
+                                           : gemv_kernel_ptr<1, HIF8_DTYPE_F16, kActCodes>());
+    const GemvPlan plan = vec_ok ? plan_gemv(s.m, s.n, s.k, kptr) : GemvPlan{};
     int status;
-    if (plan.ks == 0) {
+    if (plan.s == 0) {
       status = bf16_out ? launch_generic<HIF8_DTYPE_BF16, kActCodes>(s, stream)
                         : launch_generic<HIF8_DTYPE_F16, kActCodes>(s, stream);
     } else if (plan.nt == 1) {
@@ -429,8 +518,12 @@ int run_fused_linear(const GemvArgs &args, int x_dtype, int output_dtype, cudaSt
   const bool bf16_out = output_dtype == HIF8_DTYPE_BF16;
   const bool bf16_in = x_dtype == HIF8_DTYPE_BF16;
   const bool vec_ok = aligned16(args.a) && aligned16(args.w) && args.k % 64 == 0 && args.m <= 8;
-  const GemvPlan plan = vec_ok ? plan_gemv(args.m, args.n, args.k) : GemvPlan{};
-  if (plan.ks == 0) {
+  const void *kptr = bf16_in ? (bf16_out ? gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActBf16>()
+                                         : gemv_kernel_ptr<1, HIF8_DTYPE_F16, kActBf16>())
+                             : (bf16_out ? gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActF16>()
+                                         : gemv_kernel_ptr<1, HIF8_DTYPE_F16, kActF16>());
+  const GemvPlan plan = vec_ok ? plan_gemv(args.m, args.n, args.k, kptr) : GemvPlan{};
+  if (plan.s == 0) {
     if (bf16_in)
       return bf16_out ? launch_generic<HIF8_DTYPE_BF16, kActBf16>(args, stream)
                       : launch_generic<HIF8_DTYPE_F16, kActBf16>(args, stream);
