@@ -473,7 +473,7 @@ def run_profile_case(spec: str, launches: int) -> None:
     from hif8_b200 import native, scheme
 
     kind, shape, m = spec.split(":")
-    if kind != "gemv":
+    if kind not in ("gemv", "gemm"):
         raise SystemExit(f"unknown profile case {spec!r}")
     n, k = {name: (n, k) for name, n, k in SHAPES}[shape]
     m = int(m)

@@ -1,12 +1,436 @@
-// Prefill GEMM entry (tcgen05).  Until the tcgen05 kernel is enabled every
-// shape reports "unsupported" and soft_hif8_gemm runs the split-K kernel on
-// 16-token slices.
+// Prefill GEMM for HiF8 W8A8 on the 5th-generation tensor cores (tcgen05).
+//
+//   y[m, n] = cast((acc[m, n] * cs[n]) * ts[m] + bias[n]),
+//   acc = sum_k decode(a[m, k]) * decode(w[n, k])   (BF16 operands, FP32 in TMEM)
+//
+// Every finite HiF8 code is exactly a BF16, so decoding both operands to BF16
+// and accumulating in FP32 is exact up to the summation order.
+//
+// Work split per CTA (one 128-channel x BN-token output tile, 6 warps):
+//   * the activation is decoded once per call into a BF16 workspace
+//     [M, K]; warp 0 streams its BN x 64 tiles with TMA (128-byte swizzle)
+//     into a 4-stage shared-memory ring -- the MMA's B operand;
+//   * warps 2..5 own one weight row each per lane (128 rows), load 64 bytes
+//     of it per stage, decode them with the lane-replicated shared-memory
+//     table and write the 64 BF16 values straight into tensor memory with
+//     tcgen05.st: the MMA's A operand lives in TMEM, so the decoded weight
+//     never touches shared memory;
+//   * warp 1 issues tcgen05.mma (M=128, N=BN, K=16) from one thread and
+//     returns each stage with tcgen05.commit;
+//   * warps 2..5 then read the FP32 accumulator with tcgen05.ld (each warp
+//     its 32-lane quarter) and apply the channel scale, token scale and bias.
+// Every wait is bounded; a timed-out wait is counted in the error word of the
+// workspace and the kernel runs to completion.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "linear.cuh"
 
 namespace hif8 {
 
-bool hif8_gemm_tc_supported(int64_t, int64_t, int64_t) { return false; }
-size_t hif8_gemm_tc_workspace(int64_t, int64_t, int64_t) { return 0; }
-int hif8_gemm_tc(const GemvArgs &, int, void *, size_t, cudaStream_t) { return HIF8_ERR_INVALID_ARGUMENT; }
+constexpr int kTcBM = 128;      // weight rows (output channels) per tile = TMEM lanes
+constexpr int kTcBK = 64;       // K per stage: one 128-byte swizzle atom of BF16
+constexpr int kTcStages = 4;
+constexpr int kTcThreads = 192;
+constexpr int kTcLut = 256 * 256;  // lane-replicated decode table (see gemv.cu)
+constexpr uint64_t kWaitNs = 100ull * 1000 * 1000;  // 100 ms per pipeline wait
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for the phase with the given parity.  A wait that outlives
+// kWaitNs raises the CTA's abort flag, after which every later wait returns
+// false at once, so a broken pipeline ends the kernel within milliseconds.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+  const uint32_t addr = smem_addr(bar);
+  for (int i = 0; i < 64; ++i)
+    if (mbar_try(addr, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!*abort) {
+    if (mbar_try(addr, parity)) return true;
+    if (global_ns() - t0 > kWaitNs) *abort = 1;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// K-major, 128-byte swizzle UMMA shared-memory descriptor (8-row atoms of
+// 128 bytes, atoms 1024 bytes apart).
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void *p) {
+  const uint64_t addr = smem_addr(p);
+  uint64_t d = (addr >> 4) & 0x3FFFull;   // start address
+  d |= (uint64_t)1 << 16;                 // leading byte offset (unused with swizzle)
+  d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset between 8-row atoms
+  d |= (uint64_t)1 << 46;                 // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: BF16 A and B (both K-major), FP32 D.
+template <int BN>
+__device__ __forceinline__ constexpr uint32_t instr_desc_bf16() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kTcBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]),
+      "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ uint4 ldg_nc(const uint8_t *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t lut_pair(const uint8_t *lut, uint32_t word, uint32_t lane4, bool high) {
+  const uint32_t e0 = *reinterpret_cast<const uint32_t *>(lut + __byte_perm(word, lane4, high ? 0x5524u : 0x5504u));
+  const uint32_t e1 = *reinterpret_cast<const uint32_t *>(lut + __byte_perm(word, lane4, high ? 0x5534u : 0x5514u));
+  return __byte_perm(e0, e1, 0x5410u);
+}
+
+struct TcParams {
+  const uint8_t *w;
+  const float *ts, *cs;
+  const void *bias;
+  void *out;
+  int *err;
+  int m, n, k, bias_dtype, ts_stride;
+};
+
+template <int OUT>
+__device__ __forceinline__ uint32_t to_out_bits(float v) {
+  if constexpr (OUT == HIF8_DTYPE_BF16) return f32_to_bf16_bits(v);
+  else return f32_to_f16_bits(v);
+}
+
+template <int BN, int OUT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_hif8_tc_kernel(const __grid_constant__ CUtensorMap xmap, const TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled operand stages
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kBBytes = BN * 128;
+  uint8_t *b_stages = smem;                                  // [stages][BN][128 B] swizzled
+  uint8_t *lut = b_stages + kTcStages * kBBytes;            // 64 KB
+  uint64_t *bars = reinterpret_cast<uint64_t *>(lut + kTcLut);
+  uint64_t *full_a = bars, *full_b = bars + kTcStages, *empty = bars + 2 * kTcStages;
+  uint64_t *accum_full = bars + 3 * kTcStages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum_full + 1);
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // token tiles vary fastest, so the CTAs sharing one weight tile run together
+  // and the weight crosses HBM once while the BF16 activation stays in L2
+  const int m0 = blockIdx.x * BN, n0 = blockIdx.y * kTcBM;
+  constexpr uint32_t kTmemCols = BN + 4 * 32 <= 256 ? 256 : 512;
+  const int nkb = p.k / kTcBK;
+
+  // ---- set-up: barriers, TMEM, decode table --------------------------------
+  if (tid == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full_a[s], 4);  // one arrival per decoding warp
+      mbar_init(&full_b[s], 1);  // TMA transaction
+      mbar_init(&empty[s], 1);   // tcgen05.commit
+    }
+    mbar_init(accum_full, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // whole warp allocates: BN accumulator columns + 4 stages x 32 A columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  for (int i = tid; i < 256 * 32; i += kTcThreads) {
+    const int b = i >> 5, l = i & 31;
+    reinterpret_cast<uint32_t *>(lut)[b * 64 + l] = g_decode_f32.v[b] >> 16;
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t d_tmem = tmem;                  // columns [0, BN)
+  const uint32_t a_tmem0 = tmem + (uint32_t)BN;  // stage s: columns BN + 32 s
+
+  if (warp == 0) {
+    // ---- TMA producer of the activation (B) tiles ---------------------------
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kTcStages;
+        if (kb >= kTcStages && !mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort)) atomicAdd(p.err, 1);
+        mbar_expect_tx(&full_b[s], kBBytes);
+        tma_load_2d(b_stages + s * kBBytes, &xmap, kb * kTcBK, m0, &full_b[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----------------------------------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc_bf16<BN>();
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kTcStages;
+        const uint32_t parity = (kb / kTcStages) & 1;
+        bool ok = mbar_wait(&full_a[s], parity, abort);
+        ok = mbar_wait(&full_b[s], parity, abort) && ok;
+        if (!ok) atomicAdd(p.err, 1);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t bdesc = smem_desc_sw128(b_stages + s * kBBytes);
+#pragma unroll
+        for (int j = 0; j < kTcBK / 16; ++j)  // K = 16 per MMA: 32 bytes along the swizzled row
+          mma_ts(d_tmem, a_tmem0 + s * 32 + j * 8, bdesc + (uint64_t)(j * 2), idesc, (kb | j) != 0);
+        mma_commit(&empty[s]);
+      }
+      mma_commit(accum_full);
+    }
+  } else {
+    // ---- weight decoders (warps 2..5), then the epilogue ---------------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    const int n = n0 + row;
+    const uint8_t *wrow = p.w + (int64_t)min(n, p.n - 1) * p.k;
+    const uint32_t lane4 = (uint32_t)lane << 2;
+    uint4 cur[4], nxt[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) cur[c] = ldg_nc(wrow + c * 16);
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % kTcStages;
+      if (kb + 1 < nkb) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) nxt[c] = ldg_nc(wrow + (kb + 1) * kTcBK + c * 16);
+      }
+      uint32_t v[32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t words[4] = {cur[c].x, cur[c].y, cur[c].z, cur[c].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          v[c * 8 + q * 2] = lut_pair(lut, words[q], lane4, false);
+          v[c * 8 + q * 2 + 1] = lut_pair(lut, words[q], lane4, true);
+        }
+      }
+      if (kb >= kTcStages) {
+        if (!mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort)) atomicAdd(p.err, 1);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      }
+      tmem_st32(a_tmem0 + s * 32 + ((uint32_t)(quarter * 32) << 16), v);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_a[s]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) cur[c] = nxt[c];
+    }
+
+    // epilogue: lane = output channel n, columns = tokens
+    if (!mbar_wait(accum_full, 0, abort)) atomicAdd(p.err, 1);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const bool n_ok = n < p.n;
+    const float cs = n_ok ? p.cs[n] : 0.f;
+    float bias = 0.f;
+    if (n_ok && p.bias) {
+      const uint16_t h = static_cast<const uint16_t *>(p.bias)[n];
+      bias = p.bias_dtype == HIF8_DTYPE_BF16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
+    }
+    uint16_t *out = static_cast<uint16_t *>(p.out);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t acc[32];
+      tmem_ld32(d_tmem + (uint32_t)c0 + ((uint32_t)(quarter * 32) << 16), acc);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int m = m0 + c0 + j;
+        if (n_ok && m < p.m) {
+          float val = __uint_as_float(acc[j]) * cs;
+          val = val * p.ts[(int64_t)m * p.ts_stride];
+          val += bias;
+          out[(int64_t)m * p.n + n] = (uint16_t)to_out_bits<OUT>(val);
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// Decode HiF8 activation bytes to unscaled BF16 (exact) for the TMA B operand.
+__global__ void __launch_bounds__(256) decode_to_bf16(const uint8_t *__restrict__ a, uint16_t *__restrict__ out,
+                                                      int64_t chunks) {
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks; c += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(a + c * 16);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t r[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      r[2 * j] = __byte_perm(g_decode_f32.v[w[j] & 0xFF], g_decode_f32.v[(w[j] >> 8) & 0xFF], 0x7632u);
+      r[2 * j + 1] = __byte_perm(g_decode_f32.v[(w[j] >> 16) & 0xFF], g_decode_f32.v[w[j] >> 24], 0x7632u);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(out + c * 16);
+    dst[0] = make_uint4(r[0], r[1], r[2], r[3]);
+    dst[1] = make_uint4(r[4], r[5], r[6], r[7]);
+  }
+}
+
+// ------------------------------------------------------------------ host --
+
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+constexpr int64_t kTcMinM = 32;
+
+bool hif8_gemm_tc_supported(int64_t m, int64_t n, int64_t k) {
+  return m >= kTcMinM && n >= 64 && k % kTcBK == 0 && k >= kTcBK && m < (1LL << 31) && n <= 65535LL * kTcBM;
+}
+
+static size_t err_offset(int64_t m, int64_t k) { return ((size_t)m * k * 2 + 255) & ~size_t(255); }
+
+size_t hif8_gemm_tc_workspace(int64_t m, int64_t n, int64_t k) {
+  (void)n;
+  return err_offset(m, k) + 256;  // BF16 activation copy + error word
+}
+
+template <int BN>
+static constexpr size_t tc_smem_bytes() {
+  return 1024 + (size_t)kTcStages * BN * 128 + kTcLut + (3 * kTcStages + 1) * 8 + 16;
+}
+
+template <int BN, int OUT>
+static int launch_tc(const CUtensorMap &map, const TcParams &p, cudaStream_t stream) {
+  auto kernel = gemm_hif8_tc_kernel<BN, OUT>;
+  const size_t smem = tc_smem_bytes<BN>();
+  const int st = ensure_smem_limit(reinterpret_cast<const void *>(kernel), smem);
+  if (st != HIF8_OK) return st;
+  dim3 grid((unsigned)((p.m + BN - 1) / BN), (unsigned)((p.n + kTcBM - 1) / kTcBM), 1);
+  kernel<<<grid, kTcThreads, smem, stream>>>(map, p);
+  return check_launch();
+}
+
+int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t workspace_bytes,
+                 cudaStream_t stream) {
+  const int64_t m = args.m, n = args.n, k = args.k;
+  if (workspace_bytes < hif8_gemm_tc_workspace(m, n, k)) return HIF8_ERR_WORKSPACE;
+  auto encode = tensor_map_encoder();
+  if (!encode) return HIF8_ERR_CUDA;
+  uint16_t *xb = static_cast<uint16_t *>(workspace);
+  int *err = reinterpret_cast<int *>(static_cast<uint8_t *>(workspace) + err_offset(m, k));
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), stream);
+  if (e != cudaSuccess) {
+    set_last_error(e);
+    return HIF8_ERR_CUDA;
+  }
+  // 1. activation -> BF16 (exact), 16 bytes per thread (k % 64 == 0)
+  const int64_t chunks = m * k / 16;
+  int64_t blocks = (chunks + 255) / 256;
+  if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
+  decode_to_bf16<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint8_t *>(args.a), xb, chunks);
+  int status = check_launch();
+  if (status != HIF8_OK) return status;
+
+  // 2. the tcgen05 GEMM; BN = tokens per tile
+  const int bn = m >= 256 ? 256 : (m >= 128 ? 128 : 64);
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+  const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)bn};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return HIF8_ERR_CUDA;
+  TcParams p{args.w, args.ts, args.cs, args.bias, args.out, err, args.m, args.n, args.k, args.bias_dtype, args.ts_stride};
+  const bool bf16 = output_dtype == HIF8_DTYPE_BF16;
+  if (bn == 256) return bf16 ? launch_tc<256, HIF8_DTYPE_BF16>(map, p, stream) : launch_tc<256, HIF8_DTYPE_F16>(map, p, stream);
+  if (bn == 128) return bf16 ? launch_tc<128, HIF8_DTYPE_BF16>(map, p, stream) : launch_tc<128, HIF8_DTYPE_F16>(map, p, stream);
+  return bf16 ? launch_tc<64, HIF8_DTYPE_BF16>(map, p, stream) : launch_tc<64, HIF8_DTYPE_F16>(map, p, stream);
+}
 
 }  // namespace hif8

@@ -89,8 +89,9 @@ int hif8_scaled_decode(const uint8_t *data, int64_t rows, int64_t k, int64_t dat
  * soft_hif8_gemm replaces ops soft_hif8_gemm / soft_hif8_prefill_gemm
  * (csrc/extension/pybind.cpp:11, hif8_native.cpp:633-669), any m >= 1; small
  * m runs the split-K tensor-core GEMV, large m the tcgen05 GEMM.
- * workspace: soft_hif8_gemm_workspace_size() bytes of device memory (may be
- * NULL when that size is 0). */
+ * workspace: soft_hif8_gemm_workspace_size() bytes of device memory, 256-byte
+ * aligned (may be NULL when that size is 0); it holds the BF16 copy of the
+ * activation that the tensor-memory accelerator streams, and one error word. */
 int soft_hif8_gemv(const uint8_t *activation, const uint8_t *weight, const float *token_scale,
                    const float *channel_scale, const void *bias, int bias_dtype,
                    int output_dtype, int64_t m, int64_t n, int64_t k, void *out, void *stream);

@@ -1,0 +1,140 @@
+"""Prefill GEMM (M >= 32, K % 64 == 0) on the tcgen05 tensor cores against
+the FP64 oracle.
+
+The reference computes the same product in FP32 on its CPU/NPU paths
+(csrc/hif8_native.cpp:633-669, soft_hif8_gemm); the tolerance MAX_REL = 1e-2
+of the largest |output| covers FP32 accumulation plus the final BF16/FP16
+rounding.  The activation/weight shapes follow configs[2] of the workload
+(prefill of the Qwen3.5-9B projection shapes)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests._helpers import max_rel
+from tests.test_linear_gpu import _activations, _hif8_weights, _native, _to
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+MAX_REL = 1.0e-2
+
+
+def _err_word(workspace, m, k) -> int:
+    off = (m * k * 2 + 255) // 256 * 256
+    return int(workspace[off:off + 4].cpu().view(torch.int32)[0])
+
+
+@pytest.mark.parametrize("n,k", [(24576, 4096), (4096, 12288), (6144, 4096)])
+@pytest.mark.parametrize("m", [32, 512, 4096])
+def test_prefill_gemm_projection_shapes(m, n, k):
+    """Oracle on 192 sampled channels (FP64), torch FP32 on the GPU for all."""
+    from hif8_b200 import cabi
+
+    w, w_s = _hif8_weights(n, k, seed=11, outlier_frac=1e-3)
+    _, a, a_s, _ = _activations(m, k, seed=m + 3)
+    w_dev, ws_dev, a_dev, as_dev = _to(w), _to(w_s), _to(a), _to(a_s)
+    lib = cabi.library()
+    need = lib.soft_hif8_gemm_workspace_size(m, n, k)
+    assert need >= m * k * 2
+    workspace = torch.full((need,), 0xAB, dtype=torch.uint8, device=DEV)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+    cabi.gemm(a_dev, w_dev, as_dev, ws_dev, None, out, workspace)
+    torch.cuda.synchronize()
+    assert _err_word(workspace, m, k) == 0, "a pipeline wait timed out"
+    got = out.float().cpu().numpy()
+    cols = np.sort(np.random.default_rng(m + n).choice(n, size=192, replace=False))
+    rows = np.arange(m) if m <= 512 else np.sort(np.random.default_rng(m).choice(m, size=384, replace=False))
+    expected = oracle.linear(a[rows], w[cols], a_s[rows], w_s[cols])
+    assert max_rel(got[np.ix_(rows, cols)], expected) <= MAX_REL
+    lut = torch.from_numpy(oracle.decode_table()).to(DEV)
+    ref32 = (lut[a_dev.long()] * as_dev[:, None]) @ (lut[w_dev.long()] * ws_dev[:, None]).T
+    assert max_rel(got, ref32.cpu().numpy()) <= MAX_REL
+    again = torch.empty_like(out)
+    cabi.gemm(a_dev, w_dev, as_dev, ws_dev, None, again, workspace)
+    assert torch.equal(out, again), "run-twice determinism"
+
+
+@pytest.mark.parametrize("m,n,k", [(33, 64, 64), (130, 1000, 192), (300, 1000, 4096), (257, 130, 640)])
+def test_prefill_gemm_ragged_tiles_bias_f16(m, n, k):
+    """Token and channel tails inside a tile, K of one stage, FP16 output and
+    BF16/FP16 bias (reference tests/test_npu_ops.py:296-344)."""
+    ext = _native().load_extension()
+    w, w_s = _hif8_weights(n, k, seed=m, outlier_frac=1e-3)
+    _, a, a_s, _ = _activations(m, k, seed=n)
+    bias = (np.random.default_rng(k).random(n).astype(np.float32) - 0.5)
+    for out_dtype in (torch.float16, torch.bfloat16):
+        for bias_dtype in (torch.float16, torch.bfloat16):
+            b = _to(bias, bias_dtype)
+            out = ext.soft_hif8_gemm(_to(a), _to(w), _to(a_s), _to(w_s), b, out_dtype)
+            expected = oracle.linear(a, w, a_s, w_s, b.float().cpu().numpy())
+            assert max_rel(out.float().cpu().numpy(), expected) <= MAX_REL, (out_dtype, bias_dtype)
+
+
+def test_prefill_gemm_propagates_special_codes():
+    """NaN and +-Inf activation codes reach the output of their token row
+    (reference tests/test_npu_ops.py:179-214, at a tensor-core size)."""
+    ext = _native().load_extension()
+    one = oracle.encode_value(1.0)
+    m, n, k = 48, 128, 64
+    codes = [0x80, 0x6F, 0xEF] + [one] * (m - 3)
+    act = np.zeros((m, k), np.uint8)
+    act[:, 0] = codes
+    act[:, 1] = one
+    weight = np.zeros((n, k), np.uint8)
+    weight[:, 0] = one
+    ts = np.linspace(0.5, 2.0, m).astype(np.float32)
+    dec = oracle.decode_table()
+    for out_dtype in (torch.float16, torch.bfloat16):
+        out = ext.soft_hif8_gemm(_to(act), _to(weight), _to(ts), _to(np.ones(n, np.float32)), None, out_dtype)
+        got = out.float().cpu().numpy()
+        for r in range(m):
+            expected = float(dec[codes[r]]) * float(ts[r])
+            if np.isnan(expected):
+                assert np.isnan(got[r]).all()
+            else:
+                rounded = float(torch.tensor(expected, dtype=torch.float32).to(out_dtype).float())
+                assert (got[r] == rounded).all(), r
+
+
+def test_prefill_gemm_matches_exact_products():
+    """Small-integer operands: every partial sum is exact in FP32, so the
+    tensor-core result equals the oracle bit for bit after rounding."""
+    ext = _native().load_extension()
+    m, n, k = 96, 256, 512
+    rng = np.random.default_rng(4)
+    values = np.array([-2.0, -1.0, -0.5, 0.0, 0.5, 1.0, 2.0], np.float32)
+    a = np.vectorize(oracle.encode_value)(values[rng.integers(0, 7, (m, k))]).astype(np.uint8)
+    w = np.vectorize(oracle.encode_value)(values[rng.integers(0, 7, (n, k))]).astype(np.uint8)
+    ts = np.ones(m, np.float32)
+    cs = np.ones(n, np.float32)
+    out = ext.soft_hif8_gemm(_to(a), _to(w), _to(ts), _to(cs), None, torch.float16)
+    expected = oracle.linear(a, w, ts, cs).astype(np.float16)
+    np.testing.assert_array_equal(out.cpu().numpy(), expected)
+
+
+def test_prefill_gemm_workspace_contract():
+    """The C ABI rejects a short or misaligned workspace instead of writing
+    past it."""
+    from hif8_b200 import cabi
+
+    m, n, k = 64, 128, 256
+    lib = cabi.library()
+    need = lib.soft_hif8_gemm_workspace_size(m, n, k)
+    a = torch.zeros(m, k, dtype=torch.uint8, device=DEV)
+    w = torch.zeros(n, k, dtype=torch.uint8, device=DEV)
+    ts = torch.ones(m, device=DEV)
+    cs = torch.ones(n, device=DEV)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+    big = torch.empty(need + 256, dtype=torch.uint8, device=DEV)
+    with pytest.raises(cabi.Hif8Error) as short:
+        cabi.gemm(a, w, ts, cs, None, out, big[:need - 1])
+    assert short.value.status == cabi.HIF8_ERR_WORKSPACE
+    with pytest.raises(cabi.Hif8Error) as misaligned:
+        cabi.gemm(a, w, ts, cs, None, out, big[16:16 + need])
+    assert misaligned.value.status == cabi.HIF8_ERR_WORKSPACE
+    cabi.gemm(a, w, ts, cs, None, out, big[:need])
+    torch.cuda.synchronize()
+    assert torch.equal(out.float().cpu(), torch.zeros(m, n))
