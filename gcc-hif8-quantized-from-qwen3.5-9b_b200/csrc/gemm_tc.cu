@@ -6,19 +6,21 @@
 // Every finite HiF8 code is exactly a BF16, so decoding both operands to BF16
 // and accumulating in FP32 is exact up to the summation order.
 //
-// Work split per CTA (one 128-channel x BN-token output tile, 6 warps):
+// Work split per CTA (one 128-channel x BN-token output tile, 10 warps):
 //   * the activation is decoded once per call into a BF16 workspace
 //     [M, K]; warp 0 streams its BN x 64 tiles with TMA (128-byte swizzle)
 //     into a 4-stage shared-memory ring -- the MMA's B operand;
-//   * warps 2..5 own one weight row each per lane (128 rows), load 64 bytes
-//     of it per stage, decode them with the lane-replicated shared-memory
-//     table and write the 64 BF16 values straight into tensor memory with
-//     tcgen05.st: the MMA's A operand lives in TMEM, so the decoded weight
-//     never touches shared memory;
+//   * warps 2..9 own one weight row per lane (128 rows, two warps per row
+//     quarter, 32 bytes of each 64-byte stage each), keep 4 stages of loads
+//     in flight, decode with the lane-replicated shared-memory table and
+//     write the BF16 values straight into tensor memory with tcgen05.st: the
+//     MMA's A operand lives in TMEM, so the decoded weight never touches
+//     shared memory;
 //   * warp 1 issues tcgen05.mma (M=128, N=BN, K=16) from one thread and
 //     returns each stage with tcgen05.commit;
-//   * warps 2..5 then read the FP32 accumulator with tcgen05.ld (each warp
-//     its 32-lane quarter) and apply the channel scale, token scale and bias.
+//   * warps 2..9 then read the FP32 accumulator with tcgen05.ld (each warp
+//     half the columns of its 32-lane quarter) and apply the channel scale,
+//     token scale and bias.
 // Every wait is bounded; a timed-out wait is counted in the error word of the
 // workspace and the kernel runs to completion.
 #include <cuda.h>
@@ -33,7 +35,8 @@ namespace hif8 {
 constexpr int kTcBM = 128;      // weight rows (output channels) per tile = TMEM lanes
 constexpr int kTcBK = 64;       // K per stage: one 128-byte swizzle atom of BF16
 constexpr int kTcStages = 4;
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;  // TMA warp, MMA warp, 8 decoder/epilogue warps
+constexpr int kTcDepth = 4;      // weight stages each decoder holds in flight
 constexpr int kTcLut = 256 * 256;  // lane-replicated decode table (see gemv.cu)
 constexpr uint64_t kWaitNs = 100ull * 1000 * 1000;  // 100 ms per pipeline wait
 
@@ -124,14 +127,12 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};"
       ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
-      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]),
-      "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
 
@@ -147,11 +148,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       : "memory");
 }
 
-__device__ __forceinline__ uint4 ldg_nc(const uint8_t *p) {
+// Read-only weight load that allocates in L1, so the two 16-byte halves of a
+// 32-byte sector cost one L2 request.
+__device__ __forceinline__ uint4 ldg_l1(const uint8_t *p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
 }
 
@@ -201,7 +202,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // ---- set-up: barriers, TMEM, decode table --------------------------------
   if (tid == 0) {
     for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(&full_a[s], 4);  // one arrival per decoding warp
+      mbar_init(&full_a[s], 8);  // one arrival per decoding warp
       mbar_init(&full_b[s], 1);  // TMA transaction
       mbar_init(&empty[s], 1);   // tcgen05.commit
     }
@@ -256,45 +257,56 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mma_commit(accum_full);
     }
   } else {
-    // ---- weight decoders (warps 2..5), then the epilogue ---------------------
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    // ---- weight decoders (warps 2..9), then the epilogue ---------------------
+    // Warp w owns TMEM lane quarter w % 4 (the only lanes it may access) and
+    // half h of every 64-byte stage: lane = one weight row, 32 bytes per stage.
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const int n = n0 + row;
-    const uint8_t *wrow = p.w + (int64_t)min(n, p.n - 1) * p.k;
+    const uint8_t *wrow = p.w + (int64_t)min(n, p.n - 1) * p.k + half * 32;
     const uint32_t lane4 = (uint32_t)lane << 2;
-    uint4 cur[4], nxt[4];
+    const uint32_t a_lane = (uint32_t)(quarter * 32) << 16;
+    uint4 ring[kTcDepth][2];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) cur[c] = ldg_nc(wrow + c * 16);
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % kTcStages;
-      if (kb + 1 < nkb) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) nxt[c] = ldg_nc(wrow + (kb + 1) * kTcBK + c * 16);
+    for (int d = 0; d < kTcDepth; ++d) {
+      if (d < nkb) {
+        ring[d][0] = ldg_l1(wrow + d * kTcBK);
+        ring[d][1] = ldg_l1(wrow + d * kTcBK + 16);
       }
-      uint32_t v[32];
+    }
+    for (int kb0 = 0; kb0 < nkb; kb0 += kTcDepth) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint32_t words[4] = {cur[c].x, cur[c].y, cur[c].z, cur[c].w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          v[c * 8 + q * 2] = lut_pair(lut, words[q], lane4, false);
-          v[c * 8 + q * 2 + 1] = lut_pair(lut, words[q], lane4, true);
+      for (int d = 0; d < kTcDepth; ++d) {
+        const int kb = kb0 + d;
+        if (kb >= nkb) break;
+        const int s = kb % kTcStages;
+        const uint4 x0 = ring[d][0], x1 = ring[d][1];
+        if (kb + kTcDepth < nkb) {
+          ring[d][0] = ldg_l1(wrow + (kb + kTcDepth) * kTcBK);
+          ring[d][1] = ldg_l1(wrow + (kb + kTcDepth) * kTcBK + 16);
         }
-      }
-      if (kb >= kTcStages) {
-        if (!mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort)) atomicAdd(p.err, 1);
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      }
-      tmem_st32(a_tmem0 + s * 32 + ((uint32_t)(quarter * 32) << 16), v);
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full_a[s]);
+        const uint32_t words[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        uint32_t v[16];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) cur[c] = nxt[c];
+        for (int q = 0; q < 8; ++q) {
+          v[q * 2] = lut_pair(lut, words[q], lane4, false);
+          v[q * 2 + 1] = lut_pair(lut, words[q], lane4, true);
+        }
+        if (kb >= kTcStages) {
+          if (!mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort)) atomicAdd(p.err, 1);
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        }
+        tmem_st16(a_tmem0 + s * 32 + half * 16 + a_lane, v);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_a[s]);
+      }
     }
 
-    // epilogue: lane = output channel n, columns = tokens
+    // epilogue: lane = output channel n, columns = tokens; warp half h takes
+    // columns [h * BN / 2, (h + 1) * BN / 2)
     if (!mbar_wait(accum_full, 0, abort)) atomicAdd(p.err, 1);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const bool n_ok = n < p.n;
@@ -306,9 +318,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     uint16_t *out = static_cast<uint16_t *>(p.out);
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
+    for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
       uint32_t acc[32];
-      tmem_ld32(d_tmem + (uint32_t)c0 + ((uint32_t)(quarter * 32) << 16), acc);
+      tmem_ld32(d_tmem + (uint32_t)c0 + a_lane, acc);
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
