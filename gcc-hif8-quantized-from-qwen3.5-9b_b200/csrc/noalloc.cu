@@ -1,0 +1,91 @@
+// Paged attention whose split-KV scratch lives inside the library.
+//
+// hif8_paged_attention wants a caller-provided workspace for the partial
+// results of its split-KV pass.  Some callers have no way to provide one: a
+// plain C host that only receives the tensors and a stream from its
+// framework (the framework's caching allocator is out of its reach), or a
+// serving engine that has reserved every free byte of HBM for its KV-page
+// pool up front.  This entry point serves them from a fixed scratch array in
+// the library's own device image, so it allocates nothing.
+//
+// Limits and rules, all stated in include/hif8_b200.h:
+//   * at most HIF8_NOALLOC_ATTENTION_SCRATCH_BYTES of partials per call
+//     (hif8_paged_attention_workspace_size() of the call's sizes); larger
+//     calls are rejected with HIF8_ERR_WORKSPACE before anything is enqueued;
+//   * nothing in the scratch needs to start at zero: every partial the merge
+//     kernel reads was written by the split kernel of the same call;
+//   * the scratch is one array per device, shared by every call on that
+//     device: two calls in flight at once (different streams, or host
+//     threads without ordering) race on it.  Calls on one stream are ordered
+//     and safe;
+//   * the first call on each device resolves the array's device address with
+//     cudaGetSymbolAddress (which may load the library's device code on that
+//     device); make that first call before any stream capture.
+#include <mutex>
+
+#include "hif8_common.cuh"
+
+namespace {
+
+constexpr size_t kScratchBytes = HIF8_NOALLOC_ATTENTION_SCRATCH_BYTES;
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_attention_scratch[kScratchBytes];
+
+std::mutex g_scratch_mutex;
+void *g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of this device's scratch array, resolved once per device
+// with that device current; nullptr (and the last-error text set) on failure.
+void *scratch_for_current_device() {
+  int dev = -1;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) {
+    hif8::set_last_error(err);
+    return nullptr;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    hif8::set_last_error(cudaErrorInvalidDevice);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_ptr[dev]) {
+    void *ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_attention_scratch);
+    if (err != cudaSuccess) {
+      hif8::set_last_error(err);
+      return nullptr;
+    }
+    g_scratch_ptr[dev] = ptr;
+  }
+  return g_scratch_ptr[dev];
+}
+
+}  // namespace
+
+extern "C" int hif8_paged_attention_noalloc(const uint16_t *query, const uint8_t *key_cache,
+                                            const uint8_t *value_cache, const int32_t *block_tables,
+                                            const int32_t *seq_lens, const int32_t *query_start, int64_t batch,
+                                            int64_t num_tokens, int64_t num_heads, int64_t kv_heads,
+                                            int64_t head_size, int64_t num_blocks, int64_t block_size,
+                                            int64_t max_blocks, int64_t max_seq_len, float softmax_scale,
+                                            int causal, uint16_t *out, void *stream) {
+  // within these bounds the workspace size cannot overflow; anything else
+  // goes without scratch to the full validation of hif8_paged_attention
+  const bool sizes_ok = num_tokens >= 0 && num_heads > 0 && head_size > 0 && max_seq_len >= 0 &&
+                        num_tokens <= (1LL << 24) && num_heads <= (1LL << 10) && head_size <= 1024 &&
+                        max_seq_len <= (1LL << 24);
+  void *scratch = nullptr;
+  size_t need = 0;
+  if (sizes_ok) {
+    need = hif8_paged_attention_workspace_size(num_tokens, num_heads, head_size, max_seq_len);
+    if (need > kScratchBytes) return HIF8_ERR_WORKSPACE;
+    if (need > 0) {
+      scratch = scratch_for_current_device();
+      if (!scratch) return HIF8_ERR_CUDA;
+    }
+  }
+  return hif8_paged_attention(query, key_cache, value_cache, block_tables, seq_lens, query_start, batch,
+                              num_tokens, num_heads, kv_heads, head_size, num_blocks, block_size, max_blocks,
+                              max_seq_len, softmax_scale, causal, out, scratch, need, stream);
+}

@@ -43,6 +43,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hif8_paged_attention_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
     "hif8_paged_attention": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                     ctypes.c_float, _INT, _P, _P, _SZ, _P]),
+    "hif8_paged_attention_noalloc": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                            _I64, ctypes.c_float, _INT, _P, _P]),
     "hif8_kv_gather_decode": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P]),
 }
 
@@ -175,3 +177,14 @@ def paged_attention(query, key_cache, value_cache, block_tables, seq_lens, query
         _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables), _ptr(seq_lens), _ptr(query_start),
         block_tables.shape[0], tokens, heads, key_cache.shape[2], d, key_cache.shape[0], key_cache.shape[1],
         block_tables.shape[1], max_seq_len, float(scale), 1 if causal else 0, _ptr(out), _ptr(workspace), ws_bytes, _stream(query)))
+
+
+def paged_attention_noalloc(query, key_cache, value_cache, block_tables, seq_lens, query_start, max_seq_len,
+                            scale, out, causal: bool = True) -> None:
+    """hif8_paged_attention_noalloc: the split-KV scratch is the library's own
+    per-device array, so nothing is allocated for the call."""
+    tokens, heads, d = query.shape
+    check("hif8_paged_attention_noalloc", library().hif8_paged_attention_noalloc(
+        _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables), _ptr(seq_lens), _ptr(query_start),
+        block_tables.shape[0], tokens, heads, key_cache.shape[2], d, key_cache.shape[0], key_cache.shape[1],
+        block_tables.shape[1], max_seq_len, float(scale), 1 if causal else 0, _ptr(out), _stream(query)))

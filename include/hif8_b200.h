@@ -157,6 +157,33 @@ int hif8_paged_attention(const uint16_t *query, const uint8_t *key_cache,
                          int64_t max_blocks, int64_t max_seq_len, float softmax_scale, int causal,
                          uint16_t *out, void *workspace, size_t workspace_bytes, void *stream);
 
+/* hif8_paged_attention without a caller workspace.  No counterpart in the
+ * reference (its attention scratch comes from the framework allocator).
+ * For callers that cannot hand out device memory per call: a C host that
+ * only receives tensors and a stream from its framework, or an engine that
+ * has reserved all free HBM for its KV-page pool.  The split-KV partials go
+ * to a fixed per-device scratch array inside this library:
+ *  - at most HIF8_NOALLOC_ATTENTION_SCRATCH_BYTES (8 MiB) per call, as
+ *    hif8_paged_attention_workspace_size() counts it; larger calls return
+ *    HIF8_ERR_WORKSPACE and enqueue nothing;
+ *  - the scratch need not start at zero (each call writes every partial it
+ *    reads);
+ *  - calls in flight at the same time on one device (other streams, or host
+ *    threads without ordering) race on the shared scratch; calls on one
+ *    stream are ordered and safe;
+ *  - the first call on each device looks the scratch address up with
+ *    cudaGetSymbolAddress, with that device current; make it before any
+ *    stream capture.
+ * Other arguments and errors as hif8_paged_attention. */
+#define HIF8_NOALLOC_ATTENTION_SCRATCH_BYTES ((size_t)8 << 20)
+int hif8_paged_attention_noalloc(const uint16_t *query, const uint8_t *key_cache,
+                                 const uint8_t *value_cache, const int32_t *block_tables,
+                                 const int32_t *seq_lens, const int32_t *query_start, int64_t batch,
+                                 int64_t num_tokens, int64_t num_heads, int64_t kv_heads,
+                                 int64_t head_size, int64_t num_blocks, int64_t block_size,
+                                 int64_t max_blocks, int64_t max_seq_len, float softmax_scale,
+                                 int causal, uint16_t *out, void *stream);
+
 /* Gather + decode the rows of every request into a dense BF16 tensor, the
  * output of kv_runtime._gather_dense_hif8 (kv_runtime.py:1375-1468):
  * out[sum_b seq_lens[b], kv_heads, head_size] with out_start[b] the first
