@@ -329,6 +329,8 @@ def run_ours(args) -> None:
     cur = torch.cuda.current_stream(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        # profiler start/stop bracket the timed steps for `ncu --profile-from-start off`
+        torch.cuda.profiler.start()
         clocks.mark_start()
         start.record(cur)
         for _ in range(args.steps):
@@ -336,6 +338,7 @@ def run_ours(args) -> None:
         end.record(cur)
         torch.cuda.synchronize()
         clocks.mark_end()
+        torch.cuda.profiler.stop()
     if world > 1:
         dist.barrier()
     elapsed_ms = start.elapsed_time(end)
@@ -412,8 +415,8 @@ def gemv_roofline(calls, device, world) -> dict:
     if prof and prof.get("world") == world:
         traffic = prof.get("traffic_bytes_per_launch")
     return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "traffic": traffic, "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs, copy)" if kind == "measured"
-            else "fallback 6650 GB/s", "kernel": "gemv_hif8_kernel (split-K tcgen-free mma.sync, LUT decode)",
+            "traffic": traffic, "algorithmic_bytes_mean_per_launch": total_b / len(calls), "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs, copy)" if kind == "measured"
+            else "fallback 6650 GB/s", "kernel": "gemv_hif8_kernel (persistent split-K, LUT decode, mma.sync)",
             "algorithmic_bytes_per_launch": "N*K + 4N + M*K + 4M + 2MN (u8 activation in, BF16 out)",
             "per_launch": per, "timing": "median of 5 launches per config, each after a read-based L2 eviction, CUDA events"}
 
@@ -465,26 +468,44 @@ def measure_e2e(calls, args, device, world) -> dict:
 
 
 def run_profile_case(spec: str, launches: int) -> None:
-    """Small single-kernel case for ncu captures: ``gemv:<shape>:<m>`` runs
-    the linear kernel of one sweep call ``launches`` times (two warm-up
-    launches first), nothing else of the bench."""
+    """Small cases for ncu captures, nothing else of the bench:
+    ``gemv:<shape>:<m>`` / ``gemm:<shape>:<m>`` run the linear kernel of one
+    call ``launches`` times (two warm-up launches first); ``gemv:sweep`` runs
+    each of the 15 configs[1] calls once after a read-based L2 eviction (the
+    launches the roofline times)."""
     import torch
 
     from hif8_b200 import native, scheme
 
-    kind, shape, m = spec.split(":")
-    if kind not in ("gemv", "gemm"):
+    parts = spec.split(":")
+    if parts[0] not in ("gemv", "gemm") or len(parts) not in (2, 3):
         raise SystemExit(f"unknown profile case {spec!r}")
-    n, k = {name: (n, k) for name, n, k in SHAPES}[shape]
-    m = int(m)
     dev = torch.device("cuda", 0)
     ext = native.load_extension()
     g = torch.Generator(device=dev).manual_seed(0)
-    w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-    wq, ws = scheme.quantize_weight_rows(w)
-    del w
+    fixed = torch.tensor([4.5 / 32768.0], device=dev)
+
+    def weight(n, k):
+        w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        return scheme.quantize_weight_rows(w)
+
+    if parts[1] == "sweep":
+        flush = torch.ones(128 * 1024 * 1024, dtype=torch.float32, device=dev)
+        weights = {name: weight(n, k) for name, n, k in SHAPES}
+        for m in M_VALUES:
+            for name, n, k in SHAPES:
+                wq, ws = weights[name]
+                a, ts = native.static_quant(torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16), fixed)
+                flush.sum()
+                ext.soft_hif8_gemm(a, wq, ts, ws, None, torch.bfloat16)
+        torch.cuda.synchronize()
+        print(f"profile case {spec}: {len(M_VALUES) * len(SHAPES)} launches ok")
+        return
+    n, k = {name: (n, k) for name, n, k in SHAPES}[parts[1]]
+    m = int(parts[2])
+    wq, ws = weight(n, k)
     x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
-    a, ts = native.static_quant(x, torch.tensor([4.5 / 32768.0], device=dev))
+    a, ts = native.static_quant(x, fixed)
     for _ in range(2 + launches):
         ext.soft_hif8_gemm(a, wq, ts, ws, None, torch.bfloat16)
     torch.cuda.synchronize()

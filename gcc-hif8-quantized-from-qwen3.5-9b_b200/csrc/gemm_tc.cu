@@ -9,13 +9,14 @@
 // Work split per CTA (one 128-channel x BN-token output tile, 10 warps):
 //   * the activation is decoded once per call into a BF16 workspace
 //     [M, K]; warp 0 streams its BN x 64 tiles with TMA (128-byte swizzle)
-//     into a 4-stage shared-memory ring -- the MMA's B operand;
+//     into a 4-stage shared-memory ring -- the MMA's B operand -- together
+//     with the raw 128 x 64-byte HiF8 weight tile of the same stage (64-byte
+//     swizzle, so the row reads below are bank-conflict free);
 //   * warps 2..9 own one weight row per lane (128 rows, two warps per row
-//     quarter, 32 bytes of each 64-byte stage each), keep 4 stages of loads
-//     in flight, decode with the lane-replicated shared-memory table and
-//     write the BF16 values straight into tensor memory with tcgen05.st: the
-//     MMA's A operand lives in TMEM, so the decoded weight never touches
-//     shared memory;
+//     quarter, 32 bytes of each 64-byte stage each), decode it with the
+//     lane-replicated shared-memory table and write the BF16 values straight
+//     into tensor memory with tcgen05.st: the MMA's A operand lives in TMEM,
+//     so the decoded weight never goes back to shared memory;
 //   * warp 1 issues tcgen05.mma (M=128, N=BN, K=16) from one thread and
 //     returns each stage with tcgen05.commit;
 //   * warps 2..9 then read the FP32 accumulator with tcgen05.ld (each warp
@@ -36,7 +37,6 @@ constexpr int kTcBM = 128;      // weight rows (output channels) per tile = TMEM
 constexpr int kTcBK = 64;       // K per stage: one 128-byte swizzle atom of BF16
 constexpr int kTcStages = 4;
 constexpr int kTcThreads = 320;  // TMA warp, MMA warp, 8 decoder/epilogue warps
-constexpr int kTcDepth = 4;      // weight stages each decoder holds in flight
 constexpr int kTcLut = 256 * 256;  // lane-replicated decode table (see gemv.cu)
 constexpr uint64_t kWaitNs = 100ull * 1000 * 1000;  // 100 ms per pipeline wait
 
@@ -148,14 +148,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       : "memory");
 }
 
-// Read-only weight load that allocates in L1, so the two 16-byte halves of a
-// 32-byte sector cost one L2 request.
-__device__ __forceinline__ uint4 ldg_l1(const uint8_t *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-  return v;
-}
-
 __device__ __forceinline__ uint32_t lut_pair(const uint8_t *lut, uint32_t word, uint32_t lane4, bool high) {
   const uint32_t e0 = *reinterpret_cast<const uint32_t *>(lut + __byte_perm(word, lane4, high ? 0x5524u : 0x5504u));
   const uint32_t e1 = *reinterpret_cast<const uint32_t *>(lut + __byte_perm(word, lane4, high ? 0x5534u : 0x5514u));
@@ -179,13 +171,16 @@ __device__ __forceinline__ uint32_t to_out_bits(float v) {
 
 template <int BN, int OUT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    gemm_hif8_tc_kernel(const __grid_constant__ CUtensorMap xmap, const TcParams p) {
+    gemm_hif8_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                        const TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled operand stages
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kBBytes = BN * 128;
-  uint8_t *b_stages = smem;                                  // [stages][BN][128 B] swizzled
-  uint8_t *lut = b_stages + kTcStages * kBBytes;            // 64 KB
+  constexpr int kWBytes = kTcBM * kTcBK;                    // 128 weight rows x 64 bytes
+  uint8_t *b_stages = smem;                                  // [stages][BN][128 B], 128-byte swizzle
+  uint8_t *w_stages = b_stages + kTcStages * kBBytes;       // [stages][128][64 B], 64-byte swizzle
+  uint8_t *lut = w_stages + kTcStages * kWBytes;            // 64 KB
   uint64_t *bars = reinterpret_cast<uint64_t *>(lut + kTcLut);
   uint64_t *full_a = bars, *full_b = bars + kTcStages, *empty = bars + 2 * kTcStages;
   uint64_t *accum_full = bars + 3 * kTcStages;
@@ -203,7 +198,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&full_a[s], 8);  // one arrival per decoding warp
-      mbar_init(&full_b[s], 1);  // TMA transaction
+      mbar_init(&full_b[s], 1);  // TMA transactions (activation + weight tile)
       mbar_init(&empty[s], 1);   // tcgen05.commit
     }
     mbar_init(accum_full, 1);
@@ -228,13 +223,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t a_tmem0 = tmem + (uint32_t)BN;  // stage s: columns BN + 32 s
 
   if (warp == 0) {
-    // ---- TMA producer of the activation (B) tiles ---------------------------
+    // ---- TMA producer of the activation (B) and raw weight tiles -------------
     if (lane == 0) {
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % kTcStages;
         if (kb >= kTcStages && !mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort)) atomicAdd(p.err, 1);
-        mbar_expect_tx(&full_b[s], kBBytes);
+        mbar_expect_tx(&full_b[s], kBBytes + kWBytes);
         tma_load_2d(b_stages + s * kBBytes, &xmap, kb * kTcBK, m0, &full_b[s]);
+        tma_load_2d(w_stages + s * kWBytes, &wmap, kb * kTcBK, n0, &full_b[s]);
       }
     }
   } else if (warp == 1) {
@@ -264,45 +260,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const int n = n0 + row;
-    const uint8_t *wrow = p.w + (int64_t)min(n, p.n - 1) * p.k + half * 32;
     const uint32_t lane4 = (uint32_t)lane << 2;
     const uint32_t a_lane = (uint32_t)(quarter * 32) << 16;
-    uint4 ring[kTcDepth][2];
+    // this lane's 32 bytes of the stage: 16-byte chunks 2h and 2h+1 of row
+    // `row`, placed by the 64-byte swizzle at chunk c ^ ((row >> 1) & 3)
+    const int sw = (row >> 1) & 3;
+    const int off0 = row * kTcBK + ((2 * half) ^ sw) * 16;
+    const int off1 = row * kTcBK + ((2 * half + 1) ^ sw) * 16;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % kTcStages;
+      const uint32_t parity = (kb / kTcStages) & 1;
+      // the weight tile of this stage has landed (which also means the MMAs
+      // that read A stage s four stages ago have completed)
+      if (!mbar_wait(&full_b[s], parity, abort)) atomicAdd(p.err, 1);
+      if (kb >= kTcStages && !mbar_wait(&empty[s], parity ^ 1, abort)) atomicAdd(p.err, 1);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint8_t *ws = w_stages + s * kWBytes;
+      const uint4 x0 = *reinterpret_cast<const uint4 *>(ws + off0);
+      const uint4 x1 = *reinterpret_cast<const uint4 *>(ws + off1);
+      const uint32_t words[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      uint32_t v[16];
 #pragma unroll
-    for (int d = 0; d < kTcDepth; ++d) {
-      if (d < nkb) {
-        ring[d][0] = ldg_l1(wrow + d * kTcBK);
-        ring[d][1] = ldg_l1(wrow + d * kTcBK + 16);
+      for (int q = 0; q < 8; ++q) {
+        v[q * 2] = lut_pair(lut, words[q], lane4, false);
+        v[q * 2 + 1] = lut_pair(lut, words[q], lane4, true);
       }
-    }
-    for (int kb0 = 0; kb0 < nkb; kb0 += kTcDepth) {
-#pragma unroll
-      for (int d = 0; d < kTcDepth; ++d) {
-        const int kb = kb0 + d;
-        if (kb >= nkb) break;
-        const int s = kb % kTcStages;
-        const uint4 x0 = ring[d][0], x1 = ring[d][1];
-        if (kb + kTcDepth < nkb) {
-          ring[d][0] = ldg_l1(wrow + (kb + kTcDepth) * kTcBK);
-          ring[d][1] = ldg_l1(wrow + (kb + kTcDepth) * kTcBK + 16);
-        }
-        const uint32_t words[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-        uint32_t v[16];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          v[q * 2] = lut_pair(lut, words[q], lane4, false);
-          v[q * 2 + 1] = lut_pair(lut, words[q], lane4, true);
-        }
-        if (kb >= kTcStages) {
-          if (!mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort)) atomicAdd(p.err, 1);
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        }
-        tmem_st16(a_tmem0 + s * 32 + half * 16 + a_lane, v);
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full_a[s]);
-      }
+      tmem_st16(a_tmem0 + s * 32 + half * 16 + a_lane, v);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_a[s]);
     }
 
     // epilogue: lane = output channel n, columns = tokens; warp half h takes
@@ -392,17 +379,17 @@ size_t hif8_gemm_tc_workspace(int64_t m, int64_t n, int64_t k) {
 
 template <int BN>
 static constexpr size_t tc_smem_bytes() {
-  return 1024 + (size_t)kTcStages * BN * 128 + kTcLut + (3 * kTcStages + 1) * 8 + 16;
+  return 1024 + (size_t)kTcStages * (BN * 128 + kTcBM * kTcBK) + kTcLut + (3 * kTcStages + 1) * 8 + 16;
 }
 
 template <int BN, int OUT>
-static int launch_tc(const CUtensorMap &map, const TcParams &p, cudaStream_t stream) {
+static int launch_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const TcParams &p, cudaStream_t stream) {
   auto kernel = gemm_hif8_tc_kernel<BN, OUT>;
   const size_t smem = tc_smem_bytes<BN>();
   const int st = ensure_smem_limit(reinterpret_cast<const void *>(kernel), smem);
   if (st != HIF8_OK) return st;
   dim3 grid((unsigned)((p.m + BN - 1) / BN), (unsigned)((p.n + kTcBM - 1) / kTcBM), 1);
-  kernel<<<grid, kTcThreads, smem, stream>>>(map, p);
+  kernel<<<grid, kTcThreads, smem, stream>>>(xmap, wmap, p);
   return check_launch();
 }
 
@@ -429,20 +416,36 @@ int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t
 
   // 2. the tcgen05 GEMM; BN = tokens per tile
   const int bn = m >= 256 ? 256 : (m >= 128 ? 128 : 64);
-  CUtensorMap map;
-  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
-  const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)bn};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return HIF8_ERR_CUDA;
+  CUtensorMap xmap, wmap;
+  {  // BF16 activation [M, K]: BN x 64 boxes, 128-byte swizzle (UMMA SW128 K-major)
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+    const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)bn};
+    if (encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return HIF8_ERR_CUDA;
+  }
+  {  // HiF8 weight [N, K] bytes: 128 x 64 boxes, 64-byte swizzle (conflict-free row reads)
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)n};
+    const cuuint64_t strides[1] = {(cuuint64_t)k};
+    const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)kTcBM};
+    if (encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(args.w), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return HIF8_ERR_CUDA;
+  }
   TcParams p{args.w, args.ts, args.cs, args.bias, args.out, err, args.m, args.n, args.k, args.bias_dtype, args.ts_stride};
   const bool bf16 = output_dtype == HIF8_DTYPE_BF16;
-  if (bn == 256) return bf16 ? launch_tc<256, HIF8_DTYPE_BF16>(map, p, stream) : launch_tc<256, HIF8_DTYPE_F16>(map, p, stream);
-  if (bn == 128) return bf16 ? launch_tc<128, HIF8_DTYPE_BF16>(map, p, stream) : launch_tc<128, HIF8_DTYPE_F16>(map, p, stream);
-  return bf16 ? launch_tc<64, HIF8_DTYPE_BF16>(map, p, stream) : launch_tc<64, HIF8_DTYPE_F16>(map, p, stream);
+  if (bn == 256)
+    return bf16 ? launch_tc<256, HIF8_DTYPE_BF16>(xmap, wmap, p, stream)
+                : launch_tc<256, HIF8_DTYPE_F16>(xmap, wmap, p, stream);
+  if (bn == 128)
+    return bf16 ? launch_tc<128, HIF8_DTYPE_BF16>(xmap, wmap, p, stream)
+                : launch_tc<128, HIF8_DTYPE_F16>(xmap, wmap, p, stream);
+  return bf16 ? launch_tc<64, HIF8_DTYPE_BF16>(xmap, wmap, p, stream)
+              : launch_tc<64, HIF8_DTYPE_F16>(xmap, wmap, p, stream);
 }
 
 }  // namespace hif8
