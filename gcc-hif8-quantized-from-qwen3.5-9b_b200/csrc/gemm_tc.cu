@@ -20,8 +20,9 @@
 //   * warp 1 issues tcgen05.mma (M=128, N=BN, K=16) from one thread and
 //     returns each stage with tcgen05.commit;
 //   * warps 2..9 then read the FP32 accumulator with tcgen05.ld (each warp
-//     half the columns of its 32-lane quarter) and apply the channel scale,
-//     token scale and bias.
+//     half the columns of its 32-lane quarter), apply the channel scale,
+//     token scale and bias, stage the tile in shared memory and write it with
+//     one TMA tensor store.
 // Every wait is bounded; a timed-out wait is counted in the error word of the
 // workspace and the kernel runs to completion.
 #include <cuda.h>
@@ -36,7 +37,8 @@ namespace hif8 {
 constexpr int kTcBM = 128;      // weight rows (output channels) per tile = TMEM lanes
 constexpr int kTcBK = 64;       // K per stage: one 128-byte swizzle atom of BF16
 constexpr int kTcStages = 4;
-constexpr int kTcThreads = 320;  // TMA warp, MMA warp, 8 decoder/epilogue warps
+constexpr int kDecoderWarps = 8;
+constexpr int kTcThreads = 32 * (2 + kDecoderWarps);  // TMA warp, MMA warp, decoder/epilogue warps
 constexpr int kTcLut = 256 * 256;  // lane-replicated decode table (see gemv.cu)
 constexpr uint64_t kWaitNs = 100ull * 1000 * 1000;  // 100 ms per pipeline wait
 
@@ -172,7 +174,7 @@ __device__ __forceinline__ uint32_t to_out_bits(float v) {
 template <int BN, int OUT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_hif8_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
-                        const TcParams p) {
+                        const __grid_constant__ CUtensorMap ymap, const TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled operand stages
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -197,7 +199,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // ---- set-up: barriers, TMEM, decode table --------------------------------
   if (tid == 0) {
     for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(&full_a[s], 8);  // one arrival per decoding warp
+      mbar_init(&full_a[s], kDecoderWarps);  // one arrival per decoding warp
       mbar_init(&full_b[s], 1);  // TMA transactions (activation + weight tile)
       mbar_init(&empty[s], 1);   // tcgen05.commit
     }
@@ -293,9 +295,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 
     // epilogue: lane = output channel n, columns = tokens; warp half h takes
-    // columns [h * BN / 2, (h + 1) * BN / 2)
-    if (!mbar_wait(accum_full, 0, abort)) atomicAdd(p.err, 1);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    // columns [h * BN / 2, (h + 1) * BN / 2).  The tile is staged as
+    // [BN tokens][128 channels] in the (now idle) activation ring and written
+    // by one TMA tensor store: per-lane 2-byte stores to BN different output
+    // rows cost more than the whole main loop's issue budget.
     const bool n_ok = n < p.n;
     const float cs = n_ok ? p.cs[n] : 0.f;
     float bias = 0.f;
@@ -303,22 +306,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint16_t h = static_cast<const uint16_t *>(p.bias)[n];
       bias = p.bias_dtype == HIF8_DTYPE_BF16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
     }
-    uint16_t *out = static_cast<uint16_t *>(p.out);
-#pragma unroll 1
-    for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+    // token scales, fetched while the last MMAs run: lane l holds
+    // ts[m0 + c0 + 32 c + l] of chunk c, broadcast by shuffles below
+    constexpr int kChunks = BN / 64;  // 32-token chunks per warp half
+    const int c0 = half * (BN / 2);
+    float tsr[kChunks];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      const int m = m0 + c0 + c * 32 + lane;
+      tsr[c] = m < p.m ? p.ts[(int64_t)m * p.ts_stride] : 0.f;
+    }
+    if (!mbar_wait(accum_full, 0, abort)) atomicAdd(p.err, 1);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    uint16_t *stage_out = reinterpret_cast<uint16_t *>(b_stages);  // [BN][128]
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
       uint32_t acc[32];
-      tmem_ld32(d_tmem + (uint32_t)c0 + a_lane, acc);
+      tmem_ld32(d_tmem + (uint32_t)(c0 + c * 32) + a_lane, acc);
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int m = m0 + c0 + j;
-        if (n_ok && m < p.m) {
-          float val = __uint_as_float(acc[j]) * cs;
-          val = val * p.ts[(int64_t)m * p.ts_stride];
-          val += bias;
-          out[(int64_t)m * p.n + n] = (uint16_t)to_out_bits<OUT>(val);
-        }
+      for (int q = 0; q < 32; ++q) {
+        const float ts = __shfl_sync(0xFFFFFFFFu, tsr[c], q);
+        float val = __uint_as_float(acc[q]) * cs;
+        val = val * ts;
+        val += bias;
+        stage_out[(c0 + c * 32 + q) * kTcBM + row] = (uint16_t)to_out_bits<OUT>(val);
       }
+    }
+    // make the staged tile visible to the TMA engine, then one thread stores it
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(kDecoderWarps * 32) : "memory");
+    if (warp == 2 && lane == 0) {
+      asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                   ::"l"(&ymap), "r"(n0), "r"(m0), "r"(smem_addr(stage_out))
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // smem read before the CTA exits
     }
   }
 
@@ -367,7 +390,9 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 constexpr int64_t kTcMinM = 32;
 
 bool hif8_gemm_tc_supported(int64_t m, int64_t n, int64_t k) {
-  return m >= kTcMinM && n >= 64 && k % kTcBK == 0 && k >= kTcBK && m < (1LL << 31) && n <= 65535LL * kTcBM;
+  // n % 8: the output rows must be 16-byte strided for the TMA store
+  return m >= kTcMinM && n >= 64 && n % 8 == 0 && k % kTcBK == 0 && k >= kTcBK && m < (1LL << 31) &&
+         n <= 65535LL * kTcBM;
 }
 
 static size_t err_offset(int64_t m, int64_t k) { return ((size_t)m * k * 2 + 255) & ~size_t(255); }
@@ -383,13 +408,14 @@ static constexpr size_t tc_smem_bytes() {
 }
 
 template <int BN, int OUT>
-static int launch_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const TcParams &p, cudaStream_t stream) {
+static int launch_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const CUtensorMap &ymap, const TcParams &p,
+                     cudaStream_t stream) {
   auto kernel = gemm_hif8_tc_kernel<BN, OUT>;
   const size_t smem = tc_smem_bytes<BN>();
   const int st = ensure_smem_limit(reinterpret_cast<const void *>(kernel), smem);
   if (st != HIF8_OK) return st;
   dim3 grid((unsigned)((p.m + BN - 1) / BN), (unsigned)((p.n + kTcBM - 1) / kTcBM), 1);
-  kernel<<<grid, kTcThreads, smem, stream>>>(xmap, wmap, p);
+  kernel<<<grid, kTcThreads, smem, stream>>>(xmap, wmap, ymap, p);
   return check_launch();
 }
 
@@ -417,7 +443,7 @@ int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t
   // 2. the tcgen05 GEMM; BN = tokens per tile
   const int bn = m >= 256 ? 256 : (m >= 128 ? 128 : 64);
   const cuuint32_t estr[2] = {1, 1};
-  CUtensorMap xmap, wmap;
+  CUtensorMap xmap, wmap, ymap;
   {  // BF16 activation [M, K]: BN x 64 boxes, 128-byte swizzle (UMMA SW128 K-major)
     const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
     const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
@@ -436,16 +462,25 @@ int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return HIF8_ERR_CUDA;
   }
+  {  // output [M, N] (BF16 or FP16 bits): 128-channel x BN-token boxes for the TMA store
+    const cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
+    const cuuint64_t strides[1] = {(cuuint64_t)n * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kTcBM, (cuuint32_t)bn};
+    if (encode(&ymap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, args.out, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return HIF8_ERR_CUDA;
+  }
   TcParams p{args.w, args.ts, args.cs, args.bias, args.out, err, args.m, args.n, args.k, args.bias_dtype, args.ts_stride};
   const bool bf16 = output_dtype == HIF8_DTYPE_BF16;
   if (bn == 256)
-    return bf16 ? launch_tc<256, HIF8_DTYPE_BF16>(xmap, wmap, p, stream)
-                : launch_tc<256, HIF8_DTYPE_F16>(xmap, wmap, p, stream);
+    return bf16 ? launch_tc<256, HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream)
+                : launch_tc<256, HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream);
   if (bn == 128)
-    return bf16 ? launch_tc<128, HIF8_DTYPE_BF16>(xmap, wmap, p, stream)
-                : launch_tc<128, HIF8_DTYPE_F16>(xmap, wmap, p, stream);
-  return bf16 ? launch_tc<64, HIF8_DTYPE_BF16>(xmap, wmap, p, stream)
-              : launch_tc<64, HIF8_DTYPE_F16>(xmap, wmap, p, stream);
+    return bf16 ? launch_tc<128, HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream)
+                : launch_tc<128, HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream);
+  return bf16 ? launch_tc<64, HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream)
+              : launch_tc<64, HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream);
 }
 
 }  // namespace hif8

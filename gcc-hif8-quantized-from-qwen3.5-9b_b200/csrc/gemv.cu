@@ -577,7 +577,7 @@ extern "C" int soft_hif8_gemm(const uint8_t *activation, const uint8_t *weight, 
   GemvArgs args{activation, weight, token_scale, channel_scale, bias, out, (int)m, (int)n, (int)k, 0,
                 bias ? bias_dtype : HIF8_DTYPE_NONE, 1};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (hif8_gemm_tc_supported(m, n, k) && aligned16(activation) && aligned16(weight)) {
+  if (hif8_gemm_tc_supported(m, n, k) && aligned16(activation) && aligned16(weight) && aligned16(out)) {
     if (workspace_bytes < hif8_gemm_tc_workspace(m, n, k) || (!workspace && hif8_gemm_tc_workspace(m, n, k)))
       return HIF8_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return HIF8_ERR_WORKSPACE;  // TMA wants an aligned base
