@@ -440,8 +440,27 @@ int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t
   int status = check_launch();
   if (status != HIF8_OK) return status;
 
-  // 2. the tcgen05 GEMM; BN = tokens per tile
-  const int bn = m >= 256 ? 256 : (m >= 128 ? 128 : 64);
+  // 2. the tcgen05 GEMM; BN = tokens per tile, chosen by the estimated time
+  // of the launch: waves of tiles over the SMs times the cost of a tile.  The
+  // weight decode dominates a tile and does not shrink with BN (measured on
+  // B200, K = 4096: 37 us per tile at BN 256, 33 us at 128, 31 us at 64), so
+  // narrower tiles pay only where they fill SMs that would otherwise idle.
+  int bn = 64;
+  {
+    const double tile_cost[3] = {37.0, 33.0, 31.0};  // BN 256, 128, 64
+    const int bns[3] = {256, 128, 64};
+    double best = 0;
+    for (int i = 0; i < 3; ++i) {
+      if (bns[i] > 64 && m < bns[i] / 2) continue;
+      const int64_t tiles = ((m + bns[i] - 1) / bns[i]) * ((n + kTcBM - 1) / kTcBM);
+      const int64_t waves = (tiles + num_sms() - 1) / num_sms();
+      const double t = (double)waves * tile_cost[i];
+      if (best == 0 || t < best) {
+        best = t;
+        bn = bns[i];
+      }
+    }
+  }
   const cuuint32_t estr[2] = {1, 1};
   CUtensorMap xmap, wmap, ymap;
   {  // BF16 activation [M, K]: BN x 64 boxes, 128-byte swizzle (UMMA SW128 K-major)
