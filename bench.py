@@ -356,6 +356,12 @@ def run_ours(args) -> None:
     # -------------------------------------------- e2e: public API, host I/O
     e2e = measure_e2e(calls, args, device, world)
 
+    # ------------------- the other hot-path kernels (one GPU, timed alone) ---
+    extra = {}
+    if world == 1 and not args.no_extra:
+        extra["prefill_gemm"] = measure_prefill_gemm(device)
+        extra["paged_attention"] = measure_paged_attention(device)
+
     del graph, graph_outs
     if world > 1:
         dist.barrier()
@@ -367,11 +373,119 @@ def run_ours(args) -> None:
         "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(world),
         "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(), "roofline": roofline,
-        "e2e": e2e,
+        "e2e": e2e, **extra,
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = time_cpu_baseline(args.cpu_budget)
     print(json.dumps(line), flush=True)
+
+
+def load_peak_bf16() -> tuple[float, str]:
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(peaks["bf16_tflops"]), "measured burst (MEASURED_PEAKS.json bf16_tflops, cuBLAS 8192^3)"
+    except Exception:
+        return 1590.0, "fallback 1590 TF/s"
+
+
+def _timed_alone(fn, device, reps: int = 5) -> float:
+    """Median device time (ms) of fn() over reps launches, each after a
+    read-based L2 eviction, CUDA events on the current stream."""
+    import torch
+
+    flush = torch.ones(128 * 1024 * 1024, dtype=torch.float32, device=device)
+    cur = torch.cuda.current_stream(device)
+    times = []
+    for _ in range(reps):
+        flush.sum()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(cur)
+        fn()
+        e.record(cur)
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    return statistics.median(times)
+
+
+def measure_prefill_gemm(device) -> dict:
+    """M in {512, 4096} x the projection shapes, weights with 0.1%
+    outliers at 20 sigma; soft_hif8_gemm (activation decode pre-pass + the
+    tcgen05 GEMM) timed alone against the measured dense BF16 peak."""
+    import torch
+
+    from hif8_b200 import native, scheme
+
+    ext = native.load_extension()
+    g = torch.Generator(device=device).manual_seed(2)
+    peak, kind = load_peak_bf16()
+    per = []
+    flops_total, ms_total = 0.0, 0.0
+    for name, n, k in SHAPES:
+        w = torch.randn(n, k, device=device, generator=g) * 0.02
+        count = n * k // 1000
+        idx = torch.randint(0, n * k, (count,), device=device, generator=g)
+        sign = torch.randint(0, 2, (count,), device=device, generator=g).float() * 2 - 1
+        w.view(-1)[idx] = sign * 20 * 0.02
+        wq, ws = scheme.quantize_weight_rows(w.to(torch.bfloat16))
+        del w
+        for m in (512, 4096):
+            x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
+            a, ts = native.static_quant(x, torch.tensor([4.5 / 32768.0], device=device))
+            ext.soft_hif8_gemm(a, wq, ts, ws, None, torch.bfloat16)
+            t = _timed_alone(lambda: ext.soft_hif8_gemm(a, wq, ts, ws, None, torch.bfloat16), device)
+            flops = 2.0 * m * n * k
+            per.append({"m": m, "shape": name, "us": round(t * 1e3, 1), "tflops": round(flops / (t * 1e-3) / 1e12, 1),
+                        "frac": round(flops / (t * 1e-3) / 1e12 / peak, 3)})
+            flops_total += flops
+            ms_total += t
+    achieved = flops_total / (ms_total * 1e-3) / 1e12
+    return {"bound": "tensor", "kernel": "gemm_hif8_tc_kernel (tcgen05, TMEM A operand) + decode_to_bf16",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "TF/s", "frac": round(achieved / peak, 3),
+            "peak_kind": kind, "algorithmic": "2*M*N*K FLOPs per call", "per_call": per,
+            "timing": "median of 5 calls per config, each after a read-based L2 eviction, CUDA events"}
+
+
+def measure_paged_attention(device) -> dict:
+    """decode step of batch 4 at contexts 512 and 4096, 16 query /
+    4 KV heads, head_dim 256, 128-token HiF8 pages (shuffled block table);
+    the attention kernels timed alone against the measured HBM peak."""
+    import math
+
+    import torch
+
+    from hif8_b200 import kv_cache
+
+    kv_cache.load_ops()
+    peak, kind = load_peak_hbm()
+    g = torch.Generator(device=device).manual_seed(3)
+    batch, heads, kv_heads, d, block = 4, 16, 4, 256, 128
+    per = []
+    for ctx in (512, 4096):
+        blocks_per = ctx // block
+        total = batch * blocks_per
+        table = torch.randperm(total, device=device, generator=g).view(batch, blocks_per).to(torch.int32)
+        kc = torch.randint(0, 256, (total, block, kv_heads, d + 4), dtype=torch.uint8, device=device, generator=g)
+        vc = torch.randint(0, 256, (total, block, kv_heads, d + 4), dtype=torch.uint8, device=device, generator=g)
+        scale_bytes = torch.tensor([0.01] * (total * block * kv_heads), dtype=torch.float32,
+                                   device=device).view(torch.uint8).view(total, block, kv_heads, 4)
+        kc[..., d:] = scale_bytes
+        vc[..., d:] = scale_bytes
+        kc[..., :d] &= 0x7F  # finite magnitudes only (no NaN code)
+        vc[..., :d] &= 0x7F
+        kc[..., :d] = torch.where(kc[..., :d] == 0x6F, torch.zeros_like(kc[..., :d]), kc[..., :d])
+        vc[..., :d] = torch.where(vc[..., :d] == 0x6F, torch.zeros_like(vc[..., :d]), vc[..., :d])
+        q = torch.randn(batch, heads, d, device=device, generator=g).to(torch.bfloat16)
+        lens = torch.full((batch,), ctx, dtype=torch.int32, device=device)
+        starts = torch.arange(batch + 1, dtype=torch.int32, device=device)
+        fn = lambda: torch.ops.hif8_b200.paged_attention(q, kc, vc, table, lens, starts, ctx, 1.0 / math.sqrt(d), True)
+        fn()
+        t = _timed_alone(fn, device)
+        nbytes = 2 * batch * ctx * kv_heads * (d + 4) + 2 * 2 * batch * heads * d
+        per.append({"ctx": ctx, "batch": batch, "us": round(t * 1e3, 2), "gbs": round(nbytes / (t * 1e-3) / 1e9, 1),
+                    "frac": round(nbytes / (t * 1e-3) / 1e9 / peak, 3)})
+    return {"bound": "hbm", "kernel": "paged_attention_kernel + attention_combine_kernel", "unit": "GB/s",
+            "peak": peak, "peak_kind": kind, "algorithmic": "K and V pages read once (B*ctx*kv_heads*(D+4)*2) + Q + out",
+            "per_config": per, "timing": "median of 5 decode steps, each after a read-based L2 eviction, CUDA events"}
 
 
 def gemv_roofline(calls, device, world) -> dict:
@@ -478,6 +592,32 @@ def run_profile_case(spec: str, launches: int) -> None:
     from hif8_b200 import native, scheme
 
     parts = spec.split(":")
+    if parts[0] == "attn" and len(parts) == 2:
+        import math
+
+        dev = torch.device("cuda", 0)
+        native.load_extension()
+        from hif8_b200 import kv_cache
+
+        kv_cache.load_ops()
+        g = torch.Generator(device=dev).manual_seed(3)
+        ctx = int(parts[1])
+        batch, heads, kv_heads, d, block = 4, 16, 4, 256, 128
+        total = batch * ((ctx + block - 1) // block)
+        table = torch.randperm(total, device=dev, generator=g).view(batch, -1).to(torch.int32)
+        kc = torch.randint(0, 0x60, (total, block, kv_heads, d + 4), dtype=torch.uint8, device=dev, generator=g)
+        vc = torch.randint(0, 0x60, (total, block, kv_heads, d + 4), dtype=torch.uint8, device=dev, generator=g)
+        sb = torch.full((total, block, kv_heads), 0.01, device=dev).view(torch.uint8).view(total, block, kv_heads, 4)
+        kc[..., d:] = sb
+        vc[..., d:] = sb
+        q = torch.randn(batch, heads, d, device=dev, generator=g).to(torch.bfloat16)
+        lens = torch.full((batch,), ctx, dtype=torch.int32, device=dev)
+        starts = torch.arange(batch + 1, dtype=torch.int32, device=dev)
+        for _ in range(2 + launches):
+            torch.ops.hif8_b200.paged_attention(q, kc, vc, table, lens, starts, ctx, 1.0 / math.sqrt(d), True)
+        torch.cuda.synchronize()
+        print(f"profile case {spec}: {2 + launches} launches ok")
+        return
     if parts[0] not in ("gemv", "gemm") or len(parts) not in (2, 3):
         raise SystemExit(f"unknown profile case {spec!r}")
     dev = torch.device("cuda", 0)
@@ -520,6 +660,7 @@ def main() -> None:
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline work")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-extra", action="store_true", help="skip the prefill GEMM and attention measurements")
     parser.add_argument("--profile-case", default=None,
                         help="run one small kernel case for ncu (e.g. gemv:gate_up:1) and exit")
     parser.add_argument("--profile-launches", type=int, default=3)

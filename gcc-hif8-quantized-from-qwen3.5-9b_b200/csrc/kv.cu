@@ -252,34 +252,335 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attention_kernel(const Att
 }
 
 // Merge the split partials of one (token, head): out = sum_s o_s e^(m_s - M)
-// / sum_s l_s e^(m_s - M).
-__global__ void __launch_bounds__(256) attention_combine_kernel(const float *__restrict__ part, int64_t rows,
-                                                                int64_t d, int splits, const int32_t *q_start,
-                                                                const int32_t *seq_lens, int64_t batch,
-                                                                int64_t heads, uint16_t *__restrict__ out) {
+// / sum_s l_s e^(m_s - M).  The split weights are computed once, in
+// parallel, into shared memory (blocks of 1024 splits), then every thread
+// sums its columns with independent loads.
+constexpr int kCombineThreads = 256;
+constexpr int kCombineBlock = 1024;
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float *scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();  // scratch may still be read from a previous reduction
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  v = scratch[0];
+  for (int w = 1; w < kCombineThreads / 32; ++w) v = is_max ? fmaxf(v, scratch[w]) : v + scratch[w];
+  return v;
+}
+
+__global__ void __launch_bounds__(kCombineThreads) attention_combine_kernel(
+    const float *__restrict__ part, int64_t rows, int64_t d, int splits, int chunk, const int32_t *q_start,
+    const int32_t *seq_lens, int64_t batch, int64_t heads, uint16_t *__restrict__ out) {
+  __shared__ float wgt[kCombineBlock];
+  __shared__ float scratch[kCombineThreads / 32];
   const int64_t row = blockIdx.x;  // token * heads + head
   if (row >= rows) return;
   const int64_t tok = row / heads;
   // number of splits that hold keys for this token's request
   int64_t b = 0;
   while (b + 1 < batch && q_start[b + 1] <= tok) ++b;
-  const int64_t need = ((int64_t)seq_lens[b] + kAttnChunk - 1) / kAttnChunk;
+  const int64_t need = ((int64_t)seq_lens[b] + chunk - 1) / chunk;
   const int used = (int)(need < splits ? need : splits);
-  const float *base = part + row * splits * part_stride(d);
+  const int64_t stride = part_stride(d);
+  const float *base = part + row * splits * stride;
   float M = -CUDART_INF_F;
-  for (int s = 0; s < used; ++s) M = fmaxf(M, base[s * part_stride(d) + d]);
+  for (int s = threadIdx.x; s < used; s += kCombineThreads) M = fmaxf(M, base[s * stride + d]);
+  M = block_reduce(M, true, scratch);
   float L = 0.f;
-  for (int s = 0; s < used; ++s) {
-    const float ms = base[s * part_stride(d) + d];
-    if (ms != -CUDART_INF_F) L += base[s * part_stride(d) + d + 1] * __expf(ms - M);
+  for (int s = threadIdx.x; s < used; s += kCombineThreads) {
+    const float ms = base[s * stride + d];
+    if (ms != -CUDART_INF_F) L += base[s * stride + d + 1] * __expf(ms - M);
   }
-  for (int64_t c = threadIdx.x; c < d; c += blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < used; ++s) {
-      const float ms = base[s * part_stride(d) + d];
-      if (ms != -CUDART_INF_F) acc += base[s * part_stride(d) + c] * __expf(ms - M);
+  L = block_reduce(L, false, scratch);
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};  // columns tid + 256 j (d <= 1024)
+  for (int s0 = 0; s0 < used; s0 += kCombineBlock) {
+    const int n = min(kCombineBlock, used - s0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += kCombineThreads) {
+      const float ms = base[(s0 + i) * stride + d];
+      wgt[i] = ms == -CUDART_INF_F ? 0.f : __expf(ms - M);
     }
-    out[row * d + c] = (uint16_t)f32_to_bf16_bits(L > 0.f ? acc / L : 0.f);
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t c = threadIdx.x + (int64_t)kCombineThreads * j;
+      if (c >= d) break;
+      float a = acc[j];
+      // unconditional loads (a split without keys has weight 0 and a zero
+      // partial), so the unrolled splits' loads are in flight together
+#pragma unroll 8
+      for (int i = 0; i < n; ++i) a = fmaf(__ldg(base + (s0 + i) * stride + c), wgt[i], a);
+      acc[j] = a;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t c = threadIdx.x + (int64_t)kCombineThreads * j;
+    if (c < d) out[row * d + c] = (uint16_t)f32_to_bf16_bits(acc[j] * inv);
+  }
+}
+
+// ------------------------------------------------------ decode attention ---
+
+constexpr int kDecChunk = 64;   // keys per CTA of the decode kernel
+constexpr int kDecThreads = 128;
+constexpr int kDecHead = 256;   // head size of the decode kernel (128 threads x 2 value columns)
+constexpr int kDecBatch = 8;    // key rows whose loads a warp issues together
+
+// Split-KV attention for decode batches (normally one query row per
+// request).  CTA = (request b, KV head h, 64-key chunk); the G query heads
+// of the GQA group share every key and value load.
+//   * the scales are static per head, so the CTA builds K and V tables of
+//     BF16(decode(c) x scale) for the scale of its first row; a row with
+//     that scale decodes with one lookup, any other row multiplies and
+//     rounds as the reference materialises BF16 K and V;
+//   * the chunk's row offsets are resolved from the block table once, into
+//     shared memory (a block id outside [0, num_blocks) marks the key absent);
+//   * scores: warp w takes keys w, w+4, ...; the 32 lanes read one K row
+//     together (4 bytes per lane and 128-byte step, coalesced) and reduce the
+//     G dot products with butterfly shuffles;
+//   * softmax per head in FP32; P @ V with the same row split as the scores
+//     (warp w takes keys [16 w, 16 w + 16)), the four warps' sums added in
+//     shared memory; all row loads are unconditional, so the unrolled keys'
+//     loads are in flight together;
+//   * partials (unnormalised output, running max, sum) merge in
+//     attention_combine_kernel, or are written directly when one chunk covers
+//     the longest request.
+template <int G>
+__global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArgs p) {
+  constexpr int D = kDecHead;
+  constexpr int W = D / 128;  // 4-byte K / V words per lane per row
+  __shared__ float lut[256], klut[256], vlut[256];
+  __shared__ float ks0, vs0;
+  __shared__ int64_t rowoff[kDecChunk];
+  __shared__ float prob[G][kDecChunk];
+  __shared__ float mrow[G], lrow[G];
+  __shared__ __align__(16) float vsum[4][G][D];  // per-warp P @ V sums
+  const int b = blockIdx.x / (int)p.kv_heads, h = blockIdx.x - b * (int)p.kv_heads;
+  const int split = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int q0 = p.q_start[b], q_len = p.q_start[b + 1] - q0;
+  const int seq = p.seq_lens[b];
+  const int chunk0 = split * kDecChunk;
+  if (q_len <= 0 || chunk0 >= seq) return;  // the merge reads only chunks that hold keys
+  const int64_t width = D + 4;
+  for (int i = tid; i < 256; i += kDecThreads) lut[i] = __uint_as_float(g_decode_f32.v[i]);
+  if (tid < kDecChunk) {
+    const int key = chunk0 + tid;
+    int64_t off = -1;
+    if (key < seq) {
+      const int64_t blk = page_of(p.tables + (int64_t)b * p.max_blocks, key, p.block_size, p.max_blocks,
+                                  p.num_blocks);
+      if (blk >= 0) off = ((blk * p.block_size + key % p.block_size) * p.kv_heads + h) * width;
+    }
+    rowoff[tid] = off;
+    if (tid == 0) {  // the chunk's reference scales (NaN: no table, every row computes)
+      ks0 = off >= 0 ? *reinterpret_cast<const float *>(p.kc + off + D) : CUDART_NAN_F;
+      vs0 = off >= 0 ? *reinterpret_cast<const float *>(p.vc + off + D) : CUDART_NAN_F;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < 256; i += kDecThreads) {
+    klut[i] = bf16_bits_to_f32(f32_to_bf16_bits(lut[i] * ks0));
+    vlut[i] = bf16_bits_to_f32(f32_to_bf16_bits(lut[i] * vs0));
+  }
+  __syncthreads();
+
+  for (int r = 0; r < q_len; ++r) {
+    const int64_t tok = q0 + r;
+    const int limit = p.causal ? seq - q_len + r : seq - 1;  // last key this row sees
+    // query vectors: lane holds columns 4 (lane + 32 i) + e of every head g
+    float qv[G][4 * W];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const uint16_t *qrow = p.q + (tok * p.heads + (int64_t)h * G + g) * D;
+#pragma unroll
+      for (int i = 0; i < W; ++i) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(qrow + 4 * (lane + 32 * i));
+        qv[g][4 * i + 0] = bf16_bits_to_f32(v.x & 0xFFFFu);
+        qv[g][4 * i + 1] = bf16_bits_to_f32(v.x >> 16);
+        qv[g][4 * i + 2] = bf16_bits_to_f32(v.y & 0xFFFFu);
+        qv[g][4 * i + 3] = bf16_bits_to_f32(v.y >> 16);
+      }
+    }
+    // ---- scores, kKB = 32 / G keys per batch: all the batch's row loads
+    // (read-only path, unconditional: an absent key reads row 0 of the cache,
+    // in bounds, and is masked afterwards) are issued before any arithmetic
+    // or shared-memory store, so they are in flight together.  The batch's
+    // 32 (key, head) partial dot products are then summed across the warp by
+    // a transpose-reduction: after 16 + 8 + 4 + 2 + 1 shuffles lane l holds
+    // the total of value l.
+    constexpr int kKB = 32 / G < kDecChunk / 4 ? 32 / G : kDecChunk / 4;
+    for (int j0 = 0; j0 < kDecChunk / 4; j0 += kKB) {
+      uint32_t kw[kKB][W];
+      float ks[kKB];
+#pragma unroll
+      for (int u = 0; u < kKB; ++u) {
+        const int k = warp + 4 * (j0 + u);
+        const int64_t off = rowoff[k];
+        const uint8_t *row = p.kc + (off >= 0 ? off : 0);
+        ks[u] = __ldg(reinterpret_cast<const float *>(row + D));
+#pragma unroll
+        for (int i = 0; i < W; ++i) kw[u][i] = __ldg(reinterpret_cast<const unsigned int *>(row + 4 * (lane + 32 * i)));
+      }
+      float part[32];  // value u * G + g: key j0 + u, head g (unused values stay 0)
+#pragma unroll
+      for (int i = kKB * G; i < 32; ++i) part[i] = 0.f;
+#pragma unroll
+      for (int u = 0; u < kKB; ++u) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) part[u * G + g] = 0.f;
+        if (ks[u] == ks0) {  // uniform across the warp
+#pragma unroll
+          for (int i = 0; i < W; ++i) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float kv = klut[(kw[u][i] >> (8 * e)) & 0xFFu];
+#pragma unroll
+              for (int g = 0; g < G; ++g) part[u * G + g] = fmaf(qv[g][4 * i + e], kv, part[u * G + g]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < W; ++i) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float kv = bf16_bits_to_f32(f32_to_bf16_bits(lut[(kw[u][i] >> (8 * e)) & 0xFFu] * ks[u]));
+#pragma unroll
+              for (int g = 0; g < G; ++g) part[u * G + g] = fmaf(qv[g][4 * i + e], kv, part[u * G + g]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int half = 16; half > 0; half >>= 1) {
+        const bool upper = (lane & half) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float send = upper ? part[i] : part[i + half];
+          const float keep = upper ? part[i + half] : part[i];
+          part[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, half);
+        }
+      }
+      // lane l = u * G + g now holds the score of key j0 + u, head g
+      {
+        const int u = lane / G, g = lane - u * G;
+        if (u < kKB) {
+          const int k = warp + 4 * (j0 + u);
+          const bool valid = rowoff[k] >= 0 && chunk0 + k <= limit;
+          prob[g][k] = valid ? part[0] * p.scale : -CUDART_INF_F;
+        }
+      }
+    }
+    __syncthreads();
+    // ---- softmax per head (warp w takes heads w, w + 4)
+    for (int g = warp; g < G; g += 4) {
+      float v[kDecChunk / 32];
+      float m = -CUDART_INF_F;
+#pragma unroll
+      for (int i = 0; i < kDecChunk / 32; ++i) {
+        v[i] = prob[g][lane + 32 * i];
+        m = fmaxf(m, v[i]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+      float l = 0.f;
+#pragma unroll
+      for (int i = 0; i < kDecChunk / 32; ++i) {
+        const float e = v[i] == -CUDART_INF_F ? 0.f : __expf(v[i] - m);
+        prob[g][lane + 32 * i] = e;
+        l += e;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+      if (lane == 0) {
+        mrow[g] = m;
+        lrow[g] = l;
+      }
+    }
+    __syncthreads();
+    // ---- P @ V: warp w takes keys [32 w, 32 w + 32) and, like the K pass,
+    // lane columns 4 (lane + 32 i) + e; the four warps' sums meet in shared
+    // memory afterwards
+    float acc[G][4 * W];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int c = 0; c < 4 * W; ++c) acc[g][c] = 0.f;
+    constexpr int kKeysPerWarp = kDecChunk / 4;
+    for (int j0 = 0; j0 < kKeysPerWarp; j0 += kDecBatch) {
+      uint32_t vw[kDecBatch][W];
+      float vs[kDecBatch];
+      bool valid[kDecBatch];
+#pragma unroll
+      for (int u = 0; u < kDecBatch; ++u) {
+        const int k = warp * kKeysPerWarp + j0 + u;
+        const int64_t off = rowoff[k];
+        valid[u] = off >= 0 && chunk0 + k <= limit;
+        const uint8_t *row = p.vc + (valid[u] ? off : 0);
+        vs[u] = __ldg(reinterpret_cast<const float *>(row + D));
+#pragma unroll
+        for (int i = 0; i < W; ++i) vw[u][i] = __ldg(reinterpret_cast<const unsigned int *>(row + 4 * (lane + 32 * i)));
+      }
+#pragma unroll
+      for (int u = 0; u < kDecBatch; ++u) {
+        if (!valid[u]) continue;
+        const int k = warp * kKeysPerWarp + j0 + u;
+        float pk[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) pk[g] = prob[g][k];
+        const bool table = vs[u] == vs0;
+#pragma unroll
+        for (int i = 0; i < W; ++i) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t c = (vw[u][i] >> (8 * e)) & 0xFFu;
+            const float vv = table ? vlut[c] : bf16_bits_to_f32(f32_to_bf16_bits(lut[c] * vs[u]));
+#pragma unroll
+            for (int g = 0; g < G; ++g) acc[g][4 * i + e] = fmaf(pk[g], vv, acc[g][4 * i + e]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int i = 0; i < W; ++i)
+        *reinterpret_cast<float4 *>(&vsum[warp][g][4 * (lane + 32 * i)]) =
+            make_float4(acc[g][4 * i], acc[g][4 * i + 1], acc[g][4 * i + 2], acc[g][4 * i + 3]);
+    __syncthreads();
+    // thread t finishes columns 2 t and 2 t + 1 of every head
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        o0 += vsum[w][g][2 * tid];
+        o1 += vsum[w][g][2 * tid + 1];
+      }
+      const int64_t head = (int64_t)h * G + g;
+      if (p.splits == 1) {
+        const float l = lrow[g];
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint16_t *dst = p.out + (tok * p.heads + head) * D;
+        *reinterpret_cast<uint32_t *>(dst + 2 * tid) = f32_to_bf16_bits(o0 * inv) | (f32_to_bf16_bits(o1 * inv) << 16);
+      } else {
+        float *dst = p.part + ((tok * p.heads + head) * p.splits + split) * part_stride(D);
+        dst[2 * tid] = o0;
+        dst[2 * tid + 1] = o1;
+        if (tid == 0) {
+          dst[D] = mrow[g];
+          dst[D + 1] = lrow[g];
+        }
+      }
+    }
+    __syncthreads();  // prob / mrow / lrow are reused by the next query row
   }
 }
 
@@ -374,9 +675,10 @@ extern "C" int hif8_kv_cache_write(const void *key, const void *value, int src_d
 
 static int attn_nq(int64_t group, int64_t q_rows) { return (int)(group * q_rows); }
 
+// Sized for the finer of the two kernels' key chunks (the decode kernel's).
 extern "C" size_t hif8_paged_attention_workspace_size(int64_t num_tokens, int64_t num_heads, int64_t head_size,
                                                       int64_t max_seq_len) {
-  const int64_t splits = (max_seq_len + kAttnChunk - 1) / kAttnChunk;
+  const int64_t splits = (max_seq_len + kDecChunk - 1) / kDecChunk;
   if (splits <= 1) return 0;
   return (size_t)(num_tokens * num_heads * splits * part_stride(head_size)) * sizeof(float);
 }
@@ -408,9 +710,15 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
   if (num_tokens == 0) return HIF8_OK;
   const int64_t group = num_heads / kv_heads;
   if (group > 16) return HIF8_ERR_INVALID_ARGUMENT;
-  const int64_t splits = max_seq_len > 0 ? (max_seq_len + kAttnChunk - 1) / kAttnChunk : 1;
   const size_t need = hif8_paged_attention_workspace_size(num_tokens, num_heads, head_size, max_seq_len);
   if (need > 0 && (!workspace || workspace_bytes < need)) return HIF8_ERR_WORKSPACE;
+  // decode batches (as many query rows as requests) of head size 256 and a
+  // power-of-two GQA group take the split-KV decode kernel
+  const bool decode = num_tokens == batch && head_size == kDecHead &&
+                      (group == 1 || group == 2 || group == 4 || group == 8) &&
+                      (reinterpret_cast<uintptr_t>(query) & 7u) == 0 && (reinterpret_cast<uintptr_t>(out) & 3u) == 0;
+  const int chunk = decode ? kDecChunk : kAttnChunk;
+  const int64_t splits = max_seq_len > 0 ? (max_seq_len + chunk - 1) / chunk : 1;
   AttnArgs p{};
   p.q = query;
   p.kc = key_cache;
@@ -432,8 +740,17 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // query rows per CTA: every query vector of a CTA shares the key loads
   int status;
-  if (group <= 4) {
-    // decode steps (one query row per request) take the small variant
+  if (decode) {
+    const dim3 grid((unsigned)(batch * kv_heads), (unsigned)splits, 1);
+    switch (group) {
+      case 1: paged_decode_kernel<1><<<grid, kDecThreads, 0, s>>>(p); break;
+      case 2: paged_decode_kernel<2><<<grid, kDecThreads, 0, s>>>(p); break;
+      case 4: paged_decode_kernel<4><<<grid, kDecThreads, 0, s>>>(p); break;
+      default: paged_decode_kernel<8><<<grid, kDecThreads, 0, s>>>(p); break;
+    }
+    status = check_launch();
+  } else if (group <= 4) {
+    // prefill and mixed batches: up to 4 query vectors per CTA
     p.q_rows_per_cta = (int)(4 / group);
     const int64_t q_groups = (num_tokens + p.q_rows_per_cta - 1) / p.q_rows_per_cta;
     status = launch_attention<4>(p, batch, q_groups, s);
@@ -445,7 +762,8 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
   (void)attn_nq;
   if (status != HIF8_OK || splits == 1) return status;
   const int64_t rows = num_tokens * num_heads;
-  attention_combine_kernel<<<(unsigned)rows, 256, 0, s>>>(p.part, rows, head_size, (int)splits, query_start,
+  attention_combine_kernel<<<(unsigned)rows, kCombineThreads, 0, s>>>(p.part, rows, head_size, (int)splits, chunk,
+                                                                     query_start,
                                                          seq_lens, batch, num_heads, out);
   return check_launch();
 }

@@ -92,8 +92,10 @@ def test_paged_attention_workspace_sizes():
     from hif8_b200 import cabi
 
     lib = cabi.library()
-    assert lib.hif8_paged_attention_workspace_size(4, 16, 256, 256) == 0  # one chunk: no partials
-    assert lib.hif8_paged_attention_workspace_size(4, 16, 256, 4096) == 4 * 16 * 16 * (256 + 2) * 4
+    # partials of 64-key chunks: [tokens, heads, chunks, head_size + 2] FP32
+    assert lib.hif8_paged_attention_workspace_size(4, 16, 256, 64) == 0  # one chunk: no partials
+    assert lib.hif8_paged_attention_workspace_size(4, 16, 256, 256) == 4 * 16 * 4 * (256 + 2) * 4
+    assert lib.hif8_paged_attention_workspace_size(4, 16, 256, 4096) == 4 * 16 * 64 * (256 + 2) * 4
 
 
 def test_torch_ops_have_reference_schemas():
