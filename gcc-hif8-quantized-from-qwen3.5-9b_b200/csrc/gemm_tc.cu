@@ -213,9 +213,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  for (int i = tid; i < 256 * 32; i += kTcThreads) {
-    const int b = i >> 5, l = i & 31;
-    reinterpret_cast<uint32_t *>(lut)[b * 64 + l] = g_decode_f32.v[b] >> 16;
+  // lane-replicated table: a warp loads 16 entries (one per lane) and
+  // writes each as 32 consecutive words
+  for (int b0 = warp * 16; b0 < 256; b0 += (kTcThreads / 32) * 16) {
+    const uint32_t mine = g_decode_f32.v[b0 + (lane & 15)] >> 16;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      reinterpret_cast<uint32_t *>(lut)[(b0 + j) * 64 + lane] = __shfl_sync(0xFFFFFFFFu, mine, j);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -356,14 +360,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // Decode HiF8 activation bytes to unscaled BF16 (exact) for the TMA B operand.
 __global__ void __launch_bounds__(256) decode_to_bf16(const uint8_t *__restrict__ a, uint16_t *__restrict__ out,
                                                       int64_t chunks) {
+  __shared__ uint32_t tbl[256];  // decoded value as FP32 bits (BF16 payload in the high half)
+  tbl[threadIdx.x] = g_decode_f32.v[threadIdx.x];
+  __syncthreads();
   for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks; c += (int64_t)gridDim.x * blockDim.x) {
     const uint4 v = *reinterpret_cast<const uint4 *>(a + c * 16);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     uint32_t r[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      r[2 * j] = __byte_perm(g_decode_f32.v[w[j] & 0xFF], g_decode_f32.v[(w[j] >> 8) & 0xFF], 0x7632u);
-      r[2 * j + 1] = __byte_perm(g_decode_f32.v[(w[j] >> 16) & 0xFF], g_decode_f32.v[w[j] >> 24], 0x7632u);
+      r[2 * j] = __byte_perm(tbl[w[j] & 0xFF], tbl[(w[j] >> 8) & 0xFF], 0x7632u);
+      r[2 * j + 1] = __byte_perm(tbl[(w[j] >> 16) & 0xFF], tbl[w[j] >> 24], 0x7632u);
     }
     uint4 *dst = reinterpret_cast<uint4 *>(out + c * 16);
     dst[0] = make_uint4(r[0], r[1], r[2], r[3]);

@@ -99,6 +99,26 @@ __device__ __forceinline__ uint32_t fake_quant_bf16(uint32_t h, float s, float r
   return g_decode_f32.v[code] >> 16;
 }
 
+// The same with the encode table and the lane-replicated decode table in
+// shared memory (the prologue's copies).
+template <int ASRC>
+__device__ __forceinline__ uint32_t fake_quant_bf16_smem(uint32_t h, float s, float r, bool exact_only,
+                                                         const uint8_t *enc, const uint32_t *lut, int lane) {
+  const float f = ASRC == kActBf16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
+  float q = __fmul_rn(f, r);
+  uint32_t u = __float_as_uint(q);
+  const uint32_t low = u & 0x7FFFFu;
+  uint32_t code;
+  if (exact_only | ((low - 4u) > 0x7FFF8u) | ((u & 0x7F800000u) >= 0x7D000000u)) {
+    q = __fdiv_rn(f, s);
+    u = __float_as_uint(q);
+    code = ((u & 0x7FFFFFFFu) > 0x7F800000u) ? 0x80u : (uint32_t)enc[u >> 19];
+  } else {
+    code = enc[u >> 19];
+  }
+  return lut[code * 64 + lane];
+}
+
 template <int OUT>
 __device__ __forceinline__ void store_out(void *out, int64_t idx, float v) {
   if constexpr (OUT == HIF8_DTYPE_BF16) static_cast<uint16_t *>(out)[idx] = (uint16_t)f32_to_bf16_bits(v);
@@ -146,15 +166,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   // ---- prologue: lane-replicated decode table + this rank's activation slice
   {
     uint32_t *lut = reinterpret_cast<uint32_t *>(smem);
-    for (int i = tid; i < 256 * 32; i += kThreads) {
-      const int b = i >> 5, l = i & 31;
-      lut[b * 64 + l] = g_decode_f32.v[b] >> 16;
+    // warp w owns table entries 16 w .. 16 w + 15: one global load per lane,
+    // then each entry is broadcast and written as 32 consecutive words
+    {
+      const uint32_t mine = g_decode_f32.v[warp * 16 + (lane & 15)] >> 16;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) lut[(warp * 16 + j) * 64 + lane] = __shfl_sync(0xFFFFFFFFu, mine, j);
     }
+    // the fused quantiser's 8 KB encode table, staged in the reduction buffer
+    // (idle until the first item is reduced)
+    uint8_t *enc = reinterpret_cast<uint8_t *>(red);
+    if (ASRC != kActCodes) {
+      for (int i = tid; i < 512; i += kThreads)
+        reinterpret_cast<uint4 *>(enc)[i] = reinterpret_cast<const uint4 *>(g_static_encode.v)[i];
+    }
+    __syncthreads();
     const int chunks_per_tok = kc >> 4;  // 16 K values per chunk
+    const int real = (p.m < kTok ? p.m : kTok) * chunks_per_tok;
     for (int i = tid; i < kTok * chunks_per_tok; i += kThreads) {
       const int tok = i / chunks_per_tok, ch = i - tok * chunks_per_tok;
       uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
-      if (ASRC != kActCodes && tok < p.m) {
+      if (ASRC != kActCodes && i < real) {
         const float s = p.ts[0];
         const float r = __frcp_rn(s);
         const uint32_t re = __float_as_uint(r) & 0x7F800000u;
@@ -166,21 +198,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
         uint32_t r8[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          r8[j] = fake_quant_bf16<ASRC>(h8[j] & 0xFFFFu, s, r, exact_only) |
-                  (fake_quant_bf16<ASRC>(h8[j] >> 16, s, r, exact_only) << 16);
+          r8[j] = fake_quant_bf16_smem<ASRC>(h8[j] & 0xFFFFu, s, r, exact_only, enc, lut, lane) |
+                  (fake_quant_bf16_smem<ASRC>(h8[j] >> 16, s, r, exact_only, enc, lut, lane) << 16);
         o0 = make_uint4(r8[0], r8[1], r8[2], r8[3]);
         o1 = make_uint4(r8[4], r8[5], r8[6], r8[7]);
-      } else if (tok < p.m) {
+      } else if (i < real) {
         const uint4 v = *reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.a) + (int64_t)tok * p.k +
                                                          k0 + ch * 16);
         const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+        const uint32_t lane4 = (uint32_t)lane << 2;
         uint32_t r[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t w = w4[j];
-          r[2 * j] = __byte_perm(g_decode_f32.v[w & 0xFF], g_decode_f32.v[(w >> 8) & 0xFF], 0x7632u);
-          r[2 * j + 1] = __byte_perm(g_decode_f32.v[(w >> 16) & 0xFF], g_decode_f32.v[w >> 24], 0x7632u);
-        }
+        for (int j = 0; j < 4; ++j) decode4(smem, w4[j], lane4, r[2 * j], r[2 * j + 1]);
         o0 = make_uint4(r[0], r[1], r[2], r[3]);
         o1 = make_uint4(r[4], r[5], r[6], r[7]);
       }

@@ -105,10 +105,10 @@ HIF8_HD constexpr uint32_t decode_bf16(uint32_t b) {
   return sign | (ef << 7) | fr;
 }
 
-struct Table13 {
+struct alignas(16) Table13 {
   uint8_t v[8192];
 };
-struct Table256 {
+struct alignas(16) Table256 {
   uint32_t v[256];
 };
 
