@@ -160,8 +160,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   const int k0 = rank * kc;
   const int act_stride = act_stride_bytes(kc);
   uint8_t *act = smem + kLutBytes;
-  float *red = reinterpret_cast<float *>(act + (size_t)kTok * act_stride);  // [2][kWarps][16][kTok]
-  float *part = red + 2 * kWarps * 16 * kTok;                               // [items][16 * WR][kTok]
+  float *red = reinterpret_cast<float *>(act + (size_t)kTok * act_stride);  // [2][kWarps][kTok][16]
+  float *part = red + 2 * kWarps * 16 * kTok;                               // [items][kTok][16 * WR]
 
   // ---- prologue: lane-replicated decode table + this rank's activation slice
   {
@@ -183,39 +183,66 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
     __syncthreads();
     const int chunks_per_tok = kc >> 4;  // 16 K values per chunk
     const int real = (p.m < kTok ? p.m : kTok) * chunks_per_tok;
-    for (int i = tid; i < kTok * chunks_per_tok; i += kThreads) {
-      const int tok = i / chunks_per_tok, ch = i - tok * chunks_per_tok;
-      uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
-      if (ASRC != kActCodes && i < real) {
-        const float s = p.ts[0];
-        const float r = __frcp_rn(s);
-        const uint32_t re = __float_as_uint(r) & 0x7F800000u;
-        const bool exact_only = (re == 0u) | (re == 0x7F800000u);
-        const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p.a) +
-                                                           (int64_t)tok * p.k + k0 + ch * 16);
-        const uint4 v0 = src[0], v1 = src[1];
-        const uint32_t h8[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        uint32_t r8[8];
+    const int total_chunks = kTok * chunks_per_tok;
+    const uint32_t lane4 = (uint32_t)lane << 2;
+    float s = 1.f, r = 1.f;
+    bool exact_only = false;
+    if (ASRC != kActCodes) {
+      s = p.ts[0];
+      r = __frcp_rn(s);
+      const uint32_t re = __float_as_uint(r) & 0x7F800000u;
+      exact_only = (re == 0u) | (re == 0x7F800000u);
+    }
+    // four chunks per thread and round: their global loads are issued first
+    for (int base = 0; base < total_chunks; base += 4 * kThreads) {
+      uint4 raw[4][2];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          r8[j] = fake_quant_bf16_smem<ASRC>(h8[j] & 0xFFFFu, s, r, exact_only, enc, lut, lane) |
-                  (fake_quant_bf16_smem<ASRC>(h8[j] >> 16, s, r, exact_only, enc, lut, lane) << 16);
-        o0 = make_uint4(r8[0], r8[1], r8[2], r8[3]);
-        o1 = make_uint4(r8[4], r8[5], r8[6], r8[7]);
-      } else if (i < real) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.a) + (int64_t)tok * p.k +
+      for (int u = 0; u < 4; ++u) {
+        const int i = base + u * kThreads + tid;
+        raw[u][0] = raw[u][1] = make_uint4(0, 0, 0, 0);
+        if (i < real) {
+          const int tok = i / chunks_per_tok, ch = i - tok * chunks_per_tok;
+          if (ASRC != kActCodes) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p.a) +
+                                                               (int64_t)tok * p.k + k0 + ch * 16);
+            raw[u][0] = src[0];
+            raw[u][1] = src[1];
+          } else {
+            raw[u][0] = *reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.a) + (int64_t)tok * p.k +
                                                          k0 + ch * 16);
-        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-        const uint32_t lane4 = (uint32_t)lane << 2;
-        uint32_t r[8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) decode4(smem, w4[j], lane4, r[2 * j], r[2 * j + 1]);
-        o0 = make_uint4(r[0], r[1], r[2], r[3]);
-        o1 = make_uint4(r[4], r[5], r[6], r[7]);
+          }
+        }
       }
-      uint4 *dst = reinterpret_cast<uint4 *>(act + tok * act_stride + ch * 32);
-      dst[0] = o0;
-      dst[1] = o1;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = base + u * kThreads + tid;
+        if (i >= total_chunks) break;
+        const int tok = i / chunks_per_tok, ch = i - tok * chunks_per_tok;
+        uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
+        if (i < real) {
+          if (ASRC != kActCodes) {
+            const uint32_t h8[8] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w,
+                                    raw[u][1].x, raw[u][1].y, raw[u][1].z, raw[u][1].w};
+            uint32_t r8[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              r8[j] = fake_quant_bf16_smem<ASRC>(h8[j] & 0xFFFFu, s, r, exact_only, enc, lut, lane) |
+                      (fake_quant_bf16_smem<ASRC>(h8[j] >> 16, s, r, exact_only, enc, lut, lane) << 16);
+            o0 = make_uint4(r8[0], r8[1], r8[2], r8[3]);
+            o1 = make_uint4(r8[4], r8[5], r8[6], r8[7]);
+          } else {
+            const uint32_t w4[4] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w};
+            uint32_t rr[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) decode4(smem, w4[j], lane4, rr[2 * j], rr[2 * j + 1]);
+            o0 = make_uint4(rr[0], rr[1], rr[2], rr[3]);
+            o1 = make_uint4(rr[4], rr[5], rr[6], rr[7]);
+          }
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(act + tok * act_stride + ch * 32);
+        dst[0] = o0;
+        dst[1] = o1;
+      }
     }
   }
   __syncthreads();
@@ -224,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   const int g = lane >> 2, t = lane & 3;
   const int wr = warp / WK, wk = warp - wr * WK;  // row group / K part of this warp
   const int rows_per_item = 16 * WR;
+  const int mt = p.m < kTok ? p.m : kTok;  // real tokens of the tile
   const int n_items = (p.n + rows_per_item - 1) / rows_per_item;
   const int my_items = n_items > cluster_id ? (n_items - cluster_id + plan.clusters - 1) / plan.clusters : 0;
   const int kw0 = k0 + wk * kWarpK;  // this warp's K offset inside every item
@@ -291,29 +319,31 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
     }
 
     // ---- reduce the item: warps (fixed order), then cluster ranks ---------
+    // Partials are token-major ([token][row]) so the summing threads walk the
+    // output rows of one token consecutively: the global stores coalesce.
     const int buf = item & 1;
-    float *wred = red + ((size_t)buf * kWarps + warp) * 16 * kTok;
+    float *wred = red + ((size_t)buf * kWarps + warp) * kTok * 16;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int m = nt * 8 + 2 * t + (q & 1);
         const int rl = g + ((q < 2) ? 0 : 8);
-        wred[rl * kTok + m] = acc[0][nt][q] + acc[1][nt][q];
+        wred[m * 16 + rl] = acc[0][nt][q] + acc[1][nt][q];
       }
     }
     __syncthreads();
     const int row_base = (cluster_id + item * plan.clusters) * rows_per_item;
     float *cpart = part + (size_t)item * rows_per_item * kTok;
-    for (int e = tid; e < rows_per_item * kTok; e += kThreads) {
-      const int rl = e / kTok, m = e - rl * kTok;  // row within the item, token
+    for (int e = tid; e < rows_per_item * mt; e += kThreads) {
+      const int m = e / rows_per_item, rl = e - m * rows_per_item;  // token, row within the item
       const int grp = rl >> 4, r16 = rl & 15;
-      const float *src = red + ((size_t)buf * kWarps + grp * WK) * 16 * kTok + r16 * kTok + m;
+      const float *src = red + (((size_t)buf * kWarps + grp * WK) * kTok + m) * 16 + r16;
       float v = 0.f;
-      for (int w = 0; w < WK; ++w) v += src[(size_t)w * 16 * kTok];
+      for (int w = 0; w < WK; ++w) v += src[(size_t)w * kTok * 16];
       if (S == 1) {
         const int n = row_base + rl;
-        if (m < p.m && n < p.n) {
+        if (n < p.n) {
           v = v * __ldg(p.cs + n);
           v = v * __ldg(p.ts + m * p.ts_stride);
           if (p.bias) v += load_bias(p.bias, p.bias_dtype, n);
@@ -326,17 +356,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   }
   if (S == 1) return;
 
-  // ---- cross-rank reduction of every item, once: rank r owns the elements
-  // e with e % S == r; partials are summed in rank order (deterministic).
+  // ---- cross-rank reduction of every item, once: rank r owns a contiguous
+  // range of the (item, token, row) elements; partials are summed in rank
+  // order (deterministic) and consecutive threads store consecutive rows.
   cluster.sync();
-  const int per_item = rows_per_item * kTok;
-  for (int e = rank + S * tid; e < my_items * per_item; e += S * kThreads) {
-    float v = 0.f;
-    for (int r = 0; r < S; ++r) v += cluster.map_shared_rank(part, r)[e];
+  const int per_item = rows_per_item * mt;
+  const int total = my_items * per_item;
+  const int share = (total + S - 1) / S;
+  const int e_end = min(total, (rank + 1) * share);
+  for (int e = rank * share + tid; e < e_end; e += kThreads) {
     const int item = e / per_item, rem = e - item * per_item;
-    const int rl = rem / kTok, m = rem - rl * kTok;
+    const int m = rem / rows_per_item, rl = rem - m * rows_per_item;
+    const size_t idx = (size_t)item * rows_per_item * kTok + rem;
+    float v = 0.f;
+    for (int r = 0; r < S; ++r) v += cluster.map_shared_rank(part, r)[idx];
     const int n = (cluster_id + item * plan.clusters) * rows_per_item + rl;
-    if (m < p.m && n < p.n) {
+    if (n < p.n) {
       v = v * __ldg(p.cs + n);
       v = v * __ldg(p.ts + m * p.ts_stride);
       if (p.bias) v += load_bias(p.bias, p.bias_dtype, n);
