@@ -26,7 +26,7 @@ PKG = HERE / "hif8_b200"
 BUILD = HERE / "_build"
 INCLUDE = REPO / "include"
 
-CU_SOURCES = ["cabi.cu", "quant.cu", "gemv.cu", "gemm_tc.cu", "kv.cu", "noalloc.cu"]
+CU_SOURCES = ["cabi.cu", "quant.cu", "gemv.cu", "gemm_tc.cu", "kv.cu", "noalloc.cu", "model.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # No --use_fast_math / -ftz: the static quantiser and the decode paths rely on

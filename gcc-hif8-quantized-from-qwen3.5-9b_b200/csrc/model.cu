@@ -1,0 +1,337 @@
+// Fused glue kernels of the synthetic Qwen3.5-9B-shaped hybrid decoder that
+// drives the HiF8 path end to end (the projections themselves are the HiF8
+// linear operators).  Layer structure follows transformers' Qwen3_5 text
+// model: (1 + w) RMSNorm, SiLU-gated MLP, gated full attention with q/k
+// RMSNorm and partial rotary embedding, and the gated-delta-net linear
+// attention (causal depthwise conv + SiLU, l2-normalised q/k, decay
+// g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b), delta-rule state
+// update, gated RMSNorm).  Activations are BF16, arithmetic FP32.
+#include <math_constants.h>
+
+#include "../../include/hif8_b200_model.h"
+#include "hif8_common.cuh"
+
+namespace hif8 {
+
+__device__ __forceinline__ float bf(uint16_t h) { return bf16_bits_to_f32(h); }
+__device__ __forceinline__ uint16_t to_bf(float v) { return (uint16_t)f32_to_bf16_bits(v); }
+__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+__device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + __expf(-x)); }
+
+// Sum over the CTA (blockDim.x a multiple of 32, at most 1024).
+__device__ __forceinline__ float block_sum(float v, float *scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < warps; ++w) t += scratch[w];
+  return t;
+}
+
+// ---------------------------------------------------------------- RMSNorm --
+// One CTA of 256 threads per row; each thread keeps up to 4 chunks of 8.
+constexpr int kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const uint16_t *__restrict__ x,
+                                                               const uint16_t *__restrict__ res_in,
+                                                               uint16_t *__restrict__ res_out,
+                                                               const uint16_t *__restrict__ w, float eps,
+                                                               int one_plus, int dim, uint16_t *__restrict__ out) {
+  __shared__ float scratch[32];
+  const int64_t row = blockIdx.x;
+  float v[4][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int col = (threadIdx.x + c * kNormThreads) * 8;
+    if (col < dim) {
+      const uint4 a = *reinterpret_cast<const uint4 *>(x + row * dim + col);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      uint32_t rw[4] = {0, 0, 0, 0};
+      if (res_in) {
+        const uint4 r = *reinterpret_cast<const uint4 *>(res_in + row * dim + col);
+        rw[0] = r.x, rw[1] = r.y, rw[2] = r.z, rw[3] = r.w;
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float lo = bf(aw[i] & 0xFFFFu), hi = bf(aw[i] >> 16);
+        if (res_in) {  // the residual stream is BF16: round the sum
+          lo = bf(to_bf(lo + bf(rw[i] & 0xFFFFu)));
+          hi = bf(to_bf(hi + bf(rw[i] >> 16)));
+        }
+        v[c][2 * i] = lo;
+        v[c][2 * i + 1] = hi;
+        o[i] = to_bf(lo) | ((uint32_t)to_bf(hi) << 16);
+        ss += lo * lo + hi * hi;
+      }
+      if (res_out) *reinterpret_cast<uint4 *>(res_out + row * dim + col) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  const float inv = rsqrtf(block_sum(ss, scratch) / (float)dim + eps);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int col = (threadIdx.x + c * kNormThreads) * 8;
+    if (col < dim) {
+      const uint4 wv = *reinterpret_cast<const uint4 *>(w + col);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float w0 = bf(ww[i] & 0xFFFFu), w1 = bf(ww[i] >> 16);
+        if (one_plus) w0 += 1.f, w1 += 1.f;
+        o[i] = to_bf(v[c][2 * i] * inv * w0) | ((uint32_t)to_bf(v[c][2 * i + 1] * inv * w1) << 16);
+      }
+      *reinterpret_cast<uint4 *>(out + row * dim + col) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------- SiLU-gated MLP --
+__global__ void silu_mul_kernel(const uint16_t *__restrict__ gu, int64_t rows, int64_t inter,
+                                uint16_t *__restrict__ out) {
+  const int64_t total = rows * inter / 2;  // pairs
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = (2 * i) / inter, c = 2 * i - r * inter;
+    const uint32_t g = *reinterpret_cast<const uint32_t *>(gu + r * 2 * inter + c);
+    const uint32_t u = *reinterpret_cast<const uint32_t *>(gu + r * 2 * inter + inter + c);
+    const float lo = silu(bf(g & 0xFFFFu)) * bf(u & 0xFFFFu);
+    const float hi = silu(bf(g >> 16)) * bf(u >> 16);
+    *reinterpret_cast<uint32_t *>(out + r * inter + c) = to_bf(lo) | ((uint32_t)to_bf(hi) << 16);
+  }
+}
+
+// ------------------------------------------------------ sigmoid gate (attn) --
+__global__ void gate_mul_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ gate, int64_t n,
+                                uint16_t *__restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = to_bf(bf(x[i]) * sigmoid(bf(gate[i])));
+}
+
+// ---------------------------------------------- attention q/k/v preparation --
+// CTA = (token, head slot); slots [0, heads) are query heads (the projection
+// row holds q and its output gate side by side per head), the rest KV heads.
+// q and k: per-head (1 + w) RMSNorm, then rotary embedding on the first
+// rotary_dim dims (rotate-half form); v is copied.
+__global__ void attn_prep_kernel(const uint16_t *__restrict__ qkv, int heads, int kv_heads, int hd, int rotary_dim,
+                                 const int32_t *__restrict__ positions, const uint16_t *__restrict__ qw,
+                                 const uint16_t *__restrict__ kw, float eps, float theta,
+                                 uint16_t *__restrict__ q_out, uint16_t *__restrict__ gate_out,
+                                 uint16_t *__restrict__ k_out, uint16_t *__restrict__ v_out) {
+  __shared__ float xs[1024];
+  __shared__ float scratch[32];
+  const int64_t tok = blockIdx.x;
+  const int slot = blockIdx.y;
+  const int64_t row_len = (int64_t)heads * 2 * hd + 2 * (int64_t)kv_heads * hd;
+  const uint16_t *row = qkv + tok * row_len;
+  const uint16_t *src;
+  const uint16_t *nw;
+  uint16_t *dst;
+  if (slot < heads) {
+    src = row + (int64_t)slot * 2 * hd;
+    nw = qw;
+    dst = q_out + (tok * heads + slot) * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) gate_out[(tok * heads + slot) * hd + i] = src[hd + i];
+  } else {
+    const int kh = slot - heads;
+    const uint16_t *vsrc = row + (int64_t)heads * 2 * hd + (int64_t)kv_heads * hd + (int64_t)kh * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) v_out[(tok * kv_heads + kh) * hd + i] = vsrc[i];
+    src = row + (int64_t)heads * 2 * hd + (int64_t)kh * hd;
+    nw = kw;
+    dst = k_out + (tok * kv_heads + kh) * hd;
+  }
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+    const float v = bf(src[i]);
+    xs[i] = v;
+    ss += v * v;
+  }
+  const float inv = rsqrtf(block_sum(ss, scratch) / (float)hd + eps);
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) xs[i] = bf(to_bf(xs[i] * inv * (1.f + bf(nw[i]))));
+  __syncthreads();
+  const float pos = (float)positions[tok];
+  const int half = rotary_dim / 2;
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+    float v = xs[i];
+    if (i < rotary_dim) {
+      const int f = i < half ? i : i - half;
+      const float inv_freq = powf(theta, -2.f * (float)f / (float)rotary_dim);
+      float sn, cs;
+      sincosf(pos * inv_freq, &sn, &cs);
+      v = i < half ? xs[i] * cs - xs[i + half] * sn : xs[i] * cs + xs[i - half] * sn;
+    }
+    dst[i] = to_bf(v);
+  }
+}
+
+// -------------------------------------------------- gated delta net (GDN) --
+// CTA = (value head vh, sequence b), 256 threads; the thread pair (2 j,
+// 2 j + 1) owns column j of the head's 128 x 128 FP32 state, rows [0, 64)
+// and [64, 128), in registers for the whole call, and channel j of the
+// head's q, k, v.  The call walks the sequence's T tokens in order (T = 1
+// for a decode step).  Projection row layout (local heads):
+// [q: hk*128 | k: hk*128 | v: hv*128 | z: hv*128 | b: hv | a: hv].  q/k
+// channels are shared by the hv/hk value heads of a key head; every CTA of
+// the group computes them and the first writes their convolution state.
+constexpr int kGdnDim = 128;
+constexpr int kGdnThreads = 2 * kGdnDim;
+constexpr int kGdnRows = kGdnDim / 2;  // state rows per thread
+
+__global__ void __launch_bounds__(kGdnThreads) gdn_kernel(const Hif8GdnArgs p) {
+  __shared__ float qs[kGdnDim], ks[kGdnDim];
+  __shared__ float scratch[32];
+  const int vh = blockIdx.x, b = blockIdx.y;
+  const int j = threadIdx.x >> 1, h = threadIdx.x & 1;
+  const int ratio = p.hv / p.hk, kh = vh / ratio;
+  const bool owner = (vh % ratio) == 0;
+  const int64_t C = 2LL * p.hk * kGdnDim + (int64_t)p.hv * kGdnDim;
+  const int64_t cq = (int64_t)kh * kGdnDim + j, ck = (int64_t)p.hk * kGdnDim + cq;
+  const int64_t cv = 2LL * p.hk * kGdnDim + (int64_t)vh * kGdnDim + j;
+  const int64_t cz = C + (int64_t)vh * kGdnDim + j;
+  const int64_t cb = C + (int64_t)p.hv * kGdnDim + vh, ca = cb + p.hv;
+  float wq[4], wk[4], wv[4], sq[3], sk[3], sv[3];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    wq[i] = bf(p.conv_w[cq * 4 + i]);
+    wk[i] = bf(p.conv_w[ck * 4 + i]);
+    wv[i] = bf(p.conv_w[cv * 4 + i]);
+  }
+  float *cs_b = p.conv_state + (int64_t)b * C * 3;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    sq[i] = cs_b[cq * 3 + i];
+    sk[i] = cs_b[ck * 3 + i];
+    sv[i] = cs_b[cv * 3 + i];
+  }
+  float *st = p.rec_state + (((int64_t)b * p.hv + vh) * kGdnDim + (int64_t)h * kGdnRows) * kGdnDim + j;
+  float S[kGdnRows];
+#pragma unroll
+  for (int i = 0; i < kGdnRows; ++i) S[i] = st[(int64_t)i * kGdnDim];
+  const float A = -__expf(p.a_log[vh]);
+  const float dtb = p.dt_bias[vh];
+  const float nw = bf(p.norm_w[j]);
+  const float qscale = rsqrtf((float)kGdnDim);
+  const float *kh_s = ks + h * kGdnRows, *qh_s = qs + h * kGdnRows;
+  for (int t = 0; t < p.T; ++t) {
+    const int64_t row = (int64_t)b * p.T + t;
+    const uint16_t *pr = p.proj + row * p.proj_stride;
+    const float xq = bf(pr[cq]), xk = bf(pr[ck]), xv = bf(pr[cv]);
+    const float yq = silu(sq[0] * wq[0] + sq[1] * wq[1] + sq[2] * wq[2] + xq * wq[3]);
+    const float yk = silu(sk[0] * wk[0] + sk[1] * wk[1] + sk[2] * wk[2] + xk * wk[3]);
+    const float yv = silu(sv[0] * wv[0] + sv[1] * wv[1] + sv[2] * wv[2] + xv * wv[3]);
+    sq[0] = sq[1], sq[1] = sq[2], sq[2] = xq;
+    sk[0] = sk[1], sk[1] = sk[2], sk[2] = xk;
+    sv[0] = sv[1], sv[1] = sv[2], sv[2] = xv;
+    const float nq = rsqrtf(block_sum(h == 0 ? yq * yq : 0.f, scratch) + 1e-6f);
+    const float nk = rsqrtf(block_sum(h == 0 ? yk * yk : 0.f, scratch) + 1e-6f);
+    if (h == 0) {
+      qs[j] = yq * nq * qscale;
+      ks[j] = yk * nk;
+    }
+    __syncthreads();
+    const float beta = sigmoid(bf(pr[cb]));
+    const float a = bf(pr[ca]) + dtb;
+    const float softplus = a > 20.f ? a : log1pf(__expf(a));
+    const float decay = __expf(A * softplus);
+    float kv = 0.f;
+#pragma unroll
+    for (int i = 0; i < kGdnRows; ++i) {
+      S[i] *= decay;
+      kv = fmaf(S[i], kh_s[i], kv);
+    }
+    kv += __shfl_xor_sync(0xFFFFFFFFu, kv, 1);
+    const float delta = (yv - kv) * beta;
+    float o = 0.f;
+#pragma unroll
+    for (int i = 0; i < kGdnRows; ++i) {
+      S[i] = fmaf(kh_s[i], delta, S[i]);
+      o = fmaf(S[i], qh_s[i], o);
+    }
+    o += __shfl_xor_sync(0xFFFFFFFFu, o, 1);
+    const float ob = bf(to_bf(o));  // the core output is BF16 before the gated norm
+    const float inv = rsqrtf(block_sum(h == 0 ? ob * ob : 0.f, scratch) / (float)kGdnDim + p.eps);
+    if (h == 0) {
+      const float z = bf(pr[cz]);
+      p.out[row * (int64_t)p.hv * kGdnDim + (int64_t)vh * kGdnDim + j] = to_bf(bf(to_bf(ob * inv)) * nw * silu(z));
+    }
+    __syncthreads();  // qs / ks are rewritten by the next token
+  }
+#pragma unroll
+  for (int i = 0; i < kGdnRows; ++i) st[(int64_t)i * kGdnDim] = S[i];
+  if (h == 0) {
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      if (owner) {
+        cs_b[cq * 3 + i] = sq[i];
+        cs_b[ck * 3 + i] = sk[i];
+      }
+      cs_b[cv * 3 + i] = sv[i];
+    }
+  }
+}
+
+}  // namespace hif8
+
+using namespace hif8;
+
+extern "C" int hif8_model_rmsnorm(const uint16_t *x, const uint16_t *residual_in, uint16_t *residual_out,
+                                  const uint16_t *weight, float eps, int one_plus, int64_t rows, int64_t dim,
+                                  uint16_t *out, void *stream) {
+  if (!x || !weight || !out || rows < 0 || dim <= 0 || dim % 8 != 0 || dim > 4 * kNormThreads * 8)
+    return HIF8_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return HIF8_OK;
+  rmsnorm_kernel<<<(unsigned)rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, residual_in, residual_out, weight, eps, one_plus, (int)dim, out);
+  return check_launch();
+}
+
+extern "C" int hif8_model_silu_mul(const uint16_t *gate_up, int64_t rows, int64_t inter, uint16_t *out,
+                                   void *stream) {
+  if (!gate_up || !out || rows < 0 || inter <= 0 || inter % 2 != 0) return HIF8_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return HIF8_OK;
+  const int64_t pairs = rows * inter / 2;
+  int64_t blocks = (pairs + 255) / 256;
+  if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
+  silu_mul_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(gate_up, rows, inter, out);
+  return check_launch();
+}
+
+extern "C" int hif8_model_gate_mul(const uint16_t *x, const uint16_t *gate, int64_t n, uint16_t *out, void *stream) {
+  if (!x || !gate || !out || n < 0) return HIF8_ERR_INVALID_ARGUMENT;
+  if (n == 0) return HIF8_OK;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
+  gate_mul_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, gate, n, out);
+  return check_launch();
+}
+
+extern "C" int hif8_model_attn_prep(const uint16_t *qkv, int64_t tokens, int heads, int kv_heads, int head_dim,
+                                    int rotary_dim, const int32_t *positions, const uint16_t *q_norm_w,
+                                    const uint16_t *k_norm_w, float eps, float rope_theta, uint16_t *q_out,
+                                    uint16_t *gate_out, uint16_t *k_out, uint16_t *v_out, void *stream) {
+  if (!qkv || !positions || !q_norm_w || !k_norm_w || !q_out || !gate_out || !k_out || !v_out || tokens < 0 ||
+      heads <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim > 1024 || rotary_dim < 0 || rotary_dim > head_dim ||
+      rotary_dim % 2 != 0)
+    return HIF8_ERR_INVALID_ARGUMENT;
+  if (tokens == 0) return HIF8_OK;
+  const dim3 grid((unsigned)tokens, (unsigned)(heads + kv_heads));
+  attn_prep_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      qkv, heads, kv_heads, head_dim, rotary_dim, positions, q_norm_w, k_norm_w, eps, rope_theta, q_out, gate_out,
+      k_out, v_out);
+  return check_launch();
+}
+
+extern "C" int hif8_model_gdn(const Hif8GdnArgs *args, int64_t batch, void *stream) {
+  if (!args || batch < 0) return HIF8_ERR_INVALID_ARGUMENT;
+  const Hif8GdnArgs &p = *args;
+  if (!p.proj || !p.conv_w || !p.a_log || !p.dt_bias || !p.norm_w || !p.conv_state || !p.rec_state || !p.out ||
+      p.T < 0 || p.hk <= 0 || p.hv <= 0 || p.hv % p.hk != 0 || p.key_dim != kGdnDim || p.value_dim != kGdnDim)
+    return HIF8_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || p.T == 0) return HIF8_OK;
+  const dim3 grid((unsigned)p.hv, (unsigned)batch);
+  gdn_kernel<<<grid, kGdnThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch();
+}

@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "../../include/hif8_b200.h"
+#include "../../include/hif8_b200_model.h"
 
 namespace {
 
@@ -322,6 +323,126 @@ at::Tensor Hif8PagedAttention(const at::Tensor &query, const at::Tensor &key_cac
   return out;
 }
 
+// ---- glue of the synthetic decoder (include/hif8_b200_model.h) ----------
+
+void CheckModelTensor(const at::Tensor &t, const char *name, at::ScalarType dtype) {
+  TORCH_CHECK(t.defined() && t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  TORCH_CHECK(t.scalar_type() == dtype, name, " must be ", dtype, ", got ", t.scalar_type());
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+
+const uint16_t *Bits(const at::Tensor &t) { return reinterpret_cast<const uint16_t *>(t.data_ptr()); }
+uint16_t *MutBits(at::Tensor &t) { return reinterpret_cast<uint16_t *>(t.data_ptr()); }
+
+std::tuple<at::Tensor, at::Tensor> ModelRmsnorm(const at::Tensor &x, const std::optional<at::Tensor> &residual,
+                                                const at::Tensor &weight, double eps, bool one_plus) {
+  CheckModelTensor(x, "x", at::kBFloat16);
+  CheckModelTensor(weight, "weight", at::kBFloat16);
+  const int64_t dim = x.size(-1), rows = x.numel() / dim;
+  TORCH_CHECK(weight.numel() == dim, "weight must have one value per column");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto out = at::empty_like(x);
+  at::Tensor res_out;
+  const uint16_t *res_in = nullptr;
+  if (residual.has_value()) {
+    CheckModelTensor(*residual, "residual", at::kBFloat16);
+    TORCH_CHECK(residual->sizes() == x.sizes(), "residual must match x");
+    res_in = Bits(*residual);
+    res_out = at::empty_like(x);
+  }
+  CheckStatus(hif8_model_rmsnorm(Bits(x), res_in, res_in ? MutBits(res_out) : nullptr, Bits(weight), (float)eps,
+                                 one_plus ? 1 : 0, rows, dim, MutBits(out), Stream(x)),
+              "hif8_model_rmsnorm");
+  return {out, res_in ? res_out : x};
+}
+
+at::Tensor ModelSiluMul(const at::Tensor &gate_up) {
+  CheckModelTensor(gate_up, "gate_up", at::kBFloat16);
+  const int64_t two_i = gate_up.size(-1), rows = gate_up.numel() / two_i;
+  TORCH_CHECK(two_i % 4 == 0, "gate_up width must be a multiple of 4");
+  c10::cuda::CUDAGuard guard(gate_up.device());
+  auto sizes = gate_up.sizes().vec();
+  sizes.back() = two_i / 2;
+  auto out = at::empty(sizes, gate_up.options());
+  CheckStatus(hif8_model_silu_mul(Bits(gate_up), rows, two_i / 2, MutBits(out), Stream(gate_up)),
+              "hif8_model_silu_mul");
+  return out;
+}
+
+at::Tensor ModelGateMul(const at::Tensor &x, const at::Tensor &gate) {
+  CheckModelTensor(x, "x", at::kBFloat16);
+  CheckModelTensor(gate, "gate", at::kBFloat16);
+  TORCH_CHECK(x.numel() == gate.numel(), "gate must match x");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto out = at::empty_like(x);
+  CheckStatus(hif8_model_gate_mul(Bits(x), Bits(gate), x.numel(), MutBits(out), Stream(x)), "hif8_model_gate_mul");
+  return out;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> ModelAttnPrep(
+    const at::Tensor &qkv, const at::Tensor &positions, const at::Tensor &q_norm_w, const at::Tensor &k_norm_w,
+    int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t rotary_dim, double eps, double rope_theta) {
+  CheckModelTensor(qkv, "qkv", at::kBFloat16);
+  CheckModelTensor(positions, "positions", at::kInt);
+  CheckModelTensor(q_norm_w, "q_norm_w", at::kBFloat16);
+  CheckModelTensor(k_norm_w, "k_norm_w", at::kBFloat16);
+  const int64_t tokens = qkv.size(0);
+  TORCH_CHECK(qkv.dim() == 2 && qkv.size(1) == (2 * heads + 2 * kv_heads) * head_dim, "qkv must be [tokens, "
+              "(2 heads + 2 kv_heads) head_dim]");
+  TORCH_CHECK(positions.numel() == tokens, "positions must have one entry per token");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  auto q = at::empty({tokens, heads, head_dim}, qkv.options());
+  auto gate = at::empty({tokens, heads * head_dim}, qkv.options());
+  auto k = at::empty({tokens, kv_heads, head_dim}, qkv.options());
+  auto v = at::empty({tokens, kv_heads, head_dim}, qkv.options());
+  CheckStatus(hif8_model_attn_prep(Bits(qkv), tokens, (int)heads, (int)kv_heads, (int)head_dim, (int)rotary_dim,
+                                   positions.data_ptr<int32_t>(), Bits(q_norm_w), Bits(k_norm_w), (float)eps,
+                                   (float)rope_theta, MutBits(q), MutBits(gate), MutBits(k), MutBits(v), Stream(qkv)),
+              "hif8_model_attn_prep");
+  return {q, gate, k, v};
+}
+
+at::Tensor ModelGdn(const at::Tensor &proj, int64_t T, int64_t hk, int64_t hv, const at::Tensor &conv_w,
+                    const at::Tensor &a_log, const at::Tensor &dt_bias, const at::Tensor &norm_w,
+                    at::Tensor &conv_state, at::Tensor &rec_state, double eps) {
+  CheckModelTensor(proj, "proj", at::kBFloat16);
+  CheckModelTensor(conv_w, "conv_w", at::kBFloat16);
+  CheckModelTensor(a_log, "a_log", at::kFloat);
+  CheckModelTensor(dt_bias, "dt_bias", at::kFloat);
+  CheckModelTensor(norm_w, "norm_w", at::kBFloat16);
+  CheckModelTensor(conv_state, "conv_state", at::kFloat);
+  CheckModelTensor(rec_state, "rec_state", at::kFloat);
+  const int64_t channels = 2 * hk * 128 + hv * 128;
+  TORCH_CHECK(proj.dim() == 2 && proj.size(1) == channels + hv * 128 + 2 * hv, "proj must be [batch * T, "
+              "2 hk 128 + 2 hv 128 + 2 hv]");
+  TORCH_CHECK(T > 0 && proj.size(0) % T == 0, "proj rows must be a multiple of T");
+  const int64_t batch = proj.size(0) / T;
+  TORCH_CHECK(conv_w.numel() == channels * 4, "conv_w must be [channels, 4]");
+  TORCH_CHECK(conv_state.numel() == batch * channels * 3, "conv_state must be [batch, channels, 3]");
+  TORCH_CHECK(rec_state.numel() == batch * hv * 128 * 128, "rec_state must be [batch, hv, 128, 128]");
+  c10::cuda::CUDAGuard guard(proj.device());
+  auto out = at::empty({proj.size(0), hv * 128}, proj.options());
+  Hif8GdnArgs args{};
+  args.proj = Bits(proj);
+  args.proj_stride = proj.size(1);
+  args.T = (int)T;
+  args.hk = (int)hk;
+  args.hv = (int)hv;
+  args.key_dim = 128;
+  args.value_dim = 128;
+  args.conv_w = Bits(conv_w);
+  args.a_log = a_log.data_ptr<float>();
+  args.dt_bias = dt_bias.data_ptr<float>();
+  args.norm_w = Bits(norm_w);
+  args.conv_state = conv_state.data_ptr<float>();
+  args.rec_state = rec_state.data_ptr<float>();
+  args.out = MutBits(out);
+  args.eps = (float)eps;
+  CheckStatus(hif8_model_gdn(&args, batch, Stream(proj)), "hif8_model_gdn");
+  return out;
+}
+
 at::Tensor Hif8KvGatherDecode(const at::Tensor &cache, const at::Tensor &block_tables, const at::Tensor &seq_lens,
                               const at::Tensor &out_start, int64_t total_rows, int64_t max_seq_len) {
   CheckCudaTensor(cache, "cache");
@@ -397,10 +518,23 @@ TORCH_LIBRARY(hif8_b200, m) {
         "Tensor query_start, int max_seq_len, float softmax_scale, bool causal=True) -> Tensor");
   m.def("kv_gather_decode(Tensor cache, Tensor block_tables, Tensor seq_lens, Tensor out_start, int total_rows, "
         "int max_seq_len) -> Tensor");
+  // glue of the synthetic decoder
+  m.def("rmsnorm(Tensor x, Tensor? residual, Tensor weight, float eps, bool one_plus) -> (Tensor, Tensor)");
+  m.def("silu_mul(Tensor gate_up) -> Tensor");
+  m.def("gate_mul(Tensor x, Tensor gate) -> Tensor");
+  m.def("attn_prep(Tensor qkv, Tensor positions, Tensor q_norm_w, Tensor k_norm_w, int heads, int kv_heads, "
+        "int head_dim, int rotary_dim, float eps, float rope_theta) -> (Tensor, Tensor, Tensor, Tensor)");
+  m.def("gdn(Tensor proj, int T, int hk, int hv, Tensor conv_w, Tensor a_log, Tensor dt_bias, Tensor norm_w, "
+        "Tensor(a!) conv_state, Tensor(b!) rec_state, float eps) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(hif8_b200, CUDA, m) {
   m.impl("kv_cache_write", &Hif8KvCacheWrite);
   m.impl("paged_attention", &Hif8PagedAttention);
   m.impl("kv_gather_decode", &Hif8KvGatherDecode);
+  m.impl("rmsnorm", &ModelRmsnorm);
+  m.impl("silu_mul", &ModelSiluMul);
+  m.impl("gate_mul", &ModelGateMul);
+  m.impl("attn_prep", &ModelAttnPrep);
+  m.impl("gdn", &ModelGdn);
 }

@@ -1,0 +1,74 @@
+/*
+ * hif8_b200 -- glue kernels of the synthetic Qwen3.5-9B-shaped decoder
+ * (configs[4] of the workload) that runs the HiF8 static W8A8KV8 path end to
+ * end.  None of these has a counterpart in the reference's operator set: on
+ * the reference these steps are vLLM / torch_npu code around the plugin's
+ * projections.  They follow transformers' Qwen3_5 text model
+ * (models/qwen3_5/modeling_qwen3_5.py): (1 + w) RMSNorm, SiLU-gated MLP,
+ * gated attention with q/k RMSNorm and partial rotary embedding, and the
+ * gated-delta-net linear attention.
+ *
+ * Conventions as include/hif8_b200.h: device pointers, a cudaStream_t passed
+ * as void*, an int status.  Activations are BF16 (uint16_t bits).
+ */
+#ifndef HIF8_B200_MODEL_H
+#define HIF8_B200_MODEL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* out = RMSNorm(x [+ residual_in]) * (one_plus ? 1 + w : w), rows x dim,
+ * dim % 8 == 0 and dim <= 8192.  With residual_in the BF16 sum is also
+ * written to residual_out (the new residual stream). */
+int hif8_model_rmsnorm(const uint16_t *x, const uint16_t *residual_in, uint16_t *residual_out,
+                       const uint16_t *weight, float eps, int one_plus, int64_t rows, int64_t dim,
+                       uint16_t *out, void *stream);
+
+/* out[r, i] = silu(gate_up[r, i]) * gate_up[r, inter + i]. */
+int hif8_model_silu_mul(const uint16_t *gate_up, int64_t rows, int64_t inter, uint16_t *out, void *stream);
+
+/* out[i] = x[i] * sigmoid(gate[i]). */
+int hif8_model_gate_mul(const uint16_t *x, const uint16_t *gate, int64_t n, uint16_t *out, void *stream);
+
+/* Split a gated-attention projection row [heads x (q | gate) | k | v] into
+ * q_out [tokens, heads, head_dim] and k_out / v_out [tokens, kv_heads,
+ * head_dim] (q and k: per-head (1 + w) RMSNorm, then rotary embedding of
+ * the first rotary_dim dims at positions[token]) and gate_out [tokens,
+ * heads * head_dim]. */
+int hif8_model_attn_prep(const uint16_t *qkv, int64_t tokens, int heads, int kv_heads, int head_dim,
+                         int rotary_dim, const int32_t *positions, const uint16_t *q_norm_w,
+                         const uint16_t *k_norm_w, float eps, float rope_theta, uint16_t *q_out,
+                         uint16_t *gate_out, uint16_t *k_out, uint16_t *v_out, void *stream);
+
+/* Gated delta net over T tokens of every sequence (T = 1: one decode step).
+ * proj rows (batch * T of them, proj_stride elements apart) hold
+ * [q: hk*128 | k: hk*128 | v: hv*128 | z: hv*128 | b: hv | a: hv];
+ * conv_state [batch, 2*hk*128 + hv*128, 3] and rec_state [batch, hv, 128,
+ * 128] (FP32) are read and updated in place; out [batch * T, hv * 128]. */
+typedef struct Hif8GdnArgs {
+  const uint16_t *proj;
+  int64_t proj_stride;
+  int T;
+  int hk, hv;
+  int key_dim, value_dim;  /* both 128 */
+  const uint16_t *conv_w;  /* [channels, 4] */
+  const float *a_log;      /* [hv] */
+  const float *dt_bias;    /* [hv] */
+  const uint16_t *norm_w;  /* [value_dim] */
+  float *conv_state;
+  float *rec_state;
+  uint16_t *out;
+  float eps;
+} Hif8GdnArgs;
+
+int hif8_model_gdn(const Hif8GdnArgs *args, int64_t batch, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HIF8_B200_MODEL_H */

@@ -51,6 +51,48 @@ def test_cabi_exports_every_declared_symbol():
     assert set(cabi.SIGNATURES) == set(names)
 
 
+def test_model_glue_header_symbols_are_exported():
+    """include/hif8_b200_model.h (the synthetic decoder's glue kernels) is
+    served by the same library."""
+    from hif8_b200 import cabi
+
+    text = (ROOT / "include" / "hif8_b200_model.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^\s*int\s+(\w+)\s*\(", text, flags=re.M)
+    assert set(names) == {"hif8_model_rmsnorm", "hif8_model_silu_mul", "hif8_model_gate_mul",
+                          "hif8_model_attn_prep", "hif8_model_gdn"}
+    lib = cabi.library()
+    for name in names:
+        assert hasattr(lib, name), f"{name} is declared in include/hif8_b200_model.h but not exported"
+
+
+def test_model_glue_ops_are_registered():
+    from hif8_b200 import kv_cache
+
+    kv_cache.load_ops()
+    for op in ("rmsnorm", "silu_mul", "gate_mul", "attn_prep", "gdn"):
+        assert hasattr(torch.ops.hif8_b200, op)
+
+
+def test_decoder_config_layout_and_tp_split():
+    from hif8_b200.decoder import DecoderConfig
+
+    cfg = DecoderConfig()
+    full = [i for i in range(cfg.layers) if cfg.is_full(i)]
+    assert full == [3, 7, 11, 15, 19, 23, 27, 31]  # every 4th layer, as Qwen3_5's layer_types
+    for tp in (1, 2, 4, 8):
+        assert cfg.heads % tp == 0 and cfg.lin_k_heads % tp == 0 and cfg.lin_v_heads % tp == 0
+        assert cfg.intermediate % tp == 0 and cfg.vocab % tp == 0
+    # per-token HiF8 projection bytes of the model (one byte per weight)
+    d, v = cfg.lin_dim, cfg.lin_v_heads
+    attn = (cfg.heads * 2 * cfg.head_dim + 2 * cfg.kv_heads * cfg.head_dim) * cfg.hidden \
+        + cfg.hidden * cfg.heads * cfg.head_dim
+    gdn = (2 * cfg.lin_k_heads * d + 2 * v * d + 2 * v) * cfg.hidden + cfg.hidden * v * d
+    mlp = 3 * cfg.intermediate * cfg.hidden
+    total = len(full) * attn + (cfg.layers - len(full)) * gdn + cfg.layers * mlp
+    assert 6.9e9 < total < 7.0e9
+
+
 def test_cabi_codec_tables_match_oracle():
     from hif8_b200 import cabi
 
