@@ -361,8 +361,14 @@ def run_ours(args) -> None:
     if world == 1 and not args.no_extra:
         extra["prefill_gemm"] = measure_prefill_gemm(device)
         extra["paged_attention"] = measure_paged_attention(device)
+    if not args.no_decode:
+        del graph, graph_outs
+        graph = graph_outs = None
+        calls.clear()
+        torch.cuda.empty_cache()
+        extra["decode"] = measure_decoder(device, world, rank)
 
-    del graph, graph_outs
+    graph = graph_outs = None
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -486,6 +492,40 @@ def measure_paged_attention(device) -> dict:
     return {"bound": "hbm", "kernel": "paged_attention_kernel + attention_combine_kernel", "unit": "GB/s",
             "peak": peak, "peak_kind": kind, "algorithmic": "K and V pages read once (B*ctx*kv_heads*(D+4)*2) + Q + out",
             "per_config": per, "timing": "median of 5 decode steps, each after a read-based L2 eviction, CUDA events"}
+
+
+def measure_decoder(device, world: int, rank: int) -> dict:
+    """the random-init Qwen3.5-9B-shaped hybrid decoder, 512
+    prompt / 256 generated tokens at batch 1 and 4, tensor-parallel over the
+    bench's GPUs; the W8A8KV8 HiF8 model and its BF16 twin.  Decode steps are
+    CUDA-graph replays timed with CUDA events (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from hif8_b200.decoder import Decoder, DecoderConfig, calibrate, measure_decode
+
+    cfg = DecoderConfig()
+    calib = calibrate(cfg, device, seed=0, tokens=64, tp_rank=rank, tp_size=world)
+    out = {"model": "Qwen3.5-9B-shaped hybrid decoder (32 layers: 8 gated full-attention, 24 gated delta net; "
+                    "hidden 4096, MLP 12288, vocab 248320), random init",
+           "prompt": 512, "generated": 256, "tp": world, "timing": "CUDA-graph decode steps, CUDA events, max over ranks"}
+    for mode in ("hif8", "bf16"):
+        model = Decoder(cfg, mode, device, seed=0, tp_rank=rank, tp_size=world, max_batch=4, max_ctx=768,
+                        calibration=calib if mode == "hif8" else None)
+        res = {}
+        for batch in (1, 4):
+            r = measure_decode(model, batch)
+            ms = torch.tensor([r["ms_per_step"]], device=device, dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            res[f"batch{batch}"] = {"tok_s": round(batch / (float(ms) * 1e-3), 1), "ms_per_step": round(float(ms), 3)}
+        model.release_graphs()
+        del model
+        torch.cuda.empty_cache()
+        out["hif8_w8a8kv8" if mode == "hif8" else "bf16_twin"] = res
+    out["speedup_vs_bf16"] = {b: round(out["hif8_w8a8kv8"][b]["tok_s"] / out["bf16_twin"][b]["tok_s"], 3)
+                              for b in ("batch1", "batch4")}
+    return out
 
 
 def gemv_roofline(calls, device, world) -> dict:
@@ -661,6 +701,7 @@ def main() -> None:
     parser.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline work")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-extra", action="store_true", help="skip the prefill GEMM and attention measurements")
+    parser.add_argument("--no-decode", action="store_true", help="skip the configs[4] decoder tok/s measurement")
     parser.add_argument("--profile-case", default=None,
                         help="run one small kernel case for ncu (e.g. gemv:gate_up:1) and exit")
     parser.add_argument("--profile-launches", type=int, default=3)
