@@ -62,7 +62,8 @@ def workload_config(world: int) -> dict:
         "weights": "N(0,0.02) BF16 -> HiF8 u8, per-channel scale = row amax / 32768; seeded",
         "activations": "N(0,1) BF16, fixed input_scale = calibration absmax / 32768",
         "l2": "inputs larger than L2: 15 distinct weights (880 MB) streamed per step",
-        "parallelism": "single GPU" if world == 1 else f"tp{world} (column: gate_up, qkv; row: down + NCCL all-reduce)",
+        "parallelism": "single GPU" if world == 1 else f"{world} independent replicas (one full sweep per GPU, no "
+                       "collective); the tensor-parallel sweep is reported under tp_sweep",
         "graph": "one step captured as a CUDA graph, replayed per timed step",
     }
 
@@ -245,9 +246,10 @@ def run_reference(args) -> None:
 
 # ------------------------------------------------------------- our arm ---
 
-def build_layers(world: int, rank: int, device):
+def build_layers(world: int, rank: int, device, replica: int = 0):
     """Seeded weights and activations for every call of the sweep; this rank's
-    tensor-parallel shard when world > 1."""
+    tensor-parallel shard when world > 1 (replica: a different seed set for an
+    independent full copy)."""
     import torch
 
     from hif8_b200 import scheme
@@ -257,7 +259,7 @@ def build_layers(world: int, rank: int, device):
         for idx, (name, n, k) in enumerate(SHAPES):
             row_parallel = name == "down"
             # column shards differ per rank; row shards are slices of one seeded weight
-            seed = 1000 * m + idx + (0 if row_parallel else 7919 * rank)
+            seed = 1000 * m + idx + (0 if row_parallel else 7919 * rank) + 104729 * replica
             g = torch.Generator(device=device).manual_seed(seed)
             n_loc = n if (world == 1 or row_parallel) else n // world
             k_loc = k // world if (world > 1 and row_parallel) else k
@@ -276,6 +278,71 @@ def build_layers(world: int, rank: int, device):
     return calls
 
 
+def time_sweep(calls, args, device, world: int, local_rank: int, *, tp: bool, profile: bool):
+    """One step = every call of ``calls`` (static quant + HiF8 linear through
+    scheme.apply; row-parallel results all-reduced when ``tp``), captured as
+    a CUDA graph; W warm-up replays, then K timed replays between barriers.
+    Returns (max over ranks of the timed device ms, the clock sampler)."""
+    import torch
+    import torch.distributed as dist
+
+    from hif8_b200 import scheme
+
+    def step():
+        outs = []
+        for c in calls:
+            y = scheme.apply(c["layer"], c["x"])
+            if tp and c["row_parallel"]:
+                dist.all_reduce(y)
+            outs.append(y)
+        return outs
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        step()  # warm the private pool on the capture stream
+        torch.cuda.synchronize(device)
+        with torch.cuda.graph(graph, stream=stream):
+            graph_outs = step()
+    torch.cuda.current_stream(device).wait_stream(stream)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        # profiler start/stop bracket the timed steps for `ncu --profile-from-start off`
+        if profile:
+            torch.cuda.profiler.start()
+        clocks.mark_start()
+        start.record(cur)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(cur)
+        torch.cuda.synchronize()
+        clocks.mark_end()
+        if profile:
+            torch.cuda.profiler.stop()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    del graph, graph_outs  # graphs holding NCCL calls go before the process group
+    return elapsed_ms, clocks
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -292,83 +359,44 @@ def run_ours(args) -> None:
     from hif8_b200 import native, scheme
 
     native.load_extension()
-    calls = build_layers(world, rank, device)
-
-    def step():
-        outs = []
-        for c in calls:
-            y = scheme.apply(c["layer"], c["x"])
-            if c["row_parallel"] and world > 1:
-                dist.all_reduce(y)
-            outs.append(y)
-        return outs
-
-    for _ in range(max(args.warmup, 1)):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-
-    graph = torch.cuda.CUDAGraph()
-    stream = torch.cuda.Stream(device)
-    stream.wait_stream(torch.cuda.current_stream(device))
-    with torch.cuda.stream(stream):
-        step()  # warm the private pool on the capture stream
-        torch.cuda.synchronize(device)
-        with torch.cuda.graph(graph, stream=stream):
-            graph_outs = step()
-    torch.cuda.current_stream(device).wait_stream(stream)
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
-
-    # ------------------------------------------------ timed region ------
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    cur = torch.cuda.current_stream(device)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
-        # profiler start/stop bracket the timed steps for `ncu --profile-from-start off`
-        torch.cuda.profiler.start()
-        clocks.mark_start()
-        start.record(cur)
-        for _ in range(args.steps):
-            graph.replay()
-        end.record(cur)
-        torch.cuda.synchronize()
-        clocks.mark_end()
-        torch.cuda.profiler.stop()
-    if world > 1:
-        dist.barrier()
-    elapsed_ms = start.elapsed_time(end)
-    if world > 1:
-        t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    total_bytes = step_bytes() * args.steps
-    value = total_bytes / (elapsed_ms * 1e-3) / 1e9
+    # The headline sweep: every rank runs the full configs[1] sweep on its own
+    # weights (independent replicas, no collective; weak scaling).
+    calls = build_layers(1, 0, device, replica=rank)
+    elapsed_ms, clocks = time_sweep(calls, args, device, world, local_rank, tp=False, profile=True)
+    value = world * step_bytes() * args.steps / (elapsed_ms * 1e-3) / 1e9
     launches_per_step = sum(1 if c["m"] <= 4 else 2 for c in calls)
 
     # -------------------------- dominant kernel: the GEMV, timed alone ---
-    roofline = gemv_roofline(calls, device, world)
+    roofline = gemv_roofline(calls, device, 1)
 
     # -------------------------------------------- e2e: public API, host I/O
     e2e = measure_e2e(calls, args, device, world)
+
+    # ------------- the same sweep tensor-parallel over the ranks (strong) ---
+    tp_sweep = None
+    if world > 1:
+        calls.clear()
+        torch.cuda.empty_cache()
+        tp_calls = build_layers(world, rank, device)
+        tp_ms, _ = time_sweep(tp_calls, args, device, world, local_rank, tp=True, profile=False)
+        tp_sweep = {"value": step_bytes() * args.steps / (tp_ms * 1e-3) / 1e9, "unit": UNIT, "scaling": "strong",
+                    "ms_per_step": tp_ms / args.steps,
+                    "parallelism": f"tp{world} (column: gate_up, qkv; row: down + NCCL all-reduce)"}
+        tp_calls.clear()
+        torch.cuda.empty_cache()
 
     # ------------------- the other hot-path kernels (one GPU, timed alone) ---
     extra = {}
     if world == 1 and not args.no_extra:
         extra["prefill_gemm"] = measure_prefill_gemm(device)
         extra["paged_attention"] = measure_paged_attention(device)
+    if tp_sweep is not None:
+        extra["tp_sweep"] = tp_sweep
     if not args.no_decode:
-        del graph, graph_outs
-        graph = graph_outs = None
         calls.clear()
         torch.cuda.empty_cache()
         extra["decode"] = measure_decoder(device, world, rank)
 
-    graph = graph_outs = None
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -376,7 +404,7 @@ def run_ours(args) -> None:
         return
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(world),
         "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(), "roofline": roofline,
         "e2e": e2e, **extra,
@@ -578,7 +606,8 @@ def gemv_roofline(calls, device, world) -> dict:
 def measure_e2e(calls, args, device, world) -> dict:
     """The same sweep through the public API (hif8_b200.scheme / native ops,
     eager) with every step's activations copied from pinned host memory and
-    every output read back to pinned host memory inside the timed region."""
+    every output read back to pinned host memory inside the timed region; one
+    independent replica per rank (value aggregates the ranks)."""
     import torch
     import torch.distributed as dist
 
@@ -594,8 +623,6 @@ def measure_e2e(calls, args, device, world) -> dict:
         for i, c in enumerate(calls):
             dev_x[i].copy_(host_x[i], non_blocking=True)
             y = scheme.apply(c["layer"], dev_x[i])
-            if c["row_parallel"] and world > 1:
-                dist.all_reduce(y)
             host_y[i].copy_(y, non_blocking=True)
 
     for _ in range(max(args.warmup, 1)):
@@ -616,8 +643,8 @@ def measure_e2e(calls, args, device, world) -> dict:
         ms = float(t.item())
     h2d = sum(x.numel() * 2 for x in host_x)
     d2h = sum(y.numel() * 2 for y in host_y)
-    return {"value": step_bytes() * args.steps / (ms * 1e-3) / 1e9, "unit": UNIT, "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": ms / args.steps,
+    return {"value": world * step_bytes() * args.steps / (ms * 1e-3) / 1e9, "unit": UNIT,
+            "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * d2h, "ms_per_step": ms / args.steps,
             "path": "hif8_b200.scheme.apply (eager PyTorch ops -> C ABI), pinned host buffers"}
 
 
