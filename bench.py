@@ -536,10 +536,14 @@ def measure_decoder(device, world: int, rank: int) -> dict:
     calib = calibrate(cfg, device, seed=0, tokens=64, tp_rank=rank, tp_size=world)
     out = {"model": "Qwen3.5-9B-shaped hybrid decoder (32 layers: 8 gated full-attention, 24 gated delta net; "
                     "hidden 4096, MLP 12288, vocab 248320), random init",
-           "prompt": 512, "generated": 256, "tp": world, "timing": "CUDA-graph decode steps, CUDA events, max over ranks"}
+           "prompt": 512, "generated": 256, "tp": world, "timing": "CUDA-graph decode steps, CUDA events, max over ranks",
+           "allreduce": "single GPU" if world == 1 else "row-parallel partials summed over peer memory inside the "
+                                                       "following residual + RMSNorm kernel (prefill: NCCL)"}
     for mode in ("hif8", "bf16"):
         model = Decoder(cfg, mode, device, seed=0, tp_rank=rank, tp_size=world, max_batch=4, max_ctx=768,
                         calibration=calib if mode == "hif8" else None)
+        if world > 1:
+            model.enable_peer_allreduce()  # decode-step all-reduce fused into the following RMSNorm
         res = {}
         for batch in (1, 4):
             r = measure_decode(model, batch)
@@ -548,6 +552,12 @@ def measure_decoder(device, world: int, rank: int) -> dict:
                 dist.all_reduce(ms, op=dist.ReduceOp.MAX)
             res[f"batch{batch}"] = {"tok_s": round(batch / (float(ms) * 1e-3), 1), "ms_per_step": round(float(ms), 3)}
         model.release_graphs()
+        if model.peer is not None:
+            model.peer.check()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            model.peer.close()
         del model
         torch.cuda.empty_cache()
         out["hif8_w8a8kv8" if mode == "hif8" else "bf16_twin"] = res

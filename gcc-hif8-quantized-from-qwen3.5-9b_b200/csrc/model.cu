@@ -8,6 +8,8 @@
 // update, gated RMSNorm).  Activations are BF16, arithmetic FP32.
 #include <math_constants.h>
 
+#include <cstring>
+
 #include "../../include/hif8_b200_model.h"
 #include "hif8_common.cuh"
 
@@ -273,9 +275,173 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_kernel(const Hif8GdnArgs p) {
   }
 }
 
+// ------------------------------ TP all-reduce + residual + RMSNorm (peer) --
+constexpr int kPeerThreads = 1024;
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t gtimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__global__ void __launch_bounds__(kPeerThreads) peer_allreduce_rmsnorm_kernel(const Hif8PeerArgs p) {
+  __shared__ float rowsum[8];
+  const int tid = threadIdx.x;
+  const int64_t n = p.rows * p.dim;
+  const size_t slot_bytes = (size_t)p.max_rows * p.dim * sizeof(uint16_t);
+  const size_t flags_off = 2 * slot_bytes;
+  if (tid < 8) rowsum[tid] = 0.f;
+  // 1. this rank's partial into its own slot, visible system-wide
+  uint16_t *mine = reinterpret_cast<uint16_t *>(p.peer_buf[p.rank] + (size_t)p.slot * slot_bytes);
+  for (int64_t i = (int64_t)tid * 8; i < n; i += kPeerThreads * 8)
+    *reinterpret_cast<uint4 *>(mine + i) = *reinterpret_cast<const uint4 *>(p.local + i);
+  __threadfence_system();
+  __syncthreads();
+  // 2. signal every rank, wait for every rank
+  if (tid == 0) {
+    const uint32_t epoch = *p.epoch_counter + 1;
+    for (int q = 0; q < p.world; ++q)
+      st_release_sys(reinterpret_cast<uint32_t *>(p.peer_buf[q] + flags_off) + p.rank, epoch);
+    const uint32_t *flags = reinterpret_cast<const uint32_t *>(p.peer_buf[p.rank] + flags_off);
+    const uint64_t t0 = gtimer_ns();
+    bool ok = true;
+    for (int q = 0; q < p.world && ok; ++q) {
+      while ((int32_t)(ld_acquire_sys(flags + q) - epoch) < 0) {
+        if (gtimer_ns() - t0 > p.timeout_ns) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!ok) atomicExch(p.error, 1);
+    *p.epoch_counter = epoch;
+  }
+  __syncthreads();
+  // 3. sum in rank order, residual, RMSNorm (chunks of 8 never straddle rows: dim % 256 == 0)
+  constexpr int kMaxChunks = 4;  // rows x dim <= 4 x 1024 x 8
+  float v[kMaxChunks][8];
+  int row_of[kMaxChunks];
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int64_t i = ((int64_t)tid + (int64_t)c * kPeerThreads) * 8;
+    row_of[c] = -1;
+    if (i >= n) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int q = 0; q < p.world; ++q) {
+      const uint16_t *src = reinterpret_cast<const uint16_t *>(p.peer_buf[q] + (size_t)p.slot * slot_bytes) + i;
+      const uint4 w = __ldcv(reinterpret_cast<const uint4 *>(src));
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[2 * e] += bf(ww[e] & 0xFFFFu);
+        acc[2 * e + 1] += bf(ww[e] >> 16);
+      }
+    }
+    uint32_t rr[4] = {0, 0, 0, 0};
+    if (p.residual) {
+      const uint4 r = *reinterpret_cast<const uint4 *>(p.residual + i);
+      rr[0] = r.x, rr[1] = r.y, rr[2] = r.z, rr[3] = r.w;
+    }
+    uint32_t o[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float lo = bf(to_bf(acc[2 * e])), hi = bf(to_bf(acc[2 * e + 1]));  // the all-reduced BF16 partial
+      if (p.residual) {
+        lo = bf(to_bf(lo + bf(rr[e] & 0xFFFFu)));
+        hi = bf(to_bf(hi + bf(rr[e] >> 16)));
+      }
+      v[c][2 * e] = lo;
+      v[c][2 * e + 1] = hi;
+      o[e] = to_bf(lo) | ((uint32_t)to_bf(hi) << 16);
+      ss += lo * lo + hi * hi;
+    }
+    *reinterpret_cast<uint4 *>(p.residual_out + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    row_of[c] = (int)(i / p.dim);
+    // a warp's 32 chunks lie in one row: reduce and add once per warp
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+    if ((tid & 31) == 0) atomicAdd(&rowsum[row_of[c]], ss);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    if (row_of[c] < 0) continue;
+    const int64_t i = ((int64_t)tid + (int64_t)c * kPeerThreads) * 8;
+    const float inv = rsqrtf(rowsum[row_of[c]] / (float)p.dim + p.eps);
+    const int64_t col = i - (int64_t)row_of[c] * p.dim;
+    const uint4 wv = *reinterpret_cast<const uint4 *>(p.weight + col);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float w0 = bf(ww[e] & 0xFFFFu), w1 = bf(ww[e] >> 16);
+      if (p.one_plus) w0 += 1.f, w1 += 1.f;
+      o[e] = to_bf(v[c][2 * e] * inv * w0) | ((uint32_t)to_bf(v[c][2 * e + 1] * inv * w1) << 16);
+    }
+    *reinterpret_cast<uint4 *>(p.out + i) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 }  // namespace hif8
 
 using namespace hif8;
+
+extern "C" int hif8_model_peer_allreduce_rmsnorm(const Hif8PeerArgs *args, void *stream) {
+  if (!args) return HIF8_ERR_INVALID_ARGUMENT;
+  const Hif8PeerArgs &p = *args;
+  if (!p.local || !p.weight || !p.out || !p.residual_out || !p.peer_buf || !p.epoch_counter || !p.error ||
+      p.world < 1 || p.world > 64 || p.rank < 0 || p.rank >= p.world || p.slot < 0 || p.slot > 1 || p.rows < 0 ||
+      p.rows > p.max_rows || p.dim <= 0 || p.dim % 256 != 0 || p.rows * p.dim > (int64_t)kPeerThreads * 8 * 4 ||
+      p.rows > 8)
+    return HIF8_ERR_INVALID_ARGUMENT;
+  if (p.rows == 0) return HIF8_OK;
+  peer_allreduce_rmsnorm_kernel<<<1, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch();
+}
+
+extern "C" int hif8_peer_alloc(size_t bytes, void **ptr, void *handle64) {
+  if (!ptr || !handle64 || bytes == 0) return HIF8_ERR_INVALID_ARGUMENT;
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(handle64), *ptr);
+  if (e != cudaSuccess) {
+    set_last_error(e);
+    return HIF8_ERR_CUDA;
+  }
+  return HIF8_OK;
+}
+
+extern "C" int hif8_peer_open(const void *handle64, void **ptr) {
+  if (!ptr || !handle64) return HIF8_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    set_last_error(e);
+    return HIF8_ERR_CUDA;
+  }
+  return HIF8_OK;
+}
+
+extern "C" int hif8_peer_close(void *ptr, int opened) {
+  if (!ptr) return HIF8_OK;
+  const cudaError_t e = opened ? cudaIpcCloseMemHandle(ptr) : cudaFree(ptr);
+  if (e != cudaSuccess) {
+    set_last_error(e);
+    return HIF8_ERR_CUDA;
+  }
+  return HIF8_OK;
+}
 
 extern "C" int hif8_model_rmsnorm(const uint16_t *x, const uint16_t *residual_in, uint16_t *residual_out,
                                   const uint16_t *weight, float eps, int one_plus, int64_t rows, int64_t dim,

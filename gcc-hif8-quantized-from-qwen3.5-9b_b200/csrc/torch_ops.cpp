@@ -325,11 +325,12 @@ at::Tensor Hif8PagedAttention(const at::Tensor &query, const at::Tensor &key_cac
 
 // ---- glue of the synthetic decoder (include/hif8_b200_model.h) ----------
 
-void CheckModelTensor(const at::Tensor &t, const char *name, at::ScalarType dtype) {
+// align: the widest access the kernel makes to the tensor (16: vector loads)
+void CheckModelTensor(const at::Tensor &t, const char *name, at::ScalarType dtype, int align = 16) {
   TORCH_CHECK(t.defined() && t.is_cuda(), name, " must be a CUDA tensor");
   TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
   TORCH_CHECK(t.scalar_type() == dtype, name, " must be ", dtype, ", got ", t.scalar_type());
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % align == 0, name, " must be ", align, "-byte aligned");
 }
 
 const uint16_t *Bits(const at::Tensor &t) { return reinterpret_cast<const uint16_t *>(t.data_ptr()); }
@@ -358,7 +359,7 @@ std::tuple<at::Tensor, at::Tensor> ModelRmsnorm(const at::Tensor &x, const std::
 }
 
 at::Tensor ModelSiluMul(const at::Tensor &gate_up) {
-  CheckModelTensor(gate_up, "gate_up", at::kBFloat16);
+  CheckModelTensor(gate_up, "gate_up", at::kBFloat16, 4);
   const int64_t two_i = gate_up.size(-1), rows = gate_up.numel() / two_i;
   TORCH_CHECK(two_i % 4 == 0, "gate_up width must be a multiple of 4");
   c10::cuda::CUDAGuard guard(gate_up.device());
@@ -371,8 +372,8 @@ at::Tensor ModelSiluMul(const at::Tensor &gate_up) {
 }
 
 at::Tensor ModelGateMul(const at::Tensor &x, const at::Tensor &gate) {
-  CheckModelTensor(x, "x", at::kBFloat16);
-  CheckModelTensor(gate, "gate", at::kBFloat16);
+  CheckModelTensor(x, "x", at::kBFloat16, 2);
+  CheckModelTensor(gate, "gate", at::kBFloat16, 2);
   TORCH_CHECK(x.numel() == gate.numel(), "gate must match x");
   c10::cuda::CUDAGuard guard(x.device());
   auto out = at::empty_like(x);
@@ -383,10 +384,10 @@ at::Tensor ModelGateMul(const at::Tensor &x, const at::Tensor &gate) {
 std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> ModelAttnPrep(
     const at::Tensor &qkv, const at::Tensor &positions, const at::Tensor &q_norm_w, const at::Tensor &k_norm_w,
     int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t rotary_dim, double eps, double rope_theta) {
-  CheckModelTensor(qkv, "qkv", at::kBFloat16);
-  CheckModelTensor(positions, "positions", at::kInt);
-  CheckModelTensor(q_norm_w, "q_norm_w", at::kBFloat16);
-  CheckModelTensor(k_norm_w, "k_norm_w", at::kBFloat16);
+  CheckModelTensor(qkv, "qkv", at::kBFloat16, 2);
+  CheckModelTensor(positions, "positions", at::kInt, 4);
+  CheckModelTensor(q_norm_w, "q_norm_w", at::kBFloat16, 2);
+  CheckModelTensor(k_norm_w, "k_norm_w", at::kBFloat16, 2);
   const int64_t tokens = qkv.size(0);
   TORCH_CHECK(qkv.dim() == 2 && qkv.size(1) == (2 * heads + 2 * kv_heads) * head_dim, "qkv must be [tokens, "
               "(2 heads + 2 kv_heads) head_dim]");
@@ -406,13 +407,13 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> ModelAttnPrep(
 at::Tensor ModelGdn(const at::Tensor &proj, int64_t T, int64_t hk, int64_t hv, const at::Tensor &conv_w,
                     const at::Tensor &a_log, const at::Tensor &dt_bias, const at::Tensor &norm_w,
                     at::Tensor &conv_state, at::Tensor &rec_state, double eps) {
-  CheckModelTensor(proj, "proj", at::kBFloat16);
-  CheckModelTensor(conv_w, "conv_w", at::kBFloat16);
-  CheckModelTensor(a_log, "a_log", at::kFloat);
-  CheckModelTensor(dt_bias, "dt_bias", at::kFloat);
-  CheckModelTensor(norm_w, "norm_w", at::kBFloat16);
-  CheckModelTensor(conv_state, "conv_state", at::kFloat);
-  CheckModelTensor(rec_state, "rec_state", at::kFloat);
+  CheckModelTensor(proj, "proj", at::kBFloat16, 2);
+  CheckModelTensor(conv_w, "conv_w", at::kBFloat16, 2);
+  CheckModelTensor(a_log, "a_log", at::kFloat, 4);
+  CheckModelTensor(dt_bias, "dt_bias", at::kFloat, 4);
+  CheckModelTensor(norm_w, "norm_w", at::kBFloat16, 2);
+  CheckModelTensor(conv_state, "conv_state", at::kFloat, 4);
+  CheckModelTensor(rec_state, "rec_state", at::kFloat, 4);
   const int64_t channels = 2 * hk * 128 + hv * 128;
   TORCH_CHECK(proj.dim() == 2 && proj.size(1) == channels + hv * 128 + 2 * hv, "proj must be [batch * T, "
               "2 hk 128 + 2 hv 128 + 2 hv]");
@@ -441,6 +442,48 @@ at::Tensor ModelGdn(const at::Tensor &proj, int64_t T, int64_t hk, int64_t hv, c
   args.eps = (float)eps;
   CheckStatus(hif8_model_gdn(&args, batch, Stream(proj)), "hif8_model_gdn");
   return out;
+}
+
+std::tuple<at::Tensor, at::Tensor> ModelPeerAllreduceRmsnorm(const at::Tensor &local,
+                                                             const std::optional<at::Tensor> &residual,
+                                                             const at::Tensor &weight, const at::Tensor &peer_buf,
+                                                             at::Tensor &counter, at::Tensor &error, int64_t max_rows,
+                                                             int64_t rank, int64_t world, int64_t slot, double eps,
+                                                             bool one_plus, int64_t timeout_ns) {
+  CheckModelTensor(local, "local", at::kBFloat16);
+  CheckModelTensor(weight, "weight", at::kBFloat16);
+  CheckModelTensor(peer_buf, "peer_buf", at::kLong);
+  CheckModelTensor(counter, "counter", at::kInt, 4);
+  CheckModelTensor(error, "error", at::kInt, 4);
+  TORCH_CHECK(peer_buf.numel() == world, "peer_buf must hold one buffer per rank");
+  const int64_t dim = local.size(-1), rows = local.numel() / dim;
+  c10::cuda::CUDAGuard guard(local.device());
+  auto out = at::empty_like(local);
+  auto res_out = at::empty_like(local);
+  Hif8PeerArgs a{};
+  a.local = Bits(local);
+  if (residual.has_value()) {
+    CheckModelTensor(*residual, "residual", at::kBFloat16);
+    TORCH_CHECK(residual->sizes() == local.sizes(), "residual must match local");
+    a.residual = Bits(*residual);
+  }
+  a.weight = Bits(weight);
+  a.out = MutBits(out);
+  a.residual_out = MutBits(res_out);
+  a.peer_buf = reinterpret_cast<uint8_t *const *>(peer_buf.data_ptr<int64_t>());
+  a.epoch_counter = reinterpret_cast<uint32_t *>(counter.data_ptr<int32_t>());
+  a.error = error.data_ptr<int32_t>();
+  a.rows = rows;
+  a.dim = dim;
+  a.max_rows = max_rows;
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.slot = (int)slot;
+  a.one_plus = one_plus ? 1 : 0;
+  a.eps = (float)eps;
+  a.timeout_ns = (uint64_t)timeout_ns;
+  CheckStatus(hif8_model_peer_allreduce_rmsnorm(&a, Stream(local)), "hif8_model_peer_allreduce_rmsnorm");
+  return {out, res_out};
 }
 
 at::Tensor Hif8KvGatherDecode(const at::Tensor &cache, const at::Tensor &block_tables, const at::Tensor &seq_lens,
@@ -526,6 +569,9 @@ TORCH_LIBRARY(hif8_b200, m) {
         "int head_dim, int rotary_dim, float eps, float rope_theta) -> (Tensor, Tensor, Tensor, Tensor)");
   m.def("gdn(Tensor proj, int T, int hk, int hv, Tensor conv_w, Tensor a_log, Tensor dt_bias, Tensor norm_w, "
         "Tensor(a!) conv_state, Tensor(b!) rec_state, float eps) -> Tensor");
+  m.def("peer_allreduce_rmsnorm(Tensor local, Tensor? residual, Tensor weight, Tensor peer_buf, Tensor(a!) counter, "
+        "Tensor(b!) error, int max_rows, int rank, int world, int slot, float eps, bool one_plus, int timeout_ns) "
+        "-> (Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(hif8_b200, CUDA, m) {
@@ -537,4 +583,5 @@ TORCH_LIBRARY_IMPL(hif8_b200, CUDA, m) {
   m.impl("gate_mul", &ModelGateMul);
   m.impl("attn_prep", &ModelAttnPrep);
   m.impl("gdn", &ModelGdn);
+  m.impl("peer_allreduce_rmsnorm", &ModelPeerAllreduceRmsnorm);
 }

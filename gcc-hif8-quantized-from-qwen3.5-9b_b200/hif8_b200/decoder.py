@@ -112,6 +112,75 @@ class _Linear:
         return scheme.apply(self, x)
 
 
+class PeerReducer:
+    """Tensor-parallel all-reduce of a decode step's row-parallel partials,
+    fused with the residual add + RMSNorm that follows every one of them
+    (``torch.ops.hif8_b200.peer_allreduce_rmsnorm``): each rank's buffer is
+    mapped by its peers over NVLink through exchanged CUDA IPC handles; the
+    kernel signals and waits on epoch flags (bounded) and sums the partials
+    in rank order."""
+
+    def __init__(self, device, rank: int, world: int, max_rows: int, dim: int, group=None,
+                 timeout_ns: int = 200_000_000):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import cabi
+
+        lib = cabi.library()
+        lib.hif8_peer_alloc.restype = ctypes.c_int
+        lib.hif8_peer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
+        lib.hif8_peer_open.restype = ctypes.c_int
+        lib.hif8_peer_open.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+        lib.hif8_peer_close.restype = ctypes.c_int
+        lib.hif8_peer_close.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        self._lib = lib
+        self.rank, self.world, self.max_rows, self.dim, self.timeout_ns = rank, world, max_rows, dim, timeout_ns
+        nbytes = (2 * max_rows * dim * 2 + 4 * world + 255) // 256 * 256
+        torch.cuda.set_device(device)
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        cabi.check("hif8_peer_alloc", lib.hif8_peer_alloc(nbytes, ctypes.byref(own), handle))
+        self._own = own.value
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        bases, self._opened = [], []
+        for q in range(world):
+            if q == rank:
+                bases.append(self._own)
+                continue
+            peer = ctypes.c_void_p()
+            buf = (ctypes.c_ubyte * 64).from_buffer_copy(handles[q])
+            cabi.check("hif8_peer_open", lib.hif8_peer_open(buf, ctypes.byref(peer)))
+            bases.append(peer.value)
+            self._opened.append(peer.value)
+        self.table = torch.tensor(bases, dtype=torch.int64, device=device)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+        self.error = torch.zeros(1, dtype=torch.int32, device=device)
+        dist.barrier(group=group)  # every rank's buffer is mapped before the first signal
+
+    def __call__(self, local, residual, weight, eps: float, slot: int):
+        import torch
+
+        return torch.ops.hif8_b200.peer_allreduce_rmsnorm(local.contiguous(), residual, weight, self.table,
+                                                          self.counter, self.error, self.max_rows, self.rank,
+                                                          self.world, slot, eps, True, self.timeout_ns)
+
+    def check(self):
+        if int(self.error.item()) != 0:
+            raise RuntimeError("a peer all-reduce wait timed out")
+
+    def close(self):
+        for ptr in self._opened:
+            self._lib.hif8_peer_close(ptr, 1)
+        self._opened = []
+        if self._own:
+            self._lib.hif8_peer_close(self._own, 0)
+            self._own = None
+
+
 class Decoder:
     """The model on one rank.  ``mode`` is "hif8" or "bf16"."""
 
@@ -195,7 +264,7 @@ class Decoder:
                 L["conv_w"] = torch.cat([rows(conv, q0 + r * lq, lq), rows(conv, k0 + r * lk, lk),
                                          rows(conv, v0 + r * lv, lv)]).contiguous()
                 a_log = gen.uniform(f"{i}.A", (c.lin_v_heads,), 1e-3, 16.0).log()
-                L["a_log"] = a_log[r * self.hv:(r + 1) * self.hv].contiguous()
+                L["a_log"] = a_log[r * self.hv:(r + 1) * self.hv].clone()
                 L["dt_bias"] = torch.ones(self.hv, device=self.device)
                 L["gdn_norm"] = (1.0 + gen.normal(f"{i}.gdn_norm", (dl,), 0.02).float()).to(torch.bfloat16)
                 w_out = gen.normal(f"{i}.lin_out", (H, vd), c.init_std)
@@ -213,11 +282,21 @@ class Decoder:
         self.embed = gen.normal("embed", (c.vocab, H), c.init_std)
         self.final_w = gen.normal("final_norm", (H,), 0.02)
         head = gen.normal("lm_head", (c.vocab, H), c.init_std)
-        self.lm_head = head[r * self.vocab_local:(r + 1) * self.vocab_local].contiguous()
+        self.lm_head = head[r * self.vocab_local:(r + 1) * self.vocab_local].clone()  # frees the full head
         del head
         self._alloc_state()
-        self.calib_amax: dict | None = None  # set to a dict to record calibration maxima (BF16 twin)
+        self.calib_amax: dict | None = None  # set to a dict to record calibration samples (BF16 twin)
         self._graphs: dict[int, tuple] = {}
+        self.peer: PeerReducer | None = None  # decode-step all-reduce over peer memory (enable_peer_allreduce)
+        self._fused_reduce = False
+        self._site = 0
+
+    def enable_peer_allreduce(self):
+        """Decode steps (one token per sequence) all-reduce the row-parallel
+        partials inside the following residual + RMSNorm kernel, over peer
+        memory, instead of NCCL."""
+        if self.tp > 1 and self.peer is None:
+            self.peer = PeerReducer(self.device, self.rank, self.tp, self.max_batch, self.cfg.hidden, self.group)
 
     # ---------------------------------------------------------------- state --
     def _alloc_state(self):
@@ -252,11 +331,24 @@ class Decoder:
 
     # --------------------------------------------------------------- blocks --
     def _all_reduce(self, y):
-        if self.tp > 1:
+        """Sum of the row-parallel partials: NCCL, or deferred to the next
+        norm when the step fuses it (returns the partial unchanged then)."""
+        if self.tp > 1 and not self._fused_reduce:
             import torch.distributed as dist
 
             dist.all_reduce(y, group=self.group)
         return y
+
+    def _norm(self, x, residual, weight):
+        """(1 + w) RMSNorm of x + residual; with a fused reduce x is this
+        rank's partial and the all-reduce happens inside the norm kernel."""
+        import torch
+
+        if self._fused_reduce and residual is not None:
+            slot = self._site % 2
+            self._site += 1
+            return self.peer(x, residual, weight, self.cfg.eps, slot)
+        return torch.ops.hif8_b200.rmsnorm(x, residual, weight, self.cfg.eps, True)
 
     def _record(self, tag, x):
         """Calibration: keep a bounded sample of the values seen at ``tag``."""
@@ -330,19 +422,23 @@ class Decoder:
         import torch
 
         c = self.cfg
+        self._fused_reduce = self.peer is not None and T == 1 and batch <= self.max_batch
+        self._site = 0
         x = self.embed.index_select(0, tokens)
         residual = None
         for i, L in enumerate(self.layers):
-            h, residual = torch.ops.hif8_b200.rmsnorm(x, residual, L["in_w"], c.eps, True)
+            h, residual = self._norm(x, residual, L["in_w"])
             if L["full"]:
                 x = self._attention(i, L, h, batch, T, positions, seq_lens, slots)
             else:
                 x = self._gdn(i, L, h, batch, T)
-            h, residual = torch.ops.hif8_b200.rmsnorm(x, residual, L["post_w"], c.eps, True)
+            h, residual = self._norm(x, residual, L["post_w"])
             x = self._mlp(i, L, h)
-        last = torch.arange(batch, device=self.device) * T + (T - 1)
-        x, residual = x.index_select(0, last).contiguous(), residual.index_select(0, last).contiguous()
-        h, _ = torch.ops.hif8_b200.rmsnorm(x, residual, self.final_w, c.eps, True)
+        if T > 1:
+            last = torch.arange(batch, device=self.device) * T + (T - 1)
+            x, residual = x.index_select(0, last).contiguous(), residual.index_select(0, last).contiguous()
+        h, _ = self._norm(x, residual, self.final_w)
+        self._fused_reduce = False
         return torch.nn.functional.linear(h, self.lm_head).float()
 
     def argmax(self, logits):

@@ -67,6 +67,46 @@ typedef struct Hif8GdnArgs {
 
 int hif8_model_gdn(const Hif8GdnArgs *args, int64_t batch, void *stream);
 
+/* ---- tensor-parallel all-reduce fused with residual + RMSNorm ----------
+ * Replaces NCCL all-reduce + RMSNorm after every row-parallel projection of
+ * a decode step.  Every rank owns one device buffer (hif8_peer_alloc) that
+ * its peers map over NVLink (hif8_peer_open of the exchanged 64-byte IPC
+ * handle).  Layout of a rank's buffer: two slots of max_rows x dim BF16
+ * partials, then world uint32 flags.  One launch per rank:
+ *   1. copies this rank's partial `local` (rows x dim) into its slot;
+ *   2. system-scope fence, then writes epoch into flag[rank] of every rank's
+ *      buffer, and waits (bounded by timeout_ns of %globaltimer; on time-out
+ *      *error = 1 and the kernel finishes) until every flag of its own
+ *      buffer has reached epoch;
+ *   3. sums the ranks' partials in rank order (identical on every rank),
+ *      adds the residual (BF16) and normalises: out = RMSNorm(sum +
+ *      residual) * (one_plus ? 1 + w : w), residual_out = sum + residual.
+ * epoch = *epoch_counter + 1 (a per-rank device counter, advanced by the
+ * launch), so the launch can live in a CUDA graph.  Two slots (alternate
+ * call sites) keep a rank from overwriting a partial a slower peer still
+ * reads.  Plain peer loads and stores only (no multicast). */
+typedef struct Hif8PeerArgs {
+  const uint16_t *local;          /* this rank's partial, rows x dim */
+  const uint16_t *residual;       /* may be NULL */
+  const uint16_t *weight;         /* [dim] */
+  uint16_t *out, *residual_out;   /* rows x dim each */
+  uint8_t *const *peer_buf;       /* device array [world] of buffer bases (own + mapped peers) */
+  uint32_t *epoch_counter;        /* this rank's device counter */
+  int *error;                     /* this rank's device error word */
+  int64_t rows, dim, max_rows;
+  int rank, world, slot, one_plus;
+  float eps;
+  uint64_t timeout_ns;
+} Hif8PeerArgs;
+
+int hif8_model_peer_allreduce_rmsnorm(const Hif8PeerArgs *args, void *stream);
+
+/* Peer buffers: cudaMalloc'd device memory with its IPC handle (64 bytes),
+ * a mapping of a peer's handle, and the release of either. */
+int hif8_peer_alloc(size_t bytes, void **ptr, void *handle64);
+int hif8_peer_open(const void *handle64, void **ptr);
+int hif8_peer_close(void *ptr, int opened);
+
 #ifdef __cplusplus
 }
 #endif
