@@ -367,7 +367,7 @@ def run_ours(args) -> None:
     launches_per_step = sum(1 if c["m"] <= 4 else 2 for c in calls)
 
     # -------------------------- dominant kernel: the GEMV, timed alone ---
-    roofline = gemv_roofline(calls, device, 1)
+    roofline = gemv_roofline(calls, args, device, 1)
 
     # -------------------------------------------- e2e: public API, host I/O
     e2e = measure_e2e(calls, args, device, world)
@@ -566,51 +566,146 @@ def measure_decoder(device, world: int, rank: int) -> dict:
     return out
 
 
-def gemv_roofline(calls, device, world) -> dict:
-    """Time every GEMV launch of the sweep alone (L2 flushed before each
-    launch, CUDA events on the launching stream) and report algorithmic GB/s
-    of the GEMV kernel against the measured HBM copy peak."""
+def gemv_roofline(calls, args, device, world) -> dict:
+    """Roofline of the dominant kernel (the GEMV), measured in the timed
+    step's setting: the 15 GEMV launches of the sweep (M <= 4: the fused
+    quant + GEMV kernel on BF16 input; M = 8, 16: the GEMV on the bytes and
+    row scales of hif8_static_quant, computed once outside) are captured back
+    to back as one CUDA graph and replayed K times between two CUDA events
+    on the launching stream; achieved = algorithmic bytes of the 15 launches
+    x K / the elapsed time, i.e. bytes per launch / average launch duration.
+    The sweep's 15 distinct weights (880 MB) exceed L2, so every launch reads
+    its weight from HBM.  Reported beside it: per-launch durations from
+    timing events recorded around every launch inside a graph (event nodes
+    serialise the launches, so these read slightly long) and the same
+    launches timed alone after a read-based L2 eviction."""
     import torch
 
     from hif8_b200 import native
 
     ext = native.load_extension()
+    cur = torch.cuda.current_stream(device)
+
+    def algo_bytes(c):
+        m, n_loc, k_loc = c["m"], c["n_loc"], c["k_loc"]
+        # u8 weight + FP32 channel scale + u8 activation + FP32 row scale +
+        # BF16 out; the fused M <= 4 kernel reads BF16 activations instead
+        act = 2 * m * k_loc if m <= 4 else m * k_loc + 4 * m
+        return n_loc * k_loc + 4 * n_loc + act + 2 * m * n_loc
+
+    def capture(fn):
+        graph = torch.cuda.CUDAGraph()
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(cur)
+        with torch.cuda.stream(stream):
+            fn()
+            torch.cuda.synchronize(device)
+            with torch.cuda.graph(graph, stream=stream):
+                fn()
+        cur.wait_stream(stream)
+        return graph
+
+    quant = [native.static_quant(c["x"], c["layer"].input_scale) if c["m"] > 4 else None for c in calls]
+
+    def gemv(c, q):
+        layer = c["layer"]
+        if q is None:
+            native.soft_static_fused_linear(c["x"], layer.weight, layer.input_scale, layer.weight_scale, None,
+                                            output_dtype=torch.bfloat16)
+        else:
+            ext.soft_hif8_gemm(q[0], layer.weight, q[1], layer.weight_scale, None, torch.bfloat16)
+
+    # ------------------------------------- the 15 launches back to back ---
+    reps = max(args.steps, 5)
+    graph = capture(lambda: [gemv(c, q) for c, q in zip(calls, quant)])
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(cur)
+    for _ in range(reps):
+        graph.replay()
+    end.record(cur)
+    torch.cuda.synchronize()
+    stream_ms = start.elapsed_time(end) / reps
+    del graph
+
+    # ----------------------- per-launch events inside a graph (detail) ---
+    evs = [(torch.cuda.Event(enable_timing=True, external=True),
+            torch.cuda.Event(enable_timing=True, external=True)) for _ in calls]
+
+    def step():
+        for c, q, (s, e) in zip(calls, quant, evs):
+            s.record()
+            gemv(c, q)
+            e.record()
+
+    in_graph = None
+    try:
+        graph = capture(step)
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        torch.cuda.synchronize()
+        sums = [0.0] * len(calls)
+        for _ in range(reps):
+            graph.replay()
+            torch.cuda.synchronize()
+            for i, (s, e) in enumerate(evs):
+                sums[i] += s.elapsed_time(e)
+        del graph
+        in_graph = [t / reps for t in sums]
+    except RuntimeError as exc:  # event-record nodes unsupported: no per-launch detail
+        print(f"[bench] in-graph GEMV events unavailable ({exc})", file=sys.stderr)
+        torch.cuda.synchronize()
+
+    # --------------------------------------------- isolated, L2 evicted ---
     # L2 is evicted by READING a 512 MB buffer: writing one would leave dirty
     # lines whose write-back competes with the timed launch.
     flush = torch.ones(128 * 1024 * 1024, dtype=torch.float32, device=device)
-    cur = torch.cuda.current_stream(device)
-    per = []
-    total_b, total_ms = 0, 0.0
-    reps = 5
-    for c in calls:
-        layer = c["layer"]
-        data, row_scale = native.static_quant(c["x"], layer.input_scale)
-        m, n_loc, k_loc = c["m"], c["n_loc"], c["k_loc"]
-        b = n_loc * k_loc + 4 * n_loc + m * k_loc + 4 * m + 2 * m * n_loc
+    iso = []
+    for c, q in zip(calls, quant):
         times = []
-        for _ in range(reps):
+        for _ in range(5):
             flush.sum()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(cur)
-            ext.soft_hif8_gemm(data, layer.weight, row_scale, layer.weight_scale, None, torch.bfloat16)
+            gemv(c, q)
             e.record(cur)
             e.synchronize()
             times.append(s.elapsed_time(e))
-        t = statistics.median(times)
-        per.append({"m": m, "shape": c["name"], "us": round(t * 1e3, 2), "gbs": round(b / (t * 1e-3) / 1e9, 1)})
-        total_b += b
-        total_ms += t
+        iso.append(statistics.median(times))
+    del flush
+
+    per = []
+    total_b = sum(algo_bytes(c) for c in calls)
+    for i, c in enumerate(calls):
+        b = algo_bytes(c)
+        row = {"m": c["m"], "shape": c["name"], "bytes": b,
+               "isolated_us": round(iso[i] * 1e3, 2), "isolated_gbs": round(b / (iso[i] * 1e-3) / 1e9, 1)}
+        if in_graph is not None:
+            row["event_us"] = round(in_graph[i] * 1e3, 2)
+            row["event_gbs"] = round(b / (in_graph[i] * 1e-3) / 1e9, 1)
+        per.append(row)
     peak, kind = load_peak_hbm()
-    achieved = total_b / (total_ms * 1e-3) / 1e9
+    achieved = total_b / (stream_ms * 1e-3) / 1e9
+    iso_achieved = total_b / (sum(iso) * 1e-3) / 1e9
     prof = load_profile_traffic()
     traffic = None
     if prof and prof.get("world") == world:
         traffic = prof.get("traffic_bytes_per_launch")
     return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "traffic": traffic, "algorithmic_bytes_mean_per_launch": total_b / len(calls), "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs, copy)" if kind == "measured"
-            else "fallback 6650 GB/s", "kernel": "gemv_hif8_kernel (persistent split-K, LUT decode, mma.sync)",
-            "algorithmic_bytes_per_launch": "N*K + 4N + M*K + 4M + 2MN (u8 activation in, BF16 out)",
-            "per_launch": per, "timing": "median of 5 launches per config, each after a read-based L2 eviction, CUDA events"}
+            "traffic": traffic, "algorithmic_bytes_mean_per_launch": total_b / len(calls),
+            "launch_us_mean": stream_ms * 1e3 / len(calls),
+            "peak_kind": f"{kind} (MEASURED_PEAKS.json hbm_gbs, copy)" if kind == "measured" else "fallback 6650 GB/s",
+            "kernel": "gemv_hif8_kernel (persistent split-K, LUT decode, mma.sync)",
+            "algorithmic_bytes_per_launch": "N*K + 4N + 2N*M + (M <= 4: 2MK BF16 activation; else MK + 4M u8 "
+                                            "activation + row scale)",
+            "timing": f"the 15 GEMV launches of the sweep as one CUDA graph, {reps} replays between CUDA events "
+                      "on the launching stream",
+            "event_timing": "per_launch event_us: events recorded around each launch inside a graph (serialising)",
+            "isolated": {"achieved": iso_achieved, "frac": iso_achieved / peak,
+                         "timing": "median of 5 launches per config, each after a read-based L2 eviction"},
+            "per_launch": per}
 
 
 def measure_e2e(calls, args, device, world) -> dict:
@@ -662,8 +757,8 @@ def run_profile_case(spec: str, launches: int) -> None:
     """Small cases for ncu captures, nothing else of the bench:
     ``gemv:<shape>:<m>`` / ``gemm:<shape>:<m>`` run the linear kernel of one
     call ``launches`` times (two warm-up launches first); ``gemv:sweep`` runs
-    each of the 15 configs[1] calls once after a read-based L2 eviction (the
-    launches the roofline times)."""
+    each of the 15 configs[1] calls once after a read-based L2 eviction, M <= 4
+    through the fused quant + GEMV kernel as in the timed step."""
     import torch
 
     from hif8_b200 import native, scheme
@@ -712,9 +807,13 @@ def run_profile_case(spec: str, launches: int) -> None:
         for m in M_VALUES:
             for name, n, k in SHAPES:
                 wq, ws = weights[name]
-                a, ts = native.static_quant(torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16), fixed)
+                x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+                a, ts = native.static_quant(x, fixed)
                 flush.sum()
-                ext.soft_hif8_gemm(a, wq, ts, ws, None, torch.bfloat16)
+                if m <= 4:  # the fused quant + GEMV launch of scheme.apply
+                    native.soft_static_fused_linear(x, wq, fixed, ws, None, output_dtype=torch.bfloat16)
+                else:
+                    ext.soft_hif8_gemm(a, wq, ts, ws, None, torch.bfloat16)
         torch.cuda.synchronize()
         print(f"profile case {spec}: {len(M_VALUES) * len(SHAPES)} launches ok")
         return

@@ -1,6 +1,7 @@
 // Library-wide C-ABI plumbing: status strings, last-error text, codec tables.
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -23,6 +24,14 @@ int check_launch() {
     return HIF8_ERR_CUDA;
   }
   return HIF8_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *v = std::getenv("HIF8_DISABLE_PDL");
+    return !(v && v[0] == '1');
+  }();
+  return on;
 }
 
 int num_sms() {

@@ -12,17 +12,20 @@
 //     cluster walks row blocks ("items") round-robin, so every CTA keeps one
 //     K slice of the activation decoded in shared memory for the whole launch;
 //   * inside a CTA the 16 warps split the item as WR row groups x WK K parts;
-//     every warp always owns exactly four 64-byte K blocks per item, so its
-//     4-deep register ring of 16-byte weight loads is indexed at compile time
-//     and runs straight across item boundaries (the next item's blocks are in
-//     flight while the current one is reduced);
+//     every warp always owns exactly two 128-byte K blocks per item, so its
+//     2-deep register ring of 32-byte weight loads (one 128-byte row segment
+//     per four lanes: a load instruction of the warp moves 1 KB) is indexed
+//     at compile time and runs straight across item boundaries (the next
+//     item's blocks are in flight while the current one is reduced);
 //   * a weight byte becomes BF16 with one shared-memory lookup: entry b of
 //     lane l sits at byte (b << 8) | (l << 2), so a lane always hits its own
 //     bank, and one PRMT builds the address from the weight word;
 //   * decoded 16 x 16 weight tiles feed mma.sync m16n8k16 (BF16, FP32
 //     accumulate) against the activation fragments.  Lane (g, t) takes bytes
-//     t*16 .. t*16+15 of a 64-byte block, so the MMA's K order is a fixed
-//     permutation of memory order, applied identically to the activations;
+//     t*32 .. t*32+31 of a 128-byte block, so the MMA's K order is a fixed
+//     permutation of memory order, applied identically to the activations
+//     (stored in that order, 16-byte chunks rotated so the fragment loads are
+//     free of bank conflicts; rows of padding tokens are not loaded);
 //   * partial sums are reduced in a fixed order: the warps of an item after
 //     every item, the cluster ranks once for all items at the end, through
 //     distributed shared memory -- deterministic, no global scratch.
@@ -41,20 +44,43 @@ namespace hif8 {
 constexpr int kWarps = 16;                  // warps per CTA
 constexpr int kThreads = kWarps * 32;
 constexpr int kLutBytes = 256 * 256;        // lane-replicated table, 256 B per entry
-constexpr int kRing = 4;                    // 64-byte K blocks per warp per item (= ring depth)
-constexpr int kWarpK = kRing * 64;          // K per warp per item
+constexpr int kBlk = 128;                   // K bytes of one ring stage (32 per lane of a row)
+constexpr int kRing = 2;                    // K blocks per warp per item (= ring depth)
+constexpr int kWarpK = kRing * kBlk;        // K per warp per item
+constexpr int kRedStride = 20;              // floats per token row of a warp partial (bank-conflict-free)
 
 // Activation source of the linear kernels.
 constexpr int kActCodes = 0;  // HiF8 bytes
 constexpr int kActBf16 = 1;   // BF16, quantised in the prologue with ts[0]
 constexpr int kActF16 = 2;    // FP16, idem
 
-__device__ __forceinline__ uint4 ldg_stream(const uint8_t *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+struct U32x8 {
+  uint32_t v[8];
+};
+
+// 32 bytes per lane (a 256-bit load; p 32-byte aligned), streamed past L1.
+__device__ __forceinline__ U32x8 ldg_stream32(const uint8_t *p) {
+  U32x8 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]),
+                 "=r"(r.v[6]), "=r"(r.v[7])
                : "l"(p));
-  return v;
+  return r;
+}
+
+// Byte offset, inside one token row of the activation tile, of the 8 BF16
+// values at K index kk (kk % 8 == 0) of the CTA's slice.  Block b of 128 K
+// holds lane quarter tq's 32 values at tq*64; their four 16-byte chunks are
+// rotated by 2*(tq>>1) so that lanes t = 0..3 reading chunk c hit four
+// different 16-byte bank groups.
+__device__ __forceinline__ int act_offset(int kk) {
+  const int b = kk >> 7, w = kk & 127, tq = w >> 5, c = (w >> 3) & 3;
+  return b * 256 + tq * 64 + (((c + 2 * (tq >> 1)) & 3) << 4);
+}
+
+// Bulk prefetch of `bytes` (multiple of 16; p 16-byte aligned) into L2.
+__device__ __forceinline__ void prefetch_l2(const uint8_t *p, int bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ uint32_t lut_lookup(const uint8_t *lut, uint32_t word, uint32_t lane4, uint32_t sel) {
@@ -141,13 +167,15 @@ struct GemvPlan {
   int max_items = 0;  // row blocks per cluster (upper bound)
 };
 
+// kc * 2 is a multiple of 512, so consecutive token rows start 16 bytes
+// (one bank group) apart modulo 128.
 __host__ __device__ constexpr int act_stride_bytes(int kc) { return kc * 2 + 16; }
 
 // shared memory: table | activation tile | warp partials x2 | CTA partials
 // of every item of this cluster (reduced across the cluster once, at the end)
 __host__ __device__ constexpr size_t gemv_smem_bytes(int nt, int kc, int wr, int max_items) {
   return (size_t)kLutBytes + (size_t)(8 * nt) * act_stride_bytes(kc) +
-         2 * (size_t)kWarps * 128 * nt * sizeof(float) + (size_t)max_items * (16 * wr) * 8 * nt * sizeof(float);
+         2 * (size_t)kWarps * (8 * nt) * kRedStride * sizeof(float) + (size_t)max_items * (16 * wr) * 8 * nt * sizeof(float);
 }
 
 template <int NT, int OUT, int ASRC>
@@ -160,8 +188,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   const int k0 = rank * kc;
   const int act_stride = act_stride_bytes(kc);
   uint8_t *act = smem + kLutBytes;
-  float *red = reinterpret_cast<float *>(act + (size_t)kTok * act_stride);  // [2][kWarps][kTok][16]
-  float *part = red + 2 * kWarps * 16 * kTok;                               // [items][kTok][16 * WR]
+  float *red = reinterpret_cast<float *>(act + (size_t)kTok * act_stride);  // [2][kWarps][kTok][kRedStride]
+  float *part = red + 2 * kWarps * kRedStride * kTok;                       // [items][kTok][16 * WR]
+
+  // ---- work assignment -----------------------------------------------------
+  const int g = lane >> 2, t = lane & 3;
+  const int wr = warp / WK, wk = warp - wr * WK;  // row group / K part of this warp
+  const int rows_per_item = 16 * WR;
+  const int n_items = (p.n + rows_per_item - 1) / rows_per_item;
+  const int my_items = n_items > cluster_id ? (n_items - cluster_id + plan.clusters - 1) / plan.clusters : 0;
+  const int kw0 = k0 + wk * kWarpK;  // this warp's K offset inside every item
 
   // ---- prologue: lane-replicated decode table + this rank's activation slice
   {
@@ -180,6 +216,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
       for (int i = tid; i < 512; i += kThreads)
         reinterpret_cast<uint4 *>(enc)[i] = reinterpret_cast<const uint4 *>(g_static_encode.v)[i];
     }
+    // the first item's weight rows of this warp into L2 (256 bytes per row)
+    if (my_items > 0 && t == 0) {
+      const int row = cluster_id * rows_per_item + wr * 16 + g;
+      const int r0 = min(row, p.n - 1), r1 = min(row + 8, p.n - 1);
+      prefetch_l2(p.w + (int64_t)r0 * p.k + kw0, kWarpK);
+      prefetch_l2(p.w + (int64_t)r1 * p.k + kw0, kWarpK);
+    }
+    // everything above reads constants only; the activations and scales may
+    // come from the previous kernel of the stream
+    pdl_wait();
     __syncthreads();
     const int chunks_per_tok = kc >> 4;  // 16 K values per chunk
     const int real = (p.m < kTok ? p.m : kTok) * chunks_per_tok;
@@ -239,41 +285,40 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
             o1 = make_uint4(rr[4], rr[5], rr[6], rr[7]);
           }
         }
-        uint4 *dst = reinterpret_cast<uint4 *>(act + tok * act_stride + ch * 32);
-        dst[0] = o0;
-        dst[1] = o1;
+        uint8_t *row = act + tok * act_stride;
+        *reinterpret_cast<uint4 *>(row + act_offset(ch * 16)) = o0;
+        *reinterpret_cast<uint4 *>(row + act_offset(ch * 16 + 8)) = o1;
       }
     }
   }
   __syncthreads();
 
-  // ---- work assignment -----------------------------------------------------
-  const int g = lane >> 2, t = lane & 3;
-  const int wr = warp / WK, wk = warp - wr * WK;  // row group / K part of this warp
-  const int rows_per_item = 16 * WR;
   const int mt = p.m < kTok ? p.m : kTok;  // real tokens of the tile
-  const int n_items = (p.n + rows_per_item - 1) / rows_per_item;
-  const int my_items = n_items > cluster_id ? (n_items - cluster_id + plan.clusters - 1) / plan.clusters : 0;
-  const int kw0 = k0 + wk * kWarpK;  // this warp's K offset inside every item
   const uint8_t *lut = smem;
   const uint32_t lane4 = (uint32_t)lane << 2;
-  const uint8_t *act_lane = act + g * act_stride + (wk * kWarpK / 64) * 128 + t * 32;
+  // this lane's 64 bytes of every 128-K block: token row g (+ 8 for the
+  // second tile); rows of padding tokens (>= m) are never loaded
+  const uint8_t *act_lane = act + g * act_stride + (wk * kWarpK / kBlk) * 256 + t * 64;
+  const int rot = 2 * (t >> 1);
+  bool tok_real[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) tok_real[nt] = nt * 8 + g < p.m;
 
   auto weight_ptrs = [&](int item, const uint8_t *&w0, const uint8_t *&w1) {
     const int row = (cluster_id + item * plan.clusters) * rows_per_item + wr * 16 + g;
     const int r0 = min(row, p.n - 1), r1 = min(row + 8, p.n - 1);
-    w0 = p.w + (int64_t)r0 * p.k + kw0 + t * 16;
-    w1 = p.w + (int64_t)r1 * p.k + kw0 + t * 16;
+    w0 = p.w + (int64_t)r0 * p.k + kw0 + t * 32;
+    w1 = p.w + (int64_t)r1 * p.k + kw0 + t * 32;
   };
 
-  uint4 ring[kRing][2];
+  U32x8 ring[kRing][2];
   if (my_items > 0) {
     const uint8_t *w0, *w1;
     weight_ptrs(0, w0, w1);
 #pragma unroll
     for (int s = 0; s < kRing; ++s) {
-      ring[s][0] = ldg_stream(w0 + s * 64);
-      ring[s][1] = ldg_stream(w1 + s * 64);
+      ring[s][0] = ldg_stream32(w0 + s * kBlk);
+      ring[s][1] = ldg_stream32(w1 + s * kBlk);
     }
   }
 
@@ -291,29 +336,30 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
 
 #pragma unroll
     for (int s = 0; s < kRing; ++s) {
-      const uint4 x0 = ring[s][0], x1 = ring[s][1];
+      const U32x8 x0 = ring[s][0], x1 = ring[s][1];
       if (has_next) {  // the next item's block s goes into the freed slot
-        ring[s][0] = ldg_stream(n0 + s * 64);
-        ring[s][1] = ldg_stream(n1 + s * 64);
+        ring[s][0] = ldg_stream32(n0 + s * kBlk);
+        ring[s][1] = ldg_stream32(n1 + s * kBlk);
       }
-      uint4 bf[NT][2];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(act_lane + nt * 8 * act_stride + s * 128);
-        bf[nt][0] = src[0];
-        bf[nt][1] = src[1];
-      }
-      const uint32_t wa[4] = {x0.x, x0.y, x0.z, x0.w};
-      const uint32_t wb[4] = {x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t a[4];
-        decode4(lut, wa[j], lane4, a[0], a[2]);
-        decode4(lut, wb[j], lane4, a[1], a[3]);
+      for (int c = 0; c < 4; ++c) {  // 16-byte chunk c: K t*32 + 8c .. +7 of the block
+        uint4 bf[NT];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const uint4 &q = bf[nt][j >> 1];
-          mma_bf16_16816(acc[j & 1][nt], a, (j & 1) ? q.z : q.x, (j & 1) ? q.w : q.y);
+          bf[nt] = make_uint4(0, 0, 0, 0);
+          if (tok_real[nt])
+            bf[nt] = *reinterpret_cast<const uint4 *>(act_lane + nt * 8 * act_stride + s * 256 +
+                                                      (((c + rot) & 3) << 4));
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int j = 2 * c + h;
+          uint32_t a[4];
+          decode4(lut, x0.v[j], lane4, a[0], a[2]);
+          decode4(lut, x1.v[j], lane4, a[1], a[3]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            mma_bf16_16816(acc[h][nt], a, h ? bf[nt].z : bf[nt].x, h ? bf[nt].w : bf[nt].y);
         }
       }
     }
@@ -322,14 +368,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
     // Partials are token-major ([token][row]) so the summing threads walk the
     // output rows of one token consecutively: the global stores coalesce.
     const int buf = item & 1;
-    float *wred = red + ((size_t)buf * kWarps + warp) * kTok * 16;
+    float *wred = red + ((size_t)buf * kWarps + warp) * kTok * kRedStride;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int m = nt * 8 + 2 * t + (q & 1);
         const int rl = g + ((q < 2) ? 0 : 8);
-        wred[m * 16 + rl] = acc[0][nt][q] + acc[1][nt][q];
+        wred[m * kRedStride + rl] = acc[0][nt][q] + acc[1][nt][q];
       }
     }
     __syncthreads();
@@ -338,9 +384,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
     for (int e = tid; e < rows_per_item * mt; e += kThreads) {
       const int m = e / rows_per_item, rl = e - m * rows_per_item;  // token, row within the item
       const int grp = rl >> 4, r16 = rl & 15;
-      const float *src = red + (((size_t)buf * kWarps + grp * WK) * kTok + m) * 16 + r16;
+      const float *src = red + (((size_t)buf * kWarps + grp * WK) * kTok + m) * kRedStride + r16;
       float v = 0.f;
-      for (int w = 0; w < WK; ++w) v += src[(size_t)w * kTok * 16];
+      for (int w = 0; w < WK; ++w) v += src[(size_t)w * kTok * kRedStride];
       if (S == 1) {
         const int n = row_base + rl;
         if (n < p.n) {
@@ -385,6 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
 // a fixed per-lane order followed by a fixed shuffle tree (deterministic).
 template <int OUT, int ASRC>
 __global__ void __launch_bounds__(256) linear_hif8_generic(const GemvArgs p) {
+  pdl_wait();
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t total = (int64_t)p.m * p.n;
@@ -420,6 +467,7 @@ __global__ void __launch_bounds__(256) linear_hif8_generic(const GemvArgs p) {
 // ------------------------------------------------------------------ host --
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static bool aligned32(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
 constexpr size_t kMaxSmem = 227 * 1024;
 
@@ -520,13 +568,15 @@ static int launch_gemv(const GemvArgs &args, const GemvPlan &plan, cudaStream_t 
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)plan.s;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, args, plan);
   if (err != cudaSuccess) {
     set_last_error(err);
@@ -541,14 +591,16 @@ static int launch_generic(const GemvArgs &args, cudaStream_t stream) {
   int64_t blocks = (total + 7) / 8;
   const int64_t cap = (int64_t)num_sms() * 16;
   if (blocks > cap) blocks = cap;
-  linear_hif8_generic<OUT, ASRC><<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, stream>>>(args);
-  return check_launch();
+  return launch_pdl(linear_hif8_generic<OUT, ASRC>, dim3((unsigned)(blocks > 0 ? blocks : 1)), dim3(256), 0, stream,
+                    args);
 }
 
 // y = a @ w^T for any m: the persistent split-K kernel on 16-token slices
 // when the shape allows it, otherwise the generic kernel.
 int run_linear(GemvArgs args, int output_dtype, cudaStream_t stream) {
-  const bool vec_ok = aligned16(args.a) && aligned16(args.w) && args.k % 64 == 0;
+  // 16-byte activation loads, 32-byte weight loads (k % 256 == 0 keeps every
+  // row segment aligned)
+  const bool vec_ok = aligned16(args.a) && aligned32(args.w) && args.k % 64 == 0;
   const bool bf16_out = output_dtype == HIF8_DTYPE_BF16;
   for (int m0 = 0; m0 < args.m; m0 += 16) {
     GemvArgs s = args;
@@ -581,7 +633,7 @@ int run_linear(GemvArgs args, int output_dtype, cudaStream_t stream) {
 int run_fused_linear(const GemvArgs &args, int x_dtype, int output_dtype, cudaStream_t stream) {
   const bool bf16_out = output_dtype == HIF8_DTYPE_BF16;
   const bool bf16_in = x_dtype == HIF8_DTYPE_BF16;
-  const bool vec_ok = aligned16(args.a) && aligned16(args.w) && args.k % 64 == 0 && args.m <= 8;
+  const bool vec_ok = aligned16(args.a) && aligned32(args.w) && args.k % 64 == 0 && args.m <= 8;
   const void *kptr = bf16_in ? (bf16_out ? gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActBf16>()
                                          : gemv_kernel_ptr<1, HIF8_DTYPE_F16, kActBf16>())
                              : (bf16_out ? gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActF16>()

@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/hif8_b200.h"
 
 #define HIF8_HD __host__ __device__ __forceinline__
@@ -172,5 +174,49 @@ int num_sms();
 // skipped when the limit already suffices, so launches under CUDA-graph
 // capture issue no attribute calls after the first eager launch).
 int ensure_smem_limit(const void *kernel, size_t bytes);
+
+// ------------------------------------------- programmatic dependent launch --
+// The decode-path kernels are launched with the programmatic stream
+// serialization attribute, so the next kernel of the stream is launched as
+// soon as this one's CTAs have exited, overlapping its launch with the
+// completion of this one.  Every such kernel calls pdl_wait() before it reads
+// anything an earlier kernel of the stream may have written and before its
+// first global write: the wait returns once the preceding kernel has
+// completed and its writes are visible (immediately for an ordinary launch).
+// Work before the wait touches only constant tables and shared memory, or
+// issues L2 prefetches (L2 is the coherence point, so a prefetch never
+// yields a stale value).  No kernel signals its dependents early
+// (griddepcontrol.launch_dependents): measured on B200, an early signal
+// lets the dependent's CTAs occupy SMs while this grid still runs and made
+// the configs[1] sweep 5 % slower as a CUDA graph, while the implicit signal
+// at exit made it 2 % faster than ordinary launches.
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// False when the environment sets HIF8_DISABLE_PDL=1 (read once).
+bool pdl_enabled();
+
+// Launch `kernel` on `stream`, with the programmatic serialization attribute
+// unless disabled; returns a HIF8_* status.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess) {
+    set_last_error(err);
+    return HIF8_ERR_CUDA;
+  }
+  return check_launch();
+}
 
 }  // namespace hif8

@@ -39,6 +39,7 @@ struct KvWriteArgs {
 // into one 4-byte store; lane 0 appends the FP32 scale.
 template <int kDtype>
 __global__ void __launch_bounds__(256) kv_write_kernel(const KvWriteArgs p) {
+  pdl_wait();  // inputs come from the previous kernel of the stream
   __shared__ __align__(16) uint8_t tbl[8192];
   {
     const uint4 *src = reinterpret_cast<const uint4 *>(g_static_encode.v);
@@ -276,6 +277,7 @@ __device__ __forceinline__ float block_reduce(float v, bool is_max, float *scrat
 __global__ void __launch_bounds__(kCombineThreads) attention_combine_kernel(
     const float *__restrict__ part, int64_t rows, int64_t d, int splits, int chunk, const int32_t *q_start,
     const int32_t *seq_lens, int64_t batch, int64_t heads, uint16_t *__restrict__ out) {
+  pdl_wait();  // inputs come from the previous kernel of the stream
   __shared__ float wgt[kCombineBlock];
   __shared__ float scratch[kCombineThreads / 32];
   const int64_t row = blockIdx.x;  // token * heads + head
@@ -354,6 +356,7 @@ constexpr int kDecBatch = 8;    // key rows whose loads a warp issues together
 //     the longest request.
 template <int G>
 __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArgs p) {
+  pdl_wait();  // inputs come from the previous kernel of the stream
   constexpr int D = kDecHead;
   constexpr int W = D / 128;  // 4-byte K / V words per lane per row
   __shared__ float lut[256], klut[256], vlut[256];
@@ -668,9 +671,8 @@ extern "C" int hif8_kv_cache_write(const void *key, const void *value, int src_d
   const int64_t warps = tokens * kv_heads * p.planes;
   const int grid = attn_grid_cap((warps + 7) / 8);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (src_dtype == HIF8_DTYPE_BF16) kv_write_kernel<HIF8_DTYPE_BF16><<<grid, 256, 0, s>>>(p);
-  else kv_write_kernel<HIF8_DTYPE_F16><<<grid, 256, 0, s>>>(p);
-  return check_launch();
+  return src_dtype == HIF8_DTYPE_BF16 ? launch_pdl(kv_write_kernel<HIF8_DTYPE_BF16>, dim3(grid), dim3(256), 0, s, p)
+                                      : launch_pdl(kv_write_kernel<HIF8_DTYPE_F16>, dim3(grid), dim3(256), 0, s, p);
 }
 
 static int attn_nq(int64_t group, int64_t q_rows) { return (int)(group * q_rows); }
@@ -743,12 +745,11 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
   if (decode) {
     const dim3 grid((unsigned)(batch * kv_heads), (unsigned)splits, 1);
     switch (group) {
-      case 1: paged_decode_kernel<1><<<grid, kDecThreads, 0, s>>>(p); break;
-      case 2: paged_decode_kernel<2><<<grid, kDecThreads, 0, s>>>(p); break;
-      case 4: paged_decode_kernel<4><<<grid, kDecThreads, 0, s>>>(p); break;
-      default: paged_decode_kernel<8><<<grid, kDecThreads, 0, s>>>(p); break;
+      case 1: status = launch_pdl(paged_decode_kernel<1>, grid, dim3(kDecThreads), 0, s, p); break;
+      case 2: status = launch_pdl(paged_decode_kernel<2>, grid, dim3(kDecThreads), 0, s, p); break;
+      case 4: status = launch_pdl(paged_decode_kernel<4>, grid, dim3(kDecThreads), 0, s, p); break;
+      default: status = launch_pdl(paged_decode_kernel<8>, grid, dim3(kDecThreads), 0, s, p); break;
     }
-    status = check_launch();
   } else if (group <= 4) {
     // prefill and mixed batches: up to 4 query vectors per CTA
     p.q_rows_per_cta = (int)(4 / group);
@@ -762,10 +763,8 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
   (void)attn_nq;
   if (status != HIF8_OK || splits == 1) return status;
   const int64_t rows = num_tokens * num_heads;
-  attention_combine_kernel<<<(unsigned)rows, kCombineThreads, 0, s>>>(p.part, rows, head_size, (int)splits, chunk,
-                                                                     query_start,
-                                                         seq_lens, batch, num_heads, out);
-  return check_launch();
+  return launch_pdl(attention_combine_kernel, dim3((unsigned)rows), dim3(kCombineThreads), 0, s, (const float *)p.part,
+                    rows, head_size, (int)splits, chunk, query_start, seq_lens, batch, num_heads, out);
 }
 
 extern "C" int hif8_kv_gather_decode(const uint8_t *cache, const int32_t *block_tables, const int32_t *seq_lens,

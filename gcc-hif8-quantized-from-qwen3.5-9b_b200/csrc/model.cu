@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const uint16_t *_
                                                                uint16_t *__restrict__ res_out,
                                                                const uint16_t *__restrict__ w, float eps,
                                                                int one_plus, int dim, uint16_t *__restrict__ out) {
+  pdl_wait();  // inputs come from the previous kernel of the stream
   __shared__ float scratch[32];
   const int64_t row = blockIdx.x;
   float v[4][8];
@@ -95,6 +96,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const uint16_t *_
 // ---------------------------------------------------------- SiLU-gated MLP --
 __global__ void silu_mul_kernel(const uint16_t *__restrict__ gu, int64_t rows, int64_t inter,
                                 uint16_t *__restrict__ out) {
+  pdl_wait();  // inputs come from the previous kernel of the stream
   const int64_t total = rows * inter / 2;  // pairs
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = (2 * i) / inter, c = 2 * i - r * inter;
@@ -109,6 +111,7 @@ __global__ void silu_mul_kernel(const uint16_t *__restrict__ gu, int64_t rows, i
 // ------------------------------------------------------ sigmoid gate (attn) --
 __global__ void gate_mul_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ gate, int64_t n,
                                 uint16_t *__restrict__ out) {
+  pdl_wait();  // inputs come from the previous kernel of the stream
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = to_bf(bf(x[i]) * sigmoid(bf(gate[i])));
 }
@@ -123,6 +126,7 @@ __global__ void attn_prep_kernel(const uint16_t *__restrict__ qkv, int heads, in
                                  const uint16_t *__restrict__ kw, float eps, float theta,
                                  uint16_t *__restrict__ q_out, uint16_t *__restrict__ gate_out,
                                  uint16_t *__restrict__ k_out, uint16_t *__restrict__ v_out) {
+  pdl_wait();  // inputs come from the previous kernel of the stream
   __shared__ float xs[1024];
   __shared__ float scratch[32];
   const int64_t tok = blockIdx.x;
@@ -183,6 +187,7 @@ constexpr int kGdnThreads = 2 * kGdnDim;
 constexpr int kGdnRows = kGdnDim / 2;  // state rows per thread
 
 __global__ void __launch_bounds__(kGdnThreads) gdn_kernel(const Hif8GdnArgs p) {
+  pdl_wait();  // inputs come from the previous kernel of the stream
   __shared__ float qs[kGdnDim], ks[kGdnDim];
   __shared__ float scratch[32];
   const int vh = blockIdx.x, b = blockIdx.y;
@@ -293,6 +298,7 @@ __device__ __forceinline__ uint64_t gtimer_ns() {
 }
 
 __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_rmsnorm_kernel(const Hif8PeerArgs p) {
+  pdl_wait();  // inputs come from the previous kernel of the stream
   __shared__ float rowsum[8];
   const int tid = threadIdx.x;
   const int64_t n = p.rows * p.dim;
@@ -404,8 +410,7 @@ extern "C" int hif8_model_peer_allreduce_rmsnorm(const Hif8PeerArgs *args, void 
       p.rows > 8)
     return HIF8_ERR_INVALID_ARGUMENT;
   if (p.rows == 0) return HIF8_OK;
-  peer_allreduce_rmsnorm_kernel<<<1, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return check_launch();
+  return launch_pdl(peer_allreduce_rmsnorm_kernel, dim3(1), dim3(kPeerThreads), 0, static_cast<cudaStream_t>(stream), p);
 }
 
 extern "C" int hif8_peer_alloc(size_t bytes, void **ptr, void *handle64) {
@@ -449,9 +454,8 @@ extern "C" int hif8_model_rmsnorm(const uint16_t *x, const uint16_t *residual_in
   if (!x || !weight || !out || rows < 0 || dim <= 0 || dim % 8 != 0 || dim > 4 * kNormThreads * 8)
     return HIF8_ERR_INVALID_ARGUMENT;
   if (rows == 0) return HIF8_OK;
-  rmsnorm_kernel<<<(unsigned)rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, residual_in, residual_out, weight, eps, one_plus, (int)dim, out);
-  return check_launch();
+  return launch_pdl(rmsnorm_kernel, dim3((unsigned)rows), dim3(kNormThreads), 0, static_cast<cudaStream_t>(stream), x,
+                    residual_in, residual_out, weight, eps, one_plus, (int)dim, out);
 }
 
 extern "C" int hif8_model_silu_mul(const uint16_t *gate_up, int64_t rows, int64_t inter, uint16_t *out,
@@ -461,8 +465,8 @@ extern "C" int hif8_model_silu_mul(const uint16_t *gate_up, int64_t rows, int64_
   const int64_t pairs = rows * inter / 2;
   int64_t blocks = (pairs + 255) / 256;
   if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
-  silu_mul_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(gate_up, rows, inter, out);
-  return check_launch();
+  return launch_pdl(silu_mul_kernel, dim3((unsigned)blocks), dim3(256), 0, static_cast<cudaStream_t>(stream), gate_up,
+                    rows, inter, out);
 }
 
 extern "C" int hif8_model_gate_mul(const uint16_t *x, const uint16_t *gate, int64_t n, uint16_t *out, void *stream) {
@@ -470,8 +474,8 @@ extern "C" int hif8_model_gate_mul(const uint16_t *x, const uint16_t *gate, int6
   if (n == 0) return HIF8_OK;
   int64_t blocks = (n + 255) / 256;
   if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
-  gate_mul_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, gate, n, out);
-  return check_launch();
+  return launch_pdl(gate_mul_kernel, dim3((unsigned)blocks), dim3(256), 0, static_cast<cudaStream_t>(stream), x, gate, n,
+                    out);
 }
 
 extern "C" int hif8_model_attn_prep(const uint16_t *qkv, int64_t tokens, int heads, int kv_heads, int head_dim,
@@ -484,10 +488,8 @@ extern "C" int hif8_model_attn_prep(const uint16_t *qkv, int64_t tokens, int hea
     return HIF8_ERR_INVALID_ARGUMENT;
   if (tokens == 0) return HIF8_OK;
   const dim3 grid((unsigned)tokens, (unsigned)(heads + kv_heads));
-  attn_prep_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      qkv, heads, kv_heads, head_dim, rotary_dim, positions, q_norm_w, k_norm_w, eps, rope_theta, q_out, gate_out,
-      k_out, v_out);
-  return check_launch();
+  return launch_pdl(attn_prep_kernel, grid, dim3(128), 0, static_cast<cudaStream_t>(stream), qkv, heads, kv_heads,
+                    head_dim, rotary_dim, positions, q_norm_w, k_norm_w, eps, rope_theta, q_out, gate_out, k_out, v_out);
 }
 
 extern "C" int hif8_model_gdn(const Hif8GdnArgs *args, int64_t batch, void *stream) {
@@ -498,6 +500,5 @@ extern "C" int hif8_model_gdn(const Hif8GdnArgs *args, int64_t batch, void *stre
     return HIF8_ERR_INVALID_ARGUMENT;
   if (batch == 0 || p.T == 0) return HIF8_OK;
   const dim3 grid((unsigned)p.hv, (unsigned)batch);
-  gdn_kernel<<<grid, kGdnThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return check_launch();
+  return launch_pdl(gdn_kernel, grid, dim3(kGdnThreads), 0, static_cast<cudaStream_t>(stream), p);
 }

@@ -55,6 +55,7 @@ __global__ void __launch_bounds__(256) static_quant_vec16(const uint16_t *__rest
                                                           int64_t rows) {
   __shared__ __align__(16) uint8_t tbl[8192];
   load_encode_table(tbl);
+  pdl_wait();  // x and scale may come from the previous kernel of the stream
   write_row_scale(scale, scale_count, row_scale, rows);
   __syncthreads();
   const int64_t chunks_per_row = k >> 4;
@@ -89,6 +90,7 @@ __global__ void __launch_bounds__(256) static_quant_scalar(const uint16_t *__res
                                                            int64_t rows) {
   __shared__ __align__(16) uint8_t tbl[8192];
   load_encode_table(tbl);
+  pdl_wait();  // x and scale may come from the previous kernel of the stream
   write_row_scale(scale, scale_count, row_scale, rows);
   __syncthreads();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -202,22 +204,18 @@ extern "C" int hif8_static_quant(const void *x, int x_dtype, int64_t rows, int64
   if (k % 16 == 0 && aligned16(x) && aligned16(data)) {
     const int64_t chunks = total / 16;
     const int grid = grid_for(chunks, 256);
-    if (x_dtype == HIF8_DTYPE_BF16)
-      static_quant_vec16<HIF8_DTYPE_BF16><<<grid, 256, 0, stream>>>(xs, k, fixed_scale, scale_count, data, chunks,
-                                                                     row_scale, rows);
-    else
-      static_quant_vec16<HIF8_DTYPE_F16><<<grid, 256, 0, stream>>>(xs, k, fixed_scale, scale_count, data, chunks,
-                                                                    row_scale, rows);
-  } else {
-    const int grid = grid_for(total, 256);
-    if (x_dtype == HIF8_DTYPE_BF16)
-      static_quant_scalar<HIF8_DTYPE_BF16><<<grid, 256, 0, stream>>>(xs, k, fixed_scale, scale_count, data, total,
-                                                                      row_scale, rows);
-    else
-      static_quant_scalar<HIF8_DTYPE_F16><<<grid, 256, 0, stream>>>(xs, k, fixed_scale, scale_count, data, total,
-                                                                     row_scale, rows);
+    return x_dtype == HIF8_DTYPE_BF16
+               ? launch_pdl(static_quant_vec16<HIF8_DTYPE_BF16>, dim3(grid), dim3(256), 0, stream, xs, k,
+                            fixed_scale, scale_count, data, chunks, row_scale, rows)
+               : launch_pdl(static_quant_vec16<HIF8_DTYPE_F16>, dim3(grid), dim3(256), 0, stream, xs, k,
+                            fixed_scale, scale_count, data, chunks, row_scale, rows);
   }
-  return check_launch();
+  const int grid = grid_for(total, 256);
+  return x_dtype == HIF8_DTYPE_BF16
+             ? launch_pdl(static_quant_scalar<HIF8_DTYPE_BF16>, dim3(grid), dim3(256), 0, stream, xs, k, fixed_scale,
+                          scale_count, data, total, row_scale, rows)
+             : launch_pdl(static_quant_scalar<HIF8_DTYPE_F16>, dim3(grid), dim3(256), 0, stream, xs, k, fixed_scale,
+                          scale_count, data, total, row_scale, rows);
 }
 
 extern "C" int hif8_scaled_decode(const uint8_t *data, int64_t rows, int64_t k, int64_t data_row_stride,
