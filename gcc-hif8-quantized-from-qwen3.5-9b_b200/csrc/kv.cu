@@ -6,6 +6,9 @@
 // head_size HiF8 codes followed by the row's little-endian FP32 scale.
 #include <math_constants.h>
 
+#include <atomic>
+#include <type_traits>
+
 #include "hif8_common.cuh"
 
 namespace hif8 {
@@ -95,6 +98,7 @@ struct AttnArgs {
   float *part;                // split partials (null when splits == 1)
   int64_t heads, kv_heads, d, block_size, max_blocks, num_blocks;
   int splits;                 // KV chunks per request (grid.y)
+  int chunk;                  // keys per chunk (decode kernel)
   int q_rows_per_cta;         // query rows handled per CTA (grid.z groups)
   float scale;
   int causal;
@@ -330,260 +334,312 @@ __global__ void __launch_bounds__(kCombineThreads) attention_combine_kernel(
 
 // ------------------------------------------------------ decode attention ---
 
-constexpr int kDecChunk = 64;   // keys per CTA of the decode kernel
-constexpr int kDecThreads = 128;
-constexpr int kDecHead = 256;   // head size of the decode kernel (128 threads x 2 value columns)
-constexpr int kDecBatch = 8;    // key rows whose loads a warp issues together
+constexpr int kDecChunk = 64;      // key granularity of the decode split (the workspace is sized for it)
+constexpr int kDecMaxChunk = 256;
+constexpr int kDecWarps = 4;
+constexpr int kDecThreads = kDecWarps * 32;
+constexpr int kDecHead = 256;      // head size of the decode kernel
+constexpr int kDecBlock = 8;       // keys per MMA step of a warp
 
-// Split-KV attention for decode batches (normally one query row per
-// request).  CTA = (request b, KV head h, 64-key chunk); the G query heads
-// of the GQA group share every key and value load.
-//   * the scales are static per head, so the CTA builds K and V tables of
-//     BF16(decode(c) x scale) for the scale of its first row; a row with
-//     that scale decodes with one lookup, any other row multiplies and
-//     rounds as the reference materialises BF16 K and V;
-//   * the chunk's row offsets are resolved from the block table once, into
-//     shared memory (a block id outside [0, num_blocks) marks the key absent);
-//   * scores: warp w takes keys w, w+4, ...; the 32 lanes read one K row
-//     together (4 bytes per lane and 128-byte step, coalesced) and reduce the
-//     G dot products with butterfly shuffles;
-//   * softmax per head in FP32; P @ V with the same row split as the scores
-//     (warp w takes keys [16 w, 16 w + 16)), the four warps' sums added in
-//     shared memory; all row loads are unconditional, so the unrolled keys'
-//     loads are in flight together;
-//   * partials (unnormalised output, running max, sum) merge in
-//     attention_combine_kernel, or are written directly when one chunk covers
-//     the longest request.
+__device__ __forceinline__ void attn_mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void attn_mma1688(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm("mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// Decoded BF16 bits of byte `sel` of `word`, in the high half of the result:
+// from this lane's copy of the table (high half = the V value, low half = the
+// K value, selected by the caller), or computed with the row's own scale.
+template <bool TAB>
+__device__ __forceinline__ uint32_t kv_dec(const uint32_t *tab, const float *lut, uint32_t word, int sel, int lane,
+                                           float scale, bool value_half) {
+  const uint32_t c = (word >> (8 * sel)) & 0xFFu;
+  if constexpr (TAB) return value_half ? tab[c * 32 + lane] : tab[c * 32 + lane] << 16;
+  else return f32_to_bf16_bits(lut[c] * scale) << 16;
+}
+
+// Split-KV decode attention on the tensor cores (mma.sync, BF16 operands,
+// FP32 accumulation), for decode batches (one query row per request) of head
+// size 256 and GQA groups of 1, 2, 4 or 8.
+// CTA = (request b, KV head h, chunk of p.chunk keys); warp w walks keys
+// [w * kpw, (w + 1) * kpw) of the chunk 8 at a time:
+//   * scores S = Q K^T as one m16n8k16 tile per 16 dims: A = the G query
+//     heads (rows >= G zero), B = the decoded K rows.  K-step ks of lane
+//     (g, t) takes bytes 16 ks + 4t .. + 3 of key row g (cache rows are only
+//     4-byte aligned: 4-byte loads, 16 contiguous bytes per row and
+//     instruction), a fixed permutation of the head dimension applied
+//     identically to the query fragments;
+//   * online softmax per head on the score fragment (lane (g, t) holds head g
+//     at keys 2t, 2t+1; the 4 lanes of a head combine by two shuffles),
+//     probabilities rounded to BF16;
+//   * O^T += V^T P^T as 16 m16n8k8 tiles: A = the decoded V^T tile, B = P^T,
+//     which is exactly the score fragment (no data movement).  Lane (g, t)
+//     reads 4 bytes (dims 32 r + 4 g .. + 3) of key rows 2t and 2t+1 and
+//     packs the two keys per dimension; the 16 output tiles cover the
+//     dimensions in a permuted order that the merge undoes;
+//   * K and V bytes decode through one lane-replicated table (entry c: BF16 of
+//     decode(c) x k_scale in the low half, x v_scale in the high half, for
+//     the chunk's first row; conflict-free lookups).  When a row of the chunk
+//     carries another scale, the CTA runs the same loop with every byte
+//     decoded with its own row's scale, as the reference materialises BF16 K
+//     and V;
+//   * the next block's K rows are loaded after this block's scores and its V
+//     rows after this block's P @ V, so loads overlap the MMAs;
+//   * the 4 warps merge in shared memory into one partial (output, max, sum)
+//     per head, merged across chunks by attention_combine_kernel, or the
+//     output is written directly when one chunk covers the request.
 template <int G>
 __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArgs p) {
-  pdl_wait();  // inputs come from the previous kernel of the stream
   constexpr int D = kDecHead;
-  constexpr int W = D / 128;  // 4-byte K / V words per lane per row
-  __shared__ float lut[256], klut[256], vlut[256];
+  __shared__ uint32_t kvlut[256 * 32];  // the merge buffer afterwards
+  __shared__ float lut[256];
   __shared__ float ks0, vs0;
-  __shared__ int64_t rowoff[kDecChunk];
-  __shared__ float prob[G][kDecChunk];
-  __shared__ float mrow[G], lrow[G];
-  __shared__ __align__(16) float vsum[4][G][D];  // per-warp P @ V sums
+  __shared__ float wm[kDecWarps][G], wl[kDecWarps][G];
+  pdl_wait();  // the cache and the queries come from earlier kernels of the stream
   const int b = blockIdx.x / (int)p.kv_heads, h = blockIdx.x - b * (int)p.kv_heads;
   const int split = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
   const int q0 = p.q_start[b], q_len = p.q_start[b + 1] - q0;
   const int seq = p.seq_lens[b];
-  const int chunk0 = split * kDecChunk;
+  const int chunk0 = split * p.chunk;
   if (q_len <= 0 || chunk0 >= seq) return;  // the merge reads only chunks that hold keys
   const int64_t width = D + 4;
+  const int32_t *table = p.tables + (int64_t)b * p.max_blocks;
+  auto row_of = [&](int key) -> int64_t {  // -1: absent
+    const int64_t blk = key < seq ? page_of(table, key, p.block_size, p.max_blocks, p.num_blocks) : -1;
+    return blk >= 0 ? ((blk * p.block_size + key % p.block_size) * p.kv_heads + h) * width : -1;
+  };
   for (int i = tid; i < 256; i += kDecThreads) lut[i] = __uint_as_float(g_decode_f32.v[i]);
-  if (tid < kDecChunk) {
-    const int key = chunk0 + tid;
-    int64_t off = -1;
-    if (key < seq) {
-      const int64_t blk = page_of(p.tables + (int64_t)b * p.max_blocks, key, p.block_size, p.max_blocks,
-                                  p.num_blocks);
-      if (blk >= 0) off = ((blk * p.block_size + key % p.block_size) * p.kv_heads + h) * width;
-    }
-    rowoff[tid] = off;
-    if (tid == 0) {  // the chunk's reference scales (NaN: no table, every row computes)
-      ks0 = off >= 0 ? *reinterpret_cast<const float *>(p.kc + off + D) : CUDART_NAN_F;
-      vs0 = off >= 0 ? *reinterpret_cast<const float *>(p.vc + off + D) : CUDART_NAN_F;
-    }
+  // the chunk's reference scales (NaN: no table) and whether every row of
+  // the chunk carries them
+  float my_k[2], my_v[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int key = chunk0 + tid + kDecThreads * j;
+    const int64_t off = key < chunk0 + p.chunk ? row_of(key) : -1;
+    my_k[j] = off >= 0 ? __ldg(reinterpret_cast<const float *>(p.kc + off + D)) : 0.f;
+    my_v[j] = off >= 0 ? __ldg(reinterpret_cast<const float *>(p.vc + off + D)) : 0.f;
+    if (off < 0) my_k[j] = my_v[j] = CUDART_INF_F;  // marks "no row"
+  }
+  if (tid == 0) {
+    ks0 = my_k[0] == CUDART_INF_F ? CUDART_NAN_F : my_k[0];
+    vs0 = my_v[0] == CUDART_INF_F ? CUDART_NAN_F : my_v[0];
   }
   __syncthreads();
-  for (int i = tid; i < 256; i += kDecThreads) {
-    klut[i] = bf16_bits_to_f32(f32_to_bf16_bits(lut[i] * ks0));
-    vlut[i] = bf16_bits_to_f32(f32_to_bf16_bits(lut[i] * vs0));
-  }
-  __syncthreads();
+  const float k_ref = ks0, v_ref = vs0;
+  bool same = true;
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+    same = same && (my_k[j] == CUDART_INF_F || (my_k[j] == k_ref && my_v[j] == v_ref));
+  const bool table_ok = __syncthreads_and(same) != 0;
+  // warp w fills entries 64 w .. 64 w + 63: lane j computes entry 64 w + 32 i
+  // + j, then every entry is broadcast and stored as 32 consecutive words
+  auto fill_table = [&]() {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c0 = warp * 64 + i * 32;
+      const float dv = lut[c0 + lane];
+      const uint32_t mine = f32_to_bf16_bits(dv * k_ref) | (f32_to_bf16_bits(dv * v_ref) << 16);
+#pragma unroll 8
+      for (int j = 0; j < 32; ++j) kvlut[(c0 + j) * 32 + lane] = __shfl_sync(0xFFFFFFFFu, mine, j);
+    }
+    __syncthreads();
+  };
+  if (table_ok) fill_table();
+
+  const int kpw = p.chunk / kDecWarps;  // a multiple of 16
+  const int wk0 = chunk0 + warp * kpw;
+  const int n_keys = max(0, min(kpw, seq - wk0));
+  const int nblk = (n_keys + kDecBlock - 1) / kDecBlock;
 
   for (int r = 0; r < q_len; ++r) {
     const int64_t tok = q0 + r;
     const int limit = p.causal ? seq - q_len + r : seq - 1;  // last key this row sees
-    // query vectors: lane holds columns 4 (lane + 32 i) + e of every head g
-    float qv[G][4 * W];
+    // query fragments: k-step ks takes dims 16 ks + 4t + {0,1} (a0) and
+    // + {2,3} (a2) of head g; rows of heads >= G are zero
+    uint32_t qa[16][2];
+    {
+      const uint16_t *qrow = p.q + (tok * p.heads + (int64_t)h * G + (g < G ? g : 0)) * D;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const uint16_t *qrow = p.q + (tok * p.heads + (int64_t)h * G + g) * D;
-#pragma unroll
-      for (int i = 0; i < W; ++i) {
-        const uint2 v = *reinterpret_cast<const uint2 *>(qrow + 4 * (lane + 32 * i));
-        qv[g][4 * i + 0] = bf16_bits_to_f32(v.x & 0xFFFFu);
-        qv[g][4 * i + 1] = bf16_bits_to_f32(v.x >> 16);
-        qv[g][4 * i + 2] = bf16_bits_to_f32(v.y & 0xFFFFu);
-        qv[g][4 * i + 3] = bf16_bits_to_f32(v.y >> 16);
+      for (int ks = 0; ks < 16; ++ks) {
+        uint2 v = make_uint2(0, 0);
+        if (g < G) v = *reinterpret_cast<const uint2 *>(qrow + 16 * ks + 4 * t);
+        qa[ks][0] = v.x;
+        qa[ks][1] = v.y;
       }
     }
-    // ---- scores, kKB = 32 / G keys per batch: all the batch's row loads
-    // (read-only path, unconditional: an absent key reads row 0 of the cache,
-    // in bounds, and is masked afterwards) are issued before any arithmetic
-    // or shared-memory store, so they are in flight together.  The batch's
-    // 32 (key, head) partial dot products are then summed across the warp by
-    // a transpose-reduction: after 16 + 8 + 4 + 2 + 1 shuffles lane l holds
-    // the total of value l.
-    constexpr int kKB = 32 / G < kDecChunk / 4 ? 32 / G : kDecChunk / 4;
-    for (int j0 = 0; j0 < kDecChunk / 4; j0 += kKB) {
-      uint32_t kw[kKB][W];
-      float ks[kKB];
+    float o[16][4];
 #pragma unroll
-      for (int u = 0; u < kKB; ++u) {
-        const int k = warp + 4 * (j0 + u);
-        const int64_t off = rowoff[k];
-        const uint8_t *row = p.kc + (off >= 0 ? off : 0);
-        ks[u] = __ldg(reinterpret_cast<const float *>(row + D));
+    for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m_run = -CUDART_INF_F, l_run = 0.f;  // of head g
+
+    auto run = [&](auto tab_tag) {
+      constexpr bool TAB = decltype(tab_tag)::value;
+      uint32_t kr[16];    // K row g: word ks at bytes 16 ks + 4t
+      uint32_t vr[8][2];  // V rows 2t, 2t+1: word of dims 32 r + 4g .. + 3
+      float ksc = 0.f, vsc[2] = {0.f, 0.f};
+      int64_t koff = -1, voff[2] = {-1, -1};
+      uint32_t valid = 0;  // bit i: key i of the block is attended
+      auto offsets = [&](int blk) {
+        const int kk = blk * kDecBlock + (lane & 7);
+        const int64_t mine = kk < n_keys ? row_of(wk0 + kk) : -1;
+        valid = __ballot_sync(0xFFFFFFFFu, mine >= 0 && wk0 + kk <= limit) & 0xFFu;
+        const uint32_t lo = (uint32_t)(uint64_t)mine, hi = (uint32_t)((uint64_t)mine >> 32);
+        koff = (int64_t)(((uint64_t)__shfl_sync(0xFFFFFFFFu, hi, g) << 32) | __shfl_sync(0xFFFFFFFFu, lo, g));
 #pragma unroll
-        for (int i = 0; i < W; ++i) kw[u][i] = __ldg(reinterpret_cast<const unsigned int *>(row + 4 * (lane + 32 * i)));
+        for (int j = 0; j < 2; ++j)
+          voff[j] = (int64_t)(((uint64_t)__shfl_sync(0xFFFFFFFFu, hi, 2 * t + j) << 32) |
+                              __shfl_sync(0xFFFFFFFFu, lo, 2 * t + j));
+      };
+      // absent keys read row 0 (in bounds) and are masked
+      auto load_k = [&]() {
+        const uint8_t *row = p.kc + (koff >= 0 ? koff : 0);
+        if (!TAB) ksc = __ldg(reinterpret_cast<const float *>(row + D));
+#pragma unroll
+        for (int ks = 0; ks < 16; ++ks) kr[ks] = __ldg(reinterpret_cast<const unsigned int *>(row + 16 * ks + 4 * t));
+      };
+      auto load_v = [&]() {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const uint8_t *row = p.vc + (voff[j] >= 0 ? voff[j] : 0);
+          if (!TAB) vsc[j] = __ldg(reinterpret_cast<const float *>(row + D));
+#pragma unroll
+          for (int rr = 0; rr < 8; ++rr)
+            vr[rr][j] = __ldg(reinterpret_cast<const unsigned int *>(row + 32 * rr + 4 * g));
+        }
+      };
+      if (nblk > 0) {
+        offsets(0);
+        load_k();
+        load_v();
       }
-      float part[32];  // value u * G + g: key j0 + u, head g (unused values stay 0)
+      for (int blk = 0; blk < nblk; ++blk) {
+        const uint32_t cur_valid = valid;
+        // ---- scores of keys 0..7 of the block (B fragment = K^T: bytes 0,1 ->
+        // k-slots 2t, 2t+1; bytes 2,3 -> 2t+8, 2t+9)
+        float sa[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = kKB * G; i < 32; ++i) part[i] = 0.f;
+        for (int ks = 0; ks < 16; ++ks) {
+          const uint32_t w = kr[ks];
+          const uint32_t b0 = __byte_perm(kv_dec<TAB>(kvlut, lut, w, 0, lane, ksc, false),
+                                          kv_dec<TAB>(kvlut, lut, w, 1, lane, ksc, false), 0x7632u);
+          const uint32_t b1 = __byte_perm(kv_dec<TAB>(kvlut, lut, w, 2, lane, ksc, false),
+                                          kv_dec<TAB>(kvlut, lut, w, 3, lane, ksc, false), 0x7632u);
+          attn_mma16816(sa, qa[ks][0], qa[ks][1], b0, b1);
+        }
+        const bool more = blk + 1 < nblk;
+        if (more) {
+          offsets(blk + 1);
+          load_k();
+        }
+        // ---- online softmax of head g over keys 2t, 2t+1
+        float s0 = ((cur_valid >> (2 * t)) & 1u) ? sa[0] * p.scale : -CUDART_INF_F;
+        float s1 = ((cur_valid >> (2 * t + 1)) & 1u) ? sa[1] * p.scale : -CUDART_INF_F;
+        float mb = fmaxf(s0, s1);
+        mb = fmaxf(mb, __shfl_xor_sync(0xFFFFFFFFu, mb, 1));
+        mb = fmaxf(mb, __shfl_xor_sync(0xFFFFFFFFu, mb, 2));
+        const float m_new = fmaxf(m_run, mb);
+        const float alpha = m_run == -CUDART_INF_F ? 0.f : __expf(m_run - m_new);
+        const uint32_t p0 = s0 == -CUDART_INF_F ? 0u : f32_to_bf16_bits(__expf(s0 - m_new));
+        const uint32_t p1 = s1 == -CUDART_INF_F ? 0u : f32_to_bf16_bits(__expf(s1 - m_new));
+        float ps = bf16_bits_to_f32(p0) + bf16_bits_to_f32(p1);
+        ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 1);
+        ps += __shfl_xor_sync(0xFFFFFFFFu, ps, 2);
+        l_run = l_run * alpha + ps;
+        m_run = m_new;
+        // ---- O^T = alpha O^T + V^T P^T (columns: heads 2t, 2t+1)
+        const float al0 = __shfl_sync(0xFFFFFFFFu, alpha, 8 * t);
+        const float al1 = __shfl_sync(0xFFFFFFFFu, alpha, 8 * t + 4);
+        if (!__all_sync(0xFFFFFFFFu, al0 == 1.f && al1 == 1.f)) {
 #pragma unroll
-      for (int u = 0; u < kKB; ++u) {
-#pragma unroll
-        for (int g = 0; g < G; ++g) part[u * G + g] = 0.f;
-        if (ks[u] == ks0) {  // uniform across the warp
-#pragma unroll
-          for (int i = 0; i < W; ++i) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float kv = klut[(kw[u][i] >> (8 * e)) & 0xFFu];
-#pragma unroll
-              for (int g = 0; g < G; ++g) part[u * G + g] = fmaf(qv[g][4 * i + e], kv, part[u * G + g]);
-            }
+          for (int i = 0; i < 16; ++i) {
+            o[i][0] *= al0;
+            o[i][1] *= al1;
+            o[i][2] *= al0;
+            o[i][3] *= al1;
           }
+        }
+        const uint32_t pp = p0 | (p1 << 16);
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            // tile 2 rr + half: row g -> dim 32 rr + 4 g + 2 half, row g + 8 -> + 1
+            const uint32_t a0 = __byte_perm(kv_dec<TAB>(kvlut, lut, vr[rr][0], 2 * half, lane, vsc[0], true),
+                                            kv_dec<TAB>(kvlut, lut, vr[rr][1], 2 * half, lane, vsc[1], true),
+                                            0x7632u);
+            const uint32_t a1 = __byte_perm(kv_dec<TAB>(kvlut, lut, vr[rr][0], 2 * half + 1, lane, vsc[0], true),
+                                            kv_dec<TAB>(kvlut, lut, vr[rr][1], 2 * half + 1, lane, vsc[1], true),
+                                            0x7632u);
+            attn_mma1688(o[2 * rr + half], a0, a1, pp);
+          }
+        }
+        if (more) load_v();
+      }
+    };
+    if (table_ok) run(std::true_type{});
+    else run(std::false_type{});
+
+    // ---- merge the warps: lane 4 g (t = 0) owns head g's running max and sum
+    __syncthreads();  // every warp is done with the table: its space holds the merge
+    if (t == 0 && g < G) {
+      wm[warp][g] = m_run;
+      wl[warp][g] = l_run;
+    }
+    float *obuf = reinterpret_cast<float *>(kvlut);  // [kDecWarps][G][D]
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int d0 = 32 * rr + 4 * g + 2 * half;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int head = 2 * t + (q & 1), dim = d0 + (q >> 1);
+          if (head < G) obuf[(warp * G + head) * D + dim] = o[2 * rr + half][q];
+        }
+      }
+    __syncthreads();
+#pragma unroll
+    for (int hg = 0; hg < G; ++hg) {
+      float M = -CUDART_INF_F;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, wm[w][hg]);
+      float ew[kDecWarps], L = 0.f;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) {
+        ew[w] = wm[w][hg] == -CUDART_INF_F ? 0.f : __expf(wm[w][hg] - M);
+        L = fmaf(wl[w][hg], ew[w], L);
+      }
+      const int64_t head = (int64_t)h * G + hg;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int dim = tid + kDecThreads * k;
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < kDecWarps; ++w) acc = fmaf(obuf[(w * G + hg) * D + dim], ew[w], acc);
+        if (p.splits == 1) {
+          const float inv = L > 0.f ? 1.f / L : 0.f;
+          p.out[(tok * p.heads + head) * D + dim] = (uint16_t)f32_to_bf16_bits(acc * inv);
         } else {
-#pragma unroll
-          for (int i = 0; i < W; ++i) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float kv = bf16_bits_to_f32(f32_to_bf16_bits(lut[(kw[u][i] >> (8 * e)) & 0xFFu] * ks[u]));
-#pragma unroll
-              for (int g = 0; g < G; ++g) part[u * G + g] = fmaf(qv[g][4 * i + e], kv, part[u * G + g]);
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int half = 16; half > 0; half >>= 1) {
-        const bool upper = (lane & half) != 0;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-          const float send = upper ? part[i] : part[i + half];
-          const float keep = upper ? part[i + half] : part[i];
-          part[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, half);
-        }
-      }
-      // lane l = u * G + g now holds the score of key j0 + u, head g
-      {
-        const int u = lane / G, g = lane - u * G;
-        if (u < kKB) {
-          const int k = warp + 4 * (j0 + u);
-          const bool valid = rowoff[k] >= 0 && chunk0 + k <= limit;
-          prob[g][k] = valid ? part[0] * p.scale : -CUDART_INF_F;
-        }
-      }
-    }
-    __syncthreads();
-    // ---- softmax per head (warp w takes heads w, w + 4)
-    for (int g = warp; g < G; g += 4) {
-      float v[kDecChunk / 32];
-      float m = -CUDART_INF_F;
-#pragma unroll
-      for (int i = 0; i < kDecChunk / 32; ++i) {
-        v[i] = prob[g][lane + 32 * i];
-        m = fmaxf(m, v[i]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-      float l = 0.f;
-#pragma unroll
-      for (int i = 0; i < kDecChunk / 32; ++i) {
-        const float e = v[i] == -CUDART_INF_F ? 0.f : __expf(v[i] - m);
-        prob[g][lane + 32 * i] = e;
-        l += e;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
-      if (lane == 0) {
-        mrow[g] = m;
-        lrow[g] = l;
-      }
-    }
-    __syncthreads();
-    // ---- P @ V: warp w takes keys [32 w, 32 w + 32) and, like the K pass,
-    // lane columns 4 (lane + 32 i) + e; the four warps' sums meet in shared
-    // memory afterwards
-    float acc[G][4 * W];
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-      for (int c = 0; c < 4 * W; ++c) acc[g][c] = 0.f;
-    constexpr int kKeysPerWarp = kDecChunk / 4;
-    for (int j0 = 0; j0 < kKeysPerWarp; j0 += kDecBatch) {
-      uint32_t vw[kDecBatch][W];
-      float vs[kDecBatch];
-      bool valid[kDecBatch];
-#pragma unroll
-      for (int u = 0; u < kDecBatch; ++u) {
-        const int k = warp * kKeysPerWarp + j0 + u;
-        const int64_t off = rowoff[k];
-        valid[u] = off >= 0 && chunk0 + k <= limit;
-        const uint8_t *row = p.vc + (valid[u] ? off : 0);
-        vs[u] = __ldg(reinterpret_cast<const float *>(row + D));
-#pragma unroll
-        for (int i = 0; i < W; ++i) vw[u][i] = __ldg(reinterpret_cast<const unsigned int *>(row + 4 * (lane + 32 * i)));
-      }
-#pragma unroll
-      for (int u = 0; u < kDecBatch; ++u) {
-        if (!valid[u]) continue;
-        const int k = warp * kKeysPerWarp + j0 + u;
-        float pk[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) pk[g] = prob[g][k];
-        const bool table = vs[u] == vs0;
-#pragma unroll
-        for (int i = 0; i < W; ++i) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const uint32_t c = (vw[u][i] >> (8 * e)) & 0xFFu;
-            const float vv = table ? vlut[c] : bf16_bits_to_f32(f32_to_bf16_bits(lut[c] * vs[u]));
-#pragma unroll
-            for (int g = 0; g < G; ++g) acc[g][4 * i + e] = fmaf(pk[g], vv, acc[g][4 * i + e]);
+          float *dst = p.part + ((tok * p.heads + head) * p.splits + split) * part_stride(D);
+          dst[dim] = acc;
+          if (tid == 0 && k == 0) {
+            dst[D] = M;
+            dst[D + 1] = L;
           }
         }
       }
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-      for (int i = 0; i < W; ++i)
-        *reinterpret_cast<float4 *>(&vsum[warp][g][4 * (lane + 32 * i)]) =
-            make_float4(acc[g][4 * i], acc[g][4 * i + 1], acc[g][4 * i + 2], acc[g][4 * i + 3]);
-    __syncthreads();
-    // thread t finishes columns 2 t and 2 t + 1 of every head
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float o0 = 0.f, o1 = 0.f;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        o0 += vsum[w][g][2 * tid];
-        o1 += vsum[w][g][2 * tid + 1];
-      }
-      const int64_t head = (int64_t)h * G + g;
-      if (p.splits == 1) {
-        const float l = lrow[g];
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        uint16_t *dst = p.out + (tok * p.heads + head) * D;
-        *reinterpret_cast<uint32_t *>(dst + 2 * tid) = f32_to_bf16_bits(o0 * inv) | (f32_to_bf16_bits(o1 * inv) << 16);
-      } else {
-        float *dst = p.part + ((tok * p.heads + head) * p.splits + split) * part_stride(D);
-        dst[2 * tid] = o0;
-        dst[2 * tid + 1] = o1;
-        if (tid == 0) {
-          dst[D] = mrow[g];
-          dst[D + 1] = lrow[g];
-        }
-      }
-    }
-    __syncthreads();  // prob / mrow / lrow are reused by the next query row
+    __syncthreads();  // the buffer is rewritten by the table / the next row
+    if (r + 1 < q_len && table_ok) fill_table();
   }
 }
 
@@ -677,6 +733,45 @@ extern "C" int hif8_kv_cache_write(const void *key, const void *value, int src_d
 
 static int attn_nq(int64_t group, int64_t q_rows) { return (int)(group * q_rows); }
 
+// Resident decode CTAs per SM for GQA group g (cached per device).
+static int decode_residency(int64_t g) {
+  static std::atomic<int> cache[64][4];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  const int gi = g == 1 ? 0 : g == 2 ? 1 : g == 4 ? 2 : 3;
+  int v = cache[dev][gi].load(std::memory_order_relaxed);
+  if (v == 0) {
+    const void *k = gi == 0 ? reinterpret_cast<const void *>(paged_decode_kernel<1>)
+                    : gi == 1 ? reinterpret_cast<const void *>(paged_decode_kernel<2>)
+                    : gi == 2 ? reinterpret_cast<const void *>(paged_decode_kernel<4>)
+                              : reinterpret_cast<const void *>(paged_decode_kernel<8>);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, kDecThreads, 0) != cudaSuccess || v < 1) {
+      cudaGetLastError();
+      v = 1;
+    }
+    cache[dev][gi].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+// Keys per decode CTA: the multiple of 64 up to 256 that minimises waves of
+// resident CTAs x (keys per CTA + a fixed cost of ~32 keys for the table,
+// the query load and the merge); ties go to the smaller chunk.
+static int decode_chunk(int64_t group, int64_t seq_heads, int64_t max_seq_len) {
+  const int64_t slots = (int64_t)num_sms() * decode_residency(group);
+  int best = kDecChunk;
+  int64_t best_cost = -1;
+  for (int c = kDecChunk; c <= kDecMaxChunk; c += 64) {
+    const int64_t ctas = seq_heads * ((max_seq_len + c - 1) / c);
+    const int64_t cost = ((ctas + slots - 1) / slots) * (c + 32);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = c;
+    }
+  }
+  return best;
+}
+
 // Sized for the finer of the two kernels' key chunks (the decode kernel's).
 extern "C" size_t hif8_paged_attention_workspace_size(int64_t num_tokens, int64_t num_heads, int64_t head_size,
                                                       int64_t max_seq_len) {
@@ -719,7 +814,7 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
   const bool decode = num_tokens == batch && head_size == kDecHead &&
                       (group == 1 || group == 2 || group == 4 || group == 8) &&
                       (reinterpret_cast<uintptr_t>(query) & 7u) == 0 && (reinterpret_cast<uintptr_t>(out) & 3u) == 0;
-  const int chunk = decode ? kDecChunk : kAttnChunk;
+  const int chunk = decode ? decode_chunk(group, batch * kv_heads, max_seq_len) : kAttnChunk;
   const int64_t splits = max_seq_len > 0 ? (max_seq_len + chunk - 1) / chunk : 1;
   AttnArgs p{};
   p.q = query;
@@ -737,6 +832,7 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
   p.max_blocks = max_blocks;
   p.num_blocks = num_blocks;
   p.splits = (int)splits;
+  p.chunk = chunk;
   p.scale = softmax_scale;
   p.causal = causal;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

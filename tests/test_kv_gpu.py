@@ -89,7 +89,10 @@ def test_kv_write_rejects_out_of_range_slots():
     assert int(kc[0, 0].sum()) != 0 and int(kc[0, 1].sum()) != 0
 
 
-def _make_paged(batch, ctx, kv_heads, d, block, seed):
+def _make_paged(batch, ctx, kv_heads, d, block, seed, second_scale_every=0):
+    """Pages for `batch` requests of ctx[b] keys, scattered over a shuffled
+    block table.  With second_scale_every = n, every n-th row (i % n == n - 1)
+    is written with a second set of per-head scales."""
     rng = np.random.default_rng(seed)
     blocks_per = [(c + block - 1) // block for c in ctx]
     total_blocks = sum(blocks_per) + 3
@@ -107,8 +110,15 @@ def _make_paged(batch, ctx, kv_heads, d, block, seed):
         kx = rng.standard_normal((ctx[b], kv_heads, d)).astype(np.float32)
         vx = rng.standard_normal((ctx[b], kv_heads, d)).astype(np.float32)
         slots = np.array([table[b, i // block] * block + i % block for i in range(ctx[b])], np.int64)
-        oracle.kv_write(oracle.f32_to_bf16_bits(kx), ks, slots, kc)
-        oracle.kv_write(oracle.f32_to_bf16_bits(vx), vs, slots, vc)
+        if second_scale_every:
+            alt = (np.arange(ctx[b]) % second_scale_every) == second_scale_every - 1
+            for sel, kscale, vscale in ((~alt, ks, vs), (alt, ks * 1.75, vs * 0.6)):
+                if sel.any():
+                    oracle.kv_write(oracle.f32_to_bf16_bits(kx[sel]), kscale, slots[sel], kc)
+                    oracle.kv_write(oracle.f32_to_bf16_bits(vx[sel]), vscale, slots[sel], vc)
+        else:
+            oracle.kv_write(oracle.f32_to_bf16_bits(kx), ks, slots, kc)
+            oracle.kv_write(oracle.f32_to_bf16_bits(vx), vs, slots, vc)
     return kc, vc, table
 
 
@@ -130,6 +140,25 @@ def test_paged_decode_attention_config3(ctx_len):
     ctx = [ctx_len - 37 * b for b in range(batch)]
     kc, vc, table = _make_paged(batch, ctx, kv_heads, d, block, seed=ctx_len)
     q = oracle.round_bf16(np.random.default_rng(1).standard_normal((batch, heads, d)).astype(np.float32))
+    scale = 1.0 / math.sqrt(d)
+    expected = oracle.paged_attention(q, kc, vc, table, ctx, block_size=block, scale=scale)
+    out = kv.paged_attention(torch.from_numpy(q).to(torch.bfloat16).to(DEV), torch.from_numpy(kc).to(DEV),
+                             torch.from_numpy(vc).to(DEV), torch.from_numpy(table).to(DEV), ctx, scale=scale)
+    _check_attention(out, expected)
+
+
+@pytest.mark.parametrize("group", [1, 2, 8])
+def test_paged_decode_attention_groups_ragged_lengths_and_second_scale(group):
+    """The decode kernel for GQA groups 1, 2 and 8 over requests of 1, 3, 67
+    and 700 keys (one key, a partial round, one chunk, several chunks), with
+    every fifth row written under a second per-head scale (those rows are off
+    the chunk's scaled table and decode with their own scale)."""
+    kv = _kv()
+    kv_heads, d, block = 2, 256, 32
+    heads = kv_heads * group
+    ctx = [1, 3, 67, 700]
+    kc, vc, table = _make_paged(len(ctx), ctx, kv_heads, d, block, seed=11 + group, second_scale_every=5)
+    q = oracle.round_bf16(np.random.default_rng(3 + group).standard_normal((len(ctx), heads, d)).astype(np.float32))
     scale = 1.0 / math.sqrt(d)
     expected = oracle.paged_attention(q, kc, vc, table, ctx, block_size=block, scale=scale)
     out = kv.paged_attention(torch.from_numpy(q).to(torch.bfloat16).to(DEV), torch.from_numpy(kc).to(DEV),
