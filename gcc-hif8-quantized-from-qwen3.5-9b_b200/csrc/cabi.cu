@@ -62,6 +62,7 @@ int ensure_smem_limit(const void *kernel, size_t bytes) {
       if (e.bytes >= bytes) return HIF8_OK;
       const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
       if (err != cudaSuccess) {
+        cudaGetLastError();  // reported through the status; must not surface at the next launch check
         set_last_error(err);
         return HIF8_ERR_CUDA;
       }
@@ -71,6 +72,7 @@ int ensure_smem_limit(const void *kernel, size_t bytes) {
   }
   const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
   if (err != cudaSuccess) {
+    cudaGetLastError();  // reported through the status; must not surface at the next launch check
     set_last_error(err);
     return HIF8_ERR_CUDA;
   }

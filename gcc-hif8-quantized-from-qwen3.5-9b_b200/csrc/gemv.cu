@@ -35,6 +35,7 @@
 #include <mutex>
 #include <vector>
 
+#include "../../include/hif8_b200_model.h"
 #include "linear.cuh"
 
 namespace cg = cooperative_groups;
@@ -53,6 +54,34 @@ constexpr int kRedStride = 20;              // floats per token row of a warp pa
 constexpr int kActCodes = 0;  // HiF8 bytes
 constexpr int kActBf16 = 1;   // BF16, quantised in the prologue with ts[0]
 constexpr int kActF16 = 2;    // FP16, idem
+// BF16 produced in the prologue by a fused glue step (p.glue), then quantised
+constexpr int kActSiluMul = 3;
+constexpr int kActGateMul = 4;
+constexpr int kActRmsNorm = 5;
+
+template <int ASRC>
+__host__ __device__ constexpr bool act_is_glue() {
+  return ASRC == kActSiluMul || ASRC == kActGateMul || ASRC == kActRmsNorm;
+}
+
+// BF16 bits of the glue step for one element: x (and y: up / gate /
+// residual, w: norm weight) are BF16 bits; the arithmetic and its roundings
+// are those of the separate model kernels (silu_mul, gate_mul, rmsnorm).
+template <int ASRC>
+__device__ __forceinline__ uint32_t glue_value(uint32_t x, uint32_t y, uint32_t w, float inv, bool has_y,
+                                               bool one_plus) {
+  if constexpr (ASRC == kActSiluMul) {
+    return f32_to_bf16_bits(glue_silu(bf16_bits_to_f32(x)) * bf16_bits_to_f32(y));
+  } else if constexpr (ASRC == kActGateMul) {
+    return f32_to_bf16_bits(bf16_bits_to_f32(x) * glue_sigmoid(bf16_bits_to_f32(y)));
+  } else {
+    float v = bf16_bits_to_f32(x);
+    if (has_y) v = bf16_bits_to_f32(f32_to_bf16_bits(v + bf16_bits_to_f32(y)));  // BF16 residual stream
+    float ww = bf16_bits_to_f32(w);
+    if (one_plus) ww += 1.f;
+    return f32_to_bf16_bits(v * inv * ww);
+  }
+}
 
 struct U32x8 {
   uint32_t v[8];
@@ -182,6 +211,9 @@ template <int NT, int OUT, int ASRC>
 __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p, const GemvPlan plan) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int kTok = 8 * NT;
+  constexpr bool kGlue = act_is_glue<ASRC>();
+  constexpr int QSRC = kGlue ? kActBf16 : ASRC;  // element type the quantiser sees
+  __shared__ float norm_part[kWarps][8], norm_inv[8];  // kActRmsNorm: per-token sums / inverse RMS
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int S = plan.s, kc = plan.kc, WK = plan.wk, WR = plan.wr;
   const int rank = (int)(blockIdx.x % S), cluster_id = (int)(blockIdx.x / S);
@@ -226,6 +258,46 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
     // everything above reads constants only; the activations and scales may
     // come from the previous kernel of the stream
     pdl_wait();
+    if constexpr (ASRC == kActRmsNorm) {
+      // inverse RMS of every token's full row (x + residual), identical in
+      // every CTA; CTA 0 also writes the new BF16 residual stream
+      const uint16_t *xa = static_cast<const uint16_t *>(p.a);
+      const uint16_t *res = p.glue.aux;
+      const bool write_res = res && p.glue.residual_out && blockIdx.x == 0;
+      const int mt0 = p.m < kTok ? p.m : kTok;
+      for (int tok = 0; tok < mt0; ++tok) {
+        float ss = 0.f;
+        for (int c = tid * 8; c < p.k; c += kThreads * 8) {
+          const uint4 xv = *reinterpret_cast<const uint4 *>(xa + (int64_t)tok * p.k + c);
+          uint4 rv = make_uint4(0, 0, 0, 0);
+          if (res) rv = *reinterpret_cast<const uint4 *>(res + (int64_t)tok * p.k + c);
+          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, rw[4] = {rv.x, rv.y, rv.z, rv.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float lo = bf16_bits_to_f32(xw[i] & 0xFFFFu), hi = bf16_bits_to_f32(xw[i] >> 16);
+            if (res) {
+              lo = bf16_bits_to_f32(f32_to_bf16_bits(lo + bf16_bits_to_f32(rw[i] & 0xFFFFu)));
+              hi = bf16_bits_to_f32(f32_to_bf16_bits(hi + bf16_bits_to_f32(rw[i] >> 16)));
+            }
+            o[i] = f32_to_bf16_bits(lo) | (f32_to_bf16_bits(hi) << 16);
+            ss += lo * lo + hi * hi;
+          }
+          if (write_res)
+            *reinterpret_cast<uint4 *>(p.glue.residual_out + (int64_t)tok * p.k + c) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+        if (lane == 0) norm_part[warp][tok] = ss;
+      }
+      __syncthreads();
+      if (tid < mt0) {
+        float tsum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) tsum += norm_part[w][tid];
+        norm_inv[tid] = rsqrtf(tsum / (float)p.k + p.glue.eps);
+      }
+    }
     __syncthreads();
     const int chunks_per_tok = kc >> 4;  // 16 K values per chunk
     const int real = (p.m < kTok ? p.m : kTok) * chunks_per_tok;
@@ -239,20 +311,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
       const uint32_t re = __float_as_uint(r) & 0x7F800000u;
       exact_only = (re == 0u) | (re == 0x7F800000u);
     }
-    // four chunks per thread and round: their global loads are issued first
-    for (int base = 0; base < total_chunks; base += 4 * kThreads) {
-      uint4 raw[4][2];
+    // kPro chunks per thread and round: their global loads are issued first
+    constexpr int kPro = kGlue ? 2 : 4;
+    const int64_t a_stride = ASRC == kActSiluMul ? 2 * (int64_t)p.k : (int64_t)p.k;
+    for (int base = 0; base < total_chunks; base += kPro * kThreads) {
+      uint4 raw[kPro][2], aux[kPro][2], nw[kPro][2];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kPro; ++u) {
         const int i = base + u * kThreads + tid;
-        raw[u][0] = raw[u][1] = make_uint4(0, 0, 0, 0);
+        raw[u][0] = raw[u][1] = aux[u][0] = aux[u][1] = nw[u][0] = nw[u][1] = make_uint4(0, 0, 0, 0);
         if (i < real) {
           const int tok = i / chunks_per_tok, ch = i - tok * chunks_per_tok;
           if (ASRC != kActCodes) {
             const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p.a) +
-                                                               (int64_t)tok * p.k + k0 + ch * 16);
+                                                               (int64_t)tok * a_stride + k0 + ch * 16);
             raw[u][0] = src[0];
             raw[u][1] = src[1];
+            if constexpr (kGlue) {
+              const uint4 *asrc =
+                  ASRC == kActSiluMul ? src + p.k / 8  // up half of the gate_up row
+                  : p.glue.aux ? reinterpret_cast<const uint4 *>(p.glue.aux + (int64_t)tok * p.k + k0 + ch * 16)
+                               : nullptr;
+              if (asrc) {
+                aux[u][0] = asrc[0];
+                aux[u][1] = asrc[1];
+              }
+              if (ASRC == kActRmsNorm) {
+                const uint4 *wsrc = reinterpret_cast<const uint4 *>(p.glue.norm_w + k0 + ch * 16);
+                nw[u][0] = wsrc[0];
+                nw[u][1] = wsrc[1];
+              }
+            }
           } else {
             raw[u][0] = *reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.a) + (int64_t)tok * p.k +
                                                          k0 + ch * 16);
@@ -260,20 +349,33 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
         }
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < kPro; ++u) {
         const int i = base + u * kThreads + tid;
         if (i >= total_chunks) break;
         const int tok = i / chunks_per_tok, ch = i - tok * chunks_per_tok;
         uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
         if (i < real) {
           if (ASRC != kActCodes) {
-            const uint32_t h8[8] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w,
-                                    raw[u][1].x, raw[u][1].y, raw[u][1].z, raw[u][1].w};
+            uint32_t h8[8] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w,
+                              raw[u][1].x, raw[u][1].y, raw[u][1].z, raw[u][1].w};
+            if constexpr (kGlue) {
+              const uint32_t y8[8] = {aux[u][0].x, aux[u][0].y, aux[u][0].z, aux[u][0].w,
+                                      aux[u][1].x, aux[u][1].y, aux[u][1].z, aux[u][1].w};
+              const uint32_t w8[8] = {nw[u][0].x, nw[u][0].y, nw[u][0].z, nw[u][0].w,
+                                      nw[u][1].x, nw[u][1].y, nw[u][1].z, nw[u][1].w};
+              const float inv = ASRC == kActRmsNorm ? norm_inv[tok] : 1.f;
+              const bool has_y = ASRC == kActSiluMul || p.glue.aux != nullptr;
+              const bool one_plus = p.glue.one_plus != 0;
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                h8[j] = glue_value<ASRC>(h8[j] & 0xFFFFu, y8[j] & 0xFFFFu, w8[j] & 0xFFFFu, inv, has_y, one_plus) |
+                        (glue_value<ASRC>(h8[j] >> 16, y8[j] >> 16, w8[j] >> 16, inv, has_y, one_plus) << 16);
+            }
             uint32_t r8[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              r8[j] = fake_quant_bf16_smem<ASRC>(h8[j] & 0xFFFFu, s, r, exact_only, enc, lut, lane) |
-                      (fake_quant_bf16_smem<ASRC>(h8[j] >> 16, s, r, exact_only, enc, lut, lane) << 16);
+              r8[j] = fake_quant_bf16_smem<QSRC>(h8[j] & 0xFFFFu, s, r, exact_only, enc, lut, lane) |
+                      (fake_quant_bf16_smem<QSRC>(h8[j] >> 16, s, r, exact_only, enc, lut, lane) << 16);
             o0 = make_uint4(r8[0], r8[1], r8[2], r8[3]);
             o1 = make_uint4(r8[4], r8[5], r8[6], r8[7]);
           } else {
@@ -471,9 +573,26 @@ static bool aligned32(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 constexpr size_t kMaxSmem = 227 * 1024;
 
+// Dynamic shared memory a kernel may request: the per-block limit less its
+// static shared memory (cached per kernel).
+static size_t dyn_smem_cap(const void *kernel) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void *, size_t>> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto &e : cache)
+    if (e.first == kernel) return e.second;
+  cudaFuncAttributes attr{};
+  size_t cap = kMaxSmem;
+  if (cudaFuncGetAttributes(&attr, kernel) == cudaSuccess) cap = kMaxSmem - std::min(kMaxSmem, attr.sharedSizeBytes);
+  else cudaGetLastError();
+  cache.push_back({kernel, cap});
+  return cap;
+}
+
 // Clusters of `s` CTAs of `kernel` that can be resident at once (cached per
 // device, kernel, cluster size and shared-memory size).
-static int max_active_clusters(const void *kernel, int s, size_t smem) {
+static int max_active_clusters(const void *kernel, int s, size_t smem_request) {
+  const size_t smem = std::min(smem_request, dyn_smem_cap(kernel));
   struct Entry {
     const void *kernel;
     int device, s;
@@ -530,12 +649,13 @@ static GemvPlan plan_gemv(int64_t m, int64_t n, int64_t k, const void *kernel) {
     const int64_t items = (n + 16 * wr - 1) / (16 * wr);
     // shared memory is sized for the worst case of sms / s clusters
     const int64_t rounds_max = (items + (sms / s) - 1) / (sms / s);
+    const size_t cap = dyn_smem_cap(kernel);
     const size_t smem = gemv_smem_bytes(nt, (int)kc, wr, s > 1 ? (int)std::max<int64_t>(rounds_max, items) : 0);
-    if (gemv_smem_bytes(nt, (int)kc, wr, 0) > kMaxSmem) continue;
-    const int clusters = max_active_clusters(kernel, s, std::min(smem, kMaxSmem));
+    if (gemv_smem_bytes(nt, (int)kc, wr, 0) > cap) continue;
+    const int clusters = max_active_clusters(kernel, s, std::min(smem, cap));
     if (clusters < 1) continue;
     const int64_t rounds = (items + clusters - 1) / clusters;
-    if (gemv_smem_bytes(nt, (int)kc, wr, s > 1 ? (int)rounds : 0) > kMaxSmem) continue;
+    if (gemv_smem_bytes(nt, (int)kc, wr, s > 1 ? (int)rounds : 0) > cap) continue;
     // fraction of the machine's CTA-rounds doing useful work
     const double eff = (double)items / (double)(rounds * clusters) * (double)(clusters * s) / (double)sms;
     if (eff > best_eff + 1e-9) {
@@ -653,6 +773,36 @@ int run_fused_linear(const GemvArgs &args, int x_dtype, int output_dtype, cudaSt
                   : launch_gemv<1, HIF8_DTYPE_F16, kActF16>(args, plan, stream);
 }
 
+// Glue + static quant + linear for m <= 8 BF16 rows (decode steps of the
+// model): only the persistent kernel has the glue prologue, so a shape it
+// cannot plan is refused rather than computed another way.
+int run_glue_linear(const GemvArgs &args, cudaStream_t stream) {
+  const GlueArgs &gl = args.glue;
+  if (args.m < 1 || args.m > 8 || args.k % 256 != 0 || !aligned16(args.a) || !aligned32(args.w))
+    return HIF8_ERR_INVALID_ARGUMENT;
+  if ((gl.aux && !aligned16(gl.aux)) || (gl.norm_w && !aligned16(gl.norm_w)) ||
+      (gl.residual_out && !aligned16(gl.residual_out)))
+    return HIF8_ERR_INVALID_ARGUMENT;
+  switch (gl.kind) {
+    case kGlueSiluMul: {
+      const GemvPlan plan = plan_gemv(args.m, args.n, args.k, gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActSiluMul>());
+      return plan.s ? launch_gemv<1, HIF8_DTYPE_BF16, kActSiluMul>(args, plan, stream) : HIF8_ERR_INVALID_ARGUMENT;
+    }
+    case kGlueGateMul: {
+      if (!gl.aux) return HIF8_ERR_INVALID_ARGUMENT;
+      const GemvPlan plan = plan_gemv(args.m, args.n, args.k, gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActGateMul>());
+      return plan.s ? launch_gemv<1, HIF8_DTYPE_BF16, kActGateMul>(args, plan, stream) : HIF8_ERR_INVALID_ARGUMENT;
+    }
+    case kGlueRmsNorm: {
+      if (!gl.norm_w) return HIF8_ERR_INVALID_ARGUMENT;
+      const GemvPlan plan = plan_gemv(args.m, args.n, args.k, gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActRmsNorm>());
+      return plan.s ? launch_gemv<1, HIF8_DTYPE_BF16, kActRmsNorm>(args, plan, stream) : HIF8_ERR_INVALID_ARGUMENT;
+    }
+    default:
+      return HIF8_ERR_INVALID_ARGUMENT;
+  }
+}
+
 static int validate_linear(const void *a, const uint8_t *w, const float *ts, const float *cs, const void *bias,
                            int bias_dtype, int output_dtype, int64_t m, int64_t n, int64_t k, void *out) {
   if (!a || !w || !ts || !cs || !out) return HIF8_ERR_INVALID_ARGUMENT;
@@ -713,4 +863,21 @@ extern "C" int soft_hif8_static_fused_gemm(const void *x, int x_dtype, const uin
   GemvArgs args{x, weight, fixed_scale, channel_scale, bias, out, (int)m, (int)n, (int)k, 0,
                 bias ? bias_dtype : HIF8_DTYPE_NONE, 0};
   return run_fused_linear(args, x_dtype, output_dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hif8_model_glue_linear(const uint16_t *x, const Hif8GlueArgs *glue, int64_t m, int64_t k,
+                                      const uint8_t *weight, const float *fixed_scale, const float *channel_scale,
+                                      int64_t n, uint16_t *out, void *stream) {
+  if (!x || !glue || !weight || !fixed_scale || !channel_scale || !out || m <= 0 || n <= 0 || k <= 0 ||
+      n > 0x7FFFFFFFLL || k > 0x7FFFFFFFLL)
+    return HIF8_ERR_INVALID_ARGUMENT;
+  GemvArgs args{x, weight, fixed_scale, channel_scale, nullptr, out, (int)m, (int)n, (int)k, 0,
+                HIF8_DTYPE_NONE, 0};
+  args.glue.kind = glue->kind;
+  args.glue.aux = glue->aux;
+  args.glue.residual_out = glue->residual_out;
+  args.glue.norm_w = glue->norm_w;
+  args.glue.eps = glue->eps;
+  args.glue.one_plus = glue->one_plus;
+  return run_glue_linear(args, static_cast<cudaStream_t>(stream));
 }

@@ -161,6 +161,11 @@ __device__ __forceinline__ uint32_t f32_to_half_bits(float v) {
   else return f32_to_f16_bits(v);
 }
 
+// Elementwise producers shared by the model glue kernels and the GEMV
+// prologue that fuses them (one definition, so both round identically).
+__device__ __forceinline__ float glue_silu(float x) { return x / (1.f + __expf(-x)); }
+__device__ __forceinline__ float glue_sigmoid(float x) { return 1.f / (1.f + __expf(-x)); }
+
 // --------------------------------------------------------- error plumbing --
 
 void set_last_error(cudaError_t err);

@@ -6,6 +6,22 @@
 
 namespace hif8 {
 
+// Producer of the fused linear's activation, applied in the prologue before
+// the static quantisation (decode-step glue of the synthetic decoder).
+constexpr int kGlueNone = 0;
+constexpr int kGlueSiluMul = 1;  // silu(x[:, :k]) * x[:, k:2k], x row stride 2k
+constexpr int kGlueGateMul = 2;  // x * sigmoid(aux)
+constexpr int kGlueRmsNorm = 3;  // RMSNorm(x + aux) * (one_plus ? 1 + w : w); aux may be null
+
+struct GlueArgs {
+  int kind = kGlueNone;
+  const uint16_t *aux = nullptr;     // gate (kGlueGateMul) / residual (kGlueRmsNorm)
+  uint16_t *residual_out = nullptr;  // kGlueRmsNorm with aux: x + aux (BF16), written by CTA 0
+  const uint16_t *norm_w = nullptr;  // kGlueRmsNorm: [k]
+  float eps = 0.f;
+  int one_plus = 0;
+};
+
 struct GemvArgs {
   const void *a;          // [M, K]: HiF8 bytes, or FP16/BF16 for the fused quant path
   const uint8_t *w;       // [N, K]
@@ -17,6 +33,7 @@ struct GemvArgs {
   int kc;                 // K range per CTA (multiple of 64)
   int bias_dtype;
   int ts_stride;          // 1: one token scale per row; 0: one shared fixed scale
+  GlueArgs glue;          // fused activation producer (BF16 glue kernels only)
 };
 
 bool hif8_gemm_tc_supported(int64_t m, int64_t n, int64_t k);

@@ -17,8 +17,8 @@ namespace hif8 {
 
 __device__ __forceinline__ float bf(uint16_t h) { return bf16_bits_to_f32(h); }
 __device__ __forceinline__ uint16_t to_bf(float v) { return (uint16_t)f32_to_bf16_bits(v); }
-__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
-__device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + __expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return glue_silu(x); }
+__device__ __forceinline__ float sigmoid(float x) { return glue_sigmoid(x); }
 
 // Sum over the CTA (blockDim.x a multiple of 32, at most 1024).
 __device__ __forceinline__ float block_sum(float v, float *scratch) {

@@ -358,6 +358,59 @@ std::tuple<at::Tensor, at::Tensor> ModelRmsnorm(const at::Tensor &x, const std::
   return {out, res_in ? res_out : x};
 }
 
+// Decode-step projection with its glue fused into the quantisation prologue
+// (hif8_model_glue_linear): kind 1 silu_mul (x = gate_up [m, 2k]), 2
+// gate_mul (aux = gate), 3 rmsnorm (aux = residual or None, norm_w).
+// Returns (out [m, n] BF16, new residual: x + aux for kind 3 with aux, else x).
+std::tuple<at::Tensor, at::Tensor> ModelGlueLinear(const at::Tensor &x, const std::optional<at::Tensor> &aux,
+                                                   const std::optional<at::Tensor> &norm_w, int64_t kind, double eps,
+                                                   bool one_plus, const at::Tensor &weight,
+                                                   const at::Tensor &fixed_scale, const at::Tensor &weight_scale) {
+  CheckModelTensor(x, "x", at::kBFloat16);
+  CheckModelTensor(weight, "weight", at::kByte, 32);
+  CheckModelTensor(fixed_scale, "fixed_scale", at::kFloat, 4);
+  CheckModelTensor(weight_scale, "weight_scale", at::kFloat, 4);
+  TORCH_CHECK(kind >= 1 && kind <= 3, "glue kind must be 1 (silu_mul), 2 (gate_mul) or 3 (rmsnorm)");
+  TORCH_CHECK(weight.dim() == 2, "weight must be 2D");
+  const int64_t width = x.size(-1), rows = x.numel() / width;
+  const int64_t k = kind == 1 ? width / 2 : width;
+  TORCH_CHECK(kind != 1 || width % 2 == 0, "gate_up width must be even");
+  TORCH_CHECK(weight.size(1) == k, "weight K ", weight.size(1), " does not match the activation's ", k);
+  TORCH_CHECK(fixed_scale.numel() == 1, "fixed_scale must hold one value");
+  TORCH_CHECK(weight_scale.numel() == weight.size(0), "weight_scale must hold one value per output channel");
+  Hif8GlueArgs g{};
+  g.kind = (int)kind;
+  g.eps = (float)eps;
+  g.one_plus = one_plus ? 1 : 0;
+  at::Tensor res_out = x;
+  if (aux.has_value()) {
+    CheckModelTensor(*aux, "aux", at::kBFloat16);
+    TORCH_CHECK(kind != 1, "silu_mul takes no aux tensor");
+    TORCH_CHECK(aux->sizes() == x.sizes(), "aux must match x");
+    g.aux = Bits(*aux);
+    if (kind == 3) {
+      res_out = at::empty_like(x);
+      g.residual_out = MutBits(res_out);
+    }
+  } else {
+    TORCH_CHECK(kind != 2, "gate_mul needs the gate as aux");
+  }
+  if (kind == 3) {
+    TORCH_CHECK(norm_w.has_value(), "rmsnorm needs norm_w");
+    CheckModelTensor(*norm_w, "norm_w", at::kBFloat16);
+    TORCH_CHECK(norm_w->numel() == k, "norm_w must have one value per column");
+    g.norm_w = Bits(*norm_w);
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  auto sizes = x.sizes().vec();
+  sizes.back() = weight.size(0);
+  auto out = at::empty(sizes, x.options());
+  CheckStatus(hif8_model_glue_linear(Bits(x), &g, rows, k, weight.data_ptr<uint8_t>(), fixed_scale.data_ptr<float>(),
+                                     weight_scale.data_ptr<float>(), weight.size(0), MutBits(out), Stream(x)),
+              "hif8_model_glue_linear");
+  return {out, res_out};
+}
+
 at::Tensor ModelSiluMul(const at::Tensor &gate_up) {
   CheckModelTensor(gate_up, "gate_up", at::kBFloat16, 4);
   const int64_t two_i = gate_up.size(-1), rows = gate_up.numel() / two_i;
@@ -564,6 +617,8 @@ TORCH_LIBRARY(hif8_b200, m) {
   // glue of the synthetic decoder
   m.def("rmsnorm(Tensor x, Tensor? residual, Tensor weight, float eps, bool one_plus) -> (Tensor, Tensor)");
   m.def("silu_mul(Tensor gate_up) -> Tensor");
+  m.def("glue_linear(Tensor x, Tensor? aux, Tensor? norm_w, int kind, float eps, bool one_plus, Tensor weight, "
+        "Tensor fixed_scale, Tensor weight_scale) -> (Tensor, Tensor)");
   m.def("gate_mul(Tensor x, Tensor gate) -> Tensor");
   m.def("attn_prep(Tensor qkv, Tensor positions, Tensor q_norm_w, Tensor k_norm_w, int heads, int kv_heads, "
         "int head_dim, int rotary_dim, float eps, float rope_theta) -> (Tensor, Tensor, Tensor, Tensor)");
@@ -580,6 +635,7 @@ TORCH_LIBRARY_IMPL(hif8_b200, CUDA, m) {
   m.impl("kv_gather_decode", &Hif8KvGatherDecode);
   m.impl("rmsnorm", &ModelRmsnorm);
   m.impl("silu_mul", &ModelSiluMul);
+  m.impl("glue_linear", &ModelGlueLinear);
   m.impl("gate_mul", &ModelGateMul);
   m.impl("attn_prep", &ModelAttnPrep);
   m.impl("gdn", &ModelGdn);

@@ -289,6 +289,15 @@ class Decoder:
         self._graphs: dict[int, tuple] = {}
         self.peer: PeerReducer | None = None  # decode-step all-reduce over peer memory (enable_peer_allreduce)
         self._fused_reduce = False
+        # Glue kernels fused into the prologue of the GEMV they feed on decode
+        # steps ("rmsnorm", "silu_mul", "gate_mul").  Every CTA of the fused
+        # GEMV recomputes the glue for its K slice, so only the residual +
+        # RMSNorm of single-row steps pays off (measured on B200 at the 9B
+        # shape: batch 1 +3.7 % tok/s; at batch 4 and for the elementwise glue
+        # the fused prologue costs as much as or more than the launch it saves).
+        self.fuse_glue = {"rmsnorm"}
+        self.fuse_glue_max_rows = 1
+        self._fuse_glue = False
         self._site = 0
 
     def enable_peer_allreduce(self):
@@ -363,12 +372,29 @@ class Decoder:
             self._record(tag, x)
         return lin(x)
 
-    def _attention(self, i, L, h, batch: int, T: int, positions, seq_lens, slots):
-        """h [batch * T, hidden] -> attention output [batch * T, hidden]."""
+    def _glue(self, kind: int, x, aux, lin, norm_w=None):
+        """Decode-step projection with its glue (1 silu_mul, 2 gate_mul, 3
+        residual + RMSNorm) fused into the quantisation prologue of the GEMV:
+        (out, new residual)."""
+        import torch
+
+        return torch.ops.hif8_b200.glue_linear(x, aux, norm_w, kind, self.cfg.eps, True, lin.weight, lin.input_scale,
+                                               lin.weight_scale)
+
+    def _norm_proj(self, tag, x, residual, norm_w, lin):
+        """First projection of a block on RMSNorm(x + residual): one fused
+        launch on decode steps without a peer reduce, else norm then
+        projection.  Returns (projection, new residual)."""
+        if self._fuse_glue and "rmsnorm" in self.fuse_glue and not self._fused_reduce:
+            return self._glue(3, x, residual, lin, norm_w)
+        h, residual = self._norm(x, residual, norm_w)
+        return self._proj(tag, lin, h), residual
+
+    def _attention(self, i, L, qkv, batch: int, T: int, positions, seq_lens, slots):
+        """qkv projection [batch * T, ...] -> attention output [batch * T, hidden]."""
         import torch
 
         c = self.cfg
-        qkv = self._proj(f"{i}.qkv", L["qkv"], h)
         q, gate, k, v = torch.ops.hif8_b200.attn_prep(qkv, positions, L["q_norm"], L["k_norm"], self.heads,
                                                       self.kv_local, c.head_dim, c.rotary_dim, c.eps, c.rope_theta)
         if self.calib_amax is not None:  # per global KV head
@@ -397,22 +423,25 @@ class Decoder:
             attn = torch.nn.functional.scaled_dot_product_attention(qh, keys, vals, attn_mask=mask, scale=scale,
                                                                     enable_gqa=True)
             attn = attn.transpose(1, 2).reshape(batch * T, self.heads, c.head_dim)
-        out = torch.ops.hif8_b200.gate_mul(attn.reshape(batch * T, -1).contiguous(), gate)
+        attn = attn.reshape(batch * T, -1).contiguous()
+        if self._fuse_glue and "gate_mul" in self.fuse_glue:
+            return self._all_reduce(self._glue(2, attn, gate, L["o"])[0])
+        out = torch.ops.hif8_b200.gate_mul(attn, gate)
         return self._all_reduce(self._proj(f"{i}.o", L["o"], out))
 
-    def _gdn(self, i, L, h, batch: int, T: int):
+    def _gdn(self, i, L, proj, batch: int, T: int):
         import torch
 
-        proj = self._proj(f"{i}.lin_in", L["lin_in"], h)
         core = torch.ops.hif8_b200.gdn(proj, T, self.hk, self.hv, L["conv_w"], L["a_log"], L["dt_bias"],
                                        L["gdn_norm"], self.conv_state[i][:batch], self.rec_state[i][:batch],
                                        self.cfg.eps)
         return self._all_reduce(self._proj(f"{i}.lin_out", L["lin_out"], core))
 
-    def _mlp(self, i, L, h):
+    def _mlp(self, i, L, gu):
         import torch
 
-        gu = self._proj(f"{i}.gate_up", L["gate_up"], h)
+        if self._fuse_glue and "silu_mul" in self.fuse_glue:
+            return self._all_reduce(self._glue(1, gu, None, L["down"])[0])
         act = torch.ops.hif8_b200.silu_mul(gu)
         return self._all_reduce(self._proj(f"{i}.down", L["down"], act))
 
@@ -423,22 +452,27 @@ class Decoder:
 
         c = self.cfg
         self._fused_reduce = self.peer is not None and T == 1 and batch <= self.max_batch
+        # decode steps fuse the glue kernels into the GEMV prologues
+        self._fuse_glue = (self.mode == "hif8" and T == 1 and batch <= self.fuse_glue_max_rows
+                           and self.calib_amax is None)
         self._site = 0
         x = self.embed.index_select(0, tokens)
         residual = None
         for i, L in enumerate(self.layers):
-            h, residual = self._norm(x, residual, L["in_w"])
             if L["full"]:
-                x = self._attention(i, L, h, batch, T, positions, seq_lens, slots)
+                qkv, residual = self._norm_proj(f"{i}.qkv", x, residual, L["in_w"], L["qkv"])
+                x = self._attention(i, L, qkv, batch, T, positions, seq_lens, slots)
             else:
-                x = self._gdn(i, L, h, batch, T)
-            h, residual = self._norm(x, residual, L["post_w"])
-            x = self._mlp(i, L, h)
+                proj, residual = self._norm_proj(f"{i}.lin_in", x, residual, L["in_w"], L["lin_in"])
+                x = self._gdn(i, L, proj, batch, T)
+            gu, residual = self._norm_proj(f"{i}.gate_up", x, residual, L["post_w"], L["gate_up"])
+            x = self._mlp(i, L, gu)
         if T > 1:
             last = torch.arange(batch, device=self.device) * T + (T - 1)
             x, residual = x.index_select(0, last).contiguous(), residual.index_select(0, last).contiguous()
         h, _ = self._norm(x, residual, self.final_w)
         self._fused_reduce = False
+        self._fuse_glue = False
         return torch.nn.functional.linear(h, self.lm_head).float()
 
     def argmax(self, logits):

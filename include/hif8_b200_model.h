@@ -67,6 +67,37 @@ typedef struct Hif8GdnArgs {
 
 int hif8_model_gdn(const Hif8GdnArgs *args, int64_t batch, void *stream);
 
+/* ---- glue fused into the decode-step projection --------------------------
+ * One launch of the fused static quant + GEMV (rows m <= 8, k % 256 == 0,
+ * weight 32-byte aligned, BF16 tensors 16-byte aligned, BF16 out [m, n])
+ * whose quantised activation is produced in its prologue:
+ *   HIF8_GLUE_SILU_MUL: silu(x[:, :k]) * x[:, k:2k]              (x [m, 2k])
+ *   HIF8_GLUE_GATE_MUL: x * sigmoid(aux)                         (x, aux [m, k])
+ *   HIF8_GLUE_RMSNORM:  RMSNorm(x + aux) * (one_plus ? 1 + w : w) (aux may be
+ *                       NULL; with aux, residual_out (may be NULL) receives
+ *                       the BF16 sum x + aux)
+ * each rounded to BF16 exactly as the separate glue kernels above round it
+ * (the RMSNorm's sum of squares is reduced in another order), then encoded
+ * with fixed_scale[0] as hif8_static_quant does and multiplied with the HiF8
+ * weight as soft_hif8_static_fused_gemm does.  Shapes the persistent kernel
+ * cannot plan return HIF8_ERR_INVALID_ARGUMENT. */
+#define HIF8_GLUE_SILU_MUL 1
+#define HIF8_GLUE_GATE_MUL 2
+#define HIF8_GLUE_RMSNORM 3
+
+typedef struct Hif8GlueArgs {
+  int kind;
+  const uint16_t *aux;     /* gate (GATE_MUL) / residual (RMSNORM) */
+  uint16_t *residual_out;  /* RMSNORM: x + aux */
+  const uint16_t *norm_w;  /* RMSNORM: [k] */
+  float eps;
+  int one_plus;
+} Hif8GlueArgs;
+
+int hif8_model_glue_linear(const uint16_t *x, const Hif8GlueArgs *glue, int64_t m, int64_t k,
+                           const uint8_t *weight, const float *fixed_scale, const float *channel_scale,
+                           int64_t n, uint16_t *out, void *stream);
+
 /* ---- tensor-parallel all-reduce fused with residual + RMSNorm ----------
  * Replaces NCCL all-reduce + RMSNorm after every row-parallel projection of
  * a decode step.  Every rank owns one device buffer (hif8_peer_alloc) that

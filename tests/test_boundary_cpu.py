@@ -61,7 +61,7 @@ def test_model_glue_header_symbols_are_exported():
     names = re.findall(r"^\s*int\s+(\w+)\s*\(", text, flags=re.M)
     assert set(names) == {"hif8_model_rmsnorm", "hif8_model_silu_mul", "hif8_model_gate_mul",
                           "hif8_model_attn_prep", "hif8_model_gdn", "hif8_model_peer_allreduce_rmsnorm",
-                          "hif8_peer_alloc", "hif8_peer_open", "hif8_peer_close"}
+                          "hif8_model_glue_linear", "hif8_peer_alloc", "hif8_peer_open", "hif8_peer_close"}
     lib = cabi.library()
     for name in names:
         assert hasattr(lib, name), f"{name} is declared in include/hif8_b200_model.h but not exported"
@@ -71,7 +71,7 @@ def test_model_glue_ops_are_registered():
     from hif8_b200 import kv_cache
 
     kv_cache.load_ops()
-    for op in ("rmsnorm", "silu_mul", "gate_mul", "attn_prep", "gdn", "peer_allreduce_rmsnorm"):
+    for op in ("rmsnorm", "silu_mul", "gate_mul", "glue_linear", "attn_prep", "gdn", "peer_allreduce_rmsnorm"):
         assert hasattr(torch.ops.hif8_b200, op)
 
 

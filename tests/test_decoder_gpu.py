@@ -155,6 +155,63 @@ def test_gated_delta_net_matches_recurrent_reference(T):
     assert torch.allclose(cs, ref_conv, rtol=0, atol=1e-6)
 
 
+def _hif8_weight(n, k, seed):
+    from hif8_b200 import scheme
+
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    w = (torch.randn(n, k, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    data, scale = scheme.quantize_weight_rows(w)
+    return data, scale, torch.tensor([3.0 / 32768.0], device=DEV)
+
+
+@pytest.mark.parametrize("m", [1, 4])
+def test_glue_linear_silu_and_gate_equal_the_separate_kernels(m):
+    """SiLU-mul and sigmoid-gate fused into the GEMV prologue give the same
+    bits as the glue kernel followed by the fused quant + GEMV."""
+    from hif8_b200 import native
+
+    ops = _ops()
+    k, n = 1024, 768
+    data, scale, fixed = _hif8_weight(n, k, 11 + m)
+    g = torch.Generator(device=DEV).manual_seed(12 + m)
+    gu = torch.randn(m, 2 * k, device=DEV, generator=g).to(torch.bfloat16)
+    fused, _ = ops.glue_linear(gu, None, None, 1, 0.0, False, data, fixed, scale)
+    ref = native.soft_static_fused_linear(ops.silu_mul(gu), data, fixed, scale, None, output_dtype=torch.bfloat16)
+    assert torch.equal(fused, ref)
+    x = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    gate = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    fused, _ = ops.glue_linear(x, gate, None, 2, 0.0, False, data, fixed, scale)
+    ref = native.soft_static_fused_linear(ops.gate_mul(x, gate), data, fixed, scale, None, output_dtype=torch.bfloat16)
+    assert torch.equal(fused, ref)
+
+
+@pytest.mark.parametrize("m,n", [(1, 1024), (3, 1024), (1, 12352)])
+def test_glue_linear_rmsnorm_matches_norm_then_linear(m, n):
+    """Residual + RMSNorm fused into the GEMV prologue: the new residual
+    stream is bit-exact; the projection matches RMSNorm followed by the fused
+    quant + GEMV within 1e-2 of max |y| (the sum of squares is reduced in
+    another order, so an activation can land on a neighbouring code)."""
+    from hif8_b200 import native
+
+    ops = _ops()
+    k = 4096  # n = 12352: the gated-delta-net input projection of the 9B shape
+    data, scale, fixed = _hif8_weight(n, k, 21 + m)
+    g = torch.Generator(device=DEV).manual_seed(22 + m)
+    x = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    res = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(k, device=DEV, generator=g) * 0.1).to(torch.bfloat16)
+    fused, new_res = ops.glue_linear(x, res, w, 3, 1e-6, True, data, fixed, scale)
+    h, ref_res = ops.rmsnorm(x, res, w, 1e-6, True)
+    ref = native.soft_static_fused_linear(h, data, fixed, scale, None, output_dtype=torch.bfloat16)
+    assert torch.equal(new_res, ref_res)
+    assert _rel(fused, ref) <= 1e-2
+    fused0, same = ops.glue_linear(x, None, w, 3, 1e-6, True, data, fixed, scale)
+    h0, _ = ops.rmsnorm(x, None, w, 1e-6, True)
+    assert same.data_ptr() == x.data_ptr()
+    ref0 = native.soft_static_fused_linear(h0, data, fixed, scale, None, output_dtype=torch.bfloat16)
+    assert _rel(fused0, ref0) <= 1e-2
+
+
 def _tiny_cfg():
     from hif8_b200.decoder import DecoderConfig
 
@@ -182,11 +239,30 @@ def test_tiny_decoder_hif8_tracks_bf16_twin_and_graph_matches_eager():
     cos = torch.nn.functional.cosine_similarity(lh, lb, dim=-1)
     assert float(cos.min()) > 0.95, f"HiF8 vs BF16 logits cosine {cos.tolist()}"
 
+    # a decode step with the glue fused into the GEMV prologues tracks the
+    # step with separate glue kernels
+    hif8.reset()
+    first = hif8.prefill(prompt)
+    state = [t.clone() for t in hif8.conv_state + hif8.rec_state if t is not None]
+    pos = torch.full((2,), 40, dtype=torch.int32, device=DEV)
+    policy = hif8.fuse_glue, hif8.fuse_glue_max_rows
+    with torch.no_grad():
+        hif8.fuse_glue, hif8.fuse_glue_max_rows = {"rmsnorm", "silu_mul", "gate_mul"}, 8
+        fused = hif8.forward(first, pos, 2, 1, pos + 1, hif8._slots(2, pos))
+        for t, s0 in zip([t for t in hif8.conv_state + hif8.rec_state if t is not None], state):
+            t.copy_(s0)
+        hif8.fuse_glue = set()
+        plain = hif8.forward(first, pos, 2, 1, pos + 1, hif8._slots(2, pos))
+    hif8.fuse_glue, hif8.fuse_glue_max_rows = policy
+    cos = torch.nn.functional.cosine_similarity(fused, plain, dim=-1)
+    assert float(cos.min()) > 0.999, f"fused vs separate glue logits cosine {cos.tolist()}"
+
     # one decode step: CUDA graph replay == eager step, from the same state
-    for model in (hif8, twin):
-        graph, tokens, pos = model.decode_graph(2)
+    # (batch 1 runs the fused residual + RMSNorm GEMV prologues)
+    for model, batch in ((hif8, 2), (hif8, 1), (twin, 2)):
+        graph, tokens, pos = model.decode_graph(batch)
         model.reset()
-        first = model.prefill(prompt)
+        first = model.prefill(prompt[:batch])
         state = [t.clone() for t in model.conv_state + model.rec_state if t is not None]
         tokens.copy_(first)
         pos.fill_(40)
@@ -196,8 +272,8 @@ def test_tiny_decoder_hif8_tracks_bf16_twin_and_graph_matches_eager():
         for t, s in zip([t for t in model.conv_state + model.rec_state if t is not None], state):
             t.copy_(s)
         e_tokens = first.clone()
-        e_pos = torch.full((2,), 40, dtype=torch.int32, device=DEV)
+        e_pos = torch.full((batch,), 40, dtype=torch.int32, device=DEV)
         with torch.no_grad():
-            model._decode_step(2, e_tokens, e_pos)
-        assert torch.equal(graph_tokens, e_tokens), model.mode
+            model._decode_step(batch, e_tokens, e_pos)
+        assert torch.equal(graph_tokens, e_tokens), (model.mode, batch)
         model.release_graphs()
