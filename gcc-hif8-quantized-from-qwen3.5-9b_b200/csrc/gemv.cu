@@ -107,11 +107,6 @@ __device__ __forceinline__ int act_offset(int kk) {
   return b * 256 + tq * 64 + (((c + 2 * (tq >> 1)) & 3) << 4);
 }
 
-// Bulk prefetch of `bytes` (multiple of 16; p 16-byte aligned) into L2.
-__device__ __forceinline__ void prefetch_l2(const uint8_t *p, int bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 __device__ __forceinline__ uint32_t lut_lookup(const uint8_t *lut, uint32_t word, uint32_t lane4, uint32_t sel) {
   return *reinterpret_cast<const uint32_t *>(lut + __byte_perm(word, lane4, sel));
 }
@@ -231,33 +226,97 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   const int my_items = n_items > cluster_id ? (n_items - cluster_id + plan.clusters - 1) / plan.clusters : 0;
   const int kw0 = k0 + wk * kWarpK;  // this warp's K offset inside every item
 
+  auto weight_ptrs = [&](int item, const uint8_t *&w0, const uint8_t *&w1) {
+    const int row = (cluster_id + item * plan.clusters) * rows_per_item + wr * 16 + g;
+    const int r0 = min(row, p.n - 1), r1 = min(row + 8, p.n - 1);
+    w0 = p.w + (int64_t)r0 * p.k + kw0 + t * 32;
+    w1 = p.w + (int64_t)r1 * p.k + kw0 + t * 32;
+  };
+
+  // Every global read of the prologue may depend on the previous kernel of
+  // the stream (its activations, or weights it has just written), so all of
+  // them follow the dependency wait.  The independent loads -- the two
+  // tables' sources, the first round of activations and this warp's first
+  // item of weights, in that order -- are all issued before any of them is
+  // used, so their latencies overlap instead of adding up.
+  pdl_wait();
+  U32x8 ring[kRing][2];
+
   // ---- prologue: lane-replicated decode table + this rank's activation slice
   {
     uint32_t *lut = reinterpret_cast<uint32_t *>(smem);
-    // warp w owns table entries 16 w .. 16 w + 15: one global load per lane,
-    // then each entry is broadcast and written as 32 consecutive words
-    {
-      const uint32_t mine = g_decode_f32.v[warp * 16 + (lane & 15)] >> 16;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) lut[(warp * 16 + j) * 64 + lane] = __shfl_sync(0xFFFFFFFFu, mine, j);
-    }
-    // the fused quantiser's 8 KB encode table, staged in the reduction buffer
-    // (idle until the first item is reduced)
     uint8_t *enc = reinterpret_cast<uint8_t *>(red);
+    // warp w owns table entries 16 w .. 16 w + 15 (one load per lane); the
+    // fused quantiser's 8 KB encode table is staged in the reduction buffer
+    // (idle until the first item is reduced), one 16-byte piece per thread
+    const uint32_t mine = g_decode_f32.v[warp * 16 + (lane & 15)] >> 16;
+    static_assert(kThreads == 512, "one encode-table piece per thread");
+    uint4 enc_piece = make_uint4(0, 0, 0, 0);
+    float ts0 = 1.f;  // the fused quantiser's fixed scale
     if (ASRC != kActCodes) {
-      for (int i = tid; i < 512; i += kThreads)
-        reinterpret_cast<uint4 *>(enc)[i] = reinterpret_cast<const uint4 *>(g_static_encode.v)[i];
+      enc_piece = reinterpret_cast<const uint4 *>(g_static_encode.v)[tid];
+      ts0 = p.ts[0];
     }
-    // the first item's weight rows of this warp into L2 (256 bytes per row)
-    if (my_items > 0 && t == 0) {
-      const int row = cluster_id * rows_per_item + wr * 16 + g;
-      const int r0 = min(row, p.n - 1), r1 = min(row + 8, p.n - 1);
-      prefetch_l2(p.w + (int64_t)r0 * p.k + kw0, kWarpK);
-      prefetch_l2(p.w + (int64_t)r1 * p.k + kw0, kWarpK);
+    const int chunks_per_tok = kc >> 4;  // 16 K values per chunk
+    const int real = (p.m < kTok ? p.m : kTok) * chunks_per_tok;
+    const int total_chunks = kTok * chunks_per_tok;
+    // kPro chunks per thread and round: a round's global loads are issued
+    // before its arithmetic (the first round's before the table stores)
+    constexpr int kPro = kGlue ? 2 : 4;
+    const int64_t a_stride = ASRC == kActSiluMul ? 2 * (int64_t)p.k : (int64_t)p.k;
+    uint4 raw[kPro][2], aux[kPro][2], nw[kPro][2];
+    auto load_round = [&](int base) {
+#pragma unroll
+      for (int u = 0; u < kPro; ++u) {
+        const int i = base + u * kThreads + tid;
+        raw[u][0] = raw[u][1] = aux[u][0] = aux[u][1] = nw[u][0] = nw[u][1] = make_uint4(0, 0, 0, 0);
+        if (i < real) {
+          const int tok = i / chunks_per_tok, ch = i - tok * chunks_per_tok;
+          if (ASRC != kActCodes) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p.a) +
+                                                               (int64_t)tok * a_stride + k0 + ch * 16);
+            raw[u][0] = src[0];
+            raw[u][1] = src[1];
+            if constexpr (kGlue) {
+              const uint4 *asrc =
+                  ASRC == kActSiluMul ? src + p.k / 8  // up half of the gate_up row
+                  : p.glue.aux ? reinterpret_cast<const uint4 *>(p.glue.aux + (int64_t)tok * p.k + k0 + ch * 16)
+                               : nullptr;
+              if (asrc) {
+                aux[u][0] = asrc[0];
+                aux[u][1] = asrc[1];
+              }
+              if (ASRC == kActRmsNorm) {
+                const uint4 *wsrc = reinterpret_cast<const uint4 *>(p.glue.norm_w + k0 + ch * 16);
+                nw[u][0] = wsrc[0];
+                nw[u][1] = wsrc[1];
+              }
+            }
+          } else {
+            raw[u][0] = *reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.a) + (int64_t)tok * p.k +
+                                                         k0 + ch * 16);
+          }
+        }
+      }
+    };
+    load_round(0);
+    // the first item's weights last: the table and activation reads (L2
+    // hits) must not queue behind these HBM reads
+    if (my_items > 0) {
+      const uint8_t *w0, *w1;
+      weight_ptrs(0, w0, w1);
+#pragma unroll
+      for (int st = 0; st < kRing; ++st) {
+        ring[st][0] = ldg_stream32(w0 + st * kBlk);
+        ring[st][1] = ldg_stream32(w1 + st * kBlk);
+      }
     }
-    // everything above reads constants only; the activations and scales may
-    // come from the previous kernel of the stream
-    pdl_wait();
+
+    // table stores
+#pragma unroll
+    for (int j = 0; j < 16; ++j) lut[(warp * 16 + j) * 64 + lane] = __shfl_sync(0xFFFFFFFFu, mine, j);
+    if (ASRC != kActCodes) reinterpret_cast<uint4 *>(enc)[tid] = enc_piece;
+
     if constexpr (ASRC == kActRmsNorm) {
       // inverse RMS of every token's full row (x + residual), identical in
       // every CTA; CTA 0 also writes the new BF16 residual stream
@@ -299,55 +358,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
       }
     }
     __syncthreads();
-    const int chunks_per_tok = kc >> 4;  // 16 K values per chunk
-    const int real = (p.m < kTok ? p.m : kTok) * chunks_per_tok;
-    const int total_chunks = kTok * chunks_per_tok;
     const uint32_t lane4 = (uint32_t)lane << 2;
     float s = 1.f, r = 1.f;
     bool exact_only = false;
     if (ASRC != kActCodes) {
-      s = p.ts[0];
+      s = ts0;
       r = __frcp_rn(s);
       const uint32_t re = __float_as_uint(r) & 0x7F800000u;
       exact_only = (re == 0u) | (re == 0x7F800000u);
     }
-    // kPro chunks per thread and round: their global loads are issued first
-    constexpr int kPro = kGlue ? 2 : 4;
-    const int64_t a_stride = ASRC == kActSiluMul ? 2 * (int64_t)p.k : (int64_t)p.k;
     for (int base = 0; base < total_chunks; base += kPro * kThreads) {
-      uint4 raw[kPro][2], aux[kPro][2], nw[kPro][2];
-#pragma unroll
-      for (int u = 0; u < kPro; ++u) {
-        const int i = base + u * kThreads + tid;
-        raw[u][0] = raw[u][1] = aux[u][0] = aux[u][1] = nw[u][0] = nw[u][1] = make_uint4(0, 0, 0, 0);
-        if (i < real) {
-          const int tok = i / chunks_per_tok, ch = i - tok * chunks_per_tok;
-          if (ASRC != kActCodes) {
-            const uint4 *src = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p.a) +
-                                                               (int64_t)tok * a_stride + k0 + ch * 16);
-            raw[u][0] = src[0];
-            raw[u][1] = src[1];
-            if constexpr (kGlue) {
-              const uint4 *asrc =
-                  ASRC == kActSiluMul ? src + p.k / 8  // up half of the gate_up row
-                  : p.glue.aux ? reinterpret_cast<const uint4 *>(p.glue.aux + (int64_t)tok * p.k + k0 + ch * 16)
-                               : nullptr;
-              if (asrc) {
-                aux[u][0] = asrc[0];
-                aux[u][1] = asrc[1];
-              }
-              if (ASRC == kActRmsNorm) {
-                const uint4 *wsrc = reinterpret_cast<const uint4 *>(p.glue.norm_w + k0 + ch * 16);
-                nw[u][0] = wsrc[0];
-                nw[u][1] = wsrc[1];
-              }
-            }
-          } else {
-            raw[u][0] = *reinterpret_cast<const uint4 *>(static_cast<const uint8_t *>(p.a) + (int64_t)tok * p.k +
-                                                         k0 + ch * 16);
-          }
-        }
-      }
+      if (base > 0) load_round(base);
 #pragma unroll
       for (int u = 0; u < kPro; ++u) {
         const int i = base + u * kThreads + tid;
@@ -405,24 +426,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   bool tok_real[NT];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) tok_real[nt] = nt * 8 + g < p.m;
-
-  auto weight_ptrs = [&](int item, const uint8_t *&w0, const uint8_t *&w1) {
-    const int row = (cluster_id + item * plan.clusters) * rows_per_item + wr * 16 + g;
-    const int r0 = min(row, p.n - 1), r1 = min(row + 8, p.n - 1);
-    w0 = p.w + (int64_t)r0 * p.k + kw0 + t * 32;
-    w1 = p.w + (int64_t)r1 * p.k + kw0 + t * 32;
-  };
-
-  U32x8 ring[kRing][2];
-  if (my_items > 0) {
-    const uint8_t *w0, *w1;
-    weight_ptrs(0, w0, w1);
-#pragma unroll
-    for (int s = 0; s < kRing; ++s) {
-      ring[s][0] = ldg_stream32(w0 + s * kBlk);
-      ring[s][1] = ldg_stream32(w1 + s * kBlk);
-    }
-  }
 
   cg::cluster_group cluster = cg::this_cluster();
   for (int item = 0; item < my_items; ++item) {
@@ -516,8 +519,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
     const int item = e / per_item, rem = e - item * per_item;
     const int m = rem / rows_per_item, rl = rem - m * rows_per_item;
     const size_t idx = (size_t)item * rows_per_item * kTok + rem;
+    // every rank's partial is loaded before the sum (S <= 8), which then
+    // runs in rank order
+    float pv[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) pv[r] = r < S ? cluster.map_shared_rank(part, r)[idx] : 0.f;
     float v = 0.f;
-    for (int r = 0; r < S; ++r) v += cluster.map_shared_rank(part, r)[idx];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < S) v += pv[r];
     const int n = (cluster_id + item * plan.clusters) * rows_per_item + rl;
     if (n < p.n) {
       v = v * __ldg(p.cs + n);
