@@ -98,7 +98,14 @@ def reset_extension_cache() -> None:
     _reset_loader()
 
 
+_OPS: dict = {}
+
+
 def _op(name: str):
+    """The registered operator (resolved once per name)."""
+    operator = _OPS.get(name)
+    if operator is not None:
+        return operator
     import torch
 
     extension = load_extension()
@@ -107,6 +114,7 @@ def _op(name: str):
         operator = getattr(extension, name, None)
     if not callable(operator):
         raise NativeExtensionUnavailable(f"the native extension has no {name} operator")
+    _OPS[name] = operator
     return operator
 
 
