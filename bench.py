@@ -765,6 +765,7 @@ def measure_e2e(calls, args, device, world) -> dict:
 
 def run_profile_case(spec: str, launches: int) -> None:
     """Small cases for ncu captures, nothing else of the bench:
+    ``decode:<batch>`` runs one eager decode step of the configs[4] model;
     ``gemv:<shape>:<m>`` / ``gemm:<shape>:<m>`` run the linear kernel of one
     call ``launches`` times (two warm-up launches first); ``gemv:sweep`` runs
     each of the 15 configs[1] calls once after a read-based L2 eviction, M <= 4
@@ -774,6 +775,29 @@ def run_profile_case(spec: str, launches: int) -> None:
     from hif8_b200 import native, scheme
 
     parts = spec.split(":")
+    if parts[0] == "decode" and len(parts) == 2:
+        # one eager decode step of the configs[4] model at batch B between
+        # cudaProfilerStart/Stop (for `ncu --profile-from-start off`)
+        from hif8_b200.decoder import Decoder, DecoderConfig, calibrate
+
+        dev = torch.device("cuda", 0)
+        batch = int(parts[1])
+        cfg = DecoderConfig()
+        calib = calibrate(cfg, dev, seed=0, tokens=64)
+        model = Decoder(cfg, "hif8", dev, seed=0, max_batch=batch, max_ctx=768, calibration=calib)
+        g = torch.Generator(device=dev).manual_seed(1)
+        first = model.prefill(torch.randint(0, cfg.vocab, (batch, 512), device=dev, generator=g))
+        pos = torch.full((batch,), 512, dtype=torch.int32, device=dev)
+        with torch.no_grad():
+            for _ in range(2):
+                model._decode_step(batch, first.clone(), pos.clone())
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+            model._decode_step(batch, first.clone(), pos.clone())
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+        print(f"profile case {spec}: one decode step ok")
+        return
     if parts[0] == "attn" and len(parts) == 2:
         import math
 
