@@ -180,8 +180,9 @@ __global__ void attn_prep_kernel(const uint16_t *__restrict__ qkv, int heads, in
 // head's q, k, v.  The call walks the sequence's T tokens in order (T = 1
 // for a decode step).  Projection row layout (local heads):
 // [q: hk*128 | k: hk*128 | v: hv*128 | z: hv*128 | b: hv | a: hv].  q/k
-// channels are shared by the hv/hk value heads of a key head; every CTA of
-// the group computes them and the first writes their convolution state.
+// channels are shared by the hv/hk value heads of a key head; the
+// convolution state is kept per value head, [batch, hv, {q, k, v}, 128, 3],
+// so every CTA reads and rewrites only its own head's history.
 constexpr int kGdnDim = 128;
 constexpr int kGdnThreads = 2 * kGdnDim;
 constexpr int kGdnRows = kGdnDim / 2;  // state rows per thread
@@ -193,7 +194,6 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_kernel(const Hif8GdnArgs p) {
   const int vh = blockIdx.x, b = blockIdx.y;
   const int j = threadIdx.x >> 1, h = threadIdx.x & 1;
   const int ratio = p.hv / p.hk, kh = vh / ratio;
-  const bool owner = (vh % ratio) == 0;
   const int64_t C = 2LL * p.hk * kGdnDim + (int64_t)p.hv * kGdnDim;
   const int64_t cq = (int64_t)kh * kGdnDim + j, ck = (int64_t)p.hk * kGdnDim + cq;
   const int64_t cv = 2LL * p.hk * kGdnDim + (int64_t)vh * kGdnDim + j;
@@ -206,12 +206,14 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_kernel(const Hif8GdnArgs p) {
     wk[i] = bf(p.conv_w[ck * 4 + i]);
     wv[i] = bf(p.conv_w[cv * 4 + i]);
   }
-  float *cs_b = p.conv_state + (int64_t)b * C * 3;
+  // this head's convolution state: [q | k | v] x 128 channels x 3 taps
+  float *cs_h = p.conv_state + ((int64_t)b * p.hv + vh) * 3 * kGdnDim * 3;
+  float *cs_q = cs_h + j * 3, *cs_k = cs_h + (kGdnDim + j) * 3, *cs_v = cs_h + (2 * kGdnDim + j) * 3;
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
-    sq[i] = cs_b[cq * 3 + i];
-    sk[i] = cs_b[ck * 3 + i];
-    sv[i] = cs_b[cv * 3 + i];
+    sq[i] = cs_q[i];
+    sk[i] = cs_k[i];
+    sv[i] = cs_v[i];
   }
   float *st = p.rec_state + (((int64_t)b * p.hv + vh) * kGdnDim + (int64_t)h * kGdnRows) * kGdnDim + j;
   float S[kGdnRows];
@@ -271,11 +273,9 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_kernel(const Hif8GdnArgs p) {
   if (h == 0) {
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
-      if (owner) {
-        cs_b[cq * 3 + i] = sq[i];
-        cs_b[ck * 3 + i] = sk[i];
-      }
-      cs_b[cv * 3 + i] = sv[i];
+      cs_q[i] = sq[i];
+      cs_k[i] = sk[i];
+      cs_v[i] = sv[i];
     }
   }
 }

@@ -473,7 +473,7 @@ at::Tensor ModelGdn(const at::Tensor &proj, int64_t T, int64_t hk, int64_t hv, c
   TORCH_CHECK(T > 0 && proj.size(0) % T == 0, "proj rows must be a multiple of T");
   const int64_t batch = proj.size(0) / T;
   TORCH_CHECK(conv_w.numel() == channels * 4, "conv_w must be [channels, 4]");
-  TORCH_CHECK(conv_state.numel() == batch * channels * 3, "conv_state must be [batch, channels, 3]");
+  TORCH_CHECK(conv_state.numel() == batch * hv * 3 * 128 * 3, "conv_state must be [batch, hv, 3, 128, 3]");
   TORCH_CHECK(rec_state.numel() == batch * hv * 128 * 128, "rec_state must be [batch, hv, 128, 128]");
   c10::cuda::CUDAGuard guard(proj.device());
   auto out = at::empty({proj.size(0), hv * 128}, proj.options());

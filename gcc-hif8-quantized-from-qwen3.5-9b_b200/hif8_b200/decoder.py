@@ -312,8 +312,8 @@ class Decoder:
         import torch
 
         c, B, dev = self.cfg, self.max_batch, self.device
-        chan = 2 * self.hk * c.lin_dim + self.hv * c.lin_dim
-        self.conv_state = [torch.zeros(B, chan, c.conv - 1, device=dev) if not L["full"] else None
+        # per value head: the convolution history of its q, k and v channels
+        self.conv_state = [torch.zeros(B, self.hv, 3, c.lin_dim, c.conv - 1, device=dev) if not L["full"] else None
                            for L in self.layers]
         self.rec_state = [torch.zeros(B, self.hv, c.lin_dim, c.lin_dim, device=dev) if not L["full"] else None
                           for L in self.layers]

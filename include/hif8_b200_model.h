@@ -47,8 +47,10 @@ int hif8_model_attn_prep(const uint16_t *qkv, int64_t tokens, int heads, int kv_
 /* Gated delta net over T tokens of every sequence (T = 1: one decode step).
  * proj rows (batch * T of them, proj_stride elements apart) hold
  * [q: hk*128 | k: hk*128 | v: hv*128 | z: hv*128 | b: hv | a: hv];
- * conv_state [batch, 2*hk*128 + hv*128, 3] and rec_state [batch, hv, 128,
- * 128] (FP32) are read and updated in place; out [batch * T, hv * 128]. */
+ * conv_state [batch, hv, 3, 128, 3] (per value head: the causal-convolution
+ * history of its key head's q and k channels and of its own v channels) and
+ * rec_state [batch, hv, 128, 128] (FP32) are read and updated in place;
+ * out [batch * T, hv * 128]. */
 typedef struct Hif8GdnArgs {
   const uint16_t *proj;
   int64_t proj_stride;

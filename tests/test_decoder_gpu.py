@@ -133,11 +133,26 @@ def _gdn_ref(proj, T, hk, hv, conv_w, a_log, dt_bias, norm_w, conv_state, rec_st
     return out.reshape(B * T, hv * d), new_conv, S
 
 
-@pytest.mark.parametrize("T", [1, 7])
-def test_gated_delta_net_matches_recurrent_reference(T):
+def _per_head_conv_state(state, hk, hv, d=128):
+    """[B, 2 hk d + hv d, 3] (one history per projection channel) -> the
+    kernel's [B, hv, 3, d, 3] (per value head: its key head's q and k
+    channels and its own v channels)."""
+    ratio = hv // hk
+    heads = []
+    for vh in range(hv):
+        kh = vh // ratio
+        q = state[:, kh * d:(kh + 1) * d]
+        k = state[:, hk * d + kh * d:hk * d + (kh + 1) * d]
+        v = state[:, 2 * hk * d + vh * d:2 * hk * d + (vh + 1) * d]
+        heads.append(torch.stack([q, k, v], dim=1))
+    return torch.stack(heads, dim=1).contiguous()
+
+
+@pytest.mark.parametrize("T,B", [(1, 2), (7, 2), (1, 5)])
+def test_gated_delta_net_matches_recurrent_reference(T, B):
     ops = _ops()
-    hk, hv, B, d = 2, 4, 2, 128
-    g = torch.Generator(device=DEV).manual_seed(3 + T)
+    hk, hv, d = 2, 4, 128
+    g = torch.Generator(device=DEV).manual_seed(3 + T + B)
     C = 2 * hk * d + hv * d
     proj = torch.randn(B * T, C + hv * d + 2 * hv, device=DEV, generator=g).to(torch.bfloat16)
     conv_w = (torch.rand(C, 4, device=DEV, generator=g) - 0.5).to(torch.bfloat16)
@@ -148,11 +163,11 @@ def test_gated_delta_net_matches_recurrent_reference(T):
     rec_state = torch.randn(B, hv, d, d, device=DEV, generator=g) * 0.1
     ref_out, ref_conv, ref_S = _gdn_ref(proj, T, hk, hv, conv_w, a_log, dt_bias, norm_w, conv_state, rec_state,
                                         1e-6)
-    cs, rs = conv_state.clone(), rec_state.clone()
+    cs, rs = _per_head_conv_state(conv_state, hk, hv), rec_state.clone()
     out = ops.gdn(proj, T, hk, hv, conv_w, a_log, dt_bias, norm_w, cs, rs, 1e-6)
     assert _rel(out, ref_out) <= 2e-2
     assert _rel(rs, ref_S) <= 1e-3
-    assert torch.allclose(cs, ref_conv, rtol=0, atol=1e-6)
+    assert torch.allclose(cs, _per_head_conv_state(ref_conv, hk, hv), rtol=0, atol=1e-6)
 
 
 def _hif8_weight(n, k, seed):
