@@ -189,7 +189,16 @@ struct GemvPlan {
   int nt = 1;       // 8-token MMA tiles (1: M <= 8, 2: M <= 16)
   int clusters = 0;
   int max_items = 0;  // row blocks per cluster (upper bound)
+  // > 0 (m <= 4): every warp keeps its partial sums of up to this many items
+  // in shared memory and the items are reduced once, after the last one,
+  // instead of behind a CTA barrier after every item
+  int defer_items = 0;
 };
+
+// Shared memory of the deferred per-warp partials: [item][warp][m][16 rows].
+__host__ __device__ constexpr size_t defer_bytes(int m, int items) {
+  return (size_t)items * kWarps * m * 16 * sizeof(float);
+}
 
 // kc * 2 is a multiple of 512, so consecutive token rows start 16 bytes
 // (one bank group) apart modulo 128.
@@ -217,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   uint8_t *act = smem + kLutBytes;
   float *red = reinterpret_cast<float *>(act + (size_t)kTok * act_stride);  // [2][kWarps][kTok][kRedStride]
   float *part = red + 2 * kWarps * kRedStride * kTok;                       // [items][kTok][16 * WR]
+  float *wpd = part + (size_t)plan.max_items * 16 * WR * kTok;               // deferred: [item][warp][m][16]
 
   // ---- work assignment -----------------------------------------------------
   const int g = lane >> 2, t = lane & 3;
@@ -469,6 +479,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
       }
     }
 
+    if (plan.defer_items) {  // keep this warp's partials of the item; no barrier
+      float *dst = wpd + ((size_t)item * kWarps + warp) * mt * 16;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int m = 2 * t + (q & 1);
+        if (m < mt) dst[m * 16 + g + ((q < 2) ? 0 : 8)] = acc[0][0][q] + acc[1][0][q];
+      }
+      continue;
+    }
     // ---- reduce the item: warps (fixed order), then cluster ranks ---------
     // Partials are token-major ([token][row]) so the summing threads walk the
     // output rows of one token consecutively: the global stores coalesce.
@@ -502,6 +521,30 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
         }
       } else {
         cpart[e] = v;
+      }
+    }
+  }
+  if (plan.defer_items) {
+    // every item at once: the WK warps of a row group summed in warp order
+    __syncthreads();
+    const int per_item = rows_per_item * mt;
+    for (int e = tid; e < my_items * per_item; e += kThreads) {
+      const int item = e / per_item, rem = e - item * per_item;
+      const int m = rem / rows_per_item, rl = rem - m * rows_per_item;
+      const int grp = rl >> 4, r16 = rl & 15;
+      const float *src = wpd + ((size_t)item * kWarps + grp * WK) * mt * 16 + m * 16 + r16;
+      float v = 0.f;
+      for (int w = 0; w < WK; ++w) v += src[(size_t)w * mt * 16];
+      if (S == 1) {
+        const int n = (cluster_id + item * plan.clusters) * rows_per_item + rl;
+        if (n < p.n) {
+          v = v * __ldg(p.cs + n);
+          v = v * __ldg(p.ts + m * p.ts_stride);
+          if (p.bias) v += load_bias(p.bias, p.bias_dtype, n);
+          store_out<OUT>(p.out, (int64_t)m * p.n + n, v);
+        }
+      } else {
+        part[(size_t)item * rows_per_item * kTok + rem] = v;
       }
     }
   }
@@ -677,6 +720,9 @@ static GemvPlan plan_gemv(int64_t m, int64_t n, int64_t k, const void *kernel) {
       best.nt = nt;
       best.clusters = clusters;
       best.max_items = s > 1 ? (int)rounds : 0;
+      // deferred reduction for up to 4 tokens when its partials fit
+      const size_t base = gemv_smem_bytes(nt, (int)kc, wr, s > 1 ? (int)rounds : 0);
+      best.defer_items = (nt == 1 && m <= 4 && base + defer_bytes((int)m, (int)rounds) <= cap) ? (int)rounds : 0;
     }
   }
   return best;
@@ -689,7 +735,7 @@ static const void *gemv_kernel_ptr() {
 
 template <int NT, int OUT, int ASRC>
 static int launch_gemv(const GemvArgs &args, const GemvPlan &plan, cudaStream_t stream) {
-  const size_t smem = gemv_smem_bytes(NT, plan.kc, plan.wr, plan.max_items);
+  const size_t smem = gemv_smem_bytes(NT, plan.kc, plan.wr, plan.max_items) + defer_bytes(args.m, plan.defer_items);
   auto kernel = gemv_hif8_kernel<NT, OUT, ASRC>;
   const int st = ensure_smem_limit(reinterpret_cast<const void *>(kernel), smem);
   if (st != HIF8_OK) return st;
