@@ -177,6 +177,47 @@ __global__ void __launch_bounds__(256) scaled_decode_scalar(const uint8_t *__res
   }
 }
 
+// Embedding rows: out[t, j] = bf16_rne(decode(w[ids[t], j]) * bf16_rne(ws[ids[t]]))
+// -- the W8A8HIF8_SOFT embedding of the reference (scheme.py:120-131: BF16
+// decode table rows times the row scale cast to BF16, a BF16 product).  Both
+// factors are BF16 values, so their FP32 product is exact and is rounded
+// once.  Ids outside [0, vocab) give a zero row and count into *bad_ids.
+// VEC: 16 bytes in, 32 bytes out per thread (k % 16 == 0, aligned rows).
+template <bool VEC>
+__global__ void __launch_bounds__(256) embedding_gather(const uint8_t *__restrict__ weight,
+                                                        const float *__restrict__ weight_scale, int64_t vocab,
+                                                        int64_t k, const int64_t *__restrict__ ids,
+                                                        uint16_t *__restrict__ out, int64_t work,
+                                                        int32_t *__restrict__ bad_ids) {
+  __shared__ float tbl[256];
+  load_decode_table(tbl);  // module data: before the dependency wait
+  __syncthreads();
+  pdl_wait();  // the ids may come from the previous kernel (the last step's argmax)
+  const int64_t per_row = VEC ? k >> 4 : k;
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < work; c += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = c / per_row, j = c - t * per_row;
+    const int64_t id = __ldg(ids + t);
+    const bool ok = id >= 0 && id < vocab;
+    if (!ok && j == 0 && bad_ids) atomicAdd(bad_ids, 1);
+    const float s = ok ? bf16_bits_to_f32(f32_to_bf16_bits(__ldg(weight_scale + id))) : 0.f;
+    if constexpr (VEC) {
+      uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
+      if (ok) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(weight + id * k) + j);
+        o0 = make_uint4(decode_pair(tbl, v.x, 0, s), decode_pair(tbl, v.x, 16, s), decode_pair(tbl, v.y, 0, s),
+                        decode_pair(tbl, v.y, 16, s));
+        o1 = make_uint4(decode_pair(tbl, v.z, 0, s), decode_pair(tbl, v.z, 16, s), decode_pair(tbl, v.w, 0, s),
+                        decode_pair(tbl, v.w, 16, s));
+      }
+      uint4 *dst = reinterpret_cast<uint4 *>(out + t * k) + 2 * j;
+      dst[0] = o0;
+      dst[1] = o1;
+    } else {
+      out[t * k + j] = ok ? (uint16_t)f32_to_bf16_bits(tbl[weight[id * k + j]] * s) : (uint16_t)0;
+    }
+  }
+}
+
 static int grid_for(int64_t work, int threads) {
   const int64_t blocks = (work + threads - 1) / threads;
   const int64_t cap = (int64_t)num_sms() * 8;
@@ -235,4 +276,21 @@ extern "C" int hif8_scaled_decode(const uint8_t *data, int64_t rows, int64_t k, 
     scaled_decode_scalar<<<grid_for(total, 256), 256, 0, stream>>>(data, k, data_row_stride, scale, out, total);
   }
   return check_launch();
+}
+
+extern "C" int hif8_embedding_gather(const uint8_t *weight, const float *weight_scale, int64_t vocab, int64_t k,
+                                     const int64_t *ids, int64_t n, uint16_t *out, int32_t *bad_ids,
+                                     void *stream_ptr) {
+  if (vocab <= 0 || k <= 0 || n < 0 || (n > 0 && (!weight || !weight_scale || !ids || !out)))
+    return HIF8_ERR_INVALID_ARGUMENT;
+  if (n == 0) return HIF8_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (k % 16 == 0 && aligned16(weight) && aligned16(out)) {
+    const int64_t work = n * (k / 16);
+    return launch_pdl(embedding_gather<true>, dim3(grid_for(work, 256)), dim3(256), 0, stream, weight, weight_scale,
+                      vocab, k, ids, out, work, bad_ids);
+  }
+  const int64_t work = n * k;
+  return launch_pdl(embedding_gather<false>, dim3(grid_for(work, 256)), dim3(256), 0, stream, weight, weight_scale,
+                    vocab, k, ids, out, work, bad_ids);
 }

@@ -245,6 +245,37 @@ at::Tensor SoftHif8FusedGemm(const at::Tensor &, const at::Tensor &, const at::T
                      "use soft_hif8_static_fused_gemm with a fixed input_scale");
 }
 
+// HiF8 token embedding (reference scheme.py:120-131): gather + decode of the
+// requested rows only; [*ids.shape, hidden] BF16.
+at::Tensor Hif8EmbeddingGather(const at::Tensor &weight, const at::Tensor &weight_scale, const at::Tensor &ids,
+                               const std::optional<at::Tensor> &bad_ids) {
+  CheckCudaTensor(weight, "weight");
+  CheckCudaTensor(weight_scale, "weight_scale");
+  CheckCudaTensor(ids, "ids");
+  TORCH_CHECK(weight.scalar_type() == at::ScalarType::Byte && weight.dim() == 2,
+              "weight must be a uint8 [vocab, hidden] tensor");
+  TORCH_CHECK(weight_scale.scalar_type() == at::ScalarType::Float && weight_scale.numel() == weight.size(0),
+              "weight_scale must be float32 with one value per embedding row");
+  TORCH_CHECK(ids.scalar_type() == at::kLong, "ids must have dtype torch.int64");
+  CheckSameDevice(weight_scale, weight.device(), "weight_scale");
+  CheckSameDevice(ids, weight.device(), "ids");
+  int32_t *bad = nullptr;
+  if (bad_ids.has_value()) {
+    CheckCudaTensor(*bad_ids, "bad_ids");
+    TORCH_CHECK(bad_ids->scalar_type() == at::kInt && bad_ids->numel() >= 1, "bad_ids must be int32");
+    bad = bad_ids->data_ptr<int32_t>();
+  }
+  std::vector<int64_t> shape(ids.sizes().begin(), ids.sizes().end());
+  shape.push_back(weight.size(1));
+  c10::cuda::CUDAGuard guard(weight.device());
+  at::Tensor out = at::empty(shape, weight.options().dtype(at::kBFloat16));
+  CheckStatus(hif8_embedding_gather(weight.data_ptr<uint8_t>(), weight_scale.data_ptr<float>(), weight.size(0),
+                                    weight.size(1), ids.data_ptr<int64_t>(), ids.numel(),
+                                    reinterpret_cast<uint16_t *>(out.data_ptr()), bad, Stream(weight)),
+              "hif8_embedding_gather");
+  return out;
+}
+
 // --------------------------------------------------------------- KV ops --
 
 void Hif8KvCacheWrite(const at::Tensor &key, const at::Tensor &value, const at::Tensor &key_scale,
@@ -614,6 +645,7 @@ TORCH_LIBRARY(hif8_b200, m) {
         "Tensor query_start, int max_seq_len, float softmax_scale, bool causal=True) -> Tensor");
   m.def("kv_gather_decode(Tensor cache, Tensor block_tables, Tensor seq_lens, Tensor out_start, int total_rows, "
         "int max_seq_len) -> Tensor");
+  m.def("embedding_gather(Tensor weight, Tensor weight_scale, Tensor ids, Tensor(a!)? bad_ids=None) -> Tensor");
   // glue of the synthetic decoder
   m.def("rmsnorm(Tensor x, Tensor? residual, Tensor weight, float eps, bool one_plus) -> (Tensor, Tensor)");
   m.def("silu_mul(Tensor gate_up) -> Tensor");
@@ -633,6 +665,7 @@ TORCH_LIBRARY_IMPL(hif8_b200, CUDA, m) {
   m.impl("kv_cache_write", &Hif8KvCacheWrite);
   m.impl("paged_attention", &Hif8PagedAttention);
   m.impl("kv_gather_decode", &Hif8KvGatherDecode);
+  m.impl("embedding_gather", &Hif8EmbeddingGather);
   m.impl("rmsnorm", &ModelRmsnorm);
   m.impl("silu_mul", &ModelSiluMul);
   m.impl("glue_linear", &ModelGlueLinear);

@@ -35,6 +35,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hif8_encode_table": (None, [_P]),
     "hif8_static_quant": (_INT, [_P, _INT, _I64, _I64, _P, _I64, _P, _P, _P]),
     "hif8_scaled_decode": (_INT, [_P, _I64, _I64, _I64, _P, _P, _P]),
+    "hif8_embedding_gather": (_INT, [_P, _P, _I64, _I64, _P, _I64, _P, _P, _P]),
     "soft_hif8_gemv": (_INT, [_P, _P, _P, _P, _P, _INT, _INT, _I64, _I64, _I64, _P, _P]),
     "soft_hif8_gemm_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "soft_hif8_gemm": (_INT, [_P, _P, _P, _P, _P, _INT, _INT, _I64, _I64, _I64, _P, _P, _SZ, _P]),
@@ -118,6 +119,12 @@ def scaled_decode(data, scale, out, row_stride: int | None = None) -> None:
     rows, k = out.shape
     check("hif8_scaled_decode", library().hif8_scaled_decode(
         _ptr(data), rows, k, k if row_stride is None else row_stride, _ptr(scale), _ptr(out), _stream(out)))
+
+
+def embedding_gather(weight, weight_scale, ids, out, bad_ids=None) -> None:
+    vocab, k = weight.shape
+    check("hif8_embedding_gather", library().hif8_embedding_gather(
+        _ptr(weight), _ptr(weight_scale), vocab, k, _ptr(ids), ids.numel(), _ptr(out), _ptr(bad_ids), _stream(out)))
 
 
 def gemm(activation, weight, token_scale, channel_scale, bias, out, workspace=None) -> None:

@@ -77,6 +77,18 @@ int hif8_static_quant(const void *x, int x_dtype, int64_t rows, int64_t k,
 int hif8_scaled_decode(const uint8_t *data, int64_t rows, int64_t k, int64_t data_row_stride,
                        const float *scale, uint16_t *out, void *stream);
 
+/* ---- embedding gather-decode --------------------------------------------
+ * Replaces the HiF8 token-embedding lookup of the W8A8HIF8_SOFT scheme
+ * (src/vllm_ascend_hif8/scheme.py:120-131: index_select of the requested
+ * rows and scales, BF16 decode table, BF16 product).
+ *   out[t, j] = bf16_rne( decode(weight[ids[t], j]) * bf16_rne(weight_scale[ids[t]]) ),
+ * NaN -> 0x7FC0.  weight: [vocab, k] bytes (row-major), weight_scale: [vocab]
+ * FP32, ids: [n] int64, out: [n, k] contiguous BF16 bits.  Only the requested
+ * rows are read.  Ids outside [0, vocab) give zero rows and are counted into
+ * *bad_ids (device int32, may be NULL). */
+int hif8_embedding_gather(const uint8_t *weight, const float *weight_scale, int64_t vocab, int64_t k,
+                          const int64_t *ids, int64_t n, uint16_t *out, int32_t *bad_ids, void *stream);
+
 /* ---- linear -------------------------------------------------------------
  * y[m, n] = cast( (acc[m, n] * channel_scale[n]) * token_scale[m] + bias[n] ),
  * acc = sum_k decode(activation[m, k]) * decode(weight[n, k]) in FP32.

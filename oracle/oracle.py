@@ -15,6 +15,7 @@ plugin's CPU code:
 * ``paged_attention``   -> ``src/vllm_ascend_hif8/kv_cache.py:314-372`` with the
                            FP32 math of ``tests/test_hif8_kv_npu.py:251-295``
 * ``gather_kv_rows``    -> ``src/vllm_ascend_hif8/kv_cache.py:221-252``
+* ``embedding``         -> ``src/vllm_ascend_hif8/scheme.py:120-131`` (C decode)
 """
 
 from __future__ import annotations
@@ -148,6 +149,25 @@ def scaled_decode(data: np.ndarray, scale: np.ndarray) -> np.ndarray:
     out = np.empty((rows, k), dtype=np.uint16)
     lib().hif8o_scaled_decode(_ptr(data), rows, k, k, _ptr(scale), _ptr(out))
     return out
+
+
+def embedding(codes: np.ndarray, scale: np.ndarray, ids: np.ndarray) -> np.ndarray:
+    """BF16 bits [*ids.shape, hidden] of the HiF8 token-embedding lookup
+    (reference src/vllm_ascend_hif8/scheme.py:120-131): decode of the
+    gathered rows times the row scale rounded to BF16, one BF16 rounding of
+    the (exact) FP32 product -- i.e. scaled_decode with BF16-rounded scales.
+    NaN codes give the canonical 0x7FC0 (the reference's CPU run writes
+    0xFFFF through ATen's vectorised BF16 cast: the same value).  Ids outside
+    [0, vocab) give zero rows."""
+    codes = np.ascontiguousarray(codes, dtype=np.uint8)
+    vocab, hidden = codes.shape
+    scale = np.ascontiguousarray(scale, dtype=np.float32).reshape(-1)
+    flat = np.asarray(ids, dtype=np.int64).reshape(-1)
+    ok = (flat >= 0) & (flat < vocab)
+    safe = np.where(ok, flat, 0)
+    out = scaled_decode(codes[safe], round_bf16(scale[safe]))
+    out[~ok] = 0
+    return out.reshape(*np.shape(ids), hidden)
 
 
 # ------------------------------------------------------------------- KV ---

@@ -177,7 +177,44 @@ def main(reference_root: str) -> None:
     wdata, wscale = torch_codec.quantize_tensor_rows(wsrc, scale_factor=codec.MAX_FINITE)
     payload["wq_src"], payload["wq_data"], payload["wq_scale"] = _bf16_bits(wsrc), wdata.numpy(), wscale.numpy()
     np.savez_compressed(HERE / "linear.npz", **payload)
+    write_embedding(codec)
     print("golden fixtures written to", HERE)
+
+
+def write_embedding(codec) -> None:
+    """embedding.npz: the W8A8HIF8_SOFT token-embedding lookup.  The
+    reference's method (src/vllm_ascend_hif8/scheme.py:120-131) cannot be
+    imported here (it needs vllm_ascend), so its four tensor operations are
+    run as written there -- index_select of rows and scales, the BF16 decode
+    table of codec.ASCEND_DECODE_TABLE, a BF16 product -- on the reference
+    codec's table."""
+    lut = torch.tensor(codec.ASCEND_DECODE_TABLE, dtype=torch.bfloat16)
+
+    def lookup(weight, scale, ids):
+        flat = ids.reshape(-1)
+        rows = torch.index_select(weight, 0, flat)
+        scales = torch.index_select(scale.reshape(-1), 0, flat)
+        out = lut[rows.long()] * scales.to(torch.bfloat16).unsqueeze(-1)
+        return out.reshape(*ids.shape, weight.shape[1])
+
+    payload = {}
+    # the known answer of the reference's tests/test_embedding.py:12-47
+    values = [[-1.0, -0.5, 0.0, 0.5], [-0.5, 0.0, 0.5, 1.0], [0.25, -0.25, 0.75, -0.75]]
+    w = torch.tensor([[codec.encode_ascend(v) for v in row] for row in values], dtype=torch.uint8)
+    ws = torch.tensor([[2.0], [3.0], [4.0]], dtype=torch.float32)
+    ids = torch.tensor([[2, 0], [1, 2]], dtype=torch.int64)
+    payload["ka_w"], payload["ka_ws"], payload["ka_ids"] = w.numpy(), ws.numpy(), ids.numpy()
+    payload["ka_out"] = _bf16_bits(lookup(w, ws, ids))
+    # seeded rows with every code (NaN and Inf included) and FP32 row scales
+    # that are not BF16 values (amax / 32768 of N(0, 0.02) rows, as exported)
+    g = torch.Generator().manual_seed(7)
+    for name, vocab, hidden in (("v", 96, 64), ("s", 40, 36)):
+        w = torch.randint(0, 256, (vocab, hidden), generator=g, dtype=torch.int64).to(torch.uint8)
+        ws = ((torch.randn(vocab, 64, generator=g) * 0.02).abs().amax(-1) / 32768.0).reshape(-1, 1)
+        ids = torch.randint(0, vocab, (5, 7), generator=g, dtype=torch.int64)
+        payload[f"{name}_w"], payload[f"{name}_ws"], payload[f"{name}_ids"] = w.numpy(), ws.numpy(), ids.numpy()
+        payload[f"{name}_out"] = _bf16_bits(lookup(w, ws, ids))
+    np.savez_compressed(HERE / "embedding.npz", **payload)
 
 
 if __name__ == "__main__":

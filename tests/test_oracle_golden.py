@@ -112,3 +112,27 @@ def test_weight_row_quantisation_matches_reference():
     data, scale = oracle.quantize_rows_amax(src)
     np.testing.assert_array_equal(scale, g["wq_scale"])
     np.testing.assert_array_equal(data, g["wq_data"])
+
+
+def test_embedding_matches_reference_lookup():
+    """The W8A8HIF8_SOFT embedding (scheme.py:120-131): the reference's own
+    known answer (tests/test_embedding.py) and seeded rows with every code,
+    bit-exact."""
+    g = _load("embedding.npz")
+    for name in ("ka", "v", "s"):
+        out = oracle.embedding(g[f"{name}_w"], g[f"{name}_ws"], g[f"{name}_ids"])
+        assert_bf16_equal_nan_any(out, g[f"{name}_out"])
+    # the known answer's scales are BF16 values: FP32 decode x scale agrees
+    dec = oracle.decode_table()
+    ka = dec[g["ka_w"]] * g["ka_ws"]
+    np.testing.assert_array_equal(oracle.bf16_bits_to_f32(g["ka_out"]), ka[g["ka_ids"]])
+
+
+def assert_bf16_equal_nan_any(actual, expected):
+    """Bit-exact BF16, except that any NaN pattern equals any other: the
+    reference's CPU lookup writes NaN as 0xFFFF (ATen's vectorised float ->
+    BF16 cast), this build as the canonical 0x7FC0."""
+    a_nan = (actual & 0x7FFF) > 0x7F80
+    e_nan = (expected & 0x7FFF) > 0x7F80
+    np.testing.assert_array_equal(a_nan, e_nan)
+    np.testing.assert_array_equal(np.where(a_nan, 0, actual), np.where(e_nan, 0, expected))
