@@ -32,7 +32,6 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -123,15 +122,6 @@ __device__ __forceinline__ void decode4(const uint8_t *lut, uint32_t word, uint3
   hi = __byte_perm(e2, e3, 0x5410u);
 }
 
-// One bulk L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned
-// address.  It only fills L2, the device's coherence point, so it may be
-// issued before the dependency wait: a later load still sees every write.
-__device__ __forceinline__ void l2_prefetch_bulk(const void *p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
@@ -203,13 +193,6 @@ struct GemvPlan {
   // in shared memory and the items are reduced once, after the last one,
   // instead of behind a CTA barrier after every item
   int defer_items = 0;
-  // L2 prefetches: items 0 .. pre_items-1 before the dependency wait, and
-  // item i + prefetch while item i runs (0: off)
-  int pre_items = 0;
-  int prefetch = 0;
-  // where the CTA signals its dependents (griddepcontrol.launch_dependents):
-  // 0 never (implicit at exit), 1 at kernel start, 2 at the start of its last item
-  int trigger = 0;
 };
 
 // Shared memory of the deferred per-warp partials: [item][warp][m][16 rows].
@@ -260,30 +243,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
     w1 = p.w + (int64_t)r1 * p.k + kw0 + t * 32;
   };
 
-  // L2 prefetch of this CTA's K slice of one item's weight rows: one bulk
-  // prefetch per row (kc bytes; kc % 256 == 0 and k % 256 == 0 keep it
-  // 16-byte aligned), issued by the first rows_per_item threads.
-  auto prefetch_item = [&](int item) {
-    const int row = (cluster_id + item * plan.clusters) * rows_per_item + tid;
-    if (tid < rows_per_item && row < p.n) l2_prefetch_bulk(p.w + (int64_t)row * p.k + k0, (uint32_t)kc);
-  };
-
-  // Before the dependency wait: the sources of the two tables (module data
-  // that no kernel writes) and L2 prefetches of the first items' weights.
-  // Every other global read of the prologue may depend on the previous
-  // kernel of the stream (its activations, or weights it has just written),
-  // so it follows the wait.  The loads after the wait -- the first round of
-  // activations, then this warp's first item of weights -- are all issued
-  // before any of them is used, so their latencies overlap.
-  // warp w owns table entries 16 w .. 16 w + 15 (one load per lane); the
-  // fused quantiser's 8 KB encode table is staged in the reduction buffer
-  // (idle until the first item is reduced), one 16-byte piece per thread
-  const uint32_t mine = g_decode_f32.v[warp * 16 + (lane & 15)] >> 16;
-  static_assert(kThreads == 512, "one encode-table piece per thread");
-  uint4 enc_piece = make_uint4(0, 0, 0, 0);
-  if (ASRC != kActCodes) enc_piece = reinterpret_cast<const uint4 *>(g_static_encode.v)[tid];
-  for (int i = 0; i < plan.pre_items && i < my_items; ++i) prefetch_item(i);
-  if (plan.trigger == 1) pdl_trigger();
+  // Every global read of the prologue may depend on the previous kernel of
+  // the stream (its activations, or weights it has just written), so all of
+  // them follow the dependency wait.  The independent loads -- the two
+  // tables' sources, the first round of activations and this warp's first
+  // item of weights, in that order -- are all issued before any of them is
+  // used, so their latencies overlap instead of adding up.
   pdl_wait();
   U32x8 ring[kRing][2];
 
@@ -291,8 +256,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   {
     uint32_t *lut = reinterpret_cast<uint32_t *>(smem);
     uint8_t *enc = reinterpret_cast<uint8_t *>(red);
+    // warp w owns table entries 16 w .. 16 w + 15 (one load per lane); the
+    // fused quantiser's 8 KB encode table is staged in the reduction buffer
+    // (idle until the first item is reduced), one 16-byte piece per thread
+    const uint32_t mine = g_decode_f32.v[warp * 16 + (lane & 15)] >> 16;
+    static_assert(kThreads == 512, "one encode-table piece per thread");
+    uint4 enc_piece = make_uint4(0, 0, 0, 0);
     float ts0 = 1.f;  // the fused quantiser's fixed scale
-    if (ASRC != kActCodes) ts0 = p.ts[0];
+    if (ASRC != kActCodes) {
+      enc_piece = reinterpret_cast<const uint4 *>(g_static_encode.v)[tid];
+      ts0 = p.ts[0];
+    }
     const int chunks_per_tok = kc >> 4;  // 16 K values per chunk
     const int real = (p.m < kTok ? p.m : kTok) * chunks_per_tok;
     const int total_chunks = kTok * chunks_per_tok;
@@ -465,8 +439,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
 
   cg::cluster_group cluster = cg::this_cluster();
   for (int item = 0; item < my_items; ++item) {
-    if (plan.prefetch && item + plan.prefetch < my_items) prefetch_item(item + plan.prefetch);
-    if (plan.trigger == 2 && item + 1 == my_items) pdl_trigger();
     const uint8_t *n0 = nullptr, *n1 = nullptr;
     const bool has_next = item + 1 < my_items;
     if (has_next) weight_ptrs(item + 1, n0, n1);
@@ -712,19 +684,6 @@ static int max_active_clusters(const void *kernel, int s, size_t smem_request) {
   return clusters;
 }
 
-// Defaults of the L2 prefetch distance and the dependents' signal point
-// (GemvPlan::prefetch / trigger); HIF8_GEMV_PREFETCH and HIF8_GEMV_TRIGGER
-// override them per call (read at planning time, so a captured graph keeps
-// the values of its capture).
-constexpr int kGemvPreItems = 0;
-constexpr int kGemvPrefetch = 0;
-constexpr int kGemvTrigger = 0;
-
-static int env_int(const char *name, int fallback) {
-  const char *v = std::getenv(name);
-  return (v && v[0]) ? std::atoi(v) : fallback;
-}
-
 // Pick the K split S (cluster size) and the warp arrangement that balance the
 // rounds of row blocks over the co-resident persistent clusters best.
 static GemvPlan plan_gemv(int64_t m, int64_t n, int64_t k, const void *kernel) {
@@ -765,11 +724,6 @@ static GemvPlan plan_gemv(int64_t m, int64_t n, int64_t k, const void *kernel) {
       const size_t base = gemv_smem_bytes(nt, (int)kc, wr, s > 1 ? (int)rounds : 0);
       best.defer_items = (nt == 1 && m <= 4 && base + defer_bytes((int)m, (int)rounds) <= cap) ? (int)rounds : 0;
     }
-  }
-  if (best.s) {
-    best.pre_items = std::min(std::max(env_int("HIF8_GEMV_PRE_ITEMS", kGemvPreItems), 0), 4);
-    best.prefetch = std::min(std::max(env_int("HIF8_GEMV_PREFETCH", kGemvPrefetch), 0), 8);
-    best.trigger = std::min(std::max(env_int("HIF8_GEMV_TRIGGER", kGemvTrigger), 0), 2);
   }
   return best;
 }
