@@ -728,6 +728,31 @@ static GemvPlan plan_gemv(int64_t m, int64_t n, int64_t k, const void *kernel) {
   return best;
 }
 
+// plan_gemv memoised per (device, kernel, m, n, k): the plan is a pure
+// function of those, and the search costs microseconds of host time per call
+// (an eager decode step makes dozens of calls).
+static GemvPlan plan_gemv_cached(int64_t m, int64_t n, int64_t k, const void *kernel) {
+  struct Entry {
+    const void *kernel;
+    int device;
+    int64_t m, n, k;
+    GemvPlan plan;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry &e : cache)
+      if (e.kernel == kernel && e.device == dev && e.m == m && e.n == n && e.k == k) return e.plan;
+  }
+  const GemvPlan plan = plan_gemv(m, n, k, kernel);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() < 4096) cache.push_back({kernel, dev, m, n, k, plan});
+  return plan;
+}
+
 template <int NT, int OUT, int ASRC>
 static const void *gemv_kernel_ptr() {
   return reinterpret_cast<const void *>(gemv_hif8_kernel<NT, OUT, ASRC>);
@@ -788,7 +813,7 @@ int run_linear(GemvArgs args, int output_dtype, cudaStream_t stream) {
                                            : gemv_kernel_ptr<2, HIF8_DTYPE_F16, kActCodes>())
                                : (bf16_out ? gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActCodes>()
                                            : gemv_kernel_ptr<1, HIF8_DTYPE_F16, kActCodes>());
-    const GemvPlan plan = vec_ok ? plan_gemv(s.m, s.n, s.k, kptr) : GemvPlan{};
+    const GemvPlan plan = vec_ok ? plan_gemv_cached(s.m, s.n, s.k, kptr) : GemvPlan{};
     int status;
     if (plan.s == 0) {
       status = bf16_out ? launch_generic<HIF8_DTYPE_BF16, kActCodes>(s, stream)
@@ -814,7 +839,7 @@ int run_fused_linear(const GemvArgs &args, int x_dtype, int output_dtype, cudaSt
                                          : gemv_kernel_ptr<1, HIF8_DTYPE_F16, kActBf16>())
                              : (bf16_out ? gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActF16>()
                                          : gemv_kernel_ptr<1, HIF8_DTYPE_F16, kActF16>());
-  const GemvPlan plan = vec_ok ? plan_gemv(args.m, args.n, args.k, kptr) : GemvPlan{};
+  const GemvPlan plan = vec_ok ? plan_gemv_cached(args.m, args.n, args.k, kptr) : GemvPlan{};
   if (plan.s == 0) {
     if (bf16_in)
       return bf16_out ? launch_generic<HIF8_DTYPE_BF16, kActBf16>(args, stream)
@@ -841,17 +866,17 @@ int run_glue_linear(const GemvArgs &args, cudaStream_t stream) {
     return HIF8_ERR_INVALID_ARGUMENT;
   switch (gl.kind) {
     case kGlueSiluMul: {
-      const GemvPlan plan = plan_gemv(args.m, args.n, args.k, gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActSiluMul>());
+      const GemvPlan plan = plan_gemv_cached(args.m, args.n, args.k, gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActSiluMul>());
       return plan.s ? launch_gemv<1, HIF8_DTYPE_BF16, kActSiluMul>(args, plan, stream) : HIF8_ERR_INVALID_ARGUMENT;
     }
     case kGlueGateMul: {
       if (!gl.aux) return HIF8_ERR_INVALID_ARGUMENT;
-      const GemvPlan plan = plan_gemv(args.m, args.n, args.k, gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActGateMul>());
+      const GemvPlan plan = plan_gemv_cached(args.m, args.n, args.k, gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActGateMul>());
       return plan.s ? launch_gemv<1, HIF8_DTYPE_BF16, kActGateMul>(args, plan, stream) : HIF8_ERR_INVALID_ARGUMENT;
     }
     case kGlueRmsNorm: {
       if (!gl.norm_w) return HIF8_ERR_INVALID_ARGUMENT;
-      const GemvPlan plan = plan_gemv(args.m, args.n, args.k, gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActRmsNorm>());
+      const GemvPlan plan = plan_gemv_cached(args.m, args.n, args.k, gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActRmsNorm>());
       return plan.s ? launch_gemv<1, HIF8_DTYPE_BF16, kActRmsNorm>(args, plan, stream) : HIF8_ERR_INVALID_ARGUMENT;
     }
     default:
