@@ -714,62 +714,40 @@ def measure_e2e(calls, args, device, world) -> dict:
     """The same sweep through the public API (hif8_b200.scheme, eager) with
     host buffers inside the timed region: every step copies its 15
     activations from one packed pinned host buffer to the device (one H2D
-    transfer), runs the 15 ``scheme.apply`` calls, and reads every output
-    back into pinned host memory (15 D2H transfers).  The transfers run on two
-    copy streams and overlap the neighbouring steps' kernels, as a serving
-    loop pipelines them: the inputs and outputs are double-buffered, step
-    i+1's upload runs during step i's kernels and step i's read-back during
-    step i+1's.  The timed region spans from before the first upload to the
-    end of the last read-back, so every step's copies are inside it.  One
-    independent replica per rank (value aggregates the ranks)."""
+    transfer), runs the 15 ``scheme.apply`` calls, gathers the 15 outputs
+    into one device buffer and reads it back into pinned host memory (one D2H
+    transfer after the step's launches, so the copies do not split the chain
+    of programmatic launches; one transfer instead of 15 saves their host
+    dispatch).  One independent replica per rank (value aggregates the
+    ranks)."""
     import torch
     import torch.distributed as dist
 
     from hif8_b200 import scheme
 
-    nbuf = 2
     sizes = [c["x"].numel() for c in calls]
     offs = [sum(sizes[:i]) for i in range(len(sizes))]
     host_in = torch.cat([c["x"].reshape(-1).cpu() for c in calls]).pin_memory()
-    dev_in = [torch.empty(host_in.numel(), dtype=host_in.dtype, device=device) for _ in range(nbuf)]
-    dev_x = [[buf[o:o + n].view(c["x"].shape) for o, n, c in zip(offs, sizes, calls)] for buf in dev_in]
-    host_y = [[torch.empty(c["m"], c["n_loc"] if not c["row_parallel"] else c["n"], dtype=torch.bfloat16)
-               .pin_memory() for c in calls] for _ in range(nbuf)]
+    dev_in = torch.empty(host_in.numel(), dtype=host_in.dtype, device=device)
+    dev_x = [dev_in[o:o + n].view(c["x"].shape) for o, n, c in zip(offs, sizes, calls)]
+    out_sizes = [c["m"] * (c["n_loc"] if not c["row_parallel"] else c["n"]) for c in calls]
+    host_out = torch.empty(sum(out_sizes), dtype=torch.bfloat16).pin_memory()
     cur = torch.cuda.current_stream(device)
-    h2d_stream, d2h_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    uploaded = [torch.cuda.Event() for _ in range(nbuf)]
-    computed = [torch.cuda.Event() for _ in range(nbuf)]
-    used = [False] * nbuf
 
-    def step(i):
-        s = i % nbuf
-        if used[s]:  # the kernels that read slot s's inputs two steps ago are done
-            h2d_stream.wait_event(computed[s])
-        with torch.cuda.stream(h2d_stream):
-            dev_in[s].copy_(host_in, non_blocking=True)
-            uploaded[s].record(h2d_stream)
-        cur.wait_event(uploaded[s])
-        outs = [scheme.apply(c["layer"], x) for c, x in zip(calls, dev_x[s])]
-        computed[s].record(cur)
-        d2h_stream.wait_event(computed[s])
-        with torch.cuda.stream(d2h_stream):
-            for hy, y in zip(host_y[s], outs):
-                hy.copy_(y, non_blocking=True)
-                y.record_stream(d2h_stream)
-        used[s] = True
+    def step():
+        dev_in.copy_(host_in, non_blocking=True)
+        outs = [scheme.apply(c["layer"], x) for c, x in zip(calls, dev_x)]
+        host_out.copy_(torch.cat([y.reshape(-1) for y in outs]), non_blocking=True)
 
-    for i in range(max(args.warmup, 1)):
-        step(i)
+    for _ in range(max(args.warmup, 1)):
+        step()
     torch.cuda.synchronize()
-    used[:] = [False] * nbuf
     if world > 1:
         dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(cur)
-    h2d_stream.wait_event(start)
-    for i in range(args.steps):
-        step(i)
-    cur.wait_stream(d2h_stream)
+    for _ in range(args.steps):
+        step()
     end.record(cur)
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
@@ -777,17 +755,16 @@ def measure_e2e(calls, args, device, world) -> dict:
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    for hy, c in zip(host_y[(args.steps - 1) % nbuf], calls):  # the read-back values are the step's results
+    for hy, c in zip(host_out.split(out_sizes), calls):  # the read-back values are the step's results
         if not torch.isfinite(hy.float()).all():
             raise RuntimeError(f"e2e: non-finite output for {c['name']} M={c['m']}")
     h2d = host_in.numel() * 2
-    d2h = sum(y.numel() * 2 for y in host_y[0])
+    d2h = host_out.numel() * 2
     return {"value": world * step_bytes() * args.steps / (ms * 1e-3) / 1e9, "unit": UNIT,
             "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * d2h, "ms_per_step": ms / args.steps,
-            "transfers_per_step": {"h2d": 1, "d2h": len(calls)},
-            "path": "hif8_b200.scheme.apply (eager PyTorch ops -> C ABI), pinned host buffers; uploads and "
-                    "read-backs on two copy streams, double-buffered and overlapped with the neighbouring "
-                    "steps' kernels"}
+            "transfers_per_step": {"h2d": 1, "d2h": 1},
+            "path": "hif8_b200.scheme.apply (eager PyTorch ops -> C ABI), pinned host buffers, outputs gathered on "
+                    "the device and read back in one transfer"}
 
 
 def run_profile_case(spec: str, launches: int) -> None:

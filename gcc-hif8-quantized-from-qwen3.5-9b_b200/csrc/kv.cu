@@ -340,6 +340,24 @@ constexpr int kDecWarps = 4;
 constexpr int kDecThreads = kDecWarps * 32;
 constexpr int kDecHead = 256;      // head size of the decode kernel
 constexpr int kDecBlock = 8;       // keys per MMA step of a warp
+// Shared-memory ring of staged K/V words per warp: every lane copies (cp.async,
+// 4 bytes at a time: cache rows are only 4-byte aligned) exactly the words it
+// later feeds to its MMAs, kDecStages - 1 blocks ahead of the block it computes.
+constexpr int kDecStages = 3;
+constexpr int kStageK = 17;        // K words per lane: 16 of row g + its scale
+constexpr int kStageV = 18;        // V words per lane: 8 of rows 2t and 2t+1 each + their scales
+constexpr int kStageWords = (kStageK + kStageV) * 32;  // per warp and stage
+constexpr size_t kDecRingBytes = (size_t)kDecWarps * kDecStages * kStageWords * sizeof(uint32_t);
+
+__device__ __forceinline__ void cp_async4(uint32_t *dst, const void *src) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 __device__ __forceinline__ void attn_mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
   asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -402,6 +420,8 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArg
   __shared__ float lut[256];
   __shared__ float ks0, vs0;
   __shared__ float wm[kDecWarps][G], wl[kDecWarps][G];
+  __shared__ uint32_t wvalid[kDecWarps][kDecStages];  // attended-key mask of each staged block
+  extern __shared__ __align__(16) uint32_t dec_ring[];  // [warp][stage][kStageK + kStageV][32 lanes]
   pdl_wait();  // the cache and the queries come from earlier kernels of the stream
   const int b = blockIdx.x / (int)p.kv_heads, h = blockIdx.x - b * (int)p.kv_heads;
   const int split = blockIdx.y;
@@ -486,43 +506,76 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArg
       uint32_t kr[16];    // K row g: word ks at bytes 16 ks + 4t
       uint32_t vr[8][2];  // V rows 2t, 2t+1: word of dims 32 r + 4g .. + 3
       float ksc = 0.f, vsc[2] = {0.f, 0.f};
-      int64_t koff = -1, voff[2] = {-1, -1};
-      uint32_t valid = 0;  // bit i: key i of the block is attended
-      auto offsets = [&](int blk) {
+      uint32_t *ring = dec_ring + (size_t)warp * kDecStages * kStageWords;
+      // cache row of key (lane & 7) of a block (-1: absent) and whether it is
+      // attended; the block-table read is issued here, used by stage()
+      auto row_pre = [&](int blk, bool &att) -> int64_t {
         const int kk = blk * kDecBlock + (lane & 7);
         const int64_t mine = kk < n_keys ? row_of(wk0 + kk) : -1;
-        valid = __ballot_sync(0xFFFFFFFFu, mine >= 0 && wk0 + kk <= limit) & 0xFFu;
-        const uint32_t lo = (uint32_t)(uint64_t)mine, hi = (uint32_t)((uint64_t)mine >> 32);
-        koff = (int64_t)(((uint64_t)__shfl_sync(0xFFFFFFFFu, hi, g) << 32) | __shfl_sync(0xFFFFFFFFu, lo, g));
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-          voff[j] = (int64_t)(((uint64_t)__shfl_sync(0xFFFFFFFFu, hi, 2 * t + j) << 32) |
-                              __shfl_sync(0xFFFFFFFFu, lo, 2 * t + j));
+        att = mine >= 0 && wk0 + kk <= limit;
+        return mine;
       };
-      // absent keys read row 0 (in bounds) and are masked
-      auto load_k = [&]() {
-        const uint8_t *row = p.kc + (koff >= 0 ? koff : 0);
-        if (!TAB) ksc = __ldg(reinterpret_cast<const float *>(row + D));
-#pragma unroll
-        for (int ks = 0; ks < 16; ++ks) kr[ks] = __ldg(reinterpret_cast<const unsigned int *>(row + 16 * ks + 4 * t));
+      auto shfl_off = [&](int64_t v, int src) -> int64_t {
+        const uint32_t lo = (uint32_t)(uint64_t)v, hi = (uint32_t)((uint64_t)v >> 32);
+        return (int64_t)(((uint64_t)__shfl_sync(0xFFFFFFFFu, hi, src) << 32) | __shfl_sync(0xFFFFFFFFu, lo, src));
       };
-      auto load_v = [&]() {
+      // copy this lane's words of block blk into its ring slot; absent keys
+      // read row 0 (in bounds) and are masked
+      auto stage = [&](int blk, int64_t mine, bool att) {
+        const int slot = blk % kDecStages;
+        uint32_t *sl = ring + slot * kStageWords;
+        const uint32_t valid = __ballot_sync(0xFFFFFFFFu, att) & 0xFFu;
+        if (lane == 0) wvalid[warp][slot] = valid;
+        const int64_t koff = shfl_off(mine, g);
+        const uint8_t *krow = p.kc + (koff >= 0 ? koff : 0);
+#pragma unroll
+        for (int ks = 0; ks < 16; ++ks) cp_async4(sl + ks * 32 + lane, krow + 16 * ks + 4 * t);
+        if (!TAB) cp_async4(sl + 16 * 32 + lane, krow + D);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          const uint8_t *row = p.vc + (voff[j] >= 0 ? voff[j] : 0);
-          if (!TAB) vsc[j] = __ldg(reinterpret_cast<const float *>(row + D));
+          const int64_t voff = shfl_off(mine, 2 * t + j);
+          const uint8_t *vrow = p.vc + (voff >= 0 ? voff : 0);
 #pragma unroll
           for (int rr = 0; rr < 8; ++rr)
-            vr[rr][j] = __ldg(reinterpret_cast<const unsigned int *>(row + 32 * rr + 4 * g));
+            cp_async4(sl + (kStageK + 2 * rr + j) * 32 + lane, vrow + 32 * rr + 4 * g);
+          if (!TAB) cp_async4(sl + (kStageK + 16 + j) * 32 + lane, vrow + D);
         }
       };
-      if (nblk > 0) {
-        offsets(0);
-        load_k();
-        load_v();
+      // blocks 0 .. kDecStages - 2 in flight before the first is used; one
+      // commit group per block (empty past the last), so waiting for all but
+      // the newest kDecStages - 2 groups means the current block has landed
+#pragma unroll
+      for (int b0 = 0; b0 < kDecStages - 1; ++b0) {
+        if (b0 < nblk) {
+          bool att;
+          const int64_t mine = row_pre(b0, att);
+          stage(b0, mine, att);
+        }
+        cp_async_commit();
       }
       for (int blk = 0; blk < nblk; ++blk) {
-        const uint32_t cur_valid = valid;
+        cp_async_wait<kDecStages - 2>();
+        __syncwarp();
+        const int slot = blk % kDecStages;
+        const uint32_t *sl = ring + slot * kStageWords;
+        const uint32_t cur_valid = wvalid[warp][slot];
+#pragma unroll
+        for (int ks = 0; ks < 16; ++ks) kr[ks] = sl[ks * 32 + lane];
+        if (!TAB) ksc = __uint_as_float(sl[16 * 32 + lane]);
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) vr[rr][j] = sl[(kStageK + 2 * rr + j) * 32 + lane];
+        if (!TAB) {
+          vsc[0] = __uint_as_float(sl[(kStageK + 16) * 32 + lane]);
+          vsc[1] = __uint_as_float(sl[(kStageK + 17) * 32 + lane]);
+        }
+        // the block that reuses the slot freed one iteration ago: its table
+        // read is in flight during this block's scores
+        const int nb = blk + kDecStages - 1;
+        bool att_n = false;
+        int64_t mine_n = -1;
+        if (nb < nblk) mine_n = row_pre(nb, att_n);
         // ---- scores of keys 0..7 of the block (B fragment = K^T: bytes 0,1 ->
         // k-slots 2t, 2t+1; bytes 2,3 -> 2t+8, 2t+9)
         float sa[4] = {0.f, 0.f, 0.f, 0.f};
@@ -535,11 +588,8 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArg
                                           kv_dec<TAB>(kvlut, lut, w, 3, lane, ksc, false), 0x7632u);
           attn_mma16816(sa, qa[ks][0], qa[ks][1], b0, b1);
         }
-        const bool more = blk + 1 < nblk;
-        if (more) {
-          offsets(blk + 1);
-          load_k();
-        }
+        if (nb < nblk) stage(nb, mine_n, att_n);
+        cp_async_commit();
         // ---- online softmax of head g over keys 2t, 2t+1
         float s0 = ((cur_valid >> (2 * t)) & 1u) ? sa[0] * p.scale : -CUDART_INF_F;
         float s1 = ((cur_valid >> (2 * t + 1)) & 1u) ? sa[1] * p.scale : -CUDART_INF_F;
@@ -582,8 +632,8 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArg
             attn_mma1688(o[2 * rr + half], a0, a1, pp);
           }
         }
-        if (more) load_v();
       }
+      cp_async_wait<0>();  // nothing in flight into the ring when the warp moves on
     };
     if (table_ok) run(std::true_type{});
     else run(std::false_type{});
@@ -745,7 +795,8 @@ static int decode_residency(int64_t g) {
                     : gi == 1 ? reinterpret_cast<const void *>(paged_decode_kernel<2>)
                     : gi == 2 ? reinterpret_cast<const void *>(paged_decode_kernel<4>)
                               : reinterpret_cast<const void *>(paged_decode_kernel<8>);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, kDecThreads, 0) != cudaSuccess || v < 1) {
+    if (ensure_smem_limit(k, kDecRingBytes) != HIF8_OK ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, kDecThreads, kDecRingBytes) != cudaSuccess || v < 1) {
       cudaGetLastError();
       v = 1;
     }
@@ -840,11 +891,17 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
   int status;
   if (decode) {
     const dim3 grid((unsigned)(batch * kv_heads), (unsigned)splits, 1);
+    const void *kptr = group == 1   ? reinterpret_cast<const void *>(paged_decode_kernel<1>)
+                       : group == 2 ? reinterpret_cast<const void *>(paged_decode_kernel<2>)
+                       : group == 4 ? reinterpret_cast<const void *>(paged_decode_kernel<4>)
+                                    : reinterpret_cast<const void *>(paged_decode_kernel<8>);
+    status = ensure_smem_limit(kptr, kDecRingBytes);
+    if (status != HIF8_OK) return status;
     switch (group) {
-      case 1: status = launch_pdl(paged_decode_kernel<1>, grid, dim3(kDecThreads), 0, s, p); break;
-      case 2: status = launch_pdl(paged_decode_kernel<2>, grid, dim3(kDecThreads), 0, s, p); break;
-      case 4: status = launch_pdl(paged_decode_kernel<4>, grid, dim3(kDecThreads), 0, s, p); break;
-      default: status = launch_pdl(paged_decode_kernel<8>, grid, dim3(kDecThreads), 0, s, p); break;
+      case 1: status = launch_pdl(paged_decode_kernel<1>, grid, dim3(kDecThreads), kDecRingBytes, s, p); break;
+      case 2: status = launch_pdl(paged_decode_kernel<2>, grid, dim3(kDecThreads), kDecRingBytes, s, p); break;
+      case 4: status = launch_pdl(paged_decode_kernel<4>, grid, dim3(kDecThreads), kDecRingBytes, s, p); break;
+      default: status = launch_pdl(paged_decode_kernel<8>, grid, dim3(kDecThreads), kDecRingBytes, s, p); break;
     }
   } else if (group <= 4) {
     // prefill and mixed batches: up to 4 query vectors per CTA

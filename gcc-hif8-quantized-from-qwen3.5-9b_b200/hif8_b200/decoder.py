@@ -14,8 +14,10 @@ slice.
 The HiF8 model runs every projection through the plugin path (static
 activation quant with a calibrated input scale + HiF8 GEMV/GEMM,
 ``scheme.apply``) and keeps full-attention K/V in the packed HiF8 page cache
-with calibrated per-head scales; the BF16 twin runs the same layers with
-BF16 weights (cuBLAS) and a dense BF16 KV cache.  Both share the fused glue
+with calibrated per-head scales; its token embedding is HiF8 rows with FP32
+row scales, as the exported checkpoint stores it (W8A8HIF8_SOFT, decoded on
+lookup).  The BF16 twin runs the same layers with BF16 weights (cuBLAS), a
+BF16 embedding and a dense BF16 KV cache.  Both share the fused glue
 kernels (``torch.ops.hif8_b200.{rmsnorm, silu_mul, gate_mul, attn_prep,
 gdn}``).  Tensor parallelism: q/k/v/gate, the gated-delta-net input
 projection and gate/up are column-parallel, o_proj / out_proj / down are
@@ -279,7 +281,18 @@ class Decoder:
             L["down"] = lin(f"{i}.down", w_down[:, r * self.inter:(r + 1) * self.inter].contiguous())
             del w_down
             self.layers.append(L)
-        self.embed = gen.normal("embed", (c.vocab, H), c.init_std)
+        embed = gen.normal("embed", (c.vocab, H), c.init_std)
+        if mode == "hif8":
+            # the exported checkpoint's W8A8HIF8_SOFT token embedding: HiF8
+            # rows with FP32 row scales (the projections' calibrated row
+            # factor), requested rows decoded on lookup
+            from . import checkpoint, scheme
+
+            data, scale = scheme.quantize_weight_rows(embed, weight_factor)
+            self.embed = checkpoint.Hif8Embedding(data, scale)
+            del embed
+        else:
+            self.embed = embed
         self.final_w = gen.normal("final_norm", (H,), 0.02)
         head = gen.normal("lm_head", (c.vocab, H), c.init_std)
         self.lm_head = head[r * self.vocab_local:(r + 1) * self.vocab_local].clone()  # frees the full head
@@ -456,7 +469,7 @@ class Decoder:
         self._fuse_glue = (self.mode == "hif8" and T == 1 and batch <= self.fuse_glue_max_rows
                            and self.calib_amax is None)
         self._site = 0
-        x = self.embed.index_select(0, tokens)
+        x = self.embed(tokens) if self.mode == "hif8" else self.embed.index_select(0, tokens)
         residual = None
         for i, L in enumerate(self.layers):
             if L["full"]:
