@@ -172,6 +172,15 @@ def scaled_decode(data: "torch.Tensor", scale: "torch.Tensor") -> "torch.Tensor"
     return _op("hif8_scaled_decode")(data, scale)
 
 
+def _flat2d(tensor: "torch.Tensor") -> "torch.Tensor":
+    """[..., K] -> [rows, K] (no new view when already 2-D)."""
+    return tensor if tensor.dim() == 2 else tensor.reshape(-1, tensor.shape[-1])
+
+
+def _flat1d(tensor: "torch.Tensor") -> "torch.Tensor":
+    return tensor if tensor.dim() == 1 else tensor.reshape(-1)
+
+
 def _as_native_operand(tensor: "torch.Tensor") -> "torch.Tensor":
     """Return a tensor the native bridge accepts (contiguous, zero offset)
     (reference native.py:148-157)."""
@@ -203,9 +212,9 @@ def soft_linear(
         raise TypeError("soft HiFloat8 linear requires float32 activation and weight scales")
 
     load_extension()
-    flattened = _as_native_operand(activation.reshape(-1, activation.shape[-1]))
-    token_scale = _as_native_operand(activation_scale.reshape(-1))
-    channel_scale = _as_native_operand(weight_scale.reshape(-1))
+    flattened = _as_native_operand(_flat2d(activation))
+    token_scale = _as_native_operand(_flat1d(activation_scale))
+    channel_scale = _as_native_operand(_flat1d(weight_scale))
     if token_scale.numel() != flattened.shape[0]:
         raise ValueError("activation_scale must contain one value per token row")
     if channel_scale.numel() != weight.shape[0]:
@@ -219,7 +228,7 @@ def soft_linear(
     )
     operator = _op("soft_hif8_gemv" if use_gemv else "soft_hif8_gemm")
     output = operator(flattened, weight, token_scale, channel_scale, bias, output_dtype)
-    return output.reshape(*activation.shape[:-1], weight.shape[0])
+    return output if activation.dim() == 2 else output.reshape(*activation.shape[:-1], weight.shape[0])
 
 
 def soft_fused_linear(x, weight, weight_scale, bias=None, *, output_dtype):
@@ -254,15 +263,16 @@ def soft_static_fused_linear(
         raise TypeError("static fused soft HiFP8 linear requires one float32 activation scale")
     if weight_scale.dtype != torch.float32 or weight_scale.numel() != weight.shape[0]:
         raise TypeError("static fused soft HiFP8 linear requires one float32 scale per output channel")
-    if fixed_scale.device != x.device or weight_scale.device != x.device or weight.device != x.device:
+    device = x.device
+    if fixed_scale.device != device or weight_scale.device != device or weight.device != device:
         raise ValueError("activation, weight, fixed_scale, and weight_scale must be on the same device")
 
     load_extension()
-    flattened = _as_native_operand(x.reshape(-1, x.shape[-1]))
-    fixed = _as_native_operand(fixed_scale.reshape(-1))
-    channel_scale = _as_native_operand(weight_scale.reshape(-1))
+    flattened = _as_native_operand(_flat2d(x))
+    fixed = _as_native_operand(fixed_scale)
+    channel_scale = _as_native_operand(_flat1d(weight_scale))
     output = _op("soft_hif8_static_fused_gemm")(flattened, weight, fixed, channel_scale, bias, output_dtype)
-    return output.reshape(*x.shape[:-1], weight.shape[0])
+    return output if x.dim() == 2 else output.reshape(*x.shape[:-1], weight.shape[0])
 
 
 def _validate_quantized_activation(source, data, scale, *, operation: str = "hif8_static_quant") -> None:

@@ -245,3 +245,55 @@ def test_scheme_apply_matches_oracle():
     y_fused = layer(x)
     expected = oracle.linear(a, wq, a_s, wq_s)
     assert max_rel(y_fused.float().cpu().numpy(), expected) <= MAX_REL
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 9, 15, 16, 17, 31, 32, 33, 48])
+def test_routing_boundaries_in_m(m):
+    """Every row count across the kernel boundaries -- fused quant + GEMV
+    (<= 4 rows), quant + persistent GEMV (16-row slices), the tcgen05 GEMM
+    (>= 32 rows) -- through scheme.apply, with an output width that is not a
+    multiple of any row block (reference tests/test_npu_ops.py:346-406)."""
+    from hif8_b200 import scheme
+
+    n, k = 4104, 4096
+    w, w_s = _hif8_weights(n, k, seed=100 + m)
+    x_bits, a, a_s, input_scale = _activations(m, k, seed=200 + m)
+    layer = scheme.Hif8StaticLinear(_to(w), _to(w_s).reshape(-1, 1), _to(input_scale))
+    x = torch.from_numpy(x_bits.view(np.int16)).view(torch.bfloat16).to(DEV)
+    y = layer(x)
+    assert y.shape == (m, n) and y.dtype == torch.bfloat16
+    assert max_rel(y.float().cpu().numpy(), oracle.linear(a, w, a_s, w_s)) <= MAX_REL
+
+
+@pytest.mark.parametrize("n", [1, 17, 100, 272, 1544])
+@pytest.mark.parametrize("m", [1, 7, 16])
+def test_gemv_output_width_tails(n, m):
+    """Full and partial row blocks of the persistent GEMV, every last-item
+    shape (reference tests/test_npu_ops.py:685-716), F16 output with bias."""
+    ext = _native().load_extension()
+    k = 2048
+    w, w_s = _hif8_weights(n, k, seed=n + 7 * m)
+    _, a, a_s, _ = _activations(m, k, seed=n + 11 * m)
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(n)) * 0.1).to(torch.float16)
+    out = ext.soft_hif8_gemm(_to(a), _to(w), _to(a_s), _to(w_s), bias.to(DEV), torch.float16)
+    assert out.dtype == torch.float16 and out.shape == (m, n)
+    expected = oracle.linear(a, w, a_s, w_s) + bias.float().numpy()[None, :]
+    assert max_rel(out.float().cpu().numpy(), expected) <= MAX_REL
+
+
+@pytest.mark.parametrize("n,k", [(6144, 4096), (24576, 4096), (4096, 12288), (4096, 4096), (12288, 4096),
+                                 (4096, 8192)])
+def test_static_fused_qwen35_generation_shapes(n, k):
+    """The fused op on the 9B decoder's projection shapes at 1-4 rows, equal
+    to static quant + linear (reference tests/test_npu_ops.py:607-683)."""
+    native = _native()
+    ext = native.load_extension()
+    w, w_s = _hif8_weights(n, k, seed=n + k)
+    wd, wsd = _to(w), _to(w_s)
+    fixed = torch.tensor([5.0 / 32768.0], device=DEV)
+    for m in (1, 2, 3, 4):
+        x = torch.randn(m, k, generator=torch.Generator().manual_seed(m + k)).to(torch.bfloat16).to(DEV)
+        data, row_scale = native.static_quant(x, fixed)
+        expected = ext.soft_hif8_gemm(data, wd, row_scale, wsd, None, torch.bfloat16)
+        actual = ext.soft_hif8_static_fused_gemm(x, wd, fixed, wsd, None, torch.bfloat16)
+        torch.testing.assert_close(actual.float(), expected.float(), rtol=0, atol=0)
