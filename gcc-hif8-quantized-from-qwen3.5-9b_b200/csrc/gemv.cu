@@ -27,8 +27,11 @@
 //     (stored in that order, 16-byte chunks rotated so the fragment loads are
 //     free of bank conflicts; rows of padding tokens are not loaded);
 //   * partial sums are reduced in a fixed order: the warps of an item after
-//     every item, the cluster ranks once for all items at the end, through
-//     distributed shared memory -- deterministic, no global scratch.
+//     every item (or of all items at the end, for M <= 4), then the cluster
+//     ranks: every rank stores its partials into the owning rank's shared
+//     memory (distributed shared memory) as they are produced, and each rank
+//     sums the slots of its share once, at the end -- deterministic, no
+//     global scratch.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -204,11 +207,18 @@ __host__ __device__ constexpr size_t defer_bytes(int m, int items) {
 // (one bank group) apart modulo 128.
 __host__ __device__ constexpr int act_stride_bytes(int kc) { return kc * 2 + 16; }
 
-// shared memory: table | activation tile | warp partials x2 | CTA partials
-// of every item of this cluster (reduced across the cluster once, at the end)
+// Floats of the split-K receive buffer: S slots of ceil(total / S) partials,
+// total <= max_items * rows * tokens, so S - 1 floats of rounding at most.
+__host__ __device__ constexpr size_t gemv_part_floats(int nt, int wr, int max_items) {
+  return max_items > 0 ? (size_t)max_items * (16 * wr) * 8 * nt + 8 : 0;
+}
+
+// shared memory: table | activation tile | warp partials x2 | the split-K
+// receive buffer (partials of this rank's share of the cluster's outputs,
+// pushed by every rank; reduced once, at the end)
 __host__ __device__ constexpr size_t gemv_smem_bytes(int nt, int kc, int wr, int max_items) {
   return (size_t)kLutBytes + (size_t)(8 * nt) * act_stride_bytes(kc) +
-         2 * (size_t)kWarps * (8 * nt) * kRedStride * sizeof(float) + (size_t)max_items * (16 * wr) * 8 * nt * sizeof(float);
+         2 * (size_t)kWarps * (8 * nt) * kRedStride * sizeof(float) + gemv_part_floats(nt, wr, max_items) * sizeof(float);
 }
 
 template <int NT, int OUT, int ASRC>
@@ -225,8 +235,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   const int act_stride = act_stride_bytes(kc);
   uint8_t *act = smem + kLutBytes;
   float *red = reinterpret_cast<float *>(act + (size_t)kTok * act_stride);  // [2][kWarps][kTok][kRedStride]
-  float *part = red + 2 * kWarps * kRedStride * kTok;                       // [items][kTok][16 * WR]
-  float *wpd = part + (size_t)plan.max_items * 16 * WR * kTok;               // deferred: [item][warp][m][16]
+  float *part = red + 2 * kWarps * kRedStride * kTok;                       // [S][share] received partials
+  float *wpd = part + gemv_part_floats(NT, WR, plan.max_items);              // deferred: [item][warp][m][16]
+  // split-K ranks store into each other's shared memory from the first item
+  // on: every CTA of the cluster must have started (arrive here, wait before
+  // the first store)
+  if (S > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
   // ---- work assignment -----------------------------------------------------
   const int g = lane >> 2, t = lane & 3;
@@ -438,6 +452,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
   for (int nt = 0; nt < NT; ++nt) tok_real[nt] = nt * 8 + g < p.m;
 
   cg::cluster_group cluster = cg::this_cluster();
+  // Cross-rank reduction by push: the (item, token, row) outputs of the
+  // cluster are split into S contiguous shares; rank r owns share r, and every
+  // rank stores its partial of an output into slot [its rank] of the owner's
+  // receive buffer as soon as the item is reduced over its warps, so the
+  // transfers overlap the streaming of the next items and the end phase reads
+  // only local shared memory.
+  const int per_item = rows_per_item * mt;
+  const int share = S > 1 ? (my_items * per_item + S - 1) / S : 0;
+  auto push = [&](int idx, float v) {
+    const int owner = idx / share;
+    cluster.map_shared_rank(part, owner)[rank * share + (idx - owner * share)] = v;
+  };
+  if (S > 1) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   for (int item = 0; item < my_items; ++item) {
     const uint8_t *n0 = nullptr, *n1 = nullptr;
     const bool has_next = item + 1 < my_items;
@@ -504,7 +531,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
     }
     __syncthreads();
     const int row_base = (cluster_id + item * plan.clusters) * rows_per_item;
-    float *cpart = part + (size_t)item * rows_per_item * kTok;
     for (int e = tid; e < rows_per_item * mt; e += kThreads) {
       const int m = e / rows_per_item, rl = e - m * rows_per_item;  // token, row within the item
       const int grp = rl >> 4, r16 = rl & 15;
@@ -520,14 +546,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
           store_out<OUT>(p.out, (int64_t)m * p.n + n, v);
         }
       } else {
-        cpart[e] = v;
+        push(item * per_item + e, v);
       }
     }
   }
   if (plan.defer_items) {
     // every item at once: the WK warps of a row group summed in warp order
     __syncthreads();
-    const int per_item = rows_per_item * mt;
     for (int e = tid; e < my_items * per_item; e += kThreads) {
       const int item = e / per_item, rem = e - item * per_item;
       const int m = rem / rows_per_item, rl = rem - m * rows_per_item;
@@ -544,33 +569,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
           store_out<OUT>(p.out, (int64_t)m * p.n + n, v);
         }
       } else {
-        part[(size_t)item * rows_per_item * kTok + rem] = v;
+        push(e, v);
       }
     }
   }
   if (S == 1) return;
 
-  // ---- cross-rank reduction of every item, once: rank r owns a contiguous
-  // range of the (item, token, row) elements; partials are summed in rank
-  // order (deterministic) and consecutive threads store consecutive rows.
+  // ---- cross-rank reduction, once: the barrier makes every rank's pushed
+  // partials visible; rank r sums its share's S slots in rank order
+  // (deterministic) and consecutive threads store consecutive rows.  Nothing
+  // reads another CTA's shared memory after the barrier, so no CTA waits for
+  // its peers before leaving.
   cluster.sync();
-  const int per_item = rows_per_item * mt;
-  const int total = my_items * per_item;
-  const int share = (total + S - 1) / S;
-  const int e_end = min(total, (rank + 1) * share);
-  for (int e = rank * share + tid; e < e_end; e += kThreads) {
+  const int e_begin = rank * share;
+  const int e_end = min(my_items * per_item, e_begin + share);
+  for (int e = e_begin + tid; e < e_end; e += kThreads) {
     const int item = e / per_item, rem = e - item * per_item;
     const int m = rem / rows_per_item, rl = rem - m * rows_per_item;
-    const size_t idx = (size_t)item * rows_per_item * kTok + rem;
-    // every rank's partial is loaded before the sum (S <= 8), which then
-    // runs in rank order
-    float pv[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r) pv[r] = r < S ? cluster.map_shared_rank(part, r)[idx] : 0.f;
     float v = 0.f;
 #pragma unroll
     for (int r = 0; r < 8; ++r)
-      if (r < S) v += pv[r];
+      if (r < S) v += part[r * share + (e - e_begin)];
     const int n = (cluster_id + item * plan.clusters) * rows_per_item + rl;
     if (n < p.n) {
       v = v * __ldg(p.cs + n);
@@ -579,7 +598,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
       store_out<OUT>(p.out, (int64_t)m * p.n + n, v);
     }
   }
-  cluster.sync();  // no CTA may leave while a peer could still read its partials
 }
 
 // Any shape, any alignment: one warp per (m, n) output, FP32 accumulation in
