@@ -194,3 +194,62 @@ def test_paged_attention_matches_reference_attention_fixture():
                                       block_size=4, scale=0.25)
     _check_attention(out, expected)
     assert np.abs(out.float().cpu().numpy() - g["pa_out"]).max() < 5e-2
+
+
+def test_kv_write_fp16_source_small_pages():
+    """FP16 K/V rows (the reference's float16 serving dtype) written into
+    16-token pages: byte-exact with the oracle's quant + pack + scatter."""
+    kv = _kv()
+    tokens, heads, d, block, nblocks = 53, 4, 256, 16, 6
+    gen = torch.Generator().manual_seed(44)
+    key = (torch.randn(tokens, heads, d, generator=gen) * 2.0).to(torch.float16)
+    value = (torch.randn(tokens, heads, d, generator=gen) * 0.7).to(torch.float16)
+    ks = np.array([0.61, 0.45, 0.93, 0.27], np.float32) / 8.0
+    vs = np.array([0.33, 0.52, 0.41, 0.76], np.float32) / 8.0
+    slots = np.random.default_rng(5).permutation(nblocks * block)[:tokens].astype(np.int64)
+    slots[[3, 17]] = -1
+    kc = torch.zeros((nblocks, block, heads, d + 4), dtype=torch.uint8, device=DEV)
+    vc = torch.zeros_like(kc)
+    kv.write_static(key.to(DEV), value.to(DEV), kc, vc, torch.from_numpy(slots).to(DEV),
+                    torch.from_numpy(ks).to(DEV), torch.from_numpy(vs).to(DEV), validate=True)
+    torch.cuda.synchronize()
+    kref = np.zeros((nblocks, block, heads, d + 4), np.uint8)
+    vref = np.zeros_like(kref)
+    kbits = key.view(torch.int16).numpy().view(np.uint16)
+    vbits = value.view(torch.int16).numpy().view(np.uint16)
+    oracle.kv_write(kbits, ks, slots, kref, dtype="f16")
+    oracle.kv_write(vbits, vs, slots, vref, dtype="f16")
+    np.testing.assert_array_equal(kc.cpu().numpy(), kref)
+    np.testing.assert_array_equal(vc.cpu().numpy(), vref)
+
+
+def test_paged_decode_small_pages_and_padded_block_tables():
+    """The decode kernel (head size 256, GQA group 4) on 16-token pages, one
+    to 1000 keys per request, with every block-table entry past a request's
+    pages pointing outside the cache: those entries are never read."""
+    kv = _kv()
+    heads, kv_heads, d, block = 16, 4, 256, 16
+    ctx = [1, 17, 250, 1000]
+    kc, vc, table = _make_paged(len(ctx), ctx, kv_heads, d, block, seed=91)
+    for b, c in enumerate(ctx):
+        table[b, (c + block - 1) // block:] = kc.shape[0] + 1000
+    q = oracle.round_bf16(np.random.default_rng(9).standard_normal((len(ctx), heads, d)).astype(np.float32))
+    scale = 1.0 / math.sqrt(d)
+    expected = oracle.paged_attention(q, kc, vc, table, ctx, block_size=block, scale=scale)
+    out = kv.paged_attention(torch.from_numpy(q).to(torch.bfloat16).to(DEV), torch.from_numpy(kc).to(DEV),
+                             torch.from_numpy(vc).to(DEV), torch.from_numpy(table).to(DEV), ctx, scale=scale)
+    _check_attention(out, expected)
+
+
+def test_paged_decode_head_size_128():
+    """Decode rows of head size 128 take the general kernel (GQA group 2)."""
+    kv = _kv()
+    heads, kv_heads, d, block = 8, 4, 128, 32
+    ctx = [7, 64, 333]
+    kc, vc, table = _make_paged(len(ctx), ctx, kv_heads, d, block, seed=13, second_scale_every=7)
+    q = oracle.round_bf16(np.random.default_rng(4).standard_normal((len(ctx), heads, d)).astype(np.float32))
+    scale = 1.0 / math.sqrt(d)
+    expected = oracle.paged_attention(q, kc, vc, table, ctx, block_size=block, scale=scale)
+    out = kv.paged_attention(torch.from_numpy(q).to(torch.bfloat16).to(DEV), torch.from_numpy(kc).to(DEV),
+                             torch.from_numpy(vc).to(DEV), torch.from_numpy(table).to(DEV), ctx, scale=scale)
+    _check_attention(out, expected)
