@@ -190,13 +190,19 @@ int ensure_smem_limit(const void *kernel, size_t bytes);
 // completed and its writes are visible (immediately for an ordinary launch).
 // Work before the wait touches only constant tables and shared memory, or
 // issues L2 prefetches (L2 is the coherence point, so a prefetch never
-// yields a stale value).  No kernel signals its dependents early
-// (griddepcontrol.launch_dependents): measured on B200, an early signal
-// lets the dependent's CTAs occupy SMs while this grid still runs and made
-// the configs[1] sweep 5 % slower as a CUDA graph, while the implicit signal
-// at exit made it 2 % faster than ordinary launches.
+// yields a stale value).  Only the vectorised static quant signals its
+// dependents early (griddepcontrol.launch_dependents, at its start): its grid
+// of a few dozen CTAs leaves most SMs idle, so the following linear's CTAs
+// launch there and build their tables before they wait for its completion
+// (the configs[1] step 358.9 -> 354.7 us).  For the GEMV, which fills every
+// SM, an early signal made the sweep 5 % slower as a CUDA graph, while the
+// implicit signal at exit made it 2 % faster than ordinary launches.
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // False when the environment sets HIF8_DISABLE_PDL=1 (read once).
 bool pdl_enabled();
