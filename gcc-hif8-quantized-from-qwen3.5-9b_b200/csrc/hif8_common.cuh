@@ -190,11 +190,12 @@ int ensure_smem_limit(const void *kernel, size_t bytes);
 // completed and its writes are visible (immediately for an ordinary launch).
 // Work before the wait touches only constant tables and shared memory, or
 // issues L2 prefetches (L2 is the coherence point, so a prefetch never
-// yields a stale value).  Only the vectorised static quant signals its
-// dependents early (griddepcontrol.launch_dependents, at its start): its grid
-// of a few dozen CTAs leaves most SMs idle, so the following linear's CTAs
-// launch there and build their tables before they wait for its completion
-// (the configs[1] step 358.9 -> 354.7 us).  For the GEMV, which fills every
+// yields a stale value).  Only small grids signal their dependents early
+// (griddepcontrol.launch_dependents, at their start): the vectorised static
+// quant and the decoder's glue kernels at small batch leave most SMs idle,
+// so the following linear's CTAs launch there and build their tables before
+// they wait for the signalling grid's completion (the configs[1] step 358.9
+// -> 354.7 us).  For the GEMV, which fills every
 // SM, an early signal made the sweep 5 % slower as a CUDA graph, while the
 // implicit signal at exit made it 2 % faster than ordinary launches.
 

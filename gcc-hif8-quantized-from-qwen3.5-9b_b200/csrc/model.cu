@@ -94,9 +94,17 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const uint16_t *_
 }
 
 // ---------------------------------------------------------- SiLU-gated MLP --
+// A glue kernel whose grid leaves most SMs idle (a decode step at batch 1)
+// signals its dependent at start, so the GEMV that consumes its output
+// launches on the idle SMs and sets up before it waits for this grid's
+// completion.  Measured on the 9B decoder: batch 1 295.0 -> 299.8 tok/s; with
+// larger grids (batch 4) the early CTAs only contend, so they do not signal.
+constexpr unsigned kEarlySignalMaxCtas = 48;
+
 __global__ void silu_mul_kernel(const uint16_t *__restrict__ gu, int64_t rows, int64_t inter,
                                 uint16_t *__restrict__ out) {
   pdl_wait();  // inputs come from the previous kernel of the stream
+  if (gridDim.x * gridDim.y <= kEarlySignalMaxCtas) pdl_launch_dependents();
   const int64_t total = rows * inter / 2;  // pairs
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = (2 * i) / inter, c = 2 * i - r * inter;
@@ -112,6 +120,7 @@ __global__ void silu_mul_kernel(const uint16_t *__restrict__ gu, int64_t rows, i
 __global__ void gate_mul_kernel(const uint16_t *__restrict__ x, const uint16_t *__restrict__ gate, int64_t n,
                                 uint16_t *__restrict__ out) {
   pdl_wait();  // inputs come from the previous kernel of the stream
+  if (gridDim.x * gridDim.y <= kEarlySignalMaxCtas) pdl_launch_dependents();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = to_bf(bf(x[i]) * sigmoid(bf(gate[i])));
 }
@@ -189,6 +198,7 @@ constexpr int kGdnRows = kGdnDim / 2;  // state rows per thread
 
 __global__ void __launch_bounds__(kGdnThreads) gdn_kernel(const Hif8GdnArgs p) {
   pdl_wait();  // inputs come from the previous kernel of the stream
+  if (gridDim.x * gridDim.y <= kEarlySignalMaxCtas) pdl_launch_dependents();
   __shared__ float qs[kGdnDim], ks[kGdnDim];
   __shared__ float scratch[32];
   const int vh = blockIdx.x, b = blockIdx.y;
