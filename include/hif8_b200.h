@@ -11,6 +11,14 @@
  * Each entry point replaces one operator of the reference plugin; the cited
  * lines are in the reference project (csrc/extension/ is its ACLNN bridge,
  * src/vllm_ascend_hif8/ its Python layer).
+ *
+ * Kernels are launched with programmatic stream serialization (set
+ * HIF8_DISABLE_PDL=1 to turn it off), and hif8_static_quant may let the next
+ * programmatic launch of the stream begin before it completes.  A kernel of
+ * the caller that is itself launched with that attribute right after one of
+ * these entry points must wait for the grid dependency
+ * (cudaGridDependencySynchronize / griddepcontrol.wait) before it reads
+ * their outputs; ordinary launches are unaffected.
  */
 #ifndef HIF8_B200_H
 #define HIF8_B200_H
