@@ -128,6 +128,12 @@ def test_cabi_rejects_contract_violations_without_device_work():
     # attention: heads must be a multiple of kv heads
     assert lib.hif8_paged_attention(fake, fake, fake, fake, fake, fake, 1, 1, 6, 4, 256, 8, 128, 1, 1, 1.0, 1,
                                     fake, None, 0, None) == 1
+    # embedding gather: positive vocabulary and row size, pointers for any ids
+    assert lib.hif8_embedding_gather(fake, fake, 0, 64, fake, 1, fake, None, None) == 1
+    assert lib.hif8_embedding_gather(fake, fake, 8, 0, fake, 1, fake, None, None) == 1
+    assert lib.hif8_embedding_gather(fake, fake, 8, 64, fake, -1, fake, None, None) == 1
+    assert lib.hif8_embedding_gather(None, fake, 8, 64, fake, 1, fake, None, None) == 1
+    assert lib.hif8_embedding_gather(fake, fake, 8, 64, None, 0, fake, None, None) == cabi.HIF8_OK  # no ids
     assert lib.hif8_status_string(3) == b"workspace missing or too small"
 
 
