@@ -15,12 +15,16 @@ bytes per call = N*K weight bytes + 4N channel scales + 2MK BF16 activation
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-With N > 1 (torchrun, one rank per GPU, NCCL) every rank runs the full sweep
-on its own weights (independent replicas, no collective: "weak" scaling,
-value = all ranks' bytes / the slowest rank's time).  Beside it the line
-reports the same sweep split tensor-parallel (``tp_sweep``: gate/up and qkv
-by output channel, down by input channel + NCCL all-reduce; strong scaling)
-and the configs[4] decoder tensor-parallel over the N GPUs (``decode``).
+With N > 1 (torchrun, one rank per GPU, NCCL) the headline is the same
+problem split tensor-parallel over the ranks (gate/up and qkv by output
+channel, down by input channel + NCCL all-reduce): strong scaling, value =
+the sweep's bytes / the slowest rank's time, so value_N / (N * value_1) is
+the strong-scaling efficiency.  Before it is timed every call is checked
+against the unsharded layer of the same quantised weight, and the
+configs[4] decoder tensor-parallel over the N GPUs against its single-GPU
+model (``tp_parity``); a failed check ends the run with exit code 3.
+Beside it: ``replica_sweep`` (every rank runs the full sweep on its own
+weights, no collective: weak scaling) and ``decode`` (the decoder's tok/s).
 """
 
 from __future__ import annotations
@@ -45,6 +49,8 @@ SHAPES = (("gate_up", 24576, 4096), ("down", 4096, 12288), ("qkv", 6144, 4096))
 METRIC = "HiF8 GEMV HBM GB/s vs peak (M=1-16); W8A8KV8 decode tok/s at 1/2/4/8 B200"
 UNIT = "GB/s"
 FALLBACK_HBM_GBS = 6650.0
+TP_SWEEP_TOL = 1e-2    # north-star tolerance of a TP split (only the summation order changes)
+DECODER_TP_TOL = 2e-2  # logits after 32 layers of BF16-rounded row-parallel partials
 
 
 def call_bytes(m: int, n: int, k: int) -> int:
@@ -55,17 +61,17 @@ def step_bytes() -> int:
     return sum(call_bytes(m, n, k) for m in M_VALUES for _, n, k in SHAPES)
 
 
-def workload_config(world: int) -> dict:
+def workload_config(world: int, parallelism: str | None = None) -> dict:
     return {
         "workload": "configs[1] decode GEMV sweep: M in {1,2,4,8,16} x (N,K) in {(24576,4096) gate_up, "
                     "(4096,12288) down, (6144,4096) qkv}; one static-quant + HiF8 linear call each",
         "calls_per_step": len(M_VALUES) * len(SHAPES),
         "algorithmic_bytes_per_step": step_bytes(),
-        "weights": "N(0,0.02) BF16 -> HiF8 u8, per-channel scale = row amax / 32768; seeded",
+        "weights": "N(0,0.02) BF16 -> HiF8 u8, per-channel scale = row amax / 32768 (quantised over full rows, "
+                   "then sharded); seeded",
         "activations": "N(0,1) BF16, fixed input_scale = calibration absmax / 32768",
         "l2": "inputs larger than L2: 15 distinct weights (880 MB) streamed per step",
-        "parallelism": "single GPU" if world == 1 else f"{world} independent replicas (one full sweep per GPU, no "
-                       "collective); the tensor-parallel sweep is reported under tp_sweep",
+        "parallelism": parallelism or ("single GPU" if world == 1 else f"tp{world}"),
         "graph": "one step captured as a CUDA graph, replayed per timed step",
     }
 
@@ -248,10 +254,18 @@ def run_reference(args) -> None:
 
 # ------------------------------------------------------------- our arm ---
 
-def build_layers(world: int, rank: int, device, replica: int = 0):
+def build_layers(world: int, rank: int, device, replica: int = 0, keep_reference: bool = False):
     """Seeded weights and activations for every call of the sweep; this rank's
     tensor-parallel shard when world > 1 (replica: a different seed set for an
-    independent full copy)."""
+    independent full copy).
+
+    Every rank generates the same global weight of a call and quantises it
+    ONCE over its full rows (bytes + per-row scale), as an exported
+    checkpoint holds it; a column-parallel rank keeps its rows (and their
+    scales), a row-parallel rank its input columns with the full rows'
+    scales -- so the shards' results sum to the unsharded layer's result.
+    ``keep_reference`` also keeps the unsharded layer and activation of every
+    call (the TP-1 computation the parity check compares against)."""
     import torch
 
     from hif8_b200 import scheme
@@ -260,24 +274,119 @@ def build_layers(world: int, rank: int, device, replica: int = 0):
     for m in M_VALUES:
         for idx, (name, n, k) in enumerate(SHAPES):
             row_parallel = name == "down"
-            # column shards differ per rank; row shards are slices of one seeded weight
-            seed = 1000 * m + idx + (0 if row_parallel else 7919 * rank) + 104729 * replica
+            seed = 1000 * m + idx + 104729 * replica
             g = torch.Generator(device=device).manual_seed(seed)
             n_loc = n if (world == 1 or row_parallel) else n // world
             k_loc = k // world if (world > 1 and row_parallel) else k
-            w_full_rows = torch.randn(n_loc, k, device=device, generator=g, dtype=torch.float32).mul_(0.02)
-            w = w_full_rows[:, rank * k_loc:(rank + 1) * k_loc] if k_loc != k else w_full_rows
-            w = w.to(torch.bfloat16).contiguous()
+            w = torch.randn(n, k, device=device, generator=g, dtype=torch.float32).mul_(0.02).to(torch.bfloat16)
             calib = torch.randn(16, k, device=device, generator=g).to(torch.bfloat16)
             input_scale = (calib.float().abs().amax() / 32768.0).reshape(1).to(torch.float32)
-            layer = scheme.Hif8StaticLinear.from_float(w, input_scale)
-            x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
-            x = x[:, rank * k_loc:(rank + 1) * k_loc].contiguous() if k_loc != k else x
-            calls.append({"m": m, "name": name, "n": n, "k": k, "layer": layer, "x": x, "row_parallel": row_parallel,
-                          "n_loc": n_loc, "k_loc": k_loc})
-            del w_full_rows, w
+            data, scale = scheme.quantize_weight_rows(w)
+            del w
+            x_full = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
+            if world == 1:
+                shard, shard_scale, x = data, scale, x_full
+            elif row_parallel:
+                shard, shard_scale = data[:, rank * k_loc:(rank + 1) * k_loc].contiguous(), scale
+                x = x_full[:, rank * k_loc:(rank + 1) * k_loc].contiguous()
+            else:
+                shard = data[rank * n_loc:(rank + 1) * n_loc].contiguous()
+                shard_scale = scale[rank * n_loc:(rank + 1) * n_loc].contiguous()
+                x = x_full
+            layer = scheme.Hif8StaticLinear(shard, shard_scale.reshape(-1, 1), input_scale)
+            call = {"m": m, "name": name, "n": n, "k": k, "layer": layer, "x": x, "row_parallel": row_parallel,
+                    "n_loc": n_loc, "k_loc": k_loc}
+            if keep_reference and world > 1:
+                call["reference"] = (scheme.Hif8StaticLinear(data, scale.reshape(-1, 1), input_scale), x_full)
+            calls.append(call)
+            del data, scale
     torch.cuda.synchronize()
     return calls
+
+
+def tp_sweep_parity(calls, world: int, rank: int, device) -> dict:
+    """Every call of the tensor-parallel sweep against the unsharded (TP-1)
+    layer of the same quantised weight: column-parallel shards against their
+    rows of the TP-1 output, row-parallel results (after the all-reduce)
+    against the whole TP-1 output.  Errors are max |tp - ref| / max |ref|
+    (global) and the same per output channel; the worst over calls and
+    ranks is returned (every rank takes the same collective steps)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from hif8_b200 import scheme
+
+    worst = torch.zeros(2, dtype=torch.float64, device=device)
+    for c in calls:
+        ref_layer, x_full = c["reference"]
+        ref = scheme.apply(ref_layer, x_full).float()
+        y = scheme.apply(c["layer"], c["x"])
+        if c["row_parallel"]:
+            dist.all_reduce(y)
+        else:
+            ref = ref[:, rank * c["n_loc"]:(rank + 1) * c["n_loc"]]
+        y = y.float()
+        diff = (y - ref).abs()
+        glob = float(diff.max()) / max(float(ref.abs().max()), 1e-12)
+        floor = max(float(ref.abs().max()) * 1e-3, 1e-30)
+        chan = float((diff.amax(dim=0) / ref.abs().amax(dim=0).clamp(min=floor)).max())
+        worst = torch.maximum(worst, torch.tensor([glob, chan], dtype=torch.float64, device=device))
+    dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+    glob, chan = (float(v) for v in worst.tolist())
+    ok = bool(np.isfinite(glob) and glob <= TP_SWEEP_TOL and chan <= TP_SWEEP_TOL)
+    return {"max_rel": glob, "channel_max_rel": chan, "tol": TP_SWEEP_TOL, "pass": ok,
+            "against": "the unsharded (TP-1) layer of the same quantised weight, every call of the sweep"}
+
+
+def decoder_tp_parity(device, world: int, rank: int, calib: dict, steps: int = 8) -> dict:
+    """The configs[4] decoder tensor-parallel over the ranks (peer-memory
+    decode reduce, as measured) against the TP-1 model of the same seeded
+    weights and static scales, which every rank also builds on its own GPU:
+    prefill logits of a seeded 64-token prompt and ``steps`` teacher-forced
+    decode steps at batch 1 and 4, compared on this rank's vocabulary slice
+    (max |tp - ref| / max |ref|), plus the greedy tokens of every step."""
+    import torch
+    import torch.distributed as dist
+
+    from hif8_b200.decoder import Decoder, DecoderConfig, forced_logits
+
+    cfg = DecoderConfig()
+    g = torch.Generator(device=device).manual_seed(123)
+    prompts = {b: torch.randint(0, cfg.vocab, (b, 64), device=device, generator=g) for b in (1, 4)}
+    single = Decoder(cfg, "hif8", device, seed=0, max_batch=4, max_ctx=128, calibration=calib)
+    refs = {b: forced_logits(single, p, steps=steps) for b, p in prompts.items()}
+    del single
+    torch.cuda.empty_cache()
+    model = Decoder(cfg, "hif8", device, seed=0, tp_rank=rank, tp_size=world, max_batch=4, max_ctx=128,
+                    calibration=calib)
+    model.enable_peer_allreduce()
+    vl = model.vocab_local
+    worst = torch.zeros(1, dtype=torch.float64, device=device)
+    agree = torch.zeros(1, dtype=torch.int64, device=device)
+    total = 0
+    for b, p in prompts.items():
+        ref_logits, ref_tokens = refs[b]
+        logits, tokens = forced_logits(model, p, ref_tokens, steps=steps)
+        for lg, tk, rl, rt in zip(logits, tokens, ref_logits, ref_tokens):
+            rel = float((lg - rl[:, rank * vl:(rank + 1) * vl]).abs().max()) / max(float(rl.abs().max()), 1e-12)
+            worst = torch.maximum(worst, torch.tensor([rel], dtype=torch.float64, device=device))
+            agree += int(torch.equal(tk, rt))
+            total += 1
+    model.peer.check()
+    torch.cuda.synchronize()
+    dist.barrier()
+    model.peer.close()
+    del model
+    torch.cuda.empty_cache()
+    dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+    dist.all_reduce(agree, op=dist.ReduceOp.MIN)
+    rel = float(worst.item())
+    ok = rel <= DECODER_TP_TOL
+    return {"logits_max_rel": rel, "tol": DECODER_TP_TOL, "greedy_steps_equal": int(agree.item()),
+            "steps_compared": total, "pass": ok,
+            "against": "the TP-1 model of the same seeded weights and static scales (prefill + "
+                       f"{steps} teacher-forced decode steps, batch 1 and 4)"}
 
 
 def time_sweep(calls, args, device, world: int, local_rank: int, *, tp: bool, profile: bool):
@@ -358,62 +467,89 @@ def run_ours(args) -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
-    from hif8_b200 import native, scheme
+    from hif8_b200 import native
 
     native.load_extension()
-    # The headline sweep: every rank runs the full configs[1] sweep on its own
-    # weights (independent replicas, no collective; weak scaling).
-    calls = build_layers(1, 0, device, replica=rank)
-    elapsed_ms, clocks = time_sweep(calls, args, device, world, local_rank, tp=False, profile=True)
-    value = world * step_bytes() * args.steps / (elapsed_ms * 1e-3) / 1e9
-    launches_per_step = sum(1 if c["m"] <= 4 else 2 for c in calls)
+    extra = {}
+    parity_ok = True
+    if world == 1:
+        # The headline sweep on one GPU: the full configs[1] problem.
+        calls = build_layers(1, 0, device)
+        elapsed_ms, clocks = time_sweep(calls, args, device, world, local_rank, tp=False, profile=True)
+        value = step_bytes() * args.steps / (elapsed_ms * 1e-3) / 1e9
+        launches_per_step = sum(1 if c["m"] <= 4 else 2 for c in calls)
+        parallelism = "single GPU"
+    else:
+        # N > 1: the headline is the SAME problem (the configs[1] sweep)
+        # split tensor-parallel over the ranks (column: gate_up, qkv; row:
+        # down + all-reduce) -- strong scaling, so value_N / (N * value_1) is
+        # the strong-scaling efficiency.  Checked against the unsharded
+        # layers before it is timed; a failed check ends the run non-zero.
+        calls = build_layers(world, rank, device, keep_reference=True)
+        extra["tp_parity"] = {"sweep": tp_sweep_parity(calls, world, rank, device)}
+        parity_ok &= extra["tp_parity"]["sweep"]["pass"]
+        for c in calls:
+            c.pop("reference")
+        torch.cuda.empty_cache()
+        elapsed_ms, clocks = time_sweep(calls, args, device, world, local_rank, tp=True, profile=True)
+        value = step_bytes() * args.steps / (elapsed_ms * 1e-3) / 1e9
+        launches_per_step = sum(1 if c["m"] <= 4 else 2 for c in calls)
+        parallelism = f"tp{world} (column: gate_up, qkv; row: down + NCCL all-reduce)"
 
     # -------------------------- dominant kernel: the GEMV, timed alone ---
-    roofline = gemv_roofline(calls, args, device, 1)
+    roofline = gemv_roofline(calls, args, device, world)
 
     # -------------------------------------------- e2e: public API, host I/O
-    e2e = measure_e2e(calls, args, device, world)
+    e2e = measure_e2e(calls, args, device, world, tp=world > 1)
 
-    # ------------- the same sweep tensor-parallel over the ranks (strong) ---
-    tp_sweep = None
     if world > 1:
+        # beside the headline: N independent full-size replicas (weak)
         calls.clear()
         torch.cuda.empty_cache()
-        tp_calls = build_layers(world, rank, device)
-        tp_ms, _ = time_sweep(tp_calls, args, device, world, local_rank, tp=True, profile=False)
-        tp_sweep = {"value": step_bytes() * args.steps / (tp_ms * 1e-3) / 1e9, "unit": UNIT, "scaling": "strong",
-                    "ms_per_step": tp_ms / args.steps,
-                    "parallelism": f"tp{world} (column: gate_up, qkv; row: down + NCCL all-reduce)"}
-        tp_calls.clear()
+        rep_calls = build_layers(1, 0, device, replica=rank)
+        rep_ms, _ = time_sweep(rep_calls, args, device, world, local_rank, tp=False, profile=False)
+        extra["replica_sweep"] = {"value": world * step_bytes() * args.steps / (rep_ms * 1e-3) / 1e9, "unit": UNIT,
+                                  "scaling": "weak", "ms_per_step": rep_ms / args.steps,
+                                  "what": "every rank runs the full configs[1] sweep on its own weights, "
+                                          "no collective"}
+        rep_calls.clear()
         torch.cuda.empty_cache()
 
     # ------------------- the other hot-path kernels (one GPU, timed alone) ---
-    extra = {}
     if world == 1 and not args.no_extra:
         extra["prefill_gemm"] = measure_prefill_gemm(device)
         extra["paged_attention"] = measure_paged_attention(device)
-    if tp_sweep is not None:
-        extra["tp_sweep"] = tp_sweep
+        extra["hbm_kernels"] = measure_hbm_kernels(device)
     if not args.no_decode:
         calls.clear()
         torch.cuda.empty_cache()
-        extra["decode"] = measure_decoder(device, world, rank)
+        extra["decode"] = measure_decoder(device, world, rank, check_parity=world > 1)
+        if "tp_parity" in extra["decode"]:
+            extra.setdefault("tp_parity", {})["decoder"] = extra["decode"].pop("tp_parity")
+            parity_ok &= extra["tp_parity"]["decoder"]["pass"]
 
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
+        if not parity_ok:
+            sys.exit(3)
         return
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(world),
+        "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(world, parallelism),
         "gpu_launches": launches_per_step * args.steps, "clocks": clocks.summary(), "roofline": roofline,
         "e2e": e2e, **extra,
     }
+    if "decode" in extra:
+        line["decode_tok_s"] = {b: extra["decode"]["hif8_w8a8kv8"][b]["tok_s"] for b in ("batch1", "batch4")}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = time_cpu_baseline(args.cpu_budget)
     print(json.dumps(line), flush=True)
+    if not parity_ok:
+        print("[bench] tensor-parallel parity check FAILED (tp_parity in the line)", file=sys.stderr)
+        sys.exit(3)
 
 
 def load_peak_bf16() -> tuple[float, str]:
@@ -524,11 +660,88 @@ def measure_paged_attention(device) -> dict:
             "per_config": per, "timing": "median of 5 decode steps, each after a read-based L2 eviction, CUDA events"}
 
 
-def measure_decoder(device, world: int, rank: int) -> dict:
+HBM_KERNEL_CASES = {
+    # name: (kernel, the size where HBM is the bound, the decode-size case)
+    "quant": ("static_quant_vec16", "x [4096, 12288] BF16 (configs[2] prefill, down input)",
+              "x [16, 12288] BF16"),
+    "kv_write": ("kv_write_kernel", "16384 tokens x 4 KV heads x 256, K and V, BF16 source",
+                 "4 tokens (a batch-4 decode step)"),
+    "embedding": ("embedding_gather", "16384 ids of a [248320, 4096] HiF8 table",
+                  "4 ids (a batch-4 decode step)"),
+}
+
+
+def _hbm_kernel_inputs(name: str, big: bool, device):
+    """(callable, algorithmic bytes) of one hbm_kernels case."""
+    import torch
+
+    from hif8_b200 import checkpoint, kv_cache, native
+
+    g = torch.Generator(device=device).manual_seed(4)
+    if name == "quant":
+        m, k = (4096, 12288) if big else (16, 12288)
+        x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
+        scale = torch.tensor([4.5 / 32768.0], device=device)
+        # BF16 in, u8 out, FP32 row scale out, the fixed scale in
+        return (lambda: native.static_quant(x, scale)), 3 * m * k + 4 * m + 4
+    if name == "kv_write":
+        tokens, heads, d, block = (16384 if big else 4), 4, 256, 128
+        layout = kv_cache.Hif8KVCacheLayout(max(tokens // block, 1) * 2, block, heads, d)
+        kc, vc = layout.allocate(device)
+        key = torch.randn(tokens, heads, d, device=device, generator=g).to(torch.bfloat16)
+        val = torch.randn(tokens, heads, d, device=device, generator=g).to(torch.bfloat16)
+        ks = torch.full((heads,), 0.3, device=device)
+        vs = torch.full((heads,), 0.25, device=device)
+        slots = torch.randperm(layout.num_blocks * block, device=device, generator=g)[:tokens].contiguous()
+        fn = lambda: torch.ops.hif8_b200.kv_cache_write(key, val, ks, vs, slots, kc, vc, None)
+        # per token and plane: heads x (2 D source bytes + D + 4 page bytes); + the 8-byte slot
+        return fn, tokens * (2 * heads * (2 * d + d + 4) + 8)
+    if name == "embedding":
+        vocab, hidden = 248320, 4096
+        ids_n = 16384 if big else 4
+        data = torch.randint(0, 0x6F, (vocab, hidden), dtype=torch.uint8, device=device, generator=g)
+        scale = torch.rand(vocab, device=device, generator=g) * 1e-4 + 1e-5
+        emb = checkpoint.Hif8Embedding(data, scale)
+        ids = torch.randint(0, vocab, (ids_n,), device=device, generator=g)
+        # per id: the HiF8 row, its FP32 scale, the BF16 output row, the 8-byte id
+        return (lambda: emb(ids)), ids_n * (hidden + 4 + 2 * hidden + 8)
+    raise ValueError(name)
+
+
+def measure_hbm_kernels(device) -> dict:
+    """Roofline of the other HBM-bound kernels of the path (static quant, KV
+    page write, HiF8 embedding gather): each timed alone at a size where HBM
+    is the bound (median of 5 launches, each after a read-based L2
+    eviction, CUDA events) against the measured HBM peak, with its
+    decode-size latency beside it."""
+    import torch
+
+    peak, kind = load_peak_hbm()
+    out = {"peak": peak, "unit": "GB/s", "peak_kind": kind,
+           "timing": "median of 5 launches, each after a read-based L2 eviction, CUDA events"}
+    for name, (kernel, big_desc, small_desc) in HBM_KERNEL_CASES.items():
+        fn, nbytes = _hbm_kernel_inputs(name, True, device)
+        fn()
+        t = _timed_alone(fn, device)
+        achieved = nbytes / (t * 1e-3) / 1e9
+        sfn, sbytes = _hbm_kernel_inputs(name, False, device)
+        sfn()
+        ts = _timed_alone(sfn, device)
+        out[name] = {"kernel": kernel, "bound": "hbm", "size": big_desc, "bytes": nbytes, "us": round(t * 1e3, 2),
+                     "achieved": round(achieved, 1), "frac": round(achieved / peak, 3),
+                     "decode_size": small_desc, "decode_us": round(ts * 1e3, 2)}
+        del fn, sfn
+        torch.cuda.empty_cache()
+    return out
+
+
+def measure_decoder(device, world: int, rank: int, check_parity: bool = False) -> dict:
     """the random-init Qwen3.5-9B-shaped hybrid decoder, 512
     prompt / 256 generated tokens at batch 1 and 4, tensor-parallel over the
     bench's GPUs; the W8A8KV8 HiF8 model and its BF16 twin.  Decode steps are
-    CUDA-graph replays timed with CUDA events (max over ranks)."""
+    CUDA-graph replays timed with CUDA events (max over ranks).  With
+    ``check_parity`` the tensor-parallel HiF8 model is first compared with
+    its single-GPU model (``tp_parity`` in the result)."""
     import torch
     import torch.distributed as dist
 
@@ -541,6 +754,8 @@ def measure_decoder(device, world: int, rank: int) -> dict:
            "prompt": 512, "generated": 256, "tp": world, "timing": "CUDA-graph decode steps, CUDA events, max over ranks",
            "allreduce": "single GPU" if world == 1 else "row-parallel partials summed over peer memory inside the "
                                                        "following residual + RMSNorm kernel (prefill: NCCL)"}
+    if check_parity:
+        out["tp_parity"] = decoder_tp_parity(device, world, rank, calib)
     for mode in ("hif8", "bf16"):
         model = Decoder(cfg, mode, device, seed=0, tp_rank=rank, tp_size=world, max_batch=4, max_ctx=768,
                         calibration=calib if mode == "hif8" else None)
@@ -710,7 +925,7 @@ def gemv_roofline(calls, args, device, world) -> dict:
             "per_launch": per}
 
 
-def measure_e2e(calls, args, device, world) -> dict:
+def measure_e2e(calls, args, device, world, tp: bool = False) -> dict:
     """The same sweep through the public API (hif8_b200.scheme, eager) with
     host buffers inside the timed region: every step copies its 15
     activations from one packed pinned host buffer to the device (one H2D
@@ -718,8 +933,10 @@ def measure_e2e(calls, args, device, world) -> dict:
     into one device buffer and reads it back into pinned host memory (one D2H
     transfer after the step's launches, so the copies do not split the chain
     of programmatic launches; one transfer instead of 15 saves their host
-    dispatch).  One independent replica per rank (value aggregates the
-    ranks)."""
+    dispatch).  With ``tp`` the calls are this rank's tensor-parallel shards
+    (row-parallel results all-reduced over NCCL inside the step) and value is
+    the sweep's bytes over the slowest rank's time; without it, one
+    independent replica per rank (value aggregates the ranks)."""
     import torch
     import torch.distributed as dist
 
@@ -736,7 +953,12 @@ def measure_e2e(calls, args, device, world) -> dict:
 
     def step():
         dev_in.copy_(host_in, non_blocking=True)
-        outs = [scheme.apply(c["layer"], x) for c, x in zip(calls, dev_x)]
+        outs = []
+        for c, x in zip(calls, dev_x):
+            y = scheme.apply(c["layer"], x)
+            if tp and c["row_parallel"]:
+                dist.all_reduce(y)
+            outs.append(y)
         host_out.copy_(torch.cat([y.reshape(-1) for y in outs]), non_blocking=True)
 
     for _ in range(max(args.warmup, 1)):
@@ -760,11 +982,13 @@ def measure_e2e(calls, args, device, world) -> dict:
             raise RuntimeError(f"e2e: non-finite output for {c['name']} M={c['m']}")
     h2d = host_in.numel() * 2
     d2h = host_out.numel() * 2
-    return {"value": world * step_bytes() * args.steps / (ms * 1e-3) / 1e9, "unit": UNIT,
+    problems = 1 if tp else world  # TP: one problem split over the ranks; else one per rank
+    return {"value": problems * step_bytes() * args.steps / (ms * 1e-3) / 1e9, "unit": UNIT,
             "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * d2h, "ms_per_step": ms / args.steps,
             "transfers_per_step": {"h2d": 1, "d2h": 1},
             "path": "hif8_b200.scheme.apply (eager PyTorch ops -> C ABI), pinned host buffers, outputs gathered on "
-                    "the device and read back in one transfer"}
+                    "the device and read back in one transfer" + (", tensor-parallel shards + NCCL all-reduce"
+                                                                  if tp else "")}
 
 
 def run_profile_case(spec: str, launches: int) -> None:
@@ -825,6 +1049,17 @@ def run_profile_case(spec: str, launches: int) -> None:
         starts = torch.arange(batch + 1, dtype=torch.int32, device=dev)
         for _ in range(2 + launches):
             torch.ops.hif8_b200.paged_attention(q, kc, vc, table, lens, starts, ctx, 1.0 / math.sqrt(d), True)
+        torch.cuda.synchronize()
+        print(f"profile case {spec}: {2 + launches} launches ok")
+        return
+    if parts[0] == "hbm" and len(parts) in (2, 3):
+        # hbm:<quant|kv_write|embedding>[:small]: two warm-up launches, then
+        # `launches` launches of that kernel at the bench's HBM-bound size
+        dev = torch.device("cuda", 0)
+        native.load_extension()
+        fn, _ = _hbm_kernel_inputs(parts[1], len(parts) == 2, dev)
+        for _ in range(2 + launches):
+            fn()
         torch.cuda.synchronize()
         print(f"profile case {spec}: {2 + launches} launches ok")
         return

@@ -180,6 +180,16 @@ int num_sms();
 // capture issue no attribute calls after the first eager launch).
 int ensure_smem_limit(const void *kernel, size_t bytes);
 
+// Argument checks of hif8_paged_attention (null pointers, non-positive or
+// inconsistent sizes, GQA group above 16): HIF8_OK or
+// HIF8_ERR_INVALID_ARGUMENT.  Shared by every attention entry point so they
+// report the same status for the same bad call.
+int paged_attention_args_status(const void *query, const void *key_cache, const void *value_cache,
+                                const void *block_tables, const void *seq_lens, const void *query_start,
+                                const void *out, int64_t batch, int64_t num_tokens, int64_t num_heads,
+                                int64_t kv_heads, int64_t head_size, int64_t num_blocks, int64_t block_size,
+                                int64_t max_blocks, int64_t max_seq_len);
+
 // ------------------------------------------- programmatic dependent launch --
 // The decode-path kernels are launched with the programmatic stream
 // serialization attribute, so the next kernel of the stream is launched as

@@ -824,12 +824,40 @@ static int decode_chunk(int64_t group, int64_t seq_heads, int64_t max_seq_len) {
 }
 
 // Sized for the finer of the two kernels' key chunks (the decode kernel's).
+// The product is computed with overflow checks: sizes whose partials would
+// not fit size_t give SIZE_MAX, which no workspace (and no scratch) meets.
 extern "C" size_t hif8_paged_attention_workspace_size(int64_t num_tokens, int64_t num_heads, int64_t head_size,
                                                       int64_t max_seq_len) {
-  const int64_t splits = (max_seq_len + kDecChunk - 1) / kDecChunk;
+  if (num_tokens <= 0 || num_heads <= 0 || head_size <= 0 || max_seq_len <= 0) return 0;
+  const int64_t splits = max_seq_len / kDecChunk + (max_seq_len % kDecChunk != 0);
   if (splits <= 1) return 0;
-  return (size_t)(num_tokens * num_heads * splits * part_stride(head_size)) * sizeof(float);
+  size_t bytes = 0;
+  if (__builtin_mul_overflow((size_t)num_tokens, (size_t)num_heads, &bytes) ||
+      __builtin_mul_overflow(bytes, (size_t)splits, &bytes) ||
+      __builtin_mul_overflow(bytes, (size_t)part_stride(head_size), &bytes) ||
+      __builtin_mul_overflow(bytes, sizeof(float), &bytes))
+    return SIZE_MAX;
+  return bytes;
 }
+
+namespace hif8 {
+
+int paged_attention_args_status(const void *query, const void *key_cache, const void *value_cache,
+                                const void *block_tables, const void *seq_lens, const void *query_start,
+                                const void *out, int64_t batch, int64_t num_tokens, int64_t num_heads,
+                                int64_t kv_heads, int64_t head_size, int64_t num_blocks, int64_t block_size,
+                                int64_t max_blocks, int64_t max_seq_len) {
+  if (batch <= 0 || num_tokens < 0 || num_heads <= 0 || kv_heads <= 0 || num_heads % kv_heads != 0 ||
+      head_size <= 0 || head_size % 4 != 0 || head_size > 1024 || num_blocks <= 0 || block_size <= 0 ||
+      max_blocks <= 0 || max_seq_len < 0)
+    return HIF8_ERR_INVALID_ARGUMENT;
+  if (!query || !key_cache || !value_cache || !block_tables || !seq_lens || !query_start || !out)
+    return HIF8_ERR_INVALID_ARGUMENT;
+  if (num_heads / kv_heads > 16) return HIF8_ERR_INVALID_ARGUMENT;
+  return HIF8_OK;
+}
+
+}  // namespace hif8
 
 template <int NQ>
 static int launch_attention(AttnArgs p, int64_t batch, int64_t q_groups, cudaStream_t s) {
@@ -849,15 +877,13 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
                                     int64_t block_size, int64_t max_blocks, int64_t max_seq_len,
                                     float softmax_scale, int causal,
                                     uint16_t *out, void *workspace, size_t workspace_bytes, void *stream) {
-  if (batch <= 0 || num_tokens < 0 || num_heads <= 0 || kv_heads <= 0 || num_heads % kv_heads != 0 ||
-      head_size <= 0 || head_size % 4 != 0 || head_size > 1024 || num_blocks <= 0 || block_size <= 0 ||
-      max_blocks <= 0 || max_seq_len < 0)
-    return HIF8_ERR_INVALID_ARGUMENT;
-  if (!query || !key_cache || !value_cache || !block_tables || !seq_lens || !query_start || !out)
-    return HIF8_ERR_INVALID_ARGUMENT;
+  const int args_status =
+      paged_attention_args_status(query, key_cache, value_cache, block_tables, seq_lens, query_start, out, batch,
+                                  num_tokens, num_heads, kv_heads, head_size, num_blocks, block_size, max_blocks,
+                                  max_seq_len);
+  if (args_status != HIF8_OK) return args_status;
   if (num_tokens == 0) return HIF8_OK;
   const int64_t group = num_heads / kv_heads;
-  if (group > 16) return HIF8_ERR_INVALID_ARGUMENT;
   const size_t need = hif8_paged_attention_workspace_size(num_tokens, num_heads, head_size, max_seq_len);
   if (need > 0 && (!workspace || workspace_bytes < need)) return HIF8_ERR_WORKSPACE;
   // decode batches (as many query rows as requests) of head size 256 and a

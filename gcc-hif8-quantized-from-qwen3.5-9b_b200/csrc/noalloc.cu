@@ -9,9 +9,12 @@
 // the library's own device image, so it allocates nothing.
 //
 // Limits and rules, all stated in include/hif8_b200.h:
-//   * at most HIF8_NOALLOC_ATTENTION_SCRATCH_BYTES of partials per call
-//     (hif8_paged_attention_workspace_size() of the call's sizes); larger
-//     calls are rejected with HIF8_ERR_WORKSPACE before anything is enqueued;
+//   * the arguments are checked first, exactly as hif8_paged_attention
+//     checks them (a bad call gets HIF8_ERR_INVALID_ARGUMENT whatever its
+//     size); then at most HIF8_NOALLOC_ATTENTION_SCRATCH_BYTES of partials
+//     per call (hif8_paged_attention_workspace_size() of the call's sizes,
+//     SIZE_MAX where that product overflows); larger calls are rejected with
+//     HIF8_ERR_WORKSPACE before anything is enqueued;
 //   * nothing in the scratch needs to start at zero: every partial the merge
 //     kernel reads was written by the split kernel of the same call;
 //   * the scratch is one array per device, shared by every call on that
@@ -21,6 +24,7 @@
 //   * the first call on each device resolves the array's device address with
 //     cudaGetSymbolAddress (which may load the library's device code on that
 //     device); make that first call before any stream capture.
+#include <atomic>
 #include <mutex>
 
 #include "hif8_common.cuh"
@@ -33,10 +37,12 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_attention_scratch[kScratchBytes];
 
 std::mutex g_scratch_mutex;
-void *g_scratch_ptr[kMaxDevices] = {};
+std::atomic<void *> g_scratch_ptr[kMaxDevices] = {};
 
 // Device address of this device's scratch array, resolved once per device
 // with that device current; nullptr (and the last-error text set) on failure.
+// After the first call on a device this is one atomic load: host threads
+// driving different devices do not contend on the lock.
 void *scratch_for_current_device() {
   int dev = -1;
   cudaError_t err = cudaGetDevice(&dev);
@@ -48,17 +54,19 @@ void *scratch_for_current_device() {
     hif8::set_last_error(cudaErrorInvalidDevice);
     return nullptr;
   }
+  void *ptr = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (ptr) return ptr;
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_ptr[dev]) {
-    void *ptr = nullptr;
+  ptr = g_scratch_ptr[dev].load(std::memory_order_relaxed);
+  if (!ptr) {
     err = cudaGetSymbolAddress(&ptr, g_attention_scratch);
     if (err != cudaSuccess) {
       hif8::set_last_error(err);
       return nullptr;
     }
-    g_scratch_ptr[dev] = ptr;
+    g_scratch_ptr[dev].store(ptr, std::memory_order_release);
   }
-  return g_scratch_ptr[dev];
+  return ptr;
 }
 
 }  // namespace
@@ -70,20 +78,19 @@ extern "C" int hif8_paged_attention_noalloc(const uint16_t *query, const uint8_t
                                             int64_t head_size, int64_t num_blocks, int64_t block_size,
                                             int64_t max_blocks, int64_t max_seq_len, float softmax_scale,
                                             int causal, uint16_t *out, void *stream) {
-  // within these bounds the workspace size cannot overflow; anything else
-  // goes without scratch to the full validation of hif8_paged_attention
-  const bool sizes_ok = num_tokens >= 0 && num_heads > 0 && head_size > 0 && max_seq_len >= 0 &&
-                        num_tokens <= (1LL << 24) && num_heads <= (1LL << 10) && head_size <= 1024 &&
-                        max_seq_len <= (1LL << 24);
+  // the same argument checks as hif8_paged_attention, before the scratch
+  // test: an invalid call is an invalid call at any size
+  const int args_status = hif8::paged_attention_args_status(
+      query, key_cache, value_cache, block_tables, seq_lens, query_start, out, batch, num_tokens, num_heads,
+      kv_heads, head_size, num_blocks, block_size, max_blocks, max_seq_len);
+  if (args_status != HIF8_OK) return args_status;
+  // overflow-checked: SIZE_MAX for sizes whose partials do not fit size_t
+  const size_t need = hif8_paged_attention_workspace_size(num_tokens, num_heads, head_size, max_seq_len);
+  if (need > kScratchBytes) return HIF8_ERR_WORKSPACE;
   void *scratch = nullptr;
-  size_t need = 0;
-  if (sizes_ok) {
-    need = hif8_paged_attention_workspace_size(num_tokens, num_heads, head_size, max_seq_len);
-    if (need > kScratchBytes) return HIF8_ERR_WORKSPACE;
-    if (need > 0) {
-      scratch = scratch_for_current_device();
-      if (!scratch) return HIF8_ERR_CUDA;
-    }
+  if (need > 0) {
+    scratch = scratch_for_current_device();
+    if (!scratch) return HIF8_ERR_CUDA;
   }
   return hif8_paged_attention(query, key_cache, value_cache, block_tables, seq_lens, query_start, batch,
                               num_tokens, num_heads, kv_heads, head_size, num_blocks, block_size, max_blocks,

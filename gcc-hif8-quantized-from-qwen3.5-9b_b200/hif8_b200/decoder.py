@@ -86,20 +86,26 @@ class _Gen:
 
 class _Linear:
     """One projection: BF16 weight (twin) or HiF8 static layer (per-row
-    scale = row amax / weight_factor)."""
+    scale = row amax / weight_factor).  ``cols`` = (start, count) keeps only
+    those input columns of the weight (a row-parallel shard): the HiF8 bytes
+    are quantised over the FULL row first and then sliced, with the full
+    row's scale, as a tensor-parallel load of one exported checkpoint
+    shards it -- so the shards' partial products sum to the unsharded
+    layer's result."""
 
-    def __init__(self, weight_bf16, mode: str, input_scale=None, weight_factor: float = MAX_FINITE):
+    def __init__(self, weight_bf16, mode: str, input_scale=None, weight_factor: float = MAX_FINITE, cols=None):
         import torch
 
         self.mode = mode
         self.out_features = weight_bf16.shape[0]
+        c0, cn = cols if cols is not None else (0, weight_bf16.shape[1])
         if mode == "bf16":
-            self.weight = weight_bf16.contiguous()
+            self.weight = weight_bf16[:, c0:c0 + cn].contiguous()
         else:
             from . import scheme
 
             data, scale = scheme.quantize_weight_rows(weight_bf16, weight_factor)
-            self.weight = data
+            self.weight = data[:, c0:c0 + cn].contiguous() if cols is not None else data
             self.weight_scale = scale.reshape(-1).contiguous()
             self.input_scale = (input_scale if input_scale is not None
                                 else torch.ones(1, device=weight_bf16.device)).reshape(1).float().contiguous()
@@ -222,8 +228,8 @@ class Decoder:
 
         weight_factor = float(calib.get("weight_factor", MAX_FINITE))
 
-        def lin(tag, w):
-            return _Linear(w, mode, scale_for(tag), weight_factor)
+        def lin(tag, w, cols=None):
+            return _Linear(w, mode, scale_for(tag), weight_factor, cols)
 
         def rows(w, start, count):
             return w[start:start + count]
@@ -241,7 +247,7 @@ class Decoder:
                 w_qkv = torch.cat([rows(wq, r * self.heads * 2 * D, self.heads * 2 * D),
                                    rows(wk, kv0 * D, self.kv_local * D), rows(wv, kv0 * D, self.kv_local * D)])
                 L["qkv"] = lin(f"{i}.qkv", w_qkv)
-                L["o"] = lin(f"{i}.o", wo[:, r * self.heads * D:(r + 1) * self.heads * D].contiguous())
+                L["o"] = lin(f"{i}.o", wo, (r * self.heads * D, self.heads * D))
                 del wq, wk, wv, wo, w_qkv
                 L["q_norm"] = gen.normal(f"{i}.q_norm", (D,), 0.02)
                 L["k_norm"] = gen.normal(f"{i}.k_norm", (D,), 0.02)
@@ -270,7 +276,7 @@ class Decoder:
                 L["dt_bias"] = torch.ones(self.hv, device=self.device)
                 L["gdn_norm"] = (1.0 + gen.normal(f"{i}.gdn_norm", (dl,), 0.02).float()).to(torch.bfloat16)
                 w_out = gen.normal(f"{i}.lin_out", (H, vd), c.init_std)
-                L["lin_out"] = lin(f"{i}.lin_out", w_out[:, r * lv:(r + 1) * lv].contiguous())
+                L["lin_out"] = lin(f"{i}.lin_out", w_out, (r * lv, lv))
                 del w_out
             w_gate = gen.normal(f"{i}.gate", (c.intermediate, H), c.init_std)
             w_up = gen.normal(f"{i}.up", (c.intermediate, H), c.init_std)
@@ -278,7 +284,7 @@ class Decoder:
                                                           rows(w_up, r * self.inter, self.inter)]))
             del w_gate, w_up
             w_down = gen.normal(f"{i}.down", (H, c.intermediate), c.init_std)
-            L["down"] = lin(f"{i}.down", w_down[:, r * self.inter:(r + 1) * self.inter].contiguous())
+            L["down"] = lin(f"{i}.down", w_down, (r * self.inter, self.inter))
             del w_down
             self.layers.append(L)
         embed = gen.normal("embed", (c.vocab, H), c.init_std)
@@ -657,6 +663,36 @@ def calibrate(cfg: DecoderConfig, device, *, seed: int = 0, tokens: int = 64, tp
         calib[tag] = [per_head[h] for h in sorted(per_head)]
     torch.cuda.empty_cache()
     return calib
+
+
+def forced_logits(model: Decoder, prompt, next_tokens=None, steps: int = 8):
+    """Logits of the prefill of ``prompt`` [batch, T] and of ``steps``
+    single-token decode steps (eager, the decode path: fused reductions and
+    glue as the CUDA-graph step uses them).  Decode step s is fed
+    ``next_tokens[s]`` when given (teacher forcing, so two models can be
+    compared step by step without a flipped near-tie changing everything
+    after it), else this model's own greedy token.  Returns (list of this
+    rank's FP32 logits [batch, vocab_local], list of greedy tokens [batch])."""
+    import torch
+
+    batch, T = prompt.shape
+    model.reset()
+    logits, tokens = [], []
+    with torch.no_grad():
+        positions = torch.arange(T, dtype=torch.int32, device=model.device).repeat(batch)
+        seq_lens = torch.full((batch,), T, dtype=torch.int32, device=model.device)
+        lg = model.forward(prompt.reshape(-1), positions, batch, T, seq_lens, model._slots(batch, positions))
+        for s in range(steps + 1):
+            logits.append(lg.clone())
+            tokens.append(model.argmax(lg))
+            if s == steps:
+                break
+            tok = next_tokens[s] if next_tokens is not None else tokens[-1]
+            pos = torch.full((batch,), T + s, dtype=torch.int32, device=model.device)
+            lg = model.forward(tok.contiguous(), pos, batch, 1, pos + 1, model._slots(batch, pos))
+    if model.peer is not None:
+        model.peer.check()
+    return logits, tokens
 
 
 def measure_decode(model: Decoder, batch: int, *, prompt_len: int = 512, gen: int = 256, seed: int = 1) -> dict:

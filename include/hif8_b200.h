@@ -165,7 +165,9 @@ int hif8_kv_cache_write(const void *key, const void *value, int src_dtype, int64
  *   block_tables: [batch, max_blocks] int32; seq_lens: [batch] int32, each
  *          <= max_seq_len; table entries outside [0, num_blocks) are skipped;
  *   query_start: [batch + 1] int32 (cumulative); out: like query.
- * workspace: hif8_paged_attention_workspace_size() bytes (split-KV partials). */
+ * workspace: hif8_paged_attention_workspace_size() bytes (split-KV partials;
+ * the size function returns SIZE_MAX where that product overflows size_t, so
+ * such a call gets HIF8_ERR_WORKSPACE). */
 size_t hif8_paged_attention_workspace_size(int64_t num_tokens, int64_t num_heads,
                                            int64_t head_size, int64_t max_seq_len);
 
@@ -194,7 +196,9 @@ int hif8_paged_attention(const uint16_t *query, const uint8_t *key_cache,
  *  - the first call on each device looks the scratch address up with
  *    cudaGetSymbolAddress, with that device current; make it before any
  *    stream capture.
- * Other arguments and errors as hif8_paged_attention. */
+ * Arguments are checked first, as hif8_paged_attention checks them (a bad
+ * call gets HIF8_ERR_INVALID_ARGUMENT at any size); other arguments and
+ * errors as hif8_paged_attention. */
 #define HIF8_NOALLOC_ATTENTION_SCRATCH_BYTES ((size_t)8 << 20)
 int hif8_paged_attention_noalloc(const uint16_t *query, const uint8_t *key_cache,
                                  const uint8_t *value_cache, const int32_t *block_tables,

@@ -145,6 +145,31 @@ def test_paged_attention_workspace_sizes():
     assert lib.hif8_paged_attention_workspace_size(4, 16, 256, 64) == 0  # one chunk: no partials
     assert lib.hif8_paged_attention_workspace_size(4, 16, 256, 256) == 4 * 16 * 4 * (256 + 2) * 4
     assert lib.hif8_paged_attention_workspace_size(4, 16, 256, 4096) == 4 * 16 * 64 * (256 + 2) * 4
+    # a product beyond size_t is reported as SIZE_MAX, never wrapped to a small size
+    size_max = (1 << 64) - 1
+    assert lib.hif8_paged_attention_workspace_size(1 << 40, 1 << 10, 1024, 1 << 40) == size_max
+    assert lib.hif8_paged_attention_workspace_size(0, 16, 256, 4096) == 0  # no query rows
+
+
+def test_noalloc_attention_checks_arguments_before_the_scratch_size():
+    """The no-alloc attention reports the same status as the workspace entry
+    point for an invalid call, whatever its size; a valid call that needs
+    more than the library's scratch is refused before any device work."""
+    from hif8_b200 import cabi
+
+    lib = cabi.library()
+    fake = 256  # never dereferenced: every case is refused before a launch
+    long_ctx = 1 << 22  # far more partials than the 8 MiB scratch holds
+
+    def noalloc(query=fake, heads=16, kv_heads=4, ctx=long_ctx):
+        return lib.hif8_paged_attention_noalloc(query, fake, fake, fake, fake, fake, 4, 4, heads, kv_heads, 256,
+                                                8, 128, 1, ctx, 1.0, 1, fake, None)
+
+    assert noalloc(query=None) == cabi.HIF8_ERR_INVALID_ARGUMENT
+    assert noalloc(heads=6) == cabi.HIF8_ERR_INVALID_ARGUMENT      # heads not a multiple of kv heads
+    assert noalloc(heads=68, kv_heads=4) == cabi.HIF8_ERR_INVALID_ARGUMENT  # GQA group 17 > 16
+    assert noalloc() == cabi.HIF8_ERR_WORKSPACE
+    assert noalloc(ctx=(1 << 62)) == cabi.HIF8_ERR_WORKSPACE       # overflowing size: SIZE_MAX
 
 
 def test_torch_ops_have_reference_schemas():

@@ -4,8 +4,11 @@ the FP64 oracle.
 The reference computes the same product in FP32 on its CPU/NPU paths
 (csrc/hif8_native.cpp:633-669, soft_hif8_gemm); the tolerance MAX_REL = 1e-2
 of the largest |output| covers FP32 accumulation plus the final BF16/FP16
-rounding.  The activation/weight shapes follow configs[2] of the workload
-(prefill of the Qwen3.5-9B projection shapes)."""
+rounding; every output channel is also bounded against its own largest
+|output| (CHANNEL_REL) and every token row's cosine similarity (MIN_COSINE),
+so a wrong small channel among the 20-sigma outlier rows cannot hide under
+the global scale.  The activation/weight shapes follow configs[2] of the
+workload (prefill of the Qwen3.5-9B projection shapes)."""
 
 from __future__ import annotations
 
@@ -14,8 +17,8 @@ import pytest
 import torch
 
 from oracle import oracle
-from tests._helpers import max_rel
-from tests.test_linear_gpu import _activations, _hif8_weights, _native, _to
+from tests._helpers import channel_rel, max_rel, row_cosine_min
+from tests.test_linear_gpu import CHANNEL_REL, MIN_COSINE, _activations, _hif8_weights, _native, _to
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -49,9 +52,13 @@ def test_prefill_gemm_projection_shapes(m, n, k):
     rows = np.arange(m) if m <= 512 else np.sort(np.random.default_rng(m).choice(m, size=384, replace=False))
     expected = oracle.linear(a[rows], w[cols], a_s[rows], w_s[cols])
     assert max_rel(got[np.ix_(rows, cols)], expected) <= MAX_REL
+    assert channel_rel(got[np.ix_(rows, cols)], expected) <= CHANNEL_REL
     lut = torch.from_numpy(oracle.decode_table()).to(DEV)
     ref32 = (lut[a_dev.long()] * as_dev[:, None]) @ (lut[w_dev.long()] * ws_dev[:, None]).T
-    assert max_rel(got, ref32.cpu().numpy()) <= MAX_REL
+    ref32 = ref32.cpu().numpy()
+    assert max_rel(got, ref32) <= MAX_REL
+    assert channel_rel(got, ref32) <= CHANNEL_REL
+    assert row_cosine_min(got, ref32) >= MIN_COSINE
     again = torch.empty_like(out)
     cabi.gemm(a_dev, w_dev, as_dev, ws_dev, None, again, workspace)
     assert torch.equal(out, again), "run-twice determinism"

@@ -4,7 +4,10 @@ soft_hif8_static_fused_gemm) against the CPU oracle.
 Tolerance: max |y - y_ref| / max |y_ref| <= 1e-2 against the FP64-accumulated
 oracle (the reference's own bar is 2e-2, tests/test_npu_ops.py:296-344), and
 the element-wise rtol/atol of the reference tests on its small shapes
-(2e-2 FP16 / 8e-2 BF16, tests/test_npu_ops.py:216-294)."""
+(2e-2 FP16 / 8e-2 BF16, tests/test_npu_ops.py:216-294).  The projection-shape
+tests also bound every output channel against its own largest |y_ref|
+(CHANNEL_REL = 1e-2) and every token row's cosine similarity (>= 0.9999), so
+a wrong small-magnitude channel cannot hide under the global scale."""
 
 from __future__ import annotations
 
@@ -13,12 +16,14 @@ import pytest
 import torch
 
 from oracle import oracle
-from tests._helpers import max_rel
+from tests._helpers import channel_rel, max_rel, row_cosine_min
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden"
 MAX_REL = 1.0e-2
+CHANNEL_REL = 1.0e-2
+MIN_COSINE = 0.9999
 
 
 def _native():
@@ -129,8 +134,12 @@ def test_decode_gemv_shapes_against_oracle(n, k):
         got = out.float().cpu().numpy()
         expected = oracle.linear(a, w[cols], a_s, w_s[cols])
         assert max_rel(got[:, cols], expected) <= MAX_REL, f"m={m}"
+        assert channel_rel(got[:, cols], expected) <= CHANNEL_REL, f"m={m}"
         ref32 = (lut[_to(a).long()] * _to(a_s)[:, None]) @ (lut[w_dev.long()] * ws_dev[:, None]).T
-        assert max_rel(got, ref32.cpu().numpy()) <= MAX_REL
+        ref32 = ref32.cpu().numpy()
+        assert max_rel(got, ref32) <= MAX_REL
+        assert channel_rel(got, ref32) <= CHANNEL_REL, f"m={m}"
+        assert row_cosine_min(got, ref32) >= MIN_COSINE, f"m={m}"
         again = native.soft_linear(_to(a), w_dev, _to(a_s), ws_dev, output_dtype=torch.bfloat16)
         assert torch.equal(out, again), "run-twice determinism"
 
@@ -147,6 +156,8 @@ def test_gemm_medium_m_with_bias_against_oracle(m):
         bias_r = oracle.round_bf16(bias)
         expected = oracle.linear(a, w, a_s, w_s, bias_r)
         assert max_rel(out.float().cpu().numpy(), expected) <= MAX_REL
+        assert channel_rel(out.float().cpu().numpy(), expected) <= CHANNEL_REL
+        assert row_cosine_min(out.float().cpu().numpy(), expected) >= MIN_COSINE
 
 
 def test_gemm_unaligned_tails_and_long_k():
