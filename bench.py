@@ -662,12 +662,15 @@ def measure_paged_attention(device) -> dict:
 
 HBM_KERNEL_CASES = {
     # name: (kernel, the size where HBM is the bound, the decode-size case)
-    "quant": ("static_quant_vec16", "x [4096, 12288] BF16 (configs[2] prefill, down input)",
+    "quant": ("static_quant_vec16", "x [4096, 12288] BF16 (configs[2] prefill, down input), scale = calibration "
+                                    "absmax / 32768",
               "x [16, 12288] BF16"),
     "kv_write": ("kv_write_kernel", "16384 tokens x 4 KV heads x 256, K and V, BF16 source",
                  "4 tokens (a batch-4 decode step)"),
     "embedding": ("embedding_gather", "16384 ids of a [248320, 4096] HiF8 table",
                   "4 ids (a batch-4 decode step)"),
+    "scaled_decode": ("scaled_decode_vec", "data [65536, 256] u8 (configs[3]: batch 4 x ctx 4096 x 4 KV heads)",
+                      "data [16, 256] u8"),
 }
 
 
@@ -681,7 +684,9 @@ def _hbm_kernel_inputs(name: str, big: bool, device):
     if name == "quant":
         m, k = (4096, 12288) if big else (16, 12288)
         x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
-        scale = torch.tensor([4.5 / 32768.0], device=device)
+        # the configs' rule: global absmax of a seeded calibration batch / 32768
+        calib = torch.randn(64, k, device=device, generator=g).to(torch.bfloat16)
+        scale = (calib.float().abs().amax() / 32768.0).reshape(1)
         # BF16 in, u8 out, FP32 row scale out, the fixed scale in
         return (lambda: native.static_quant(x, scale)), 3 * m * k + 4 * m + 4
     if name == "kv_write":
@@ -705,6 +710,12 @@ def _hbm_kernel_inputs(name: str, big: bool, device):
         ids = torch.randint(0, vocab, (ids_n,), device=device, generator=g)
         # per id: the HiF8 row, its FP32 scale, the BF16 output row, the 8-byte id
         return (lambda: emb(ids)), ids_n * (hidden + 4 + 2 * hidden + 8)
+    if name == "scaled_decode":
+        rows, d = (65536, 256) if big else (16, 256)
+        data = torch.randint(0, 0x6F, (rows, d), dtype=torch.uint8, device=device, generator=g)
+        scale = torch.rand(rows, device=device, generator=g) + 0.25
+        # u8 in, FP32 row scale in, BF16 out
+        return (lambda: native.scaled_decode(data, scale)), rows * d * 3 + 4 * rows
     raise ValueError(name)
 
 

@@ -127,8 +127,22 @@ HIF8_HD constexpr Table256 make_decode_table_f32() {
   return t;
 }
 
+struct alignas(16) Table12 {
+  uint8_t v[4096];
+};
+
+// The positive half of the static-saturating encode (index: exponent field
+// and top-4 mantissa bits of |q|); a negative value's code is the same
+// magnitude code with bit 7 set, except zero, which has no negative code.
+HIF8_HD constexpr Table12 make_static_encode_mag_table() {
+  Table12 t{};
+  for (uint32_t i = 0; i < 4096u; ++i) t.v[i] = static_encode13(i);
+  return t;
+}
+
 // Device copies of the tables (one per translation unit that uses them).
 static __device__ const Table13 g_static_encode = make_static_encode_table();
+static __device__ const Table12 g_static_encode_mag = make_static_encode_mag_table();
 static __device__ const Table256 g_decode_f32 = make_decode_table_f32();
 
 // ---------------------------------------------------- float conversions --
@@ -159,6 +173,146 @@ template <int kDtype>
 __device__ __forceinline__ uint32_t f32_to_half_bits(float v) {
   if constexpr (kDtype == HIF8_DTYPE_BF16) return f32_to_bf16_bits(v);
   else return f32_to_f16_bits(v);
+}
+
+// Two FP32 values as a BF16 pair (lo in bits 0-15) by the hardware
+// round-to-nearest-even conversion.  It equals f32_to_bf16_bits on every
+// finite or infinite input that is not an FP32 subnormal; callers keep NaN
+// and subnormals away from it (f32_to_bf16_bits canonicalises NaN to 0x7FC0).
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// True when no byte of w is the NaN code 0x80.
+__device__ __forceinline__ bool no_nan_code(uint32_t w) {
+  const uint32_t x = w ^ 0x80808080u;  // a 0x80 byte becomes a zero byte
+  return ((x - 0x01010101u) & ~x & 0x80808080u) == 0u;
+}
+
+// A scale whose product with any finite HiF8 value (2^-22 .. 2^15) is a
+// normal FP32 or +-Inf: 2^-100 <= |s| < 2^111.
+__device__ __forceinline__ bool decode_scale_ok(float s) {
+  const uint32_t e = (__float_as_uint(s) >> 23) & 0xFFu;
+  return e - 27u < 211u;
+}
+
+// ------------------------------------------------- static quantisation --
+
+// Shared-memory copy of g_static_encode_mag (4 KB, 16-byte pieces).
+__device__ __forceinline__ void load_encode_mag_table(uint8_t *smem) {
+  const uint4 *src = reinterpret_cast<const uint4 *>(g_static_encode_mag.v);
+  for (int i = threadIdx.x; i < 4096 / 16; i += blockDim.x) reinterpret_cast<uint4 *>(smem)[i] = src[i];
+}
+
+// Exact code of the static quantisation of an FP16/BF16 value f by the fixed
+// FP32 scale s, given r64 = RN64(1/s) (__drcp_rn).  The reference forms the
+// FP32 quotient RN32(f / s) and encodes it.  f / s is a ratio of an integer
+// of at most 11 bits and one of at most 24 bits (times a power of two), so
+// when it is not itself an FP32 rounding midpoint it lies at least 2^-49
+// (relative) away from every midpoint, and no such ratio is a midpoint
+// (that would need a 25-bit odd integer to divide out of the 11-bit
+// numerator).  The FP64 product f * r64 is within 2^-52 (relative) of f / s,
+// so converting it to FP32 rounds to RN32(f / s) for every f and s --
+// zero, infinite and NaN scales included (f * Inf, f * 0 and NaN follow the
+// IEEE quotient).  The magnitude code then comes from the table, NaN gives
+// 0x80 and a nonzero code takes the quotient's sign.
+__device__ __forceinline__ uint32_t static_code_exact(float f, double r64, const uint8_t *__restrict__ mag) {
+  const uint32_t v = __float_as_uint((float)((double)f * r64));
+  if ((v & 0x7FFFFFFFu) > 0x7F800000u) return 0x80u;
+  const uint32_t m = mag[(v >> 19) & 0xFFFu];
+  return m == 0u ? 0u : m | ((v >> 24) & 0x80u);
+}
+
+// HiF8 code of the static quantisation of f by the fixed scale s with r =
+// RN32(1/s) and r64 = RN64(1/s) (exact_only: take the exact path, for a
+// reciprocal that is zero or infinite or a scale that is not positive).  The
+// product q = f * r is within two units in the last place of the correctly
+// rounded quotient RN32(f / s), and the magnitude code is a non-decreasing
+// function of the value, so when |q| - 4 ulp and |q| + 4 ulp have the same
+// code, RN32(f / s) has it too.  The codes of both ends come from the
+// magnitude table (index: exponent field and top-4 mantissa bits), the sign
+// is OR'd into bit 7 of a nonzero code.  A quotient within 4 ulp of a code
+// boundary, an |q| of 2^123 or more and NaN / Inf take static_code_exact.
+// `mag` is the shared-memory copy of g_static_encode_mag: with the sign out
+// of the index, a warp's lookups over 8 consecutive binades fall into
+// distinct banks.
+__device__ __forceinline__ uint32_t static_code(float f, float r, double r64, bool exact_only,
+                                                const uint8_t *__restrict__ mag) {
+  const uint32_t u = __float_as_uint(__fmul_rn(f, r));
+  const uint32_t a = max(u & 0x7FFFFFFFu, 4u);
+  // a - 4 >= 0; a + 4 can pass 2^31 only for a NaN, which the check below
+  // sends to the exact path: the mask keeps that lookup inside the table
+  const uint32_t lo = mag[(a - 4u) >> 19], hi = mag[((a + 4u) >> 19) & 0xFFFu];
+  if (exact_only | (lo != hi) | (a >= 0x7D000000u)) return static_code_exact(f, r64, mag);
+  return lo == 0u ? 0u : lo | ((u >> 24) & 0x80u);
+}
+
+// Static codes of 16 consecutive FP16/BF16 elements (w: their 8 words,
+// element 2i in the low half of w[i]) by the product with the reciprocal r
+// of a POSITIVE fixed scale, four codes per output word in element order:
+// the rule of static_code with one check for the whole chunk (every
+// element's codes at |q| -+ 4 ulp agree, every |q| below 2^123).  Returns
+// false when any element fails -- the caller then takes static_codes16_exact
+// (a chunk-wide branch keeps a warp's lanes together where a per-element one
+// would not).  Each nonzero code gets its element's sign, read straight from
+// the input words.
+template <int kDtype>
+__device__ __forceinline__ bool static_codes16(const uint32_t (&w)[8], float r, const uint8_t *__restrict__ mag,
+                                               uint32_t (&out)[4]) {
+  uint32_t diff = 0u, amax = 0u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t c[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t word = w[2 * j + (e >> 1)];
+      float f;
+      if constexpr (kDtype == HIF8_DTYPE_BF16) f = __uint_as_float((e & 1) ? (word & 0xFFFF0000u) : (word << 16));
+      else f = __half2float(__ushort_as_half((unsigned short)((e & 1) ? (word >> 16) : (word & 0xFFFFu))));
+      const uint32_t a = max(__float_as_uint(__fmul_rn(f, r)) & 0x7FFFFFFFu, 4u);
+      amax = max(amax, a);
+      c[e] = mag[(a - 4u) >> 19];
+      diff |= c[e] ^ mag[((a + 4u) >> 19) & 0xFFFu];  // masked: see static_code
+    }
+    const uint32_t codes = __byte_perm(__byte_perm(c[0], c[1], 0x0040u), __byte_perm(c[2], c[3], 0x0040u), 0x5410u);
+    // bit 7 of every byte: the element's sign (bit 15 of each FP16/BF16)
+    const uint32_t signs = __byte_perm(w[2 * j], w[2 * j + 1], 0x7531u);
+    // codes are below 0x80, so + 0x7F sets bit 7 of exactly the nonzero ones
+    out[j] = codes | (signs & (codes + 0x7F7F7F7Fu) & 0x80808080u);
+  }
+  return diff == 0u && amax < 0x7D000000u;
+}
+
+// The 16 codes by static_code_exact.
+template <int kDtype>
+__device__ __forceinline__ void static_codes16_exact(const uint32_t (&w)[8], double r64,
+                                                     const uint8_t *__restrict__ mag, uint32_t (&out)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t word = w[2 * j + (e >> 1)];
+      const uint32_t h = (e & 1) ? (word >> 16) : (word & 0xFFFFu);
+      v |= static_code_exact(half_bits_to_f32<kDtype>(h), r64, mag) << (8 * e);
+    }
+    out[j] = v;
+  }
+}
+
+// Lane-replicated FP32 decode table in shared memory (32 KB): entry b of
+// lane l is the word at (b << 5) | l, so every lane reads its own bank and a
+// warp's 32 lookups are one wavefront whatever the codes.
+constexpr int kLaneDecodeWords = 256 * 32;
+
+__device__ __forceinline__ void load_lane_decode_table(float *smem) {
+  for (int i = threadIdx.x; i < kLaneDecodeWords; i += blockDim.x)
+    smem[i] = __uint_as_float(g_decode_f32.v[i >> 5]);
+}
+
+__device__ __forceinline__ float lane_decode(const float *tbl, uint32_t code, uint32_t lane) {
+  return tbl[(code << 5) | lane];
 }
 
 // Elementwise producers shared by the model glue kernels and the GEMV

@@ -15,17 +15,11 @@ namespace hif8 {
 
 // ------------------------------------------------------------ KV write ---
 
-__device__ __forceinline__ uint32_t kv_quant_one(float f, float s, float r, bool exact_only,
+// Static quantisation of one K/V element with its head's scale: the rule of
+// hif8_static_quant (static_code), so page bytes equal the quantised rows.
+__device__ __forceinline__ uint32_t kv_quant_one(float f, float r, double r64, bool exact_only,
                                                  const uint8_t *__restrict__ tbl) {
-  float q = __fmul_rn(f, r);
-  uint32_t u = __float_as_uint(q);
-  const uint32_t low = u & 0x7FFFFu;
-  if (exact_only | ((low - 4u) > 0x7FFF8u) | ((u & 0x7F800000u) >= 0x7D000000u)) {
-    q = __fdiv_rn(f, s);  // correctly rounded quotient near a code boundary
-    u = __float_as_uint(q);
-    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x80u;
-  }
-  return tbl[u >> 19];
+  return static_code(f, r, r64, exact_only, tbl);
 }
 
 struct KvWriteArgs {
@@ -35,51 +29,121 @@ struct KvWriteArgs {
   const int64_t *slots;
   int32_t *bad_slots;
   int64_t tokens, heads, d, token_stride, num_blocks, block_size;
-  int planes;  // 1 = K only, 2 = K and V
+  int64_t cache_slots;  // num_blocks * block_size: slots at or above are out of range
+  int64_t units;        // planes * tokens * heads * (d / elements per unit), < 2^32
+  int planes;           // 1 = K only, 2 = K and V
 };
 
-// One warp per (plane, token, head) row: 4 elements per lane and step, packed
-// into one 4-byte store; lane 0 appends the FP32 scale.
-template <int kDtype>
+constexpr int kKvUnroll = 4;      // units in flight per thread
+constexpr int kKvScaleSlots = 64;  // heads whose scale / reciprocal a CTA stages in shared memory
+
+// Quantise ELEMS consecutive elements of one (plane, token, head) row per
+// unit (ELEMS = 16: two 16-byte loads; 4: one 8-byte load) and store them
+// into the row's page slot with 4-byte stores (a page row is D + 4 bytes,
+// so rows are only 4-byte aligned).  A page row starts at
+// (slot * heads + head) * (D + 4): slot = block * block_size + offset, so no
+// division is needed; a slot at or beyond num_blocks * block_size is out of
+// range (counted once per token), a negative slot is skipped.  The unit
+// holding a row's last elements also writes the row's FP32 scale.  Every
+// thread keeps kKvUnroll units in flight (slot and source loads of all of
+// them first), and the per-head reciprocals are formed once per CTA.
+template <int kDtype, int ELEMS>
 __global__ void __launch_bounds__(256) kv_write_kernel(const KvWriteArgs p) {
+  __shared__ __align__(16) uint8_t tbl[4096];
+  __shared__ float sh_s[2 * kKvScaleSlots], sh_r[2 * kKvScaleSlots];
+  __shared__ double sh_r64[2 * kKvScaleSlots];
+  __shared__ uint8_t sh_exact[2 * kKvScaleSlots];
+  load_encode_mag_table(tbl);  // module data: before the dependency wait
   pdl_wait();  // inputs come from the previous kernel of the stream
-  __shared__ __align__(16) uint8_t tbl[8192];
-  {
-    const uint4 *src = reinterpret_cast<const uint4 *>(g_static_encode.v);
-    for (int i = threadIdx.x; i < 512; i += blockDim.x) reinterpret_cast<uint4 *>(tbl)[i] = src[i];
+  const bool staged = p.heads <= kKvScaleSlots;
+  if (staged) {
+    for (int i = threadIdx.x; i < p.planes * p.heads; i += blockDim.x) {
+      const int plane = i / (int)p.heads, h = i - plane * (int)p.heads;
+      const float s = p.scale[plane][h];
+      const float r = __frcp_rn(s);
+      const uint32_t re = __float_as_uint(r) & 0x7F800000u;
+      sh_s[plane * kKvScaleSlots + h] = s;
+      sh_r[plane * kKvScaleSlots + h] = r;
+      sh_r64[plane * kKvScaleSlots + h] = __drcp_rn((double)s);
+      sh_exact[plane * kKvScaleSlots + h] = (re == 0u) | (re == 0x7F800000u) | !(s > 0.f);
+    }
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int64_t rows = p.tokens * p.heads;
-  const int64_t total = rows * p.planes;
+  const uint32_t upr = (uint32_t)(p.d / ELEMS);  // units per row
+  const uint32_t heads = (uint32_t)p.heads;
+  const uint32_t per_plane = (uint32_t)(p.units / p.planes);
   const int64_t width = p.d + 4;
-  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < total;
-       row += (int64_t)gridDim.x * (blockDim.x >> 5)) {
-    const int plane = (int)(row / rows);
-    const int64_t rr = row - plane * rows;
-    const int64_t tok = rr / p.heads, h = rr - tok * p.heads;
-    const int64_t slot = p.slots[tok];
-    if (slot < 0) continue;
-    const int64_t block = slot / p.block_size, off = slot - block * p.block_size;
-    if (block >= p.num_blocks) {
-      if (lane == 0 && p.bad_slots && plane == 0 && h == 0) atomicAdd(p.bad_slots, 1);
-      continue;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t u0 = blockIdx.x * blockDim.x + threadIdx.x; u0 < (uint32_t)p.units; u0 += kKvUnroll * stride) {
+    int64_t slot[kKvUnroll];
+    uint32_t row[kKvUnroll], chunk[kKvUnroll];
+    int plane[kKvUnroll];
+    uint4 a[kKvUnroll], b[kKvUnroll];
+#pragma unroll
+    for (int u = 0; u < kKvUnroll; ++u) {
+      const uint64_t uu = (uint64_t)u0 + (uint64_t)u * stride;
+      slot[u] = -1;
+      if (uu < (uint64_t)p.units) {
+        plane[u] = uu >= per_plane;
+        const uint32_t rem = (uint32_t)uu - (plane[u] ? per_plane : 0u);
+        row[u] = rem / upr;
+        chunk[u] = rem - row[u] * upr;
+        const uint32_t tok = row[u] / heads;
+        slot[u] = __ldg(p.slots + tok);
+        const uint16_t *src = p.src[plane[u]] + (int64_t)tok * p.token_stride +
+                              (int64_t)(row[u] - tok * heads) * p.d + (int64_t)chunk[u] * ELEMS;
+        if constexpr (ELEMS == 16) {
+          a[u] = __ldcs(reinterpret_cast<const uint4 *>(src));
+          b[u] = __ldcs(reinterpret_cast<const uint4 *>(src) + 1);
+        } else {
+          const uint2 v = __ldcs(reinterpret_cast<const uint2 *>(src));
+          a[u] = make_uint4(v.x, v.y, 0, 0);
+        }
+      }
     }
-    const float s = p.scale[plane][h];
-    const float r = __frcp_rn(s);
-    const uint32_t re = __float_as_uint(r) & 0x7F800000u;
-    const bool exact_only = (re == 0u) | (re == 0x7F800000u);
-    const uint16_t *src = p.src[plane] + tok * p.token_stride + h * p.d;
-    uint8_t *dst = p.cache[plane] + ((block * p.block_size + off) * p.heads + h) * width;
-    for (int64_t c = lane * 4; c < p.d; c += 128) {
-      const uint2 v = *reinterpret_cast<const uint2 *>(src + c);
-      const uint32_t b0 = kv_quant_one(half_bits_to_f32<kDtype>(v.x & 0xFFFFu), s, r, exact_only, tbl);
-      const uint32_t b1 = kv_quant_one(half_bits_to_f32<kDtype>(v.x >> 16), s, r, exact_only, tbl);
-      const uint32_t b2 = kv_quant_one(half_bits_to_f32<kDtype>(v.y & 0xFFFFu), s, r, exact_only, tbl);
-      const uint32_t b3 = kv_quant_one(half_bits_to_f32<kDtype>(v.y >> 16), s, r, exact_only, tbl);
-      *reinterpret_cast<uint32_t *>(dst + c) = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+#pragma unroll
+    for (int u = 0; u < kKvUnroll; ++u) {
+      if (slot[u] < 0) continue;  // skipped (negative) or past the end of the work
+      const uint32_t tok = row[u] / heads, h = row[u] - tok * heads;
+      if (slot[u] >= p.cache_slots) {
+        if (p.bad_slots && plane[u] == 0 && h == 0 && chunk[u] == 0) atomicAdd(p.bad_slots, 1);
+        continue;
+      }
+      float s, r;
+      double r64;
+      bool exact_only;
+      if (staged) {
+        s = sh_s[plane[u] * kKvScaleSlots + h];
+        r = sh_r[plane[u] * kKvScaleSlots + h];
+        r64 = sh_r64[plane[u] * kKvScaleSlots + h];
+        exact_only = sh_exact[plane[u] * kKvScaleSlots + h] != 0;
+      } else {
+        s = p.scale[plane[u]][h];
+        r = __frcp_rn(s);
+        r64 = __drcp_rn((double)s);
+        const uint32_t re = __float_as_uint(r) & 0x7F800000u;
+        exact_only = (re == 0u) | (re == 0x7F800000u) | !(s > 0.f);
+      }
+      uint8_t *dst_row = p.cache[plane[u]] + (slot[u] * (int64_t)heads + h) * width;
+      uint32_t *dst = reinterpret_cast<uint32_t *>(dst_row + (int64_t)chunk[u] * ELEMS);
+      const uint32_t w[8] = {a[u].x, a[u].y, a[u].z, a[u].w, b[u].x, b[u].y, b[u].z, b[u].w};
+      uint32_t o[4];
+      // the 16-element chunk path (one check per chunk); each element by
+      // division-capable static_code where that check fails
+      if constexpr (ELEMS == 16) {
+        if (exact_only || !static_codes16<kDtype>(w, r, tbl, o)) static_codes16_exact<kDtype>(w, r64, tbl, o);
+      } else {
+        const uint32_t lo = w[0], hi = w[1];
+        const uint32_t b0 = kv_quant_one(half_bits_to_f32<kDtype>(lo & 0xFFFFu), r, r64, exact_only, tbl);
+        const uint32_t b1 = kv_quant_one(half_bits_to_f32<kDtype>(lo >> 16), r, r64, exact_only, tbl);
+        const uint32_t b2 = kv_quant_one(half_bits_to_f32<kDtype>(hi & 0xFFFFu), r, r64, exact_only, tbl);
+        const uint32_t b3 = kv_quant_one(half_bits_to_f32<kDtype>(hi >> 16), r, r64, exact_only, tbl);
+        o[0] = __byte_perm(b0 | (b1 << 8), b2 | (b3 << 8), 0x5410u);
+      }
+#pragma unroll
+      for (int j = 0; j < ELEMS / 4; ++j) dst[j] = o[j];
+      if (chunk[u] == upr - 1) *reinterpret_cast<float *>(dst_row + p.d) = s;
     }
-    if (lane == 0) *reinterpret_cast<float *>(dst + p.d) = s;
   }
 }
 
@@ -774,11 +838,22 @@ extern "C" int hif8_kv_cache_write(const void *key, const void *value, int src_d
   p.num_blocks = num_blocks;
   p.block_size = block_size;
   p.planes = with_v ? 2 : 1;
-  const int64_t warps = tokens * kv_heads * p.planes;
-  const int grid = attn_grid_cap((warps + 7) / 8);
+  p.cache_slots = num_blocks * block_size;
+  // 16-element units where the source rows allow 16-byte loads
+  const bool vec16 = head_size % 16 == 0 && src_token_stride % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(key) & 15u) == 0 &&
+                     (!value || (reinterpret_cast<uintptr_t>(value) & 15u) == 0);
+  const int elems = vec16 ? 16 : 4;
+  p.units = p.planes * tokens * kv_heads * (head_size / elems);
+  if (p.units > 0x7FFFFFFFLL) return HIF8_ERR_INVALID_ARGUMENT;  // 32-bit unit indices
+  const int grid = attn_grid_cap((p.units + 255) / 256);  // one wave at most; then kKvUnroll per step
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return src_dtype == HIF8_DTYPE_BF16 ? launch_pdl(kv_write_kernel<HIF8_DTYPE_BF16>, dim3(grid), dim3(256), 0, s, p)
-                                      : launch_pdl(kv_write_kernel<HIF8_DTYPE_F16>, dim3(grid), dim3(256), 0, s, p);
+  const bool bf16 = src_dtype == HIF8_DTYPE_BF16;
+  if (vec16)
+    return bf16 ? launch_pdl(kv_write_kernel<HIF8_DTYPE_BF16, 16>, dim3(grid), dim3(256), 0, s, p)
+                : launch_pdl(kv_write_kernel<HIF8_DTYPE_F16, 16>, dim3(grid), dim3(256), 0, s, p);
+  return bf16 ? launch_pdl(kv_write_kernel<HIF8_DTYPE_BF16, 4>, dim3(grid), dim3(256), 0, s, p)
+              : launch_pdl(kv_write_kernel<HIF8_DTYPE_F16, 4>, dim3(grid), dim3(256), 0, s, p);
 }
 
 static int attn_nq(int64_t group, int64_t q_rows) { return (int)(group * q_rows); }

@@ -1,45 +1,31 @@
 // Activation static quantisation and scaled decode (HBM-streaming kernels).
 //
 // hif8_static_quant: data = enc_sat(fp32(x) / s), bit-exact with
-// calibration.static_quantize_tensor (reference calibration.py:182-201).
-// The quotient is formed as x * (1/s) (both correctly rounded, so within two
-// units in the last place of the exact quotient); the HiF8 code depends only
-// on the exponent and the top four mantissa bits, so whenever the low 19
-// mantissa bits of that product are at least 4 units away from a multiple of
-// 2^19 the exact IEEE quotient has the same code.  Otherwise -- and for
-// overflow, NaN/Inf, or a denormal reciprocal -- the kernel recomputes the
-// quotient with the correctly rounded division __fdiv_rn.
+// calibration.static_quantize_tensor (reference calibration.py:182-201); the
+// per-element rule (a product with the reciprocal, the correctly rounded
+// division near code boundaries) is static_code in hif8_common.cuh.
 #include "hif8_common.cuh"
 
 namespace hif8 {
 
-__device__ __forceinline__ uint32_t quant_one(float f, float s, float r, bool exact_only,
+__device__ __forceinline__ uint32_t quant_one(float f, float r, double r64, bool exact_only,
                                               const uint8_t *__restrict__ tbl) {
-  float q = __fmul_rn(f, r);
-  uint32_t u = __float_as_uint(q);
-  const uint32_t low = u & 0x7FFFFu;
-  if (exact_only | ((low - 4u) > 0x7FFF8u) | ((u & 0x7F800000u) >= 0x7D000000u)) {
-    q = __fdiv_rn(f, s);
-    u = __float_as_uint(q);
-    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x80u;
-  }
-  return tbl[u >> 19];
+  return static_code(f, r, r64, exact_only, tbl);
 }
 
-__device__ __forceinline__ void load_encode_table(uint8_t *smem) {
-  const uint4 *src = reinterpret_cast<const uint4 *>(g_static_encode.v);
-  uint4 *dst = reinterpret_cast<uint4 *>(smem);
-  for (int i = threadIdx.x; i < 8192 / 16; i += blockDim.x) dst[i] = src[i];
-}
+__device__ __forceinline__ void load_encode_table(uint8_t *smem) { load_encode_mag_table(smem); }
 
-__device__ __forceinline__ float reciprocal(float s, bool &exact_only) {
+// RN32(1/s) and RN64(1/s); exact_only (every element by the exact FP64
+// path) for a reciprocal that is zero, infinite or NaN, and for a scale that
+// is not positive (the chunk path reads each code's sign from its input).
+__device__ __forceinline__ float reciprocal(float s, bool &exact_only, double &r64) {
   const float r = __frcp_rn(s);
   const uint32_t e = __float_as_uint(r) & 0x7F800000u;
-  exact_only = (e == 0u) | (e == 0x7F800000u);
+  exact_only = (e == 0u) | (e == 0x7F800000u) | !(s > 0.f);
+  r64 = __drcp_rn((double)s);
   return r;
 }
 
-// 16 elements per thread and iteration: two 16-byte loads, one 16-byte store.
 __device__ __forceinline__ void write_row_scale(const float *__restrict__ scale, int64_t scale_count,
                                                 float *__restrict__ row_scale, int64_t rows) {
   if (!row_scale) return;
@@ -47,13 +33,33 @@ __device__ __forceinline__ void write_row_scale(const float *__restrict__ scale,
     row_scale[r] = scale[r % scale_count];
 }
 
+// 16 elements (two 16-byte loads, one 16-byte store) per chunk; every thread
+// keeps kQuantUnroll chunks in flight (all loads issued before any
+// arithmetic), so the kernel streams at the HBM rate instead of waiting one
+// load latency per chunk.  The reciprocal of the fixed scale is formed once
+// per thread (kPerRow: once per change of the scale along the thread's
+// chunks), and a chunk's row is a 32-bit division only when scales differ
+// per row (chunks < 2^32, checked by the launcher).
+constexpr int kQuantUnroll = 4;
+
 template <int kDtype>
+__device__ __forceinline__ uint4 quant_chunk(const uint4 a, const uint4 b, float r, double r64, bool exact_only,
+                                             const uint8_t *__restrict__ tbl) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t o[4];
+  // some element within 4 ulp of a code boundary (or zero, or huge): the
+  // whole chunk by the exact FP64 path
+  if (exact_only || !static_codes16<kDtype>(w, r, tbl, o)) static_codes16_exact<kDtype>(w, r64, tbl, o);
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <int kDtype, bool kPerRow>
 __global__ void __launch_bounds__(256) static_quant_vec16(const uint16_t *__restrict__ x, int64_t k,
                                                           const float *__restrict__ scale,
                                                           int64_t scale_count, uint8_t *__restrict__ out,
                                                           int64_t chunks, float *__restrict__ row_scale,
                                                           int64_t rows) {
-  __shared__ __align__(16) uint8_t tbl[8192];
+  __shared__ __align__(16) uint8_t tbl[4096];
   load_encode_table(tbl);
   pdl_wait();  // x and scale may come from the previous kernel of the stream
   // Let the dependent linear launch now: its CTAs take the SMs this small
@@ -63,27 +69,38 @@ __global__ void __launch_bounds__(256) static_quant_vec16(const uint16_t *__rest
   pdl_launch_dependents();
   write_row_scale(scale, scale_count, row_scale, rows);
   __syncthreads();
-  const int64_t chunks_per_row = k >> 4;
-  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
-       c += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = c / chunks_per_row;
-    const float s = __ldg(scale + (scale_count == 1 ? 0 : row % scale_count));
-    bool exact_only;
-    const float r = reciprocal(s, exact_only);
-    const uint4 *src = reinterpret_cast<const uint4 *>(x + (c << 4));
-    const uint4 a = __ldcs(src), b = __ldcs(src + 1);
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    uint32_t o[4];
+  const uint32_t chunks_per_row = (uint32_t)(k >> 4);
+  int64_t cur = 0;  // scale index of s / r
+  float s = __ldg(scale);
+  bool exact_only;
+  double r64;
+  float r = reciprocal(s, exact_only, r64);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t c0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c0 < chunks; c0 += kQuantUnroll * stride) {
+    uint4 a[kQuantUnroll], b[kQuantUnroll];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t lo = w[2 * j], hi = w[2 * j + 1];
-      const uint32_t c0 = quant_one(half_bits_to_f32<kDtype>(lo & 0xFFFFu), s, r, exact_only, tbl);
-      const uint32_t c1 = quant_one(half_bits_to_f32<kDtype>(lo >> 16), s, r, exact_only, tbl);
-      const uint32_t c2 = quant_one(half_bits_to_f32<kDtype>(hi & 0xFFFFu), s, r, exact_only, tbl);
-      const uint32_t c3 = quant_one(half_bits_to_f32<kDtype>(hi >> 16), s, r, exact_only, tbl);
-      o[j] = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
+    for (int u = 0; u < kQuantUnroll; ++u) {
+      const int64_t c = c0 + u * stride;
+      if (c < chunks) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + (c << 4));
+        a[u] = __ldcs(src);
+        b[u] = __ldcs(src + 1);
+      }
     }
-    __stcs(reinterpret_cast<uint4 *>(out + (c << 4)), make_uint4(o[0], o[1], o[2], o[3]));
+#pragma unroll
+    for (int u = 0; u < kQuantUnroll; ++u) {
+      const int64_t c = c0 + u * stride;
+      if (c >= chunks) break;
+      if constexpr (kPerRow) {
+        const int64_t sidx = (int64_t)((uint32_t)c / chunks_per_row) % scale_count;
+        if (sidx != cur) {
+          cur = sidx;
+          s = __ldg(scale + sidx);
+          r = reciprocal(s, exact_only, r64);
+        }
+      }
+      __stcs(reinterpret_cast<uint4 *>(out + (c << 4)), quant_chunk<kDtype>(a[u], b[u], r, r64, exact_only, tbl));
+    }
   }
 }
 
@@ -93,7 +110,7 @@ __global__ void __launch_bounds__(256) static_quant_scalar(const uint16_t *__res
                                                            int64_t scale_count, uint8_t *__restrict__ out,
                                                            int64_t total, float *__restrict__ row_scale,
                                                            int64_t rows) {
-  __shared__ __align__(16) uint8_t tbl[8192];
+  __shared__ __align__(16) uint8_t tbl[4096];
   load_encode_table(tbl);
   pdl_wait();  // x and scale may come from the previous kernel of the stream
   write_row_scale(scale, scale_count, row_scale, rows);
@@ -103,8 +120,9 @@ __global__ void __launch_bounds__(256) static_quant_scalar(const uint16_t *__res
     const int64_t row = i / k;
     const float s = __ldg(scale + row % scale_count);
     bool exact_only;
-    const float r = reciprocal(s, exact_only);
-    out[i] = (uint8_t)quant_one(half_bits_to_f32<kDtype>(x[i]), s, r, exact_only, tbl);
+    double r64;
+    const float r = reciprocal(s, exact_only, r64);
+    out[i] = (uint8_t)quant_one(half_bits_to_f32<kDtype>(x[i]), r, r64, exact_only, tbl);
   }
 }
 
@@ -120,52 +138,107 @@ __device__ __forceinline__ uint32_t decode_pair(const float *tbl, uint32_t word,
   return lo | (hi << 16);
 }
 
-// 16 bytes in, 32 bytes out per thread and iteration (rows of k % 16 == 0).
-__global__ void __launch_bounds__(256) scaled_decode_vec16(const uint8_t *__restrict__ data, int64_t k,
-                                                           int64_t stride, const float *__restrict__ scale,
-                                                           uint16_t *__restrict__ out, int64_t chunks) {
-  __shared__ float tbl[256];
-  load_decode_table(tbl);
-  __syncthreads();
-  const int64_t per_row = k >> 4;
-  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
-       c += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = c / per_row, col = (c - row * per_row) << 4;
-    const float s = __ldg(scale + row);
-    const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(data + row * stride + col));
-    uint4 o0, o1;
-    o0.x = decode_pair(tbl, v.x, 0, s);
-    o0.y = decode_pair(tbl, v.x, 16, s);
-    o0.z = decode_pair(tbl, v.y, 0, s);
-    o0.w = decode_pair(tbl, v.y, 16, s);
-    o1.x = decode_pair(tbl, v.z, 0, s);
-    o1.y = decode_pair(tbl, v.z, 16, s);
-    o1.z = decode_pair(tbl, v.w, 0, s);
-    o1.w = decode_pair(tbl, v.w, 16, s);
-    uint4 *dst = reinterpret_cast<uint4 *>(out + row * k + col);
-    __stcs(dst, o0);
-    __stcs(dst + 1, o1);
+// The same through the lane-replicated table (conflict-free lookups).
+__device__ __forceinline__ uint32_t lane_decode_pair(const float *tbl, uint32_t word, int shift, float s,
+                                                     uint32_t lane) {
+  const uint32_t lo = f32_to_bf16_bits(lane_decode(tbl, (word >> shift) & 0xFFu, lane) * s);
+  const uint32_t hi = f32_to_bf16_bits(lane_decode(tbl, (word >> (shift + 8)) & 0xFFu, lane) * s);
+  return lo | (hi << 16);
+}
+
+__device__ __forceinline__ uint4 lane_decode16(const float *tbl, const uint32_t (&w)[4], float s, uint32_t lane,
+                                               int half) {
+  return make_uint4(lane_decode_pair(tbl, w[2 * half], 0, s, lane), lane_decode_pair(tbl, w[2 * half], 16, s, lane),
+                    lane_decode_pair(tbl, w[2 * half + 1], 0, s, lane),
+                    lane_decode_pair(tbl, w[2 * half + 1], 16, s, lane));
+}
+
+// The pair through the hardware BF16 conversion (callers: no NaN code in the
+// word and decode_scale_ok(s), so it equals lane_decode_pair).
+__device__ __forceinline__ uint32_t lane_decode_pair_hw(const float *tbl, uint32_t word, int shift, float s,
+                                                        uint32_t lane) {
+  return bf16x2_rn(lane_decode(tbl, (word >> shift) & 0xFFu, lane) * s,
+                   lane_decode(tbl, (word >> (shift + 8)) & 0xFFu, lane) * s);
+}
+
+// 16 bytes -> 32 bytes (two uint4 of BF16 pairs): the hardware conversion
+// when the chunk allows it, else the exact-NaN software rounding.
+__device__ __forceinline__ void lane_decode_chunk(const float *tbl, const uint32_t (&w)[4], float s, uint32_t lane,
+                                                  uint4 &o0, uint4 &o1) {
+  if (decode_scale_ok(s) && no_nan_code(w[0]) && no_nan_code(w[1]) && no_nan_code(w[2]) && no_nan_code(w[3])) {
+    o0 = make_uint4(lane_decode_pair_hw(tbl, w[0], 0, s, lane), lane_decode_pair_hw(tbl, w[0], 16, s, lane),
+                    lane_decode_pair_hw(tbl, w[1], 0, s, lane), lane_decode_pair_hw(tbl, w[1], 16, s, lane));
+    o1 = make_uint4(lane_decode_pair_hw(tbl, w[2], 0, s, lane), lane_decode_pair_hw(tbl, w[2], 16, s, lane),
+                    lane_decode_pair_hw(tbl, w[3], 0, s, lane), lane_decode_pair_hw(tbl, w[3], 16, s, lane));
+  } else {
+    o0 = lane_decode16(tbl, w, s, lane, 0);
+    o1 = lane_decode16(tbl, w, s, lane, 1);
   }
 }
 
-// 4 bytes in, 8 bytes out (rows with k % 4 == 0, e.g. KV rows with the
-// 4-byte sidecar between them).
-__global__ void __launch_bounds__(256) scaled_decode_vec4(const uint8_t *__restrict__ data, int64_t k,
-                                                          int64_t stride, const float *__restrict__ scale,
-                                                          uint16_t *__restrict__ out, int64_t chunks) {
-  __shared__ float tbl[256];
-  load_decode_table(tbl);
+// Scaled decode units: 16 bytes in, 32 bytes out (ELEMS = 16, rows of k % 16
+// == 0) or 4 bytes in, 8 bytes out (ELEMS = 4, e.g. KV rows with the 4-byte
+// sidecar between them).  kDecodeUnroll units per thread in flight, the row
+// of a unit a 32-bit division (units < 2^32, checked by the launcher), the
+// decode through the lane-replicated table.
+constexpr int kDecodeUnroll = 4;
+
+template <int ELEMS>
+__global__ void __launch_bounds__(256) scaled_decode_vec(const uint8_t *__restrict__ data, int64_t k,
+                                                         int64_t stride, const float *__restrict__ scale,
+                                                         uint16_t *__restrict__ out, int64_t chunks) {
+  __shared__ float tbl[kLaneDecodeWords];
+  load_lane_decode_table(tbl);
   __syncthreads();
-  const int64_t per_row = k >> 2;
-  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
-       c += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = c / per_row, col = (c - row * per_row) << 2;
-    const float s = __ldg(scale + row);
-    const uint32_t v = __ldcs(reinterpret_cast<const unsigned int *>(data + row * stride + col));
-    uint2 o;
-    o.x = decode_pair(tbl, v, 0, s);
-    o.y = decode_pair(tbl, v, 16, s);
-    __stcs(reinterpret_cast<uint2 *>(out + row * k + col), o);
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t per_row = (uint32_t)(k / ELEMS);
+  const int64_t gstride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t c0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c0 < chunks; c0 += kDecodeUnroll * gstride) {
+    uint32_t w[kDecodeUnroll][4];
+    int64_t row[kDecodeUnroll], col[kDecodeUnroll];
+    float sc[kDecodeUnroll];
+#pragma unroll
+    for (int u = 0; u < kDecodeUnroll; ++u) {
+      const int64_t c = c0 + u * gstride;
+      row[u] = c < chunks ? (int64_t)((uint32_t)c / per_row) : 0;
+      col[u] = (c - row[u] * per_row) * ELEMS;
+      w[u][0] = w[u][1] = w[u][2] = w[u][3] = 0;
+      sc[u] = 0.f;
+      if (c < chunks) {
+        sc[u] = __ldg(scale + row[u]);
+        if constexpr (ELEMS == 16) {
+          const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(data + row[u] * stride + col[u]));
+          w[u][0] = v.x;
+          w[u][1] = v.y;
+          w[u][2] = v.z;
+          w[u][3] = v.w;
+        } else {
+          w[u][0] = __ldcs(reinterpret_cast<const unsigned int *>(data + row[u] * stride + col[u]));
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kDecodeUnroll; ++u) {
+      const int64_t c = c0 + u * gstride;
+      if (c >= chunks) break;
+      if constexpr (ELEMS == 16) {
+        uint4 *dst = reinterpret_cast<uint4 *>(out + row[u] * k + col[u]);
+        uint4 o0, o1;
+        lane_decode_chunk(tbl, w[u], sc[u], lane, o0, o1);
+        __stcs(dst, o0);
+        __stcs(dst + 1, o1);
+      } else {
+        uint2 o;
+        if (decode_scale_ok(sc[u]) && no_nan_code(w[u][0])) {
+          o.x = lane_decode_pair_hw(tbl, w[u][0], 0, sc[u], lane);
+          o.y = lane_decode_pair_hw(tbl, w[u][0], 16, sc[u], lane);
+        } else {
+          o.x = lane_decode_pair(tbl, w[u][0], 0, sc[u], lane);
+          o.y = lane_decode_pair(tbl, w[u][0], 16, sc[u], lane);
+        }
+        __stcs(reinterpret_cast<uint2 *>(out + row[u] * k + col[u]), o);
+      }
+    }
   }
 }
 
@@ -187,37 +260,70 @@ __global__ void __launch_bounds__(256) scaled_decode_scalar(const uint8_t *__res
 // decode table rows times the row scale cast to BF16, a BF16 product).  Both
 // factors are BF16 values, so their FP32 product is exact and is rounded
 // once.  Ids outside [0, vocab) give a zero row and count into *bad_ids.
-// VEC: 16 bytes in, 32 bytes out per thread (k % 16 == 0, aligned rows).
+// VEC: 16 bytes in, 32 bytes out per unit (k % 16 == 0, aligned rows), and
+// kEmbedUnroll units per thread in flight: the id loads of all of them, then
+// their scale and row loads, then the decode -- two dependent load latencies
+// per kEmbedUnroll units instead of per unit.  A unit's row is a 32-bit
+// division (units < 2^32, checked by the launcher).
+constexpr int kEmbedUnroll = 4;
+
 template <bool VEC>
 __global__ void __launch_bounds__(256) embedding_gather(const uint8_t *__restrict__ weight,
                                                         const float *__restrict__ weight_scale, int64_t vocab,
                                                         int64_t k, const int64_t *__restrict__ ids,
                                                         uint16_t *__restrict__ out, int64_t work,
                                                         int32_t *__restrict__ bad_ids) {
-  __shared__ float tbl[256];
-  load_decode_table(tbl);  // module data: before the dependency wait
+  __shared__ float tbl[VEC ? kLaneDecodeWords : 256];
+  if constexpr (VEC) load_lane_decode_table(tbl);  // module data: before the dependency wait
+  else load_decode_table(tbl);
   __syncthreads();
   pdl_wait();  // the ids may come from the previous kernel (the last step's argmax)
-  const int64_t per_row = VEC ? k >> 4 : k;
-  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < work; c += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = c / per_row, j = c - t * per_row;
-    const int64_t id = __ldg(ids + t);
-    const bool ok = id >= 0 && id < vocab;
-    if (!ok && j == 0 && bad_ids) atomicAdd(bad_ids, 1);
-    const float s = ok ? bf16_bits_to_f32(f32_to_bf16_bits(__ldg(weight_scale + id))) : 0.f;
-    if constexpr (VEC) {
-      uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
-      if (ok) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(weight + id * k) + j);
-        o0 = make_uint4(decode_pair(tbl, v.x, 0, s), decode_pair(tbl, v.x, 16, s), decode_pair(tbl, v.y, 0, s),
-                        decode_pair(tbl, v.y, 16, s));
-        o1 = make_uint4(decode_pair(tbl, v.z, 0, s), decode_pair(tbl, v.z, 16, s), decode_pair(tbl, v.w, 0, s),
-                        decode_pair(tbl, v.w, 16, s));
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if constexpr (VEC) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t per_row = (uint32_t)(k >> 4);
+    for (int64_t c0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c0 < work; c0 += kEmbedUnroll * stride) {
+      int64_t t[kEmbedUnroll], id[kEmbedUnroll];
+      uint32_t j[kEmbedUnroll];
+#pragma unroll
+      for (int u = 0; u < kEmbedUnroll; ++u) {
+        const int64_t c = c0 + u * stride;
+        t[u] = c < work ? (int64_t)((uint32_t)c / per_row) : 0;
+        j[u] = (uint32_t)(c - t[u] * per_row);
+        id[u] = c < work ? __ldg(ids + t[u]) : -1;
       }
-      uint4 *dst = reinterpret_cast<uint4 *>(out + t * k) + 2 * j;
-      dst[0] = o0;
-      dst[1] = o1;
-    } else {
+      float sc[kEmbedUnroll];
+      uint4 v[kEmbedUnroll];
+#pragma unroll
+      for (int u = 0; u < kEmbedUnroll; ++u) {
+        const bool ok = id[u] >= 0 && id[u] < vocab;
+        sc[u] = ok ? __ldg(weight_scale + id[u]) : 0.f;
+        v[u] = ok ? __ldg(reinterpret_cast<const uint4 *>(weight + id[u] * k) + j[u]) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kEmbedUnroll; ++u) {
+        const int64_t c = c0 + u * stride;
+        if (c >= work) break;
+        const bool ok = id[u] >= 0 && id[u] < vocab;
+        if (!ok && j[u] == 0 && bad_ids) atomicAdd(bad_ids, 1);
+        const float s = ok ? bf16_bits_to_f32(f32_to_bf16_bits(sc[u])) : 0.f;
+        uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
+        if (ok) {
+          const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+          lane_decode_chunk(tbl, w, s, lane, o0, o1);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(out + t[u] * k) + 2 * j[u];
+        __stcs(dst, o0);
+        __stcs(dst + 1, o1);
+      }
+    }
+  } else {
+    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < work; c += stride) {
+      const int64_t t = c / k, j = c - t * k;
+      const int64_t id = __ldg(ids + t);
+      const bool ok = id >= 0 && id < vocab;
+      if (!ok && j == 0 && bad_ids) atomicAdd(bad_ids, 1);
+      const float s = ok ? bf16_bits_to_f32(f32_to_bf16_bits(__ldg(weight_scale + id))) : 0.f;
       out[t * k + j] = ok ? (uint16_t)f32_to_bf16_bits(tbl[weight[id * k + j]] * s) : (uint16_t)0;
     }
   }
@@ -247,14 +353,21 @@ extern "C" int hif8_static_quant(const void *x, int x_dtype, int64_t rows, int64
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const uint16_t *xs = static_cast<const uint16_t *>(x);
   const int64_t total = rows * k;
-  if (k % 16 == 0 && aligned16(x) && aligned16(data)) {
+  if (k % 16 == 0 && aligned16(x) && aligned16(data) && total / 16 <= 0xFFFFFFFFLL) {
     const int64_t chunks = total / 16;
+    // one chunk per thread up to 8 CTAs per SM; beyond that wave each thread
+    // walks its chunks kQuantUnroll at a time
     const int grid = grid_for(chunks, 256);
-    return x_dtype == HIF8_DTYPE_BF16
-               ? launch_pdl(static_quant_vec16<HIF8_DTYPE_BF16>, dim3(grid), dim3(256), 0, stream, xs, k,
-                            fixed_scale, scale_count, data, chunks, row_scale, rows)
-               : launch_pdl(static_quant_vec16<HIF8_DTYPE_F16>, dim3(grid), dim3(256), 0, stream, xs, k,
-                            fixed_scale, scale_count, data, chunks, row_scale, rows);
+    const bool bf16 = x_dtype == HIF8_DTYPE_BF16;
+    if (scale_count == 1)
+      return bf16 ? launch_pdl(static_quant_vec16<HIF8_DTYPE_BF16, false>, dim3(grid), dim3(256), 0, stream, xs, k,
+                               fixed_scale, scale_count, data, chunks, row_scale, rows)
+                  : launch_pdl(static_quant_vec16<HIF8_DTYPE_F16, false>, dim3(grid), dim3(256), 0, stream, xs, k,
+                               fixed_scale, scale_count, data, chunks, row_scale, rows);
+    return bf16 ? launch_pdl(static_quant_vec16<HIF8_DTYPE_BF16, true>, dim3(grid), dim3(256), 0, stream, xs, k,
+                             fixed_scale, scale_count, data, chunks, row_scale, rows)
+                : launch_pdl(static_quant_vec16<HIF8_DTYPE_F16, true>, dim3(grid), dim3(256), 0, stream, xs, k,
+                             fixed_scale, scale_count, data, chunks, row_scale, rows);
   }
   const int grid = grid_for(total, 256);
   return x_dtype == HIF8_DTYPE_BF16
@@ -270,12 +383,16 @@ extern "C" int hif8_scaled_decode(const uint8_t *data, int64_t rows, int64_t k, 
     return HIF8_ERR_INVALID_ARGUMENT;
   if (rows == 0) return HIF8_OK;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  if (k % 16 == 0 && data_row_stride % 16 == 0 && aligned16(data) && aligned16(out)) {
+  if (k % 16 == 0 && data_row_stride % 16 == 0 && aligned16(data) && aligned16(out) &&
+      rows * (k / 16) <= 0xFFFFFFFFLL) {
     const int64_t chunks = rows * (k / 16);
-    scaled_decode_vec16<<<grid_for(chunks, 256), 256, 0, stream>>>(data, k, data_row_stride, scale, out, chunks);
-  } else if (k % 4 == 0 && data_row_stride % 4 == 0 && aligned4(data) && aligned4(out)) {
+    scaled_decode_vec<16><<<grid_for(chunks, 256), 256, 0, stream>>>(
+        data, k, data_row_stride, scale, out, chunks);
+  } else if (k % 4 == 0 && data_row_stride % 4 == 0 && aligned4(data) && aligned4(out) &&
+             rows * (k / 4) <= 0xFFFFFFFFLL) {
     const int64_t chunks = rows * (k / 4);
-    scaled_decode_vec4<<<grid_for(chunks, 256), 256, 0, stream>>>(data, k, data_row_stride, scale, out, chunks);
+    scaled_decode_vec<4><<<grid_for(chunks, 256), 256, 0, stream>>>(
+        data, k, data_row_stride, scale, out, chunks);
   } else {
     const int64_t total = rows * k;
     scaled_decode_scalar<<<grid_for(total, 256), 256, 0, stream>>>(data, k, data_row_stride, scale, out, total);
@@ -290,10 +407,10 @@ extern "C" int hif8_embedding_gather(const uint8_t *weight, const float *weight_
     return HIF8_ERR_INVALID_ARGUMENT;
   if (n == 0) return HIF8_OK;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  if (k % 16 == 0 && aligned16(weight) && aligned16(out)) {
+  if (k % 16 == 0 && aligned16(weight) && aligned16(out) && n * (k / 16) <= 0xFFFFFFFFLL) {
     const int64_t work = n * (k / 16);
-    return launch_pdl(embedding_gather<true>, dim3(grid_for(work, 256)), dim3(256), 0, stream, weight, weight_scale,
-                      vocab, k, ids, out, work, bad_ids);
+    return launch_pdl(embedding_gather<true>, dim3(grid_for(work, 256)),
+                      dim3(256), 0, stream, weight, weight_scale, vocab, k, ids, out, work, bad_ids);
   }
   const int64_t work = n * k;
   return launch_pdl(embedding_gather<false>, dim3(grid_for(work, 256)), dim3(256), 0, stream, weight, weight_scale,
