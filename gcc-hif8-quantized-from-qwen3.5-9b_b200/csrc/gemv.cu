@@ -152,26 +152,6 @@ __device__ __forceinline__ uint32_t fake_quant_bf16(uint32_t h, float s, float r
   return g_decode_f32.v[code] >> 16;
 }
 
-// The same with the encode table and the lane-replicated decode table in
-// shared memory (the prologue's copies).
-template <int ASRC>
-__device__ __forceinline__ uint32_t fake_quant_bf16_smem(uint32_t h, float s, float r, bool exact_only,
-                                                         const uint8_t *enc, const uint32_t *lut, int lane) {
-  const float f = ASRC == kActBf16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
-  float q = __fmul_rn(f, r);
-  uint32_t u = __float_as_uint(q);
-  const uint32_t low = u & 0x7FFFFu;
-  uint32_t code;
-  if (exact_only | ((low - 4u) > 0x7FFF8u) | ((u & 0x7F800000u) >= 0x7D000000u)) {
-    q = __fdiv_rn(f, s);
-    u = __float_as_uint(q);
-    code = ((u & 0x7FFFFFFFu) > 0x7F800000u) ? 0x80u : (uint32_t)enc[u >> 19];
-  } else {
-    code = enc[u >> 19];
-  }
-  return lut[code * 64 + lane];
-}
-
 template <int OUT>
 __device__ __forceinline__ void store_out(void *out, int64_t idx, float v) {
   if constexpr (OUT == HIF8_DTYPE_BF16) static_cast<uint16_t *>(out)[idx] = (uint16_t)f32_to_bf16_bits(v);
@@ -257,33 +237,42 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
     w1 = p.w + (int64_t)r1 * p.k + kw0 + t * 32;
   };
 
-  // Every global read of the prologue may depend on the previous kernel of
-  // the stream (its activations, or weights it has just written), so all of
-  // them follow the dependency wait.  The independent loads -- the two
-  // tables' sources, the first round of activations and this warp's first
-  // item of weights, in that order -- are all issued before any of them is
-  // used, so their latencies overlap instead of adding up.
-  pdl_wait();
   U32x8 ring[kRing][2];
 
   // ---- prologue: lane-replicated decode table + this rank's activation slice
   {
     uint32_t *lut = reinterpret_cast<uint32_t *>(smem);
-    uint8_t *enc = reinterpret_cast<uint8_t *>(red);
-    // warp w owns table entries 16 w .. 16 w + 15 (one load per lane); the
-    // fused quantiser's 8 KB encode table is staged in the reduction buffer
-    // (idle until the first item is reduced), one 16-byte piece per thread
-    const uint32_t mine = g_decode_f32.v[warp * 16 + (lane & 15)] >> 16;
-    static_assert(kThreads == 512, "one encode-table piece per thread");
-    uint4 enc_piece = make_uint4(0, 0, 0, 0);
-    float ts0 = 1.f;  // the fused quantiser's fixed scale
-    if (ASRC != kActCodes) {
-      enc_piece = reinterpret_cast<const uint4 *>(g_static_encode.v)[tid];
-      ts0 = p.ts[0];
+    // the fused quantiser's tables, staged in the reduction buffer (idle
+    // until the first item is reduced): the fake-quant table (decoded BF16 of
+    // the static code per magnitude index, 8 KB) and the magnitude encode
+    // table of the exact path (4 KB)
+    uint16_t *fq = reinterpret_cast<uint16_t *>(red);
+    uint8_t *mag = reinterpret_cast<uint8_t *>(red) + 8192;
+    // Module constants only before the dependency wait: the tables are built
+    // while the previous kernel of the stream completes.  warp w owns table
+    // entries 16 w .. 16 w + 15 (one load per lane).
+    {
+      const uint32_t mine = g_decode_f32.v[warp * 16 + (lane & 15)] >> 16;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) lut[(warp * 16 + j) * 64 + lane] = __shfl_sync(0xFFFFFFFFu, mine, j);
+      static_assert(kThreads == 512, "one fake-quant table piece per thread");
+      if (ASRC != kActCodes) {
+        reinterpret_cast<uint4 *>(fq)[tid] = reinterpret_cast<const uint4 *>(g_fake_quant_bf16.v)[tid];
+        if (tid < 256) reinterpret_cast<uint4 *>(mag)[tid] = reinterpret_cast<const uint4 *>(g_static_encode_mag.v)[tid];
+      }
     }
+    // Every other global read of the prologue may depend on the previous
+    // kernel of the stream (its activations, or weights it has just
+    // written), so it follows the dependency wait.  The activation loads and
+    // this warp's first item of weights are all issued before any of them is
+    // used, so their latencies overlap instead of adding up.
+    pdl_wait();
+    float ts0 = 1.f;  // the fused quantiser's fixed scale
+    if (ASRC != kActCodes) ts0 = p.ts[0];
     const int chunks_per_tok = kc >> 4;  // 16 K values per chunk
+    // only the real tokens' rows: fragment rows of padding tokens (>= m) are
+    // never loaded, so their tile rows are never written either
     const int real = (p.m < kTok ? p.m : kTok) * chunks_per_tok;
-    const int total_chunks = kTok * chunks_per_tok;
     // kPro chunks per thread and round: a round's global loads are issued
     // before its arithmetic (the first round's before the table stores)
     constexpr int kPro = kGlue ? 2 : 4;
@@ -324,22 +313,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
       }
     };
     load_round(0);
-    // the first item's weights last: the table and activation reads (L2
-    // hits) must not queue behind these HBM reads
-    if (my_items > 0) {
-      const uint8_t *w0, *w1;
-      weight_ptrs(0, w0, w1);
-#pragma unroll
-      for (int st = 0; st < kRing; ++st) {
-        ring[st][0] = ldg_stream32(w0 + st * kBlk);
-        ring[st][1] = ldg_stream32(w1 + st * kBlk);
-      }
-    }
-
-    // table stores
-#pragma unroll
-    for (int j = 0; j < 16; ++j) lut[(warp * 16 + j) * 64 + lane] = __shfl_sync(0xFFFFFFFFu, mine, j);
-    if (ASRC != kActCodes) reinterpret_cast<uint4 *>(enc)[tid] = enc_piece;
 
     if constexpr (ASRC == kActRmsNorm) {
       // inverse RMS of every token's full row (x + residual), identical in
@@ -383,23 +356,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
     }
     __syncthreads();
     const uint32_t lane4 = (uint32_t)lane << 2;
-    float s = 1.f, r = 1.f;
+    float r = 1.f;
+    double r64 = 1.0;
     bool exact_only = false;
     if (ASRC != kActCodes) {
-      s = ts0;
-      r = __frcp_rn(s);
+      r = __frcp_rn(ts0);
+      r64 = __drcp_rn((double)ts0);
       const uint32_t re = __float_as_uint(r) & 0x7F800000u;
-      exact_only = (re == 0u) | (re == 0x7F800000u);
+      exact_only = (re == 0u) | (re == 0x7F800000u) | !(ts0 > 0.f);
     }
-    for (int base = 0; base < total_chunks; base += kPro * kThreads) {
+    for (int base = 0; base < real; base += kPro * kThreads) {
       if (base > 0) load_round(base);
 #pragma unroll
       for (int u = 0; u < kPro; ++u) {
         const int i = base + u * kThreads + tid;
-        if (i >= total_chunks) break;
+        if (i >= real) break;
         const int tok = i / chunks_per_tok, ch = i - tok * chunks_per_tok;
-        uint4 o0 = make_uint4(0, 0, 0, 0), o1 = o0;
-        if (i < real) {
+        uint4 o0, o1;
+        {
           if (ASRC != kActCodes) {
             uint32_t h8[8] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w,
                               raw[u][1].x, raw[u][1].y, raw[u][1].z, raw[u][1].w};
@@ -416,11 +390,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
                 h8[j] = glue_value<ASRC>(h8[j] & 0xFFFFu, y8[j] & 0xFFFFu, w8[j] & 0xFFFFu, inv, has_y, one_plus) |
                         (glue_value<ASRC>(h8[j] >> 16, y8[j] >> 16, w8[j] >> 16, inv, has_y, one_plus) << 16);
             }
+            // decode(static code) of the 16 values, bit-identical to
+            // hif8_static_quant and a decode of its bytes: the fake-quant
+            // table with its chunk-wide check, else the exact FP64 path
             uint32_t r8[8];
+            if (exact_only || !fake_quant16<QSRC>(h8, r, fq, r8)) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              r8[j] = fake_quant_bf16_smem<QSRC>(h8[j] & 0xFFFFu, s, r, exact_only, enc, lut, lane) |
-                      (fake_quant_bf16_smem<QSRC>(h8[j] >> 16, s, r, exact_only, enc, lut, lane) << 16);
+              for (int j = 0; j < 8; ++j)
+                r8[j] = lut[static_code_exact(half_bits_to_f32<QSRC>(h8[j] & 0xFFFFu), r64, mag) * 64 + lane] |
+                        (lut[static_code_exact(half_bits_to_f32<QSRC>(h8[j] >> 16), r64, mag) * 64 + lane] << 16);
+            }
             o0 = make_uint4(r8[0], r8[1], r8[2], r8[3]);
             o1 = make_uint4(r8[4], r8[5], r8[6], r8[7]);
           } else {
@@ -435,6 +414,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
         uint8_t *row = act + tok * act_stride;
         *reinterpret_cast<uint4 *>(row + act_offset(ch * 16)) = o0;
         *reinterpret_cast<uint4 *>(row + act_offset(ch * 16 + 8)) = o1;
+      }
+    }
+    // The first item's weights after this thread's activation work: issued
+    // before it, the burst of HBM reads from every SM (~10 MB) queued ahead
+    // of the activation reads and delayed them by microseconds; issued as
+    // soon as those reads had returned it was slower again (configs[1]
+    // sweep: 328 us before, 318 us after, 328 us at the earlier point).
+    if (my_items > 0) {
+      const uint8_t *w0, *w1;
+      weight_ptrs(0, w0, w1);
+#pragma unroll
+      for (int st = 0; st < kRing; ++st) {
+        ring[st][0] = ldg_stream32(w0 + st * kBlk);
+        ring[st][1] = ldg_stream32(w1 + st * kBlk);
       }
     }
   }

@@ -140,10 +140,26 @@ HIF8_HD constexpr Table12 make_static_encode_mag_table() {
   return t;
 }
 
+struct alignas(16) TableFq {
+  uint16_t v[4096];
+};
+
+// BF16 payload of decode(static code) per magnitude index (the exponent
+// field and top-4 mantissa bits of |q|): fake quantisation straight to the
+// decoded value, for the prologues that quantise an activation and use it
+// decoded.  A negative input's value is this with the sign bit set, except
+// zero (code 0 decodes to +0).
+HIF8_HD constexpr TableFq make_fake_quant_table() {
+  TableFq t{};
+  for (uint32_t i = 0; i < 4096u; ++i) t.v[i] = (uint16_t)decode_bf16(static_encode13(i));
+  return t;
+}
+
 // Device copies of the tables (one per translation unit that uses them).
 static __device__ const Table13 g_static_encode = make_static_encode_table();
 static __device__ const Table12 g_static_encode_mag = make_static_encode_mag_table();
 static __device__ const Table256 g_decode_f32 = make_decode_table_f32();
+static __device__ const TableFq g_fake_quant_bf16 = make_fake_quant_table();
 
 // ---------------------------------------------------- float conversions --
 
@@ -299,6 +315,37 @@ __device__ __forceinline__ void static_codes16_exact(const uint32_t (&w)[8], dou
     }
     out[j] = v;
   }
+}
+
+// BF16 payloads of decode(static code) of 16 FP16/BF16 elements (w: their 8
+// words, element 2i in the low half of w[i]) quantised with the reciprocal r
+// of a POSITIVE fixed scale, two per output word in element order -- the
+// rule of static_codes16 with the decoded values looked up directly
+// (`fq`: shared-memory copy of g_fake_quant_bf16); the values at |q| -+ 4 ulp
+// also serve as the check.  Returns false when any element needs the exact
+// path.  A nonzero value takes its element's sign from the input word.
+template <int kDtype>
+__device__ __forceinline__ bool fake_quant16(const uint32_t (&w)[8], float r, const uint16_t *__restrict__ fq,
+                                             uint32_t (&out)[8]) {
+  uint32_t diff = 0u, amax = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint32_t v[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float f;
+      if constexpr (kDtype == HIF8_DTYPE_BF16) f = __uint_as_float(e ? (w[j] & 0xFFFF0000u) : (w[j] << 16));
+      else f = __half2float(__ushort_as_half((unsigned short)(e ? (w[j] >> 16) : (w[j] & 0xFFFFu))));
+      const uint32_t a = max(__float_as_uint(__fmul_rn(f, r)) & 0x7FFFFFFFu, 4u);
+      amax = max(amax, a);
+      v[e] = fq[(a - 4u) >> 19];
+      diff |= v[e] ^ fq[((a + 4u) >> 19) & 0xFFFu];  // masked: see static_code
+    }
+    const uint32_t pair = v[0] | (v[1] << 16);
+    // payloads are below 0x8000: + 0x7FFF sets bit 15 of exactly the nonzero ones
+    out[j] = pair | (w[j] & (pair + 0x7FFF7FFFu) & 0x80008000u);
+  }
+  return diff == 0u && amax < 0x7D000000u;
 }
 
 // Lane-replicated FP32 decode table in shared memory (32 KB): entry b of
