@@ -286,12 +286,12 @@ def build_layers(world: int, rank: int, device, replica: int = 0, keep_reference
             x_full = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
             if world == 1:
                 shard, shard_scale, x = data, scale, x_full
-            elif row_parallel:
-                shard, shard_scale = data[:, rank * k_loc:(rank + 1) * k_loc].contiguous(), scale
-                x = x_full[:, rank * k_loc:(rank + 1) * k_loc].contiguous()
+            elif row_parallel:  # clone: an owned tensor (the op wants storage offset 0)
+                shard, shard_scale = data[:, rank * k_loc:(rank + 1) * k_loc].clone(), scale
+                x = x_full[:, rank * k_loc:(rank + 1) * k_loc].clone()
             else:
-                shard = data[rank * n_loc:(rank + 1) * n_loc].contiguous()
-                shard_scale = scale[rank * n_loc:(rank + 1) * n_loc].contiguous()
+                shard = data[rank * n_loc:(rank + 1) * n_loc].clone()
+                shard_scale = scale[rank * n_loc:(rank + 1) * n_loc].clone()
                 x = x_full
             layer = scheme.Hif8StaticLinear(shard, shard_scale.reshape(-1, 1), input_scale)
             call = {"m": m, "name": name, "n": n, "k": k, "layer": layer, "x": x, "row_parallel": row_parallel,
@@ -304,7 +304,63 @@ def build_layers(world: int, rank: int, device, replica: int = 0, keep_reference
     return calls
 
 
-def tp_sweep_parity(calls, world: int, rank: int, device) -> dict:
+def tp_apply(c, x, tp: bool):
+    """One call of the sweep: scheme.apply, or -- for a row-parallel call
+    under tensor parallelism -- this rank's FP32 partial product (summed over
+    the ranks before its one BF16 rounding)."""
+    import torch
+
+    from hif8_b200 import scheme
+
+    layer = c["layer"]
+    if tp and c["row_parallel"]:
+        return torch.ops.hif8_b200.linear_partial_f32(x, layer.weight, layer.input_scale, layer.weight_scale)
+    return scheme.apply(layer, x)
+
+
+class RowParallelReduce:
+    """The all-reduce after a row-parallel call of the tensor-parallel sweep:
+    the push exchange over NVLink peer memory (``PeerReducer.sum``: one
+    launch, every rank sums the partials in rank order) or NCCL.  Call sites
+    alternate between the reducer's two slots."""
+
+    def __init__(self, device, rank: int, world: int, kind: str):
+        self.kind = kind
+        self.peer = None
+        if kind == "peer":
+            from hif8_b200.decoder import PeerReducer
+
+            self.peer = PeerReducer(device, rank, world, max_rows=max(M_VALUES), dim=4096)
+        self.site = 0
+
+    def begin_step(self):
+        self.site = 0
+
+    def __call__(self, y):
+        """All-reduce of an FP32 partial; the BF16 sum (one rounding)."""
+        import torch
+        import torch.distributed as dist
+
+        if self.peer is None:
+            dist.all_reduce(y)
+            return y.to(torch.bfloat16)
+        out = self.peer.sum(y, self.site % 2)
+        self.site += 1
+        return out
+
+    def close(self):
+        if self.peer is not None:
+            import torch
+            import torch.distributed as dist
+
+            self.peer.check()
+            torch.cuda.synchronize()
+            dist.barrier()
+            self.peer.close()
+            self.peer = None
+
+
+def tp_sweep_parity(calls, world: int, rank: int, device, reduce) -> dict:
     """Every call of the tensor-parallel sweep against the unsharded (TP-1)
     layer of the same quantised weight: column-parallel shards against their
     rows of the TP-1 output, row-parallel results (after the all-reduce)
@@ -318,12 +374,13 @@ def tp_sweep_parity(calls, world: int, rank: int, device) -> dict:
     from hif8_b200 import scheme
 
     worst = torch.zeros(2, dtype=torch.float64, device=device)
+    reduce.begin_step()
     for c in calls:
         ref_layer, x_full = c["reference"]
         ref = scheme.apply(ref_layer, x_full).float()
-        y = scheme.apply(c["layer"], c["x"])
+        y = tp_apply(c, c["x"], True)
         if c["row_parallel"]:
-            dist.all_reduce(y)
+            y = reduce(y)
         else:
             ref = ref[:, rank * c["n_loc"]:(rank + 1) * c["n_loc"]]
         y = y.float()
@@ -336,6 +393,7 @@ def tp_sweep_parity(calls, world: int, rank: int, device) -> dict:
     glob, chan = (float(v) for v in worst.tolist())
     ok = bool(np.isfinite(glob) and glob <= TP_SWEEP_TOL and chan <= TP_SWEEP_TOL)
     return {"max_rel": glob, "channel_max_rel": chan, "tol": TP_SWEEP_TOL, "pass": ok,
+            "reduce": reduce.kind,
             "against": "the unsharded (TP-1) layer of the same quantised weight, every call of the sweep"}
 
 
@@ -389,7 +447,7 @@ def decoder_tp_parity(device, world: int, rank: int, calib: dict, steps: int = 8
                        f"{steps} teacher-forced decode steps, batch 1 and 4)"}
 
 
-def time_sweep(calls, args, device, world: int, local_rank: int, *, tp: bool, profile: bool):
+def time_sweep(calls, args, device, world: int, local_rank: int, *, tp: bool, profile: bool, reduce=None):
     """One step = every call of ``calls`` (static quant + HiF8 linear through
     scheme.apply; row-parallel results all-reduced when ``tp``), captured as
     a CUDA graph; W warm-up replays, then K timed replays between barriers.
@@ -401,10 +459,12 @@ def time_sweep(calls, args, device, world: int, local_rank: int, *, tp: bool, pr
 
     def step():
         outs = []
+        if tp:
+            reduce.begin_step()
         for c in calls:
-            y = scheme.apply(c["layer"], c["x"])
+            y = tp_apply(c, c["x"], tp)
             if tp and c["row_parallel"]:
-                dist.all_reduce(y)
+                y = reduce(y)
             outs.append(y)
         return outs
 
@@ -486,21 +546,26 @@ def run_ours(args) -> None:
         # the strong-scaling efficiency.  Checked against the unsharded
         # layers before it is timed; a failed check ends the run non-zero.
         calls = build_layers(world, rank, device, keep_reference=True)
-        extra["tp_parity"] = {"sweep": tp_sweep_parity(calls, world, rank, device)}
+        reduce = RowParallelReduce(device, rank, world, args.tp_allreduce)
+        extra["tp_parity"] = {"sweep": tp_sweep_parity(calls, world, rank, device, reduce)}
         parity_ok &= extra["tp_parity"]["sweep"]["pass"]
         for c in calls:
             c.pop("reference")
         torch.cuda.empty_cache()
-        elapsed_ms, clocks = time_sweep(calls, args, device, world, local_rank, tp=True, profile=True)
+        elapsed_ms, clocks = time_sweep(calls, args, device, world, local_rank, tp=True, profile=True, reduce=reduce)
         value = step_bytes() * args.steps / (elapsed_ms * 1e-3) / 1e9
-        launches_per_step = sum(1 if c["m"] <= 4 else 2 for c in calls)
-        parallelism = f"tp{world} (column: gate_up, qkv; row: down + NCCL all-reduce)"
+        launches_per_step = sum(1 if c["m"] <= 4 else 2 for c in calls) + (
+            sum(1 for c in calls if c["row_parallel"]) if reduce.kind == "peer" else 0)
+        parallelism = (f"tp{world} (column: gate_up, qkv; row: down + all-reduce "
+                       f"{'over NVLink peer memory (push exchange kernel)' if reduce.kind == 'peer' else 'NCCL'})")
 
     # -------------------------- dominant kernel: the GEMV, timed alone ---
     roofline = gemv_roofline(calls, args, device, world)
 
     # -------------------------------------------- e2e: public API, host I/O
-    e2e = measure_e2e(calls, args, device, world, tp=world > 1)
+    e2e = measure_e2e(calls, args, device, world, tp=world > 1, reduce=reduce if world > 1 else None)
+    if world > 1:
+        reduce.close()
 
     if world > 1:
         # beside the headline: N independent full-size replicas (weak)
@@ -936,7 +1001,7 @@ def gemv_roofline(calls, args, device, world) -> dict:
             "per_launch": per}
 
 
-def measure_e2e(calls, args, device, world, tp: bool = False) -> dict:
+def measure_e2e(calls, args, device, world, tp: bool = False, reduce=None) -> dict:
     """The same sweep through the public API (hif8_b200.scheme, eager) with
     host buffers inside the timed region: every step copies its 15
     activations from one packed pinned host buffer to the device (one H2D
@@ -965,10 +1030,12 @@ def measure_e2e(calls, args, device, world, tp: bool = False) -> dict:
     def step():
         dev_in.copy_(host_in, non_blocking=True)
         outs = []
+        if tp:
+            reduce.begin_step()
         for c, x in zip(calls, dev_x):
-            y = scheme.apply(c["layer"], x)
+            y = tp_apply(c, x, tp)
             if tp and c["row_parallel"]:
-                dist.all_reduce(y)
+                y = reduce(y)
             outs.append(y)
         host_out.copy_(torch.cat([y.reshape(-1) for y in outs]), non_blocking=True)
 
@@ -998,8 +1065,8 @@ def measure_e2e(calls, args, device, world, tp: bool = False) -> dict:
             "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * d2h, "ms_per_step": ms / args.steps,
             "transfers_per_step": {"h2d": 1, "d2h": 1},
             "path": "hif8_b200.scheme.apply (eager PyTorch ops -> C ABI), pinned host buffers, outputs gathered on "
-                    "the device and read back in one transfer" + (", tensor-parallel shards + NCCL all-reduce"
-                                                                  if tp else "")}
+                    "the device and read back in one transfer" + (f", tensor-parallel shards + {reduce.kind} "
+                                                                  "all-reduce" if tp else "")}
 
 
 def run_profile_case(spec: str, launches: int) -> None:
@@ -1014,6 +1081,70 @@ def run_profile_case(spec: str, launches: int) -> None:
     from hif8_b200 import native, scheme
 
     parts = spec.split(":")
+    if parts[0] == "decode-tp" and len(parts) == 2:
+        # one CUDA-graph decode step of the configs[4] model tensor-parallel
+        # over the torchrun ranks, kernels recorded by torch.profiler (CUPTI)
+        # on rank 0; prints the kernel time per name (device time, the step
+        # replayed as in the bench)
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        from hif8_b200.decoder import Decoder, DecoderConfig, calibrate
+
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dev = torch.device("cuda", local)
+        if world > 1:
+            dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        batch = int(parts[1])
+        cfg = DecoderConfig()
+        calib = calibrate(cfg, dev, seed=0, tokens=64, tp_rank=rank, tp_size=world)
+        model = Decoder(cfg, "hif8", dev, seed=0, tp_rank=rank, tp_size=world, max_batch=batch, max_ctx=768,
+                        calibration=calib)
+        if world > 1:
+            model.enable_peer_allreduce()
+        g = torch.Generator(device=dev).manual_seed(1)
+        prompt = torch.randint(0, cfg.vocab, (batch, 512), device=dev, generator=g)
+        graph, tokens, pos = model.decode_graph(batch)
+        with torch.no_grad():
+            tokens.copy_(model.prefill(prompt))
+        pos.fill_(512)
+        for _ in range(5):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            graph.replay()
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        if rank == 0:
+            rows = {}
+            for ev in prof.events():
+                if ev.device_type == torch.autograd.DeviceType.CUDA and ev.device_time > 0:
+                    r = rows.setdefault(ev.name[:60], [0, 0.0])
+                    r[0] += 1
+                    r[1] += ev.device_time
+            total = sum(v[1] for v in rows.values())
+            print(f"decode step, batch {batch}, tp {world}: {sum(v[0] for v in rows.values())} launches, "
+                  f"{total:.1f} us of kernel time (rank 0, torch.profiler)")
+            for name, (n, t) in sorted(rows.items(), key=lambda kv: -kv[1][1]):
+                print(f"{name:60s} {n:6d} {t:10.1f} {100 * t / total:6.1f}%")
+        model.release_graphs()
+        if model.peer is not None:
+            model.peer.check()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            model.peer.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
     if parts[0] == "decode" and len(parts) == 2:
         # one eager decode step of the configs[4] model at batch B between
         # cudaProfilerStart/Stop (for `ncu --profile-from-start off`)
@@ -1125,6 +1256,8 @@ def main() -> None:
     parser.add_argument("--profile-case", default=None,
                         help="run one small kernel case for ncu (e.g. gemv:gate_up:1) and exit")
     parser.add_argument("--profile-launches", type=int, default=3)
+    parser.add_argument("--tp-allreduce", choices=("peer", "nccl"), default="peer",
+                        help="all-reduce of the tensor-parallel sweep's row-parallel calls (N > 1)")
     args = parser.parse_args()
     if args.profile_case:
         run_profile_case(args.profile_case, args.profile_launches)

@@ -322,7 +322,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (!mbar_wait(accum_full, 0, abort)) atomicAdd(p.err, 1);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    uint16_t *stage_out = reinterpret_cast<uint16_t *>(b_stages);  // [BN][128]
+    // [BN][128] output values; an FP32 tile (BN x 512 bytes) fills the
+    // activation ring exactly (kTcStages x BN x 128 bytes)
+    static_assert(kTcStages * kTcBK * 2 >= kTcBM * 4, "the FP32 output tile fits the activation ring");
+    uint16_t *stage_out = reinterpret_cast<uint16_t *>(b_stages);
+    float *stage_out32 = reinterpret_cast<float *>(b_stages);
 #pragma unroll
     for (int c = 0; c < kChunks; ++c) {
       uint32_t acc[32];
@@ -334,7 +338,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         float val = __uint_as_float(acc[q]) * cs;
         val = val * ts;
         val += bias;
-        stage_out[(c0 + c * 32 + q) * kTcBM + row] = (uint16_t)to_out_bits<OUT>(val);
+        if constexpr (OUT == HIF8_DTYPE_F32) stage_out32[(c0 + c * 32 + q) * kTcBM + row] = val;
+        else stage_out[(c0 + c * 32 + q) * kTcBM + row] = (uint16_t)to_out_bits<OUT>(val);
       }
     }
     // make the staged tile visible to the TMA engine, then one thread stores it
@@ -488,17 +493,24 @@ int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return HIF8_ERR_CUDA;
   }
-  {  // output [M, N] (BF16 or FP16 bits): 128-channel x BN-token boxes for the TMA store
+  const bool f32 = output_dtype == HIF8_DTYPE_F32;
+  {  // output [M, N] (BF16 / FP16 bits, or FP32 partials): 128-channel x BN-token boxes for the TMA store
     const cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
-    const cuuint64_t strides[1] = {(cuuint64_t)n * 2};
+    const cuuint64_t strides[1] = {(cuuint64_t)n * (f32 ? 4 : 2)};
     const cuuint32_t box[2] = {(cuuint32_t)kTcBM, (cuuint32_t)bn};
-    if (encode(&ymap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, args.out, dims, strides, box, estr,
+    if (encode(&ymap, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, args.out, dims,
+               strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return HIF8_ERR_CUDA;
   }
   TcParams p{args.w, args.ts, args.cs, args.bias, args.out, err, args.m, args.n, args.k, args.bias_dtype, args.ts_stride};
   const bool bf16 = output_dtype == HIF8_DTYPE_BF16;
+  if (f32) {
+    if (bn == 256) return launch_tc<256, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream);
+    if (bn == 128) return launch_tc<128, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream);
+    return launch_tc<64, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream);
+  }
   if (bn == 256)
     return bf16 ? launch_tc<256, HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream)
                 : launch_tc<256, HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream);

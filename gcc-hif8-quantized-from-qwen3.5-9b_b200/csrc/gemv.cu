@@ -155,6 +155,7 @@ __device__ __forceinline__ uint32_t fake_quant_bf16(uint32_t h, float s, float r
 template <int OUT>
 __device__ __forceinline__ void store_out(void *out, int64_t idx, float v) {
   if constexpr (OUT == HIF8_DTYPE_BF16) static_cast<uint16_t *>(out)[idx] = (uint16_t)f32_to_bf16_bits(v);
+  else if constexpr (OUT == HIF8_DTYPE_F32) static_cast<float *>(out)[idx] = v;  // TP partial products
   else static_cast<uint16_t *>(out)[idx] = (uint16_t)f32_to_f16_bits(v);
 }
 
@@ -809,60 +810,63 @@ static int launch_generic(const GemvArgs &args, cudaStream_t stream) {
 
 // y = a @ w^T for any m: the persistent split-K kernel on 16-token slices
 // when the shape allows it, otherwise the generic kernel.
-int run_linear(GemvArgs args, int output_dtype, cudaStream_t stream) {
+template <int OUT>
+static int run_linear_out(GemvArgs args, cudaStream_t stream) {
   // 16-byte activation loads, 32-byte weight loads (k % 256 == 0 keeps every
   // row segment aligned)
   const bool vec_ok = aligned16(args.a) && aligned32(args.w) && args.k % 64 == 0;
-  const bool bf16_out = output_dtype == HIF8_DTYPE_BF16;
+  constexpr int64_t out_bytes = OUT == HIF8_DTYPE_F32 ? 4 : 2;
   for (int m0 = 0; m0 < args.m; m0 += 16) {
     GemvArgs s = args;
     s.m = min(16, args.m - m0);
     s.a = static_cast<const uint8_t *>(args.a) + (int64_t)m0 * args.k;
     s.ts = args.ts + m0;
-    s.out = static_cast<uint8_t *>(args.out) + (int64_t)m0 * args.n * 2;
-    const void *kptr = s.m > 8 ? (bf16_out ? gemv_kernel_ptr<2, HIF8_DTYPE_BF16, kActCodes>()
-                                           : gemv_kernel_ptr<2, HIF8_DTYPE_F16, kActCodes>())
-                               : (bf16_out ? gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActCodes>()
-                                           : gemv_kernel_ptr<1, HIF8_DTYPE_F16, kActCodes>());
+    s.out = static_cast<uint8_t *>(args.out) + (int64_t)m0 * args.n * out_bytes;
+    const void *kptr = s.m > 8 ? gemv_kernel_ptr<2, OUT, kActCodes>() : gemv_kernel_ptr<1, OUT, kActCodes>();
     const GemvPlan plan = vec_ok ? plan_gemv_cached(s.m, s.n, s.k, kptr) : GemvPlan{};
     int status;
-    if (plan.s == 0) {
-      status = bf16_out ? launch_generic<HIF8_DTYPE_BF16, kActCodes>(s, stream)
-                        : launch_generic<HIF8_DTYPE_F16, kActCodes>(s, stream);
-    } else if (plan.nt == 1) {
-      status = bf16_out ? launch_gemv<1, HIF8_DTYPE_BF16, kActCodes>(s, plan, stream)
-                        : launch_gemv<1, HIF8_DTYPE_F16, kActCodes>(s, plan, stream);
-    } else {
-      status = bf16_out ? launch_gemv<2, HIF8_DTYPE_BF16, kActCodes>(s, plan, stream)
-                        : launch_gemv<2, HIF8_DTYPE_F16, kActCodes>(s, plan, stream);
-    }
+    if (plan.s == 0) status = launch_generic<OUT, kActCodes>(s, stream);
+    else if (plan.nt == 1) status = launch_gemv<1, OUT, kActCodes>(s, plan, stream);
+    else status = launch_gemv<2, OUT, kActCodes>(s, plan, stream);
     if (status != HIF8_OK) return status;
   }
   return HIF8_OK;
 }
 
-// Fused static quant + linear for m <= 8 rows of FP16/BF16 activations.
-int run_fused_linear(const GemvArgs &args, int x_dtype, int output_dtype, cudaStream_t stream) {
-  const bool bf16_out = output_dtype == HIF8_DTYPE_BF16;
-  const bool bf16_in = x_dtype == HIF8_DTYPE_BF16;
-  const bool vec_ok = aligned16(args.a) && aligned32(args.w) && args.k % 64 == 0 && args.m <= 8;
-  const void *kptr = bf16_in ? (bf16_out ? gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActBf16>()
-                                         : gemv_kernel_ptr<1, HIF8_DTYPE_F16, kActBf16>())
-                             : (bf16_out ? gemv_kernel_ptr<1, HIF8_DTYPE_BF16, kActF16>()
-                                         : gemv_kernel_ptr<1, HIF8_DTYPE_F16, kActF16>());
-  const GemvPlan plan = vec_ok ? plan_gemv_cached(args.m, args.n, args.k, kptr) : GemvPlan{};
-  if (plan.s == 0) {
-    if (bf16_in)
-      return bf16_out ? launch_generic<HIF8_DTYPE_BF16, kActBf16>(args, stream)
-                      : launch_generic<HIF8_DTYPE_F16, kActBf16>(args, stream);
-    return bf16_out ? launch_generic<HIF8_DTYPE_BF16, kActF16>(args, stream)
-                    : launch_generic<HIF8_DTYPE_F16, kActF16>(args, stream);
+int run_linear(GemvArgs args, int output_dtype, cudaStream_t stream) {
+  switch (output_dtype) {
+    case HIF8_DTYPE_BF16: return run_linear_out<HIF8_DTYPE_BF16>(args, stream);
+    case HIF8_DTYPE_F16: return run_linear_out<HIF8_DTYPE_F16>(args, stream);
+    case HIF8_DTYPE_F32: return run_linear_out<HIF8_DTYPE_F32>(args, stream);
+    default: return HIF8_ERR_INVALID_ARGUMENT;
   }
-  if (bf16_in)
-    return bf16_out ? launch_gemv<1, HIF8_DTYPE_BF16, kActBf16>(args, plan, stream)
-                    : launch_gemv<1, HIF8_DTYPE_F16, kActBf16>(args, plan, stream);
-  return bf16_out ? launch_gemv<1, HIF8_DTYPE_BF16, kActF16>(args, plan, stream)
-                  : launch_gemv<1, HIF8_DTYPE_F16, kActF16>(args, plan, stream);
+}
+
+// Fused static quant + linear for m <= 8 rows of FP16/BF16 activations.
+template <int OUT, int ASRC>
+static int run_fused_linear_out(const GemvArgs &args, cudaStream_t stream) {
+  const bool vec_ok = aligned16(args.a) && aligned32(args.w) && args.k % 64 == 0 && args.m <= 8;
+  const GemvPlan plan = vec_ok ? plan_gemv_cached(args.m, args.n, args.k, gemv_kernel_ptr<1, OUT, ASRC>())
+                               : GemvPlan{};
+  if (plan.s == 0) return launch_generic<OUT, ASRC>(args, stream);
+  return launch_gemv<1, OUT, ASRC>(args, plan, stream);
+}
+
+int run_fused_linear(const GemvArgs &args, int x_dtype, int output_dtype, cudaStream_t stream) {
+  const bool bf16_in = x_dtype == HIF8_DTYPE_BF16;
+  switch (output_dtype) {
+    case HIF8_DTYPE_BF16:
+      return bf16_in ? run_fused_linear_out<HIF8_DTYPE_BF16, kActBf16>(args, stream)
+                     : run_fused_linear_out<HIF8_DTYPE_BF16, kActF16>(args, stream);
+    case HIF8_DTYPE_F16:
+      return bf16_in ? run_fused_linear_out<HIF8_DTYPE_F16, kActBf16>(args, stream)
+                     : run_fused_linear_out<HIF8_DTYPE_F16, kActF16>(args, stream);
+    case HIF8_DTYPE_F32:
+      return bf16_in ? run_fused_linear_out<HIF8_DTYPE_F32, kActBf16>(args, stream)
+                     : run_fused_linear_out<HIF8_DTYPE_F32, kActF16>(args, stream);
+    default:
+      return HIF8_ERR_INVALID_ARGUMENT;
+  }
 }
 
 // Glue + static quant + linear for m <= 8 BF16 rows (decode steps of the
@@ -972,4 +976,34 @@ extern "C" int hif8_model_glue_linear(const uint16_t *x, const Hif8GlueArgs *glu
   args.glue.eps = glue->eps;
   args.glue.one_plus = glue->one_plus;
   return run_glue_linear(args, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hif8_linear_partial_f32(const uint8_t *activation, const uint8_t *weight, const float *token_scale,
+                                       const float *channel_scale, int64_t m, int64_t n, int64_t k, float *out,
+                                       void *workspace, size_t workspace_bytes, void *stream) {
+  int status = validate_linear(activation, weight, token_scale, channel_scale, nullptr, HIF8_DTYPE_NONE,
+                               HIF8_DTYPE_BF16, m, n, k, out);
+  if (status != HIF8_OK) return status;
+  GemvArgs args{activation, weight, token_scale, channel_scale, nullptr, out, (int)m, (int)n, (int)k, 0,
+                HIF8_DTYPE_NONE, 1};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (hif8_gemm_tc_supported(m, n, k) && aligned16(activation) && aligned16(weight) && aligned16(out)) {
+    if (workspace_bytes < hif8_gemm_tc_workspace(m, n, k) || (!workspace && hif8_gemm_tc_workspace(m, n, k)))
+      return HIF8_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return HIF8_ERR_WORKSPACE;
+    return hif8_gemm_tc(args, HIF8_DTYPE_F32, workspace, workspace_bytes, s);
+  }
+  return run_linear(args, HIF8_DTYPE_F32, s);
+}
+
+extern "C" int hif8_static_fused_linear_partial_f32(const void *x, int x_dtype, const uint8_t *weight,
+                                                    const float *fixed_scale, const float *channel_scale, int64_t m,
+                                                    int64_t n, int64_t k, float *out, void *stream) {
+  int status = validate_linear(x, weight, fixed_scale, channel_scale, nullptr, HIF8_DTYPE_NONE, HIF8_DTYPE_BF16, m,
+                               n, k, out);
+  if (status != HIF8_OK) return status;
+  if (m > 8) return HIF8_ERR_INVALID_ARGUMENT;
+  if (x_dtype != HIF8_DTYPE_F16 && x_dtype != HIF8_DTYPE_BF16) return HIF8_ERR_INVALID_ARGUMENT;
+  GemvArgs args{x, weight, fixed_scale, channel_scale, nullptr, out, (int)m, (int)n, (int)k, 0, HIF8_DTYPE_NONE, 0};
+  return run_fused_linear(args, x_dtype, HIF8_DTYPE_F32, static_cast<cudaStream_t>(stream));
 }

@@ -307,25 +307,65 @@ __device__ __forceinline__ uint64_t gtimer_ns() {
   return t;
 }
 
+// Bytes of one rank's peer buffer: two slots of `world` partials
+// (max_rows x dim FP32 each, one per source rank), then `world` flags.
+__host__ __device__ inline size_t peer_part_bytes(int64_t max_rows, int64_t dim) {
+  return (size_t)max_rows * dim * sizeof(float);
+}
+
+// Push all-reduce of one decode step's row-parallel FP32 partials, optionally
+// fused with the following residual add + RMSNorm (weight != null).  One CTA
+// per rank (decode sizes: rows x dim <= 4 x 1024 x 8 values):
+//   1. this rank's partial is stored into slot [rank] of every rank's buffer
+//      (its own first, then the peers after it in rank order) -- one-way
+//      NVLink stores, no remote read on the critical path;
+//   2. a system-scope fence, then epoch into flag[rank] of every rank's
+//      buffer (st.release.sys), and a bounded wait on this rank's own flags;
+//   3. the `world` partials are summed in FP32 from local memory in rank
+//      order, the same order on every rank, so every rank computes identical
+//      bits, and the sum is rounded to BF16 once -- as the unsharded
+//      projection rounds its FP32 accumulator once.
+// The CTA signals its dependents as soon as its inputs are visible: the
+// following linear's CTAs launch on the SMs this single CTA leaves idle and
+// build their tables while the exchange runs.
 __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_rmsnorm_kernel(const Hif8PeerArgs p) {
   pdl_wait();  // inputs come from the previous kernel of the stream
+  pdl_launch_dependents();
   __shared__ float rowsum[8];
   const int tid = threadIdx.x;
   const int64_t n = p.rows * p.dim;
-  const size_t slot_bytes = (size_t)p.max_rows * p.dim * sizeof(uint16_t);
+  const size_t part_bytes = peer_part_bytes(p.max_rows, p.dim);
+  const size_t slot_bytes = (size_t)p.world * part_bytes;
   const size_t flags_off = 2 * slot_bytes;
   if (tid < 8) rowsum[tid] = 0.f;
-  // 1. this rank's partial into its own slot, visible system-wide
-  uint16_t *mine = reinterpret_cast<uint16_t *>(p.peer_buf[p.rank] + (size_t)p.slot * slot_bytes);
-  for (int64_t i = (int64_t)tid * 8; i < n; i += kPeerThreads * 8)
-    *reinterpret_cast<uint4 *>(mine + i) = *reinterpret_cast<const uint4 *>(p.local + i);
+  constexpr int kMaxChunks = 4;  // with the norm: rows x dim <= 4 x 1024 x 8
+  // 1. push: every 8-value chunk of the partial to every rank's buffer
+  for (int64_t i = (int64_t)tid * 8; i < n; i += (int64_t)kPeerThreads * 8) {
+    uint4 x0, x1;
+    if (p.local_dtype == HIF8_DTYPE_F32) {
+      x0 = *reinterpret_cast<const uint4 *>(static_cast<const float *>(p.local) + i);
+      x1 = *reinterpret_cast<const uint4 *>(static_cast<const float *>(p.local) + i + 4);
+    } else {  // BF16 partial: widened exactly
+      const uint4 h = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p.local) + i);
+      x0 = make_uint4(h.x << 16, h.x & 0xFFFF0000u, h.y << 16, h.y & 0xFFFF0000u);
+      x1 = make_uint4(h.z << 16, h.z & 0xFFFF0000u, h.w << 16, h.w & 0xFFFF0000u);
+    }
+    for (int d = 0; d < p.world; ++d) {
+      const int q = (p.rank + d) % p.world;
+      float *dst = reinterpret_cast<float *>(p.peer_buf[q] + (size_t)p.slot * slot_bytes + (size_t)p.rank * part_bytes);
+      *reinterpret_cast<uint4 *>(dst + i) = x0;
+      *reinterpret_cast<uint4 *>(dst + i + 4) = x1;
+    }
+  }
   __threadfence_system();
   __syncthreads();
-  // 2. signal every rank, wait for every rank
+  // 2. signal every rank, wait for every rank (bounded)
   if (tid == 0) {
     const uint32_t epoch = *p.epoch_counter + 1;
-    for (int q = 0; q < p.world; ++q)
+    for (int d = 0; d < p.world; ++d) {
+      const int q = (p.rank + d) % p.world;
       st_release_sys(reinterpret_cast<uint32_t *>(p.peer_buf[q] + flags_off) + p.rank, epoch);
+    }
     const uint32_t *flags = reinterpret_cast<const uint32_t *>(p.peer_buf[p.rank] + flags_off);
     const uint64_t t0 = gtimer_ns();
     bool ok = true;
@@ -341,8 +381,33 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_rmsnorm_kernel(co
     *p.epoch_counter = epoch;
   }
   __syncthreads();
-  // 3. sum in rank order, residual, RMSNorm (chunks of 8 never straddle rows: dim % 256 == 0)
-  constexpr int kMaxChunks = 4;  // rows x dim <= 4 x 1024 x 8
+  // 3. sum in rank order from local memory, then (optional) residual + RMSNorm
+  const uint8_t *own = p.peer_buf[p.rank] + (size_t)p.slot * slot_bytes;
+  const bool norm = p.weight != nullptr;
+  // rank q's FP32 values i .. i + 7, written by the peers over NVLink: read
+  // past L1, summed in rank order
+  auto sum8 = [&](int64_t i, float (&acc)[8]) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int q = 0; q < p.world; ++q) {
+      const float *src = reinterpret_cast<const float *>(own + (size_t)q * part_bytes) + i;
+      const float4 a = __ldcv(reinterpret_cast<const float4 *>(src));
+      const float4 b = __ldcv(reinterpret_cast<const float4 *>(src + 4));
+      acc[0] += a.x, acc[1] += a.y, acc[2] += a.z, acc[3] += a.w;
+      acc[4] += b.x, acc[5] += b.y, acc[6] += b.z, acc[7] += b.w;
+    }
+  };
+  if (!norm) {  // the sum alone: stream the chunks
+    for (int64_t i = (int64_t)tid * 8; i < n; i += (int64_t)kPeerThreads * 8) {
+      float acc[8];
+      sum8(i, acc);
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = to_bf(acc[2 * e]) | ((uint32_t)to_bf(acc[2 * e + 1]) << 16);
+      *reinterpret_cast<uint4 *>(p.out + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    return;
+  }
   float v[kMaxChunks][8];
   int row_of[kMaxChunks];
 #pragma unroll
@@ -350,17 +415,8 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_rmsnorm_kernel(co
     const int64_t i = ((int64_t)tid + (int64_t)c * kPeerThreads) * 8;
     row_of[c] = -1;
     if (i >= n) continue;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int q = 0; q < p.world; ++q) {
-      const uint16_t *src = reinterpret_cast<const uint16_t *>(p.peer_buf[q] + (size_t)p.slot * slot_bytes) + i;
-      const uint4 w = __ldcv(reinterpret_cast<const uint4 *>(src));
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        acc[2 * e] += bf(ww[e] & 0xFFFFu);
-        acc[2 * e + 1] += bf(ww[e] >> 16);
-      }
-    }
+    float acc[8];
+    sum8(i, acc);
     uint32_t rr[4] = {0, 0, 0, 0};
     if (p.residual) {
       const uint4 r = *reinterpret_cast<const uint4 *>(p.residual + i);
@@ -370,7 +426,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_rmsnorm_kernel(co
     float ss = 0.f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float lo = bf(to_bf(acc[2 * e])), hi = bf(to_bf(acc[2 * e + 1]));  // the all-reduced BF16 partial
+      float lo = bf(to_bf(acc[2 * e])), hi = bf(to_bf(acc[2 * e + 1]));  // the all-reduced sum, one BF16 rounding
       if (p.residual) {
         lo = bf(to_bf(lo + bf(rr[e] & 0xFFFFu)));
         hi = bf(to_bf(hi + bf(rr[e] >> 16)));
@@ -414,13 +470,24 @@ using namespace hif8;
 extern "C" int hif8_model_peer_allreduce_rmsnorm(const Hif8PeerArgs *args, void *stream) {
   if (!args) return HIF8_ERR_INVALID_ARGUMENT;
   const Hif8PeerArgs &p = *args;
-  if (!p.local || !p.weight || !p.out || !p.residual_out || !p.peer_buf || !p.epoch_counter || !p.error ||
+  // weight == NULL: the sum only (out = all-reduced partials; residual and
+  // residual_out unused)
+  if (!p.local || !p.out || (p.weight && !p.residual_out) || !p.peer_buf || !p.epoch_counter || !p.error ||
       p.world < 1 || p.world > 64 || p.rank < 0 || p.rank >= p.world || p.slot < 0 || p.slot > 1 || p.rows < 0 ||
-      p.rows > p.max_rows || p.dim <= 0 || p.dim % 256 != 0 || p.rows * p.dim > (int64_t)kPeerThreads * 8 * 4 ||
-      p.rows > 8)
+      p.rows > p.max_rows || p.dim <= 0 || p.dim % 256 != 0 ||
+      (p.local_dtype != HIF8_DTYPE_F32 && p.local_dtype != HIF8_DTYPE_BF16))
     return HIF8_ERR_INVALID_ARGUMENT;
+  // the fused norm keeps each thread's values in registers: rows x dim <=
+  // 4 x 8 x threads, at most 8 rows
+  if (p.weight && (p.rows * p.dim > (int64_t)kPeerThreads * 8 * 4 || p.rows > 8)) return HIF8_ERR_INVALID_ARGUMENT;
   if (p.rows == 0) return HIF8_OK;
   return launch_pdl(peer_allreduce_rmsnorm_kernel, dim3(1), dim3(kPeerThreads), 0, static_cast<cudaStream_t>(stream), p);
+}
+
+extern "C" size_t hif8_peer_buffer_bytes(int64_t world, int64_t max_rows, int64_t dim) {
+  if (world < 1 || max_rows < 1 || dim < 1) return 0;
+  const size_t bytes = 2 * (size_t)world * peer_part_bytes(max_rows, dim) + (size_t)world * sizeof(uint32_t);
+  return (bytes + 255) / 256 * 256;
 }
 
 extern "C" int hif8_peer_alloc(size_t bytes, void **ptr, void *handle64) {

@@ -528,13 +528,64 @@ at::Tensor ModelGdn(const at::Tensor &proj, int64_t T, int64_t hk, int64_t hv, c
   return out;
 }
 
+// Tensor-parallel partial product of a row-parallel static linear: x
+// (FP16/BF16 [M, K], this rank's input columns) statically quantised with
+// input_scale, times this rank's weight columns, as FP32 [M, N] without
+// rounding (the ranks' partials are summed before the one BF16 rounding).
+// M <= 8: one fused quant + GEMV launch; larger M: static quant, then the
+// GEMV / tcgen05 GEMM with FP32 output.
+at::Tensor Hif8LinearPartialF32(const at::Tensor &x_in, const at::Tensor &weight_in, const at::Tensor &input_scale_in,
+                                const at::Tensor &weight_scale_in) {
+  // an internal operator: any CUDA layout is accepted and made contiguous
+  // (the kernels pick their vector paths by alignment)
+  for (const at::Tensor *t : {&x_in, &weight_in, &input_scale_in, &weight_scale_in})
+    TORCH_CHECK(t->defined() && t->is_cuda(), "linear_partial_f32 operands must be CUDA tensors");
+  const at::Tensor x = x_in.contiguous(), weight = weight_in.contiguous();
+  const at::Tensor input_scale = input_scale_in.contiguous(), weight_scale = weight_scale_in.contiguous();
+  TORCH_CHECK(x.scalar_type() == at::ScalarType::Half || x.scalar_type() == at::ScalarType::BFloat16,
+              "x must have dtype torch.float16 or torch.bfloat16");
+  TORCH_CHECK(weight.scalar_type() == at::ScalarType::Byte && weight.dim() == 2, "weight must be uint8 [N, K]");
+  TORCH_CHECK(input_scale.scalar_type() == at::ScalarType::Float && input_scale.numel() == 1,
+              "input_scale must be one float32 value");
+  TORCH_CHECK(weight_scale.scalar_type() == at::ScalarType::Float && weight_scale.numel() == weight.size(0),
+              "weight_scale must contain one float32 value per output channel");
+  TORCH_CHECK(x.size(-1) == weight.size(1), "x and weight K dimensions differ");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t k = x.size(-1), m = x.numel() / k, n = weight.size(0);
+  auto out = at::empty({m, n}, x.options().dtype(at::kFloat));
+  if (m == 0) return out;
+  const int x_dtype = DtypeCode(x.scalar_type());
+  if (m <= 8) {
+    CheckStatus(hif8_static_fused_linear_partial_f32(x.data_ptr(), x_dtype, weight.data_ptr<uint8_t>(),
+                                                     input_scale.data_ptr<float>(), weight_scale.data_ptr<float>(), m,
+                                                     n, k, out.data_ptr<float>(), Stream(x)),
+                "hif8_static_fused_linear_partial_f32");
+    return out;
+  }
+  auto data = at::empty({m, k}, x.options().dtype(at::kByte));
+  auto row_scale = at::empty({m}, x.options().dtype(at::kFloat));
+  CheckStatus(hif8_static_quant(x.data_ptr(), x_dtype, m, k, input_scale.data_ptr<float>(), 1,
+                                data.data_ptr<uint8_t>(), row_scale.data_ptr<float>(), Stream(x)),
+              "hif8_static_quant");
+  const size_t ws_bytes = soft_hif8_gemm_workspace_size(m, n, k);
+  at::Tensor ws;
+  if (ws_bytes) ws = at::empty({(int64_t)ws_bytes}, x.options().dtype(at::kByte));
+  CheckStatus(hif8_linear_partial_f32(data.data_ptr<uint8_t>(), weight.data_ptr<uint8_t>(),
+                                      row_scale.data_ptr<float>(), weight_scale.data_ptr<float>(), m, n, k,
+                                      out.data_ptr<float>(), ws_bytes ? ws.data_ptr() : nullptr, ws_bytes, Stream(x)),
+              "hif8_linear_partial_f32");
+  return out;
+}
+
 std::tuple<at::Tensor, at::Tensor> ModelPeerAllreduceRmsnorm(const at::Tensor &local,
                                                              const std::optional<at::Tensor> &residual,
                                                              const at::Tensor &weight, const at::Tensor &peer_buf,
                                                              at::Tensor &counter, at::Tensor &error, int64_t max_rows,
                                                              int64_t rank, int64_t world, int64_t slot, double eps,
                                                              bool one_plus, int64_t timeout_ns) {
-  CheckModelTensor(local, "local", at::kBFloat16);
+  TORCH_CHECK(local.scalar_type() == at::kFloat || local.scalar_type() == at::kBFloat16,
+              "local must be a float32 or bfloat16 partial");
+  CheckModelTensor(local, "local", local.scalar_type());
   CheckModelTensor(weight, "weight", at::kBFloat16);
   CheckModelTensor(peer_buf, "peer_buf", at::kLong);
   CheckModelTensor(counter, "counter", at::kInt, 4);
@@ -542,10 +593,11 @@ std::tuple<at::Tensor, at::Tensor> ModelPeerAllreduceRmsnorm(const at::Tensor &l
   TORCH_CHECK(peer_buf.numel() == world, "peer_buf must hold one buffer per rank");
   const int64_t dim = local.size(-1), rows = local.numel() / dim;
   c10::cuda::CUDAGuard guard(local.device());
-  auto out = at::empty_like(local);
-  auto res_out = at::empty_like(local);
+  auto out = at::empty(local.sizes(), local.options().dtype(at::kBFloat16));
+  auto res_out = at::empty(local.sizes(), local.options().dtype(at::kBFloat16));
   Hif8PeerArgs a{};
-  a.local = Bits(local);
+  a.local = local.data_ptr();
+  a.local_dtype = local.scalar_type() == at::kFloat ? HIF8_DTYPE_F32 : HIF8_DTYPE_BF16;
   if (residual.has_value()) {
     CheckModelTensor(*residual, "residual", at::kBFloat16);
     TORCH_CHECK(residual->sizes() == local.sizes(), "residual must match local");
@@ -568,6 +620,39 @@ std::tuple<at::Tensor, at::Tensor> ModelPeerAllreduceRmsnorm(const at::Tensor &l
   a.timeout_ns = (uint64_t)timeout_ns;
   CheckStatus(hif8_model_peer_allreduce_rmsnorm(&a, Stream(local)), "hif8_model_peer_allreduce_rmsnorm");
   return {out, res_out};
+}
+
+// The all-reduced sum of the ranks' partials (no norm): the same push
+// exchange with a null weight.
+at::Tensor ModelPeerAllreduce(const at::Tensor &local, const at::Tensor &peer_buf, at::Tensor &counter,
+                              at::Tensor &error, int64_t max_rows, int64_t rank, int64_t world, int64_t slot,
+                              int64_t timeout_ns) {
+  TORCH_CHECK(local.scalar_type() == at::kFloat || local.scalar_type() == at::kBFloat16,
+              "local must be a float32 or bfloat16 partial");
+  CheckModelTensor(local, "local", local.scalar_type());
+  CheckModelTensor(peer_buf, "peer_buf", at::kLong);
+  CheckModelTensor(counter, "counter", at::kInt, 4);
+  CheckModelTensor(error, "error", at::kInt, 4);
+  TORCH_CHECK(peer_buf.numel() == world, "peer_buf must hold one buffer per rank");
+  const int64_t dim = local.size(-1), rows = local.numel() / dim;
+  c10::cuda::CUDAGuard guard(local.device());
+  auto out = at::empty(local.sizes(), local.options().dtype(at::kBFloat16));
+  Hif8PeerArgs a{};
+  a.local = local.data_ptr();
+  a.local_dtype = local.scalar_type() == at::kFloat ? HIF8_DTYPE_F32 : HIF8_DTYPE_BF16;
+  a.out = MutBits(out);
+  a.peer_buf = reinterpret_cast<uint8_t *const *>(peer_buf.data_ptr<int64_t>());
+  a.epoch_counter = reinterpret_cast<uint32_t *>(counter.data_ptr<int32_t>());
+  a.error = error.data_ptr<int32_t>();
+  a.rows = rows;
+  a.dim = dim;
+  a.max_rows = max_rows;
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.slot = (int)slot;
+  a.timeout_ns = (uint64_t)timeout_ns;
+  CheckStatus(hif8_model_peer_allreduce_rmsnorm(&a, Stream(local)), "hif8_model_peer_allreduce_rmsnorm");
+  return out;
 }
 
 at::Tensor Hif8KvGatherDecode(const at::Tensor &cache, const at::Tensor &block_tables, const at::Tensor &seq_lens,
@@ -659,6 +744,9 @@ TORCH_LIBRARY(hif8_b200, m) {
   m.def("peer_allreduce_rmsnorm(Tensor local, Tensor? residual, Tensor weight, Tensor peer_buf, Tensor(a!) counter, "
         "Tensor(b!) error, int max_rows, int rank, int world, int slot, float eps, bool one_plus, int timeout_ns) "
         "-> (Tensor, Tensor)");
+  m.def("peer_allreduce(Tensor local, Tensor peer_buf, Tensor(a!) counter, Tensor(b!) error, int max_rows, int rank, "
+        "int world, int slot, int timeout_ns) -> Tensor");
+  m.def("linear_partial_f32(Tensor x, Tensor weight, Tensor input_scale, Tensor weight_scale) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(hif8_b200, CUDA, m) {
@@ -673,4 +761,6 @@ TORCH_LIBRARY_IMPL(hif8_b200, CUDA, m) {
   m.impl("attn_prep", &ModelAttnPrep);
   m.impl("gdn", &ModelGdn);
   m.impl("peer_allreduce_rmsnorm", &ModelPeerAllreduceRmsnorm);
+  m.impl("peer_allreduce", &ModelPeerAllreduce);
+  m.impl("linear_partial_f32", &Hif8LinearPartialF32);
 }

@@ -119,14 +119,34 @@ class _Linear:
 
         return scheme.apply(self, x)
 
+    def partial(self, x):
+        """This rank's partial product of a row-parallel projection, before
+        the all-reduce: FP32 for the HiF8 layer (summed over the ranks
+        before its one BF16 rounding, so the sum equals the unsharded
+        projection up to the FP32 summation order), the BF16 product for the
+        twin (cuBLAS)."""
+        import torch
+
+        if self.mode == "bf16":
+            return torch.nn.functional.linear(x, self.weight)
+        from . import scheme
+
+        scale = self.input_scale
+        factor = scheme.static_scale_factor()
+        if factor != 1.0:
+            scale = scale * factor
+        return torch.ops.hif8_b200.linear_partial_f32(x.reshape(-1, x.shape[-1]).contiguous(), self.weight, scale,
+                                                      self.weight_scale)
+
 
 class PeerReducer:
     """Tensor-parallel all-reduce of a decode step's row-parallel partials,
     fused with the residual add + RMSNorm that follows every one of them
-    (``torch.ops.hif8_b200.peer_allreduce_rmsnorm``): each rank's buffer is
-    mapped by its peers over NVLink through exchanged CUDA IPC handles; the
-    kernel signals and waits on epoch flags (bounded) and sums the partials
-    in rank order."""
+    (``torch.ops.hif8_b200.peer_allreduce_rmsnorm``) or alone (``sum``):
+    each rank's buffer is mapped by its peers over NVLink through exchanged
+    CUDA IPC handles; every rank pushes its partial into every rank's
+    buffer, signals and waits on epoch flags (bounded) and sums the partials
+    in rank order from its own memory."""
 
     def __init__(self, device, rank: int, world: int, max_rows: int, dim: int, group=None,
                  timeout_ns: int = 200_000_000):
@@ -144,9 +164,11 @@ class PeerReducer:
         lib.hif8_peer_open.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
         lib.hif8_peer_close.restype = ctypes.c_int
         lib.hif8_peer_close.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        lib.hif8_peer_buffer_bytes.restype = ctypes.c_size_t
+        lib.hif8_peer_buffer_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]
         self._lib = lib
         self.rank, self.world, self.max_rows, self.dim, self.timeout_ns = rank, world, max_rows, dim, timeout_ns
-        nbytes = (2 * max_rows * dim * 2 + 4 * world + 255) // 256 * 256
+        nbytes = lib.hif8_peer_buffer_bytes(world, max_rows, dim)
         torch.cuda.set_device(device)
         own = ctypes.c_void_p()
         handle = (ctypes.c_ubyte * 64)()
@@ -175,6 +197,13 @@ class PeerReducer:
         return torch.ops.hif8_b200.peer_allreduce_rmsnorm(local.contiguous(), residual, weight, self.table,
                                                           self.counter, self.error, self.max_rows, self.rank,
                                                           self.world, slot, eps, True, self.timeout_ns)
+
+    def sum(self, local, slot: int):
+        """The all-reduced sum of every rank's ``local`` (BF16 rows x dim)."""
+        import torch
+
+        return torch.ops.hif8_b200.peer_allreduce(local.contiguous(), self.table, self.counter, self.error,
+                                                  self.max_rows, self.rank, self.world, slot, self.timeout_ns)
 
     def check(self):
         if int(self.error.item()) != 0:
@@ -359,13 +388,26 @@ class Decoder:
 
     # --------------------------------------------------------------- blocks --
     def _all_reduce(self, y):
-        """Sum of the row-parallel partials: NCCL, or deferred to the next
-        norm when the step fuses it (returns the partial unchanged then)."""
+        """Sum of the row-parallel partials (BF16 result): NCCL, or deferred
+        to the next norm when the step fuses it (returns the partial
+        unchanged then)."""
         if self.tp > 1 and not self._fused_reduce:
+            import torch
             import torch.distributed as dist
 
             dist.all_reduce(y, group=self.group)
+            if y.dtype != torch.bfloat16:
+                y = y.to(torch.bfloat16)  # the one rounding of the FP32 sum
         return y
+
+    def _row_proj(self, tag, lin, x):
+        """A row-parallel projection (o, out, down): the plain projection on
+        one GPU, this rank's partial product under tensor parallelism."""
+        if self.tp == 1:
+            return self._proj(tag, lin, x)
+        if self.calib_amax is not None:
+            self._record(tag, x)
+        return lin.partial(x)
 
     def _norm(self, x, residual, weight):
         """(1 + w) RMSNorm of x + residual; with a fused reduce x is this
@@ -443,10 +485,10 @@ class Decoder:
                                                                     enable_gqa=True)
             attn = attn.transpose(1, 2).reshape(batch * T, self.heads, c.head_dim)
         attn = attn.reshape(batch * T, -1).contiguous()
-        if self._fuse_glue and "gate_mul" in self.fuse_glue:
+        if self._fuse_glue and "gate_mul" in self.fuse_glue and self.tp == 1:
             return self._all_reduce(self._glue(2, attn, gate, L["o"])[0])
         out = torch.ops.hif8_b200.gate_mul(attn, gate)
-        return self._all_reduce(self._proj(f"{i}.o", L["o"], out))
+        return self._all_reduce(self._row_proj(f"{i}.o", L["o"], out))
 
     def _gdn(self, i, L, proj, batch: int, T: int):
         import torch
@@ -454,15 +496,15 @@ class Decoder:
         core = torch.ops.hif8_b200.gdn(proj, T, self.hk, self.hv, L["conv_w"], L["a_log"], L["dt_bias"],
                                        L["gdn_norm"], self.conv_state[i][:batch], self.rec_state[i][:batch],
                                        self.cfg.eps)
-        return self._all_reduce(self._proj(f"{i}.lin_out", L["lin_out"], core))
+        return self._all_reduce(self._row_proj(f"{i}.lin_out", L["lin_out"], core))
 
     def _mlp(self, i, L, gu):
         import torch
 
-        if self._fuse_glue and "silu_mul" in self.fuse_glue:
+        if self._fuse_glue and "silu_mul" in self.fuse_glue and self.tp == 1:
             return self._all_reduce(self._glue(1, gu, None, L["down"])[0])
         act = torch.ops.hif8_b200.silu_mul(gu)
-        return self._all_reduce(self._proj(f"{i}.down", L["down"], act))
+        return self._all_reduce(self._row_proj(f"{i}.down", L["down"], act))
 
     def forward(self, tokens, positions, batch: int, T: int, seq_lens, slots):
         """tokens / positions [batch * T] (sequence-major) -> logits of each
@@ -638,6 +680,13 @@ def calibrate(cfg: DecoderConfig, device, *, seed: int = 0, tokens: int = 64, tp
     del twin
     if tp_size > 1:  # every rank's samples of a tag -> one pooled sample
         import torch.distributed as dist
+
+        # one weight factor for the whole model: each rank measured it on its
+        # own shard, and ranks quantising with different factors would not sum
+        # to the single-GPU model (rank 0's choice is broadcast)
+        wf = torch.tensor([weight_factor], dtype=torch.float64, device=device)
+        dist.broadcast(wf, src=0, group=group)
+        weight_factor = float(wf.item())
 
         pooled = {}
         for tag in sorted(samples):

@@ -41,6 +41,7 @@ extern "C" {
 #define HIF8_DTYPE_F16 0
 #define HIF8_DTYPE_BF16 1
 #define HIF8_DTYPE_NONE -1 /* "no bias" */
+#define HIF8_DTYPE_F32 2   /* FP32: output of the tensor-parallel partial products only */
 
 /* Human-readable text for a status code. */
 const char *hif8_status_string(int status);
@@ -122,6 +123,29 @@ int soft_hif8_gemm(const uint8_t *activation, const uint8_t *weight, const float
                    const float *channel_scale, const void *bias, int bias_dtype,
                    int output_dtype, int64_t m, int64_t n, int64_t k, void *out,
                    void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---- tensor-parallel partial products ---------------------------------
+ * No counterpart in the reference, which runs a projection on one device.
+ * When a row-parallel projection is split over ranks by its input columns,
+ * every rank's partial product must be summed before it is rounded: these
+ * write the partial y[m, n] = (acc[m, n] * channel_scale[n]) * ts[m] as
+ * FP32 (no bias, no rounding), so the ranks' partials summed in FP32 and
+ * rounded to BF16 once give the unsharded projection's output up to the
+ * order of the FP32 sums (rounding each partial to BF16 first moves
+ * elements by an ulp, and a static HiF8 quantisation downstream turns such
+ * an ulp into a whole code step).
+ * hif8_linear_partial_f32: HiF8 activation bytes + token scales, any m;
+ * workspace as soft_hif8_gemm (soft_hif8_gemm_workspace_size; out 16-byte
+ * aligned for the tcgen05 path).
+ * hif8_static_fused_linear_partial_f32: FP16/BF16 x (x_dtype) statically
+ * quantised with fixed_scale[0] inside the kernel, m <= 8. */
+int hif8_linear_partial_f32(const uint8_t *activation, const uint8_t *weight, const float *token_scale,
+                            const float *channel_scale, int64_t m, int64_t n, int64_t k, float *out,
+                            void *workspace, size_t workspace_bytes, void *stream);
+
+int hif8_static_fused_linear_partial_f32(const void *x, int x_dtype, const uint8_t *weight,
+                                         const float *fixed_scale, const float *channel_scale, int64_t m,
+                                         int64_t n, int64_t k, float *out, void *stream);
 
 /* ---- fused static quant + linear ---------------------------------------
  * Replaces op soft_hif8_static_fused_gemm (csrc/extension/pybind.cpp:13,

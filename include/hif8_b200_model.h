@@ -10,6 +10,16 @@
  *
  * Conventions as include/hif8_b200.h: device pointers, a cudaStream_t passed
  * as void*, an int status.  Activations are BF16 (uint16_t bits).
+ *
+ * Programmatic launch ordering: like the operators of hif8_b200.h, these
+ * kernels are launched with programmatic stream serialization, and some
+ * let the next programmatic launch of the stream begin before they
+ * complete: hif8_model_silu_mul, hif8_model_gate_mul and hif8_model_gdn
+ * when their grid is small (decode batches), and
+ * hif8_model_peer_allreduce_rmsnorm always.  A kernel of the caller that is
+ * itself launched with that attribute right after one of them must wait for
+ * the grid dependency (cudaGridDependencySynchronize / griddepcontrol.wait)
+ * before it reads their outputs; ordinary launches are unaffected.
  */
 #ifndef HIF8_B200_MODEL_H
 #define HIF8_B200_MODEL_H
@@ -100,26 +110,38 @@ int hif8_model_glue_linear(const uint16_t *x, const Hif8GlueArgs *glue, int64_t 
                            const uint8_t *weight, const float *fixed_scale, const float *channel_scale,
                            int64_t n, uint16_t *out, void *stream);
 
-/* ---- tensor-parallel all-reduce fused with residual + RMSNorm ----------
- * Replaces NCCL all-reduce + RMSNorm after every row-parallel projection of
- * a decode step.  Every rank owns one device buffer (hif8_peer_alloc) that
- * its peers map over NVLink (hif8_peer_open of the exchanged 64-byte IPC
- * handle).  Layout of a rank's buffer: two slots of max_rows x dim BF16
- * partials, then world uint32 flags.  One launch per rank:
- *   1. copies this rank's partial `local` (rows x dim) into its slot;
+/* ---- tensor-parallel all-reduce (fused with residual + RMSNorm) ---------
+ * Replaces NCCL all-reduce (+ RMSNorm) after every row-parallel projection
+ * of a decode step.  Every rank owns one device buffer (hif8_peer_alloc) of
+ * hif8_peer_buffer_bytes(world, max_rows, dim) bytes that its peers map over
+ * NVLink (hif8_peer_open of the exchanged 64-byte IPC handle).  Layout of a
+ * rank's buffer: two slots, each holding `world` partials of max_rows x dim
+ * FP32 (partial q = rank q's), then `world` uint32 flags.  One launch (one
+ * CTA) per rank:
+ *   1. stores this rank's partial `local` (rows x dim; FP32, the unrounded
+ *      output of hif8_linear_partial_f32 / hif8_static_fused_linear_partial_f32,
+ *      or BF16, widened) as FP32 into partial [rank] of
+ *      the slot in every rank's buffer (its own first): one-way peer stores;
  *   2. system-scope fence, then writes epoch into flag[rank] of every rank's
  *      buffer, and waits (bounded by timeout_ns of %globaltimer; on time-out
  *      *error = 1 and the kernel finishes) until every flag of its own
  *      buffer has reached epoch;
- *   3. sums the ranks' partials in rank order (identical on every rank),
- *      adds the residual (BF16) and normalises: out = RMSNorm(sum +
- *      residual) * (one_plus ? 1 + w : w), residual_out = sum + residual.
+ *   3. sums the ranks' partials in FP32 from its own buffer in rank order
+ *      (identical on every rank) and rounds the sum to BF16 once; with
+ *      `weight` it adds the residual (BF16) and
+ *      normalises: out = RMSNorm(sum + residual) * (one_plus ? 1 + w : w),
+ *      residual_out = sum + residual; with weight == NULL, out = the sum.
+ * dim % 256 == 0; with weight, rows <= 8 and rows x dim <= 32768.
  * epoch = *epoch_counter + 1 (a per-rank device counter, advanced by the
  * launch), so the launch can live in a CUDA graph.  Two slots (alternate
- * call sites) keep a rank from overwriting a partial a slower peer still
- * reads.  Plain peer loads and stores only (no multicast). */
+ * call sites) keep a rank from overwriting partials a slower peer still
+ * reads.  Plain peer loads and stores only (no multicast).  The kernel
+ * signals programmatic dependents once its inputs are visible (see
+ * hif8_b200.h on the ordering contract). */
+size_t hif8_peer_buffer_bytes(int64_t world, int64_t max_rows, int64_t dim);
+
 typedef struct Hif8PeerArgs {
-  const uint16_t *local;          /* this rank's partial, rows x dim */
+  const void *local;              /* this rank's partial, rows x dim, in local_dtype */
   const uint16_t *residual;       /* may be NULL */
   const uint16_t *weight;         /* [dim] */
   uint16_t *out, *residual_out;   /* rows x dim each */
@@ -130,6 +152,7 @@ typedef struct Hif8PeerArgs {
   int rank, world, slot, one_plus;
   float eps;
   uint64_t timeout_ns;
+  int local_dtype;                /* HIF8_DTYPE_F32 (an unrounded partial) or HIF8_DTYPE_BF16 */
 } Hif8PeerArgs;
 
 int hif8_model_peer_allreduce_rmsnorm(const Hif8PeerArgs *args, void *stream);

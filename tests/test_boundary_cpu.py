@@ -62,6 +62,14 @@ def test_model_glue_header_symbols_are_exported():
     assert set(names) == {"hif8_model_rmsnorm", "hif8_model_silu_mul", "hif8_model_gate_mul",
                           "hif8_model_attn_prep", "hif8_model_gdn", "hif8_model_peer_allreduce_rmsnorm",
                           "hif8_model_glue_linear", "hif8_peer_alloc", "hif8_peer_open", "hif8_peer_close"}
+    assert re.search(r"^\s*size_t\s+hif8_peer_buffer_bytes\s*\(", text, flags=re.M)
+    import ctypes
+
+    fn = cabi.library().hif8_peer_buffer_bytes
+    fn.restype, fn.argtypes = ctypes.c_size_t, [ctypes.c_int64] * 3
+    # two slots of `world` FP32 partials (max_rows x dim), world flags, 256-byte multiple
+    assert fn(2, 4, 4096) == 2 * 2 * 4 * 4096 * 4 + 256
+    assert fn(0, 4, 4096) == 0
     lib = cabi.library()
     for name in names:
         assert hasattr(lib, name), f"{name} is declared in include/hif8_b200_model.h but not exported"

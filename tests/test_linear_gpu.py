@@ -308,3 +308,40 @@ def test_static_fused_qwen35_generation_shapes(n, k):
         expected = ext.soft_hif8_gemm(data, wd, row_scale, wsd, None, torch.bfloat16)
         actual = ext.soft_hif8_static_fused_gemm(x, wd, fixed, wsd, None, torch.bfloat16)
         torch.testing.assert_close(actual.float(), expected.float(), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("m", [1, 4, 8, 16, 64, 512])
+def test_tensor_parallel_partial_products_fp32(m):
+    """hif8_b200::linear_partial_f32 (the row-parallel partial product of a
+    tensor-parallel split, kept in FP32): against the FP32 torch reference on
+    every route (fused quant + GEMV for m <= 8, static quant + GEMV for
+    m <= 16, the tcgen05 GEMM beyond), and the split property -- the two
+    halves of the K dimension summed in FP32 and rounded once match the
+    unsharded BF16 projection within one BF16 unit in the last place."""
+    _native()
+    n, k = 4096, 2048
+    w, w_s = _hif8_weights(n, k, seed=40 + m)
+    bits, a, a_s, scale = _activations(m, k, seed=41 + m)
+    x = _to(bits.view(np.int16)).view(torch.bfloat16)
+    w_dev, ws_dev, s_dev = _to(w), _to(w_s), _to(scale)
+    full = torch.ops.hif8_b200.linear_partial_f32(x, w_dev, s_dev, ws_dev)
+    assert full.dtype == torch.float32 and full.shape == (m, n)
+    lut = torch.from_numpy(oracle.decode_table()).to(DEV)
+    ref32 = ((lut[_to(a).long()] * _to(a_s)[:, None]) @ (lut[w_dev.long()] * ws_dev[:, None]).T).cpu().numpy()
+    assert max_rel(full.cpu().numpy(), ref32) <= 1e-4, f"m={m}"
+    half = k // 2
+    # each rank's input columns, as a row-parallel split holds them (owned tensors)
+    p0 = torch.ops.hif8_b200.linear_partial_f32(x[:, :half].clone(), w_dev[:, :half].clone(), s_dev, ws_dev)
+    p1 = torch.ops.hif8_b200.linear_partial_f32(x[:, half:].clone(), w_dev[:, half:].clone(), s_dev, ws_dev)
+    summed = (p0 + p1).to(torch.bfloat16)
+    from hif8_b200 import scheme
+
+    lin = scheme.Hif8StaticLinear(w_dev, ws_dev.reshape(-1, 1), s_dev)
+    unsharded = scheme.apply(lin, x)
+    # the two differ only in the order of the FP32 sums: within BF16 rounding
+    # of the largest output, and at most one BF16 ulp on almost every element
+    # (an output that is a small difference of large terms carries the FP32
+    # order error as several of its own ulps)
+    assert max_rel(summed.float().cpu().numpy(), unsharded.float().cpu().numpy()) <= 2.0**-8, f"m={m}"
+    ulps = (summed.view(torch.int16).int() - unsharded.view(torch.int16).int()).abs()
+    assert float((ulps > 1).float().mean()) <= 1e-3, f"m={m}: split partials differ by more than one BF16 ulp"
