@@ -1135,6 +1135,7 @@ def run_profile_case(spec: str, launches: int) -> None:
                   f"{total:.1f} us of kernel time (rank 0, torch.profiler)")
             for name, (n, t) in sorted(rows.items(), key=lambda kv: -kv[1][1]):
                 print(f"{name:60s} {n:6d} {t:10.1f} {100 * t / total:6.1f}%")
+        del graph  # a graph holding NCCL calls goes before the process group
         model.release_graphs()
         if model.peer is not None:
             model.peer.check()
