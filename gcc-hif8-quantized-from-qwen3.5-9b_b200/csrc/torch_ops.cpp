@@ -532,7 +532,7 @@ at::Tensor ModelGdn(const at::Tensor &proj, int64_t T, int64_t hk, int64_t hv, c
 // (FP16/BF16 [M, K], this rank's input columns) statically quantised with
 // input_scale, times this rank's weight columns, as FP32 [M, N] without
 // rounding (the ranks' partials are summed before the one BF16 rounding).
-// M <= 8: one fused quant + GEMV launch; larger M: static quant, then the
+// M <= 4: one fused quant + GEMV launch; larger M: static quant, then the
 // GEMV / tcgen05 GEMM with FP32 output.
 at::Tensor Hif8LinearPartialF32(const at::Tensor &x_in, const at::Tensor &weight_in, const at::Tensor &input_scale_in,
                                 const at::Tensor &weight_scale_in) {
@@ -555,7 +555,10 @@ at::Tensor Hif8LinearPartialF32(const at::Tensor &x_in, const at::Tensor &weight
   auto out = at::empty({m, n}, x.options().dtype(at::kFloat));
   if (m == 0) return out;
   const int x_dtype = DtypeCode(x.scalar_type());
-  if (m <= 8) {
+  // fused quant + GEMV for the rows the scheme fuses (<= 4): beyond that
+  // every CTA would quantise all rows of its K slice, where one quant launch
+  // does it once
+  if (m <= 4) {
     CheckStatus(hif8_static_fused_linear_partial_f32(x.data_ptr(), x_dtype, weight.data_ptr<uint8_t>(),
                                                      input_scale.data_ptr<float>(), weight_scale.data_ptr<float>(), m,
                                                      n, k, out.data_ptr<float>(), Stream(x)),

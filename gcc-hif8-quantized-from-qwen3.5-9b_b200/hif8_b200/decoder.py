@@ -123,12 +123,13 @@ class _Linear:
         """This rank's partial product of a row-parallel projection, before
         the all-reduce: FP32 for the HiF8 layer (summed over the ranks
         before its one BF16 rounding, so the sum equals the unsharded
-        projection up to the FP32 summation order), the BF16 product for the
-        twin (cuBLAS)."""
+        projection up to the FP32 summation order); likewise FP32 for the twin
+        (cuBLAS with BF16 operands and an FP32 result)."""
         import torch
 
         if self.mode == "bf16":
-            return torch.nn.functional.linear(x, self.weight)
+            x2 = x.reshape(-1, x.shape[-1])
+            return torch.mm(x2, self.weight.t(), out_dtype=torch.float32)
         from . import scheme
 
         scale = self.input_scale
