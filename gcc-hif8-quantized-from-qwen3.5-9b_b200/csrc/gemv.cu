@@ -1007,3 +1007,32 @@ extern "C" int hif8_static_fused_linear_partial_f32(const void *x, int x_dtype, 
   GemvArgs args{x, weight, fixed_scale, channel_scale, nullptr, out, (int)m, (int)n, (int)k, 0, HIF8_DTYPE_NONE, 0};
   return run_fused_linear(args, x_dtype, HIF8_DTYPE_F32, static_cast<cudaStream_t>(stream));
 }
+
+extern "C" size_t soft_hif8_fused_gemm_workspace_size(int64_t m, int64_t n, int64_t k) {
+  (void)n;
+  if (m <= 0 || k <= 0) return 0;
+  return ((size_t)m * k + 255) / 256 * 256 + ((size_t)m * sizeof(float) + 255) / 256 * 256;
+}
+
+extern "C" int soft_hif8_fused_gemm(const void *x, int x_dtype, const uint8_t *weight, const float *channel_scale,
+                                    const void *bias, int bias_dtype, int output_dtype, int64_t m, int64_t n,
+                                    int64_t k, void *out, void *workspace, size_t workspace_bytes, void *stream) {
+  const float *no_scale = channel_scale;  // token scales come from the dynamic quant
+  int status = validate_linear(x, weight, no_scale, channel_scale, bias, bias_dtype, output_dtype, m, n, k, out);
+  if (status != HIF8_OK) return status;
+  if (m > 2) return HIF8_ERR_INVALID_ARGUMENT;  // reference contract: soft_hif8_fused_gemm requires M <= 2
+  if (x_dtype != HIF8_DTYPE_F16 && x_dtype != HIF8_DTYPE_BF16) return HIF8_ERR_INVALID_ARGUMENT;
+  const size_t need = soft_hif8_fused_gemm_workspace_size(m, n, k);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return HIF8_ERR_WORKSPACE;
+  uint8_t *codes = static_cast<uint8_t *>(workspace);
+  float *scales = reinterpret_cast<float *>(codes + ((size_t)m * k + 255) / 256 * 256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the scale needs the whole row before any of it is encoded: the dynamic
+  // quant launch (it signals the linear's launch at its start), then the GEMV
+  status = hif8_dynamic_quant(x, x_dtype, m, k, codes, scales, 1, s);
+  if (status != HIF8_OK) return status;
+  GemvArgs args{codes, weight, scales, channel_scale, bias, out, (int)m, (int)n, (int)k, 0,
+                bias ? bias_dtype : HIF8_DTYPE_NONE, 1};
+  return run_linear(args, output_dtype, s);
+}

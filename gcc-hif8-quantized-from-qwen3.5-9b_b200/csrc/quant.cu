@@ -126,6 +126,169 @@ __global__ void __launch_bounds__(256) static_quant_scalar(const uint16_t *__res
   }
 }
 
+// ---------------------------------------------------------- dynamic quant
+//
+// hif8_dynamic_quant (reference csrc/opp/op_kernel/hif8_dynamic_quant.cpp
+// :11-221; CPU rule codec.py:205-255): per row, scale = max(amax of the
+// row's finite |x|, 1e-12) and data = encode(x / scale), NaN / Inf keeping
+// their codes.  The amax is the largest 15-bit magnitude pattern below the
+// Inf/NaN exponent (the patterns of non-negative values order like the
+// values).  |x / scale| <= 1 for finite x, so the static-saturating rule of
+// static_code gives the plain encode here.  When the scale is the row's
+// amax -- one of its own FP16/BF16 values, at most 11 significant bits --
+// the exact quotient x / scale is either a HiF8 code boundary itself or at
+// least 2^-17 (relative) away from every boundary (a boundary has at most 5
+// significant bits), so the FP32 quotient has the code of the reference's
+// double-precision division.  A row whose finite amax is at most 1e-12 is
+// divided by the floor 1e-12, which the reference's CPU rule applies as the
+// double nearest 1e-12 (not its FP32 rounding, the row scale it stores):
+// those rows take the codes of the double quotient (code_of_double).  One
+// CTA per row (grid-stride), the row held in registers up to 16384 values.
+constexpr int kDynThreads = 256;
+constexpr int kDynKeep = 4;  // 16-value chunks per thread held in registers
+constexpr double kDynFloorScale = 1.0e-12;
+constexpr float kDynFloorScaleF = 1.0e-12f;
+
+// HiF8 code (nearest, ties away) of a double q.  The code boundaries are
+// FP32 values, so RN32(q) has q's code unless |q| is below |RN32(q)|: then
+// no boundary lies strictly between them, and the FP32 value just below
+// RN32(q) in magnitude has q's code (a boundary itself takes the code above
+// it, as q does when RN32(q) is the next value up).
+__device__ __forceinline__ uint32_t code_of_double(double q, const uint8_t *__restrict__ mag) {
+  const float qf = (float)q;
+  uint32_t v = __float_as_uint(qf);
+  if ((v & 0x7FFFFFFFu) > 0x7F800000u) return 0x80u;
+  if (fabs(q) < (double)fabsf(qf)) v -= 1u;  // |qf| > 0 here: the sign bit stays
+  const uint32_t m = mag[(v >> 19) & 0xFFFu];
+  return m == 0u ? 0u : m | ((v >> 24) & 0x80u);
+}
+
+// The 16 codes of a chunk of a floor-scale row.
+template <int kDtype>
+__device__ __forceinline__ uint4 floor_chunk(const uint4 a, const uint4 b, const uint8_t *__restrict__ tbl) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t o[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const uint32_t h = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+    o[e >> 2] |= code_of_double((double)half_bits_to_f32<kDtype>(h) / kDynFloorScale, tbl) << (8 * (e & 3));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <int kDtype>
+__device__ __forceinline__ uint32_t finite_mag_max16(const uint4 a, const uint4 b, uint32_t m) {
+  constexpr uint32_t kInf = kDtype == HIF8_DTYPE_BF16 ? 0x7F80u : 0x7C00u;
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t lo = w[j] & 0x7FFFu, hi = (w[j] >> 16) & 0x7FFFu;
+    m = max(m, lo < kInf ? lo : 0u);
+    m = max(m, hi < kInf ? hi : 0u);
+  }
+  return m;
+}
+
+template <int kDtype>
+__global__ void __launch_bounds__(kDynThreads) dynamic_quant_vec16(const uint16_t *__restrict__ x, int64_t rows,
+                                                                   int64_t k, uint8_t *__restrict__ out,
+                                                                   float *__restrict__ row_scale,
+                                                                   int64_t scale_stride) {
+  __shared__ __align__(16) uint8_t tbl[4096];
+  __shared__ uint32_t warp_max[kDynThreads / 32];
+  load_encode_mag_table(tbl);  // module data: before the dependency wait
+  pdl_wait();                  // x may come from the previous kernel of the stream
+  pdl_launch_dependents();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t chunks = k >> 4;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * k);
+    uint4 a[kDynKeep], b[kDynKeep];
+    uint32_t m = 0;
+#pragma unroll
+    for (int u = 0; u < kDynKeep; ++u) {
+      const int64_t c = tid + (int64_t)u * kDynThreads;
+      if (c < chunks) {
+        a[u] = __ldcs(xr + 2 * c);
+        b[u] = __ldcs(xr + 2 * c + 1);
+        m = finite_mag_max16<kDtype>(a[u], b[u], m);
+      }
+    }
+    for (int64_t c = tid + (int64_t)kDynKeep * kDynThreads; c < chunks; c += kDynThreads)
+      m = finite_mag_max16<kDtype>(__ldg(xr + 2 * c), __ldg(xr + 2 * c + 1), m);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    if (lane == 0) warp_max[warp] = m;
+    __syncthreads();
+    m = 0;
+#pragma unroll
+    for (int w = 0; w < kDynThreads / 32; ++w) m = max(m, warp_max[w]);
+    const float amax = half_bits_to_f32<kDtype>(m);
+    const bool floor_row = !(amax > kDynFloorScaleF);
+    const float s = floor_row ? kDynFloorScaleF : amax;
+    if (tid == 0 && row_scale) row_scale[row * scale_stride] = s;
+    bool exact_only;
+    double r64;
+    const float r = reciprocal(s, exact_only, r64);
+    uint4 *orow = reinterpret_cast<uint4 *>(out + row * k);
+#pragma unroll
+    for (int u = 0; u < kDynKeep; ++u) {
+      const int64_t c = tid + (int64_t)u * kDynThreads;
+      if (c < chunks)
+        __stcs(orow + c, floor_row ? floor_chunk<kDtype>(a[u], b[u], tbl)
+                                   : quant_chunk<kDtype>(a[u], b[u], r, r64, exact_only, tbl));
+    }
+    for (int64_t c = tid + (int64_t)kDynKeep * kDynThreads; c < chunks; c += kDynThreads) {
+      const uint4 a1 = __ldg(xr + 2 * c), b1 = __ldg(xr + 2 * c + 1);
+      __stcs(orow + c, floor_row ? floor_chunk<kDtype>(a1, b1, tbl)
+                                 : quant_chunk<kDtype>(a1, b1, r, r64, exact_only, tbl));
+    }
+    __syncthreads();  // warp_max is rewritten by the next row
+  }
+}
+
+// Any k and alignment: one CTA per row, one value per thread and step.
+template <int kDtype>
+__global__ void __launch_bounds__(kDynThreads) dynamic_quant_scalar(const uint16_t *__restrict__ x, int64_t rows,
+                                                                    int64_t k, uint8_t *__restrict__ out,
+                                                                    float *__restrict__ row_scale,
+                                                                    int64_t scale_stride) {
+  __shared__ __align__(16) uint8_t tbl[4096];
+  __shared__ uint32_t warp_max[kDynThreads / 32];
+  load_encode_mag_table(tbl);
+  pdl_wait();
+  constexpr uint32_t kInf = kDtype == HIF8_DTYPE_BF16 ? 0x7F80u : 0x7C00u;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const uint16_t *xr = x + row * k;
+    uint32_t m = 0;
+    for (int64_t c = tid; c < k; c += kDynThreads) {
+      const uint32_t mag = xr[c] & 0x7FFFu;
+      m = max(m, mag < kInf ? mag : 0u);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    if (lane == 0) warp_max[warp] = m;
+    __syncthreads();
+    m = 0;
+#pragma unroll
+    for (int w = 0; w < kDynThreads / 32; ++w) m = max(m, warp_max[w]);
+    const float amax = half_bits_to_f32<kDtype>(m);
+    const bool floor_row = !(amax > kDynFloorScaleF);
+    const float s = floor_row ? kDynFloorScaleF : amax;
+    if (tid == 0 && row_scale) row_scale[row * scale_stride] = s;
+    bool exact_only;
+    double r64;
+    const float r = reciprocal(s, exact_only, r64);
+    for (int64_t c = tid; c < k; c += kDynThreads) {
+      const float f = half_bits_to_f32<kDtype>(xr[c]);
+      out[row * k + c] = (uint8_t)(floor_row ? code_of_double((double)f / kDynFloorScale, tbl)
+                                             : quant_one(f, r, r64, exact_only, tbl));
+    }
+    __syncthreads();
+  }
+}
+
 // ------------------------------------------------------------ scaled decode
 
 __device__ __forceinline__ void load_decode_table(float *smem) {
@@ -375,6 +538,28 @@ extern "C" int hif8_static_quant(const void *x, int x_dtype, int64_t rows, int64
                           scale_count, data, total, row_scale, rows)
              : launch_pdl(static_quant_scalar<HIF8_DTYPE_F16>, dim3(grid), dim3(256), 0, stream, xs, k, fixed_scale,
                           scale_count, data, total, row_scale, rows);
+}
+
+extern "C" int hif8_dynamic_quant(const void *x, int x_dtype, int64_t rows, int64_t k, uint8_t *data,
+                                  float *row_scale, int64_t scale_stride, void *stream_ptr) {
+  if (rows < 0 || k <= 0 || scale_stride < 1 || (rows > 0 && (!x || !data || !row_scale)))
+    return HIF8_ERR_INVALID_ARGUMENT;
+  if (x_dtype != HIF8_DTYPE_F16 && x_dtype != HIF8_DTYPE_BF16) return HIF8_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return HIF8_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const uint16_t *xs = static_cast<const uint16_t *>(x);
+  const int64_t cap = (int64_t)num_sms() * 8;
+  const dim3 grid((unsigned)(rows < cap ? rows : cap));
+  const bool bf16 = x_dtype == HIF8_DTYPE_BF16;
+  if (k % 16 == 0 && aligned16(x) && aligned16(data))
+    return bf16 ? launch_pdl(dynamic_quant_vec16<HIF8_DTYPE_BF16>, grid, dim3(kDynThreads), 0, stream, xs, rows, k,
+                             data, row_scale, scale_stride)
+                : launch_pdl(dynamic_quant_vec16<HIF8_DTYPE_F16>, grid, dim3(kDynThreads), 0, stream, xs, rows, k,
+                             data, row_scale, scale_stride);
+  return bf16 ? launch_pdl(dynamic_quant_scalar<HIF8_DTYPE_BF16>, grid, dim3(kDynThreads), 0, stream, xs, rows, k,
+                           data, row_scale, scale_stride)
+              : launch_pdl(dynamic_quant_scalar<HIF8_DTYPE_F16>, grid, dim3(kDynThreads), 0, stream, xs, rows, k,
+                           data, row_scale, scale_stride);
 }
 
 extern "C" int hif8_scaled_decode(const uint8_t *data, int64_t rows, int64_t k, int64_t data_row_stride,

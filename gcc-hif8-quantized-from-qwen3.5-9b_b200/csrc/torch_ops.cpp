@@ -234,15 +234,77 @@ at::Tensor SoftHif8StaticFusedGemm(const at::Tensor &activation, const at::Tenso
   return out;
 }
 
-std::tuple<at::Tensor, at::Tensor> Hif8DynamicQuant(const at::Tensor &) {
-  TORCH_CHECK(false, "hif8_dynamic_quant is not provided by the B200 build: only the static "
-                     "W8A8HIF8_STATIC path (fixed input_scale) is implemented");
+// Dynamic per-row quant (reference hif8_native.cpp:433-486): data like x
+// (uint8), token scales as a [rows] view of stride 16 (the reference's
+// layout), checks and messages of the reference wrapper.
+std::tuple<at::Tensor, at::Tensor> Hif8DynamicQuant(const at::Tensor &x) {
+  CheckCudaTensor(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::ScalarType::Half || x.scalar_type() == at::ScalarType::BFloat16,
+              "x must have dtype torch.float16 or torch.bfloat16");
+  TORCH_CHECK(x.dim() >= 1, "x must have at least one dimension");
+  CheckPositiveDimensions(x, "x");
+  const int64_t rows = x.numel() / x.size(-1);
+  CheckFitsUint32(rows, "activation row count");
+  CheckFitsUint32(x.size(-1), "K");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto data = at::empty(x.sizes(), x.options().dtype(at::kByte));
+  constexpr int64_t kScaleStride = 16;
+  auto storage = at::empty({rows * kScaleStride}, x.options().dtype(at::kFloat));
+  auto token_scale = storage.as_strided({rows}, {kScaleStride});
+  CheckStatus(hif8_dynamic_quant(x.data_ptr(), DtypeCode(x.scalar_type()), rows, x.size(-1),
+                                 data.data_ptr<uint8_t>(), storage.data_ptr<float>(), kScaleStride, Stream(x)),
+              "hif8_dynamic_quant");
+  return {data, token_scale};
 }
 
-at::Tensor SoftHif8FusedGemm(const at::Tensor &, const at::Tensor &, const at::Tensor &,
-                             const std::optional<at::Tensor> &, at::ScalarType) {
-  TORCH_CHECK(false, "soft_hif8_fused_gemm (dynamic activation quant) is not provided by the B200 build; "
-                     "use soft_hif8_static_fused_gemm with a fixed input_scale");
+// Dynamic quant + linear (reference hif8_native.cpp:676-760), M <= 2.
+at::Tensor SoftHif8FusedGemm(const at::Tensor &activation, const at::Tensor &weight, const at::Tensor &channel_scale,
+                             const std::optional<at::Tensor> &bias, at::ScalarType output_type) {
+  CheckCudaTensor(activation, "activation");
+  CheckCudaTensor(weight, "weight");
+  CheckCudaTensor(channel_scale, "channel_scale");
+  TORCH_CHECK(activation.scalar_type() == at::ScalarType::Half || activation.scalar_type() == at::ScalarType::BFloat16,
+              "activation must have dtype torch.float16 or torch.bfloat16");
+  TORCH_CHECK(weight.scalar_type() == at::ScalarType::Byte, "weight must have dtype torch.uint8");
+  TORCH_CHECK(channel_scale.scalar_type() == at::ScalarType::Float, "channel_scale must have dtype torch.float32");
+  TORCH_CHECK(activation.dim() == 2, "activation must have shape [M, K]");
+  TORCH_CHECK(weight.dim() == 2, "weight must have shape [N, K]");
+  TORCH_CHECK(channel_scale.dim() == 1, "channel_scale must have shape [N]");
+  CheckPositiveDimensions(activation, "activation");
+  CheckPositiveDimensions(weight, "weight");
+  TORCH_CHECK(activation.size(0) <= 2, "soft_hif8_fused_gemm requires M <= 2");
+  TORCH_CHECK(activation.size(1) == weight.size(1), "activation and weight K dimensions differ: ", activation.size(1),
+              " != ", weight.size(1));
+  TORCH_CHECK(channel_scale.numel() == weight.size(0), "channel_scale must contain one value per output channel");
+  CheckFitsUint32(activation.size(0), "M");
+  CheckFitsUint32(weight.size(0), "N");
+  CheckFitsUint32(activation.size(1), "K");
+  CheckSameDevice(weight, activation.device(), "weight");
+  CheckSameDevice(channel_scale, activation.device(), "channel_scale");
+  int bias_dtype = HIF8_DTYPE_NONE;
+  if (bias.has_value()) {
+    CheckCudaTensor(*bias, "bias");
+    CheckSameDevice(*bias, activation.device(), "bias");
+    TORCH_CHECK(bias->dim() == 1, "bias must have shape [N]");
+    TORCH_CHECK(bias->numel() == weight.size(0), "bias must contain N values");
+    TORCH_CHECK(bias->scalar_type() == at::ScalarType::Half || bias->scalar_type() == at::ScalarType::BFloat16,
+                "bias must have dtype torch.float16 or torch.bfloat16");
+    bias_dtype = DtypeCode(bias->scalar_type());
+  }
+  TORCH_CHECK(output_type == at::ScalarType::Half || output_type == at::ScalarType::BFloat16,
+              "output_dtype must be torch.float16 or torch.bfloat16");
+  c10::cuda::CUDAGuard guard(activation.device());
+  const int64_t m = activation.size(0), k = activation.size(1), n = weight.size(0);
+  auto out = at::empty({m, n}, activation.options().dtype(output_type));
+  const size_t ws_bytes = soft_hif8_fused_gemm_workspace_size(m, n, k);
+  auto ws = at::empty({(int64_t)ws_bytes}, activation.options().dtype(at::kByte));
+  CheckStatus(soft_hif8_fused_gemm(activation.data_ptr(), DtypeCode(activation.scalar_type()),
+                                   weight.data_ptr<uint8_t>(), channel_scale.data_ptr<float>(),
+                                   bias.has_value() ? bias->data_ptr() : nullptr, bias_dtype,
+                                   DtypeCode(output_type), m, n, k, out.data_ptr(), ws.data_ptr(), ws_bytes,
+                                   Stream(activation)),
+              "soft_hif8_fused_gemm");
+  return out;
 }
 
 // HiF8 token embedding (reference scheme.py:120-131): gather + decode of the
@@ -724,6 +786,14 @@ TORCH_LIBRARY_IMPL(vllm_ascend_hif8, Meta, m) {
   m.impl("soft_hif8_gemv", linear_meta);
   m.impl("soft_hif8_gemm", linear_meta);
   m.impl("soft_hif8_static_fused_gemm", linear_meta);
+  m.impl("hif8_dynamic_quant", [](const at::Tensor &x) -> std::tuple<at::Tensor, at::Tensor> {
+    return {at::empty_like(x, x.options().dtype(at::kByte)),
+            at::empty({x.numel() / x.size(-1)}, x.options().dtype(at::kFloat))};
+  });
+  m.impl("soft_hif8_fused_gemm", [](const at::Tensor &activation, const at::Tensor &weight, const at::Tensor &,
+                                    const std::optional<at::Tensor> &, at::ScalarType output_dtype) -> at::Tensor {
+    return at::empty({activation.size(0), weight.size(0)}, activation.options().dtype(output_dtype));
+  });
 }
 
 TORCH_LIBRARY(hif8_b200, m) {

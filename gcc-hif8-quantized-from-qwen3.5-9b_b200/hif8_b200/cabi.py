@@ -40,6 +40,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "soft_hif8_gemm_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "soft_hif8_gemm": (_INT, [_P, _P, _P, _P, _P, _INT, _INT, _I64, _I64, _I64, _P, _P, _SZ, _P]),
     "hif8_linear_partial_f32": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _SZ, _P]),
+    "hif8_dynamic_quant": (_INT, [_P, _INT, _I64, _I64, _P, _P, _I64, _P]),
+    "soft_hif8_fused_gemm_workspace_size": (_SZ, [_I64, _I64, _I64]),
+    "soft_hif8_fused_gemm": (_INT, [_P, _INT, _P, _P, _P, _INT, _INT, _I64, _I64, _I64, _P, _P, _SZ, _P]),
     "hif8_static_fused_linear_partial_f32": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soft_hif8_static_fused_gemm": (_INT, [_P, _INT, _P, _P, _P, _P, _INT, _INT, _I64, _I64, _I64, _P, _P]),
     "hif8_kv_cache_write": (_INT, [_P, _P, _INT, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _P]),

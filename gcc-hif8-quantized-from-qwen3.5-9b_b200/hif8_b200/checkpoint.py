@@ -35,9 +35,7 @@ import math
 import re
 from pathlib import Path
 
-from .scheme import STATIC_QUANT_TYPE, Hif8StaticLinear
-
-DYNAMIC_QUANT_TYPE = "W8A8HIF8_SOFT"
+from .scheme import DYNAMIC_QUANT_TYPE, STATIC_QUANT_TYPE, Hif8StaticLinear
 QUANT_DESCRIPTION_FILENAME = "quant_model_description.json"
 METADATA_FILENAME = "hif8_metadata.json"
 INDEX_FILENAME = "model.safetensors.index.json"

@@ -19,6 +19,7 @@ if TYPE_CHECKING:
     import torch
 
 _REQUIRED_SYMBOLS = (
+    "hif8_dynamic_quant",
     "hif8_static_quant",
     "hif8_scaled_decode",
     "soft_hif8_gemv",
@@ -119,12 +120,14 @@ def _op(name: str):
 
 
 def dynamic_quant(x: "torch.Tensor") -> tuple["torch.Tensor", "torch.Tensor"]:
-    """Dynamic (per-row amax) activation quant is not part of the static
-    W8A8KV8 path this build provides."""
-    raise NativeExtensionUnavailable(
-        "hif8_dynamic_quant is not provided by the B200 build; use static_quant with the "
-        "checkpoint's fixed input_scale (W8A8HIF8_STATIC)"
-    )
+    """Quantize BF16/FP16 activations into U8 HiFloat8 with one FP32 scale
+    per row (the row's finite amax, at least 1e-12) -- the W8A8HIF8_SOFT
+    activation path (reference native.py:77-87); the scales come back as the
+    reference's stride-16 view."""
+    load_extension()
+    data, scale = _op("hif8_dynamic_quant")(x)
+    _validate_quantized_activation(x, data, scale, operation="hif8_dynamic_quant")
+    return data, scale
 
 
 def static_quant(x: "torch.Tensor", fixed_scale: "torch.Tensor") -> tuple["torch.Tensor", "torch.Tensor"]:
@@ -231,13 +234,34 @@ def soft_linear(
     return output if activation.dim() == 2 else output.reshape(*activation.shape[:-1], weight.shape[0])
 
 
-def soft_fused_linear(x, weight, weight_scale, bias=None, *, output_dtype):
-    """Dynamic-quant fused linear: not part of the static path (see
-    ``dynamic_quant``)."""
-    raise NativeExtensionUnavailable(
-        "soft_hif8_fused_gemm (dynamic activation quant) is not provided by the B200 build; "
-        "use soft_static_fused_linear with the checkpoint's fixed input_scale"
-    )
+def soft_fused_linear(
+    x: "torch.Tensor",
+    weight: "torch.Tensor",
+    weight_scale: "torch.Tensor",
+    bias: "torch.Tensor | None" = None,
+    *,
+    output_dtype: "torch.dtype",
+) -> "torch.Tensor":
+    """Dynamic activation quant fused with the U8-weight linear, M <= 2
+    (reference native.py:204-240; the result equals dynamic_quant then
+    soft_linear bit for bit)."""
+    import torch
+
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError(f"fused soft HiFP8 linear requires FP16/BF16 activation, got {x.dtype}")
+    if weight.dtype != torch.uint8 or weight.ndim != 2:
+        raise TypeError("fused soft HiFP8 linear requires a 2D uint8 weight tensor")
+    if x.ndim < 2 or x.shape[-1] != weight.shape[-1]:
+        raise ValueError("activation and weight must have compatible final K dimensions")
+    if weight_scale.dtype != torch.float32 or weight_scale.numel() != weight.shape[0]:
+        raise TypeError("fused soft HiFP8 linear requires one float32 scale per output channel")
+    flattened = _as_native_operand(x.reshape(-1, x.shape[-1]))
+    if flattened.shape[0] > 2:
+        raise ValueError("fused soft HiFP8 linear supports M <= 2")
+    channel_scale = _as_native_operand(weight_scale.reshape(-1))
+    load_extension()
+    output = _op("soft_hif8_fused_gemm")(flattened, weight, channel_scale, bias, output_dtype)
+    return output.reshape(*x.shape[:-1], weight.shape[0])
 
 
 def soft_static_fused_linear(

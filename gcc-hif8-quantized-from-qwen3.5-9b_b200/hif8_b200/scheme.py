@@ -1,11 +1,13 @@
-"""W8A8HIF8_STATIC linear: the parameter contract and ``apply`` of the
-reference quant scheme (src/vllm_ascend_hif8/scheme.py:134-211) without the
-vLLM-Ascend registration layer.
+"""W8A8HIF8_STATIC and W8A8HIF8_SOFT linears: the parameter contracts and
+``apply`` of the reference quant schemes (src/vllm_ascend_hif8/scheme.py:134-211
+static, 43-132 dynamic) without the vLLM-Ascend registration layer.
 
 Parameters of a layer:
   ``weight``       uint8 [N, K] HiF8 bytes (row-major, K contiguous)
   ``weight_scale`` float32 [N, 1] (flattened to [N] after loading)
   ``input_scale``  float32 [1], positive and finite, fixed for every call
+                   (static scheme only; the dynamic scheme computes one
+                   scale per token row from its amax)
 """
 
 from __future__ import annotations
@@ -16,7 +18,9 @@ import os
 from . import native
 
 STATIC_QUANT_TYPE = "W8A8HIF8_STATIC"
+DYNAMIC_QUANT_TYPE = "W8A8HIF8_SOFT"
 _STATIC_FUSED_GENERATION_ENV = "HIF8_STATIC_FUSED_GENERATION"
+_SOFT_FUSED_GENERATION_ENV = "HIF8_SOFT_FUSED_GENERATION"
 _STATIC_SCALE_FACTOR_ENV = "HIF8_STATIC_SCALE_FACTOR"
 _COMPUTE_BACKEND_ENV = "HIF8_COMPUTE_BACKEND"
 MAX_FINITE = 32768.0
@@ -25,6 +29,9 @@ MAX_FINITE = 32768.0
 # scheme.py:185-189); on B200 it is cheaper than quant + linear at every K,
 # so it is the default for rows <= 4 unless HIF8_STATIC_FUSED_GENERATION=0.
 _FUSED_MAX_ROWS = 4
+# The dynamic fused kernel is opt-in (HIF8_SOFT_FUSED_GENERATION=1) for at
+# most two token rows, as in the reference (scheme.py:101-109).
+_SOFT_FUSED_MAX_ROWS = 2
 
 
 def static_scale_factor() -> float:
@@ -87,6 +94,33 @@ def apply(layer, x, bias=None):
     return native.soft_linear(activation, layer.weight, row_scale, layer.weight_scale, bias, output_dtype=x.dtype)
 
 
+def process_dynamic_weights_after_loading(layer) -> None:
+    """Validate and normalise a loaded W8A8HIF8_SOFT layer in place
+    (scheme.py:56-91): uint8 weight, FP32 per-channel scale flattened to
+    [N]; no input_scale."""
+    import torch
+
+    if layer.weight.dtype != torch.uint8:
+        raise TypeError(f"{DYNAMIC_QUANT_TYPE} checkpoint weight must be torch.uint8, got {layer.weight.dtype}")
+    if layer.weight.ndim != 2:
+        raise ValueError(f"{DYNAMIC_QUANT_TYPE} weight must be a 2D uint8 tensor")
+    layer.weight.data = layer.weight.data.contiguous()
+    ws = layer.weight_scale.data.to(torch.float32).reshape(-1)
+    if ws.numel() != layer.weight.shape[0]:
+        raise ValueError("weight_scale must contain one value per output channel")
+    layer.weight_scale.data = ws.contiguous()
+    _check_backend()
+
+
+def apply_dynamic(layer, x, bias=None):
+    """Dynamic per-token activation quant + HiF8 linear (scheme.py:93-116)."""
+    token_rows = x.numel() // x.shape[-1]
+    if token_rows <= _SOFT_FUSED_MAX_ROWS and os.environ.get(_SOFT_FUSED_GENERATION_ENV) == "1":
+        return native.soft_fused_linear(x, layer.weight, layer.weight_scale, bias, output_dtype=x.dtype)
+    activation, row_scale = native.dynamic_quant(x)
+    return native.soft_linear(activation, layer.weight, row_scale, layer.weight_scale, bias, output_dtype=x.dtype)
+
+
 def quantize_weight_rows(weight, scale_factor: float = MAX_FINITE):
     """Per-output-channel HiF8 weight quantisation on the device:
     scale = max(row amax, 1e-12) / scale_factor and bytes = encode(w / scale)
@@ -129,3 +163,32 @@ class Hif8StaticLinear:
 
     def __call__(self, x):
         return apply(self, x, self.bias)
+
+
+class Hif8SoftLinear:
+    """A standalone W8A8HIF8_SOFT projection: per-channel HiF8 weights and a
+    per-token activation scale computed on every call."""
+
+    def __init__(self, weight, weight_scale, bias=None):
+        import torch
+
+        self.weight = torch.nn.Parameter(weight, requires_grad=False)
+        self.weight_scale = torch.nn.Parameter(weight_scale, requires_grad=False)
+        self.bias = bias
+        process_dynamic_weights_after_loading(self)
+
+    @classmethod
+    def from_float(cls, weight, bias=None, scale_factor: float = MAX_FINITE):
+        data, scale = quantize_weight_rows(weight, scale_factor)
+        return cls(data, scale.reshape(-1, 1), bias)
+
+    @property
+    def out_features(self) -> int:
+        return self.weight.shape[0]
+
+    @property
+    def in_features(self) -> int:
+        return self.weight.shape[1]
+
+    def __call__(self, x):
+        return apply_dynamic(self, x, self.bias)

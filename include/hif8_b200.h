@@ -124,6 +124,29 @@ int soft_hif8_gemm(const uint8_t *activation, const uint8_t *weight, const float
                    int output_dtype, int64_t m, int64_t n, int64_t k, void *out,
                    void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- dynamic path (W8A8HIF8_SOFT checkpoints) ----------------------------
+ * hif8_dynamic_quant replaces op hif8_dynamic_quant (csrc/extension/
+ * pybind.cpp:58, hif8_native.cpp:433-486, kernel csrc/opp/op_kernel/
+ * hif8_dynamic_quant.cpp:11-221; CPU rule codec.py:205-255): per row r,
+ * scale = max(amax of the row's finite |x|, 1e-12) and data = the HiF8 code
+ * of x / scale (nearest, ties away; NaN and Inf keep their codes), bit-exact
+ * with the reference's double-precision quotient.  x: [rows, k] FP16/BF16
+ * (x_dtype); data: [rows, k]; row_scale[r * scale_stride] receives the scale
+ * (the reference returns it as a stride-16 view).
+ * soft_hif8_fused_gemm replaces op soft_hif8_fused_gemm (pybind.cpp:12,
+ * hif8_native.cpp:676-760): the dynamic quant of x followed by the linear
+ * (bit-identical to hif8_dynamic_quant + soft_hif8_gemm), m <= 2 as the
+ * reference; workspace: soft_hif8_fused_gemm_workspace_size() bytes, 256-byte
+ * aligned (the codes and row scales). */
+int hif8_dynamic_quant(const void *x, int x_dtype, int64_t rows, int64_t k, uint8_t *data,
+                       float *row_scale, int64_t scale_stride, void *stream);
+
+size_t soft_hif8_fused_gemm_workspace_size(int64_t m, int64_t n, int64_t k);
+
+int soft_hif8_fused_gemm(const void *x, int x_dtype, const uint8_t *weight, const float *channel_scale,
+                         const void *bias, int bias_dtype, int output_dtype, int64_t m, int64_t n,
+                         int64_t k, void *out, void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- tensor-parallel partial products ---------------------------------
  * No counterpart in the reference, which runs a projection on one device.
  * When a row-parallel projection is split over ranks by its input columns,

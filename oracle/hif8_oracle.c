@@ -95,9 +95,12 @@ static float bits_f32(uint32_t u) {
 }
 
 /* codec.py:148-180 -- nearest, ties away from zero; under/overflow ties. */
-uint8_t hif8o_encode_value(float value_f) {
+static uint8_t encode_double(double value);
+
+uint8_t hif8o_encode_value(float value_f) { return encode_double((double)value_f); }
+
+static uint8_t encode_double(double value) {
     build_positive();
-    double value = (double)value_f;
     if (isnan(value)) return HIF8_NAN;
     if (isinf(value)) return value < 0.0 ? HIF8_NINF : HIF8_PINF;
     double magnitude = fabs(value);
@@ -281,6 +284,24 @@ void hif8o_static_quant(const uint16_t *x, int x_dtype, int64_t rows, int64_t k,
         float s = scale[r % scale_count];
         if (row_scale) row_scale[r] = s;
         for (int64_t c = 0; c < k; ++c) out[r * k + c] = static_encode(load_half(x, x_dtype, r * k + c), s);
+    }
+}
+
+/* codec.py:205-255 (choose_row_scale + quantize_rows, scale_factor 1):
+ * per row, scale = max(amax of the finite |x|, 1e-12) and every code is
+ * encode_ascend(x / scale) with the quotient in double precision, as the
+ * Python reference divides Python floats.  NaN / Inf keep their codes. */
+void hif8o_dynamic_quant(const uint16_t *x, int x_dtype, int64_t rows, int64_t k, uint8_t *out,
+                         float *row_scale) {
+    for (int64_t r = 0; r < rows; ++r) {
+        double amax = 0.0;
+        for (int64_t c = 0; c < k; ++c) {
+            const double v = (double)load_half(x, x_dtype, r * k + c);
+            if (isfinite(v) && fabs(v) > amax) amax = fabs(v);
+        }
+        const double scale = amax > 1.0e-12 ? amax : 1.0e-12;
+        if (row_scale) row_scale[r] = (float)scale;
+        for (int64_t c = 0; c < k; ++c) out[r * k + c] = encode_double((double)load_half(x, x_dtype, r * k + c) / scale);
     }
 }
 

@@ -55,6 +55,11 @@ void hif8o_encode_tensor(const float *x, int64_t n, uint8_t *out);
  *   out[r, k] = encode_tensor(q)
  * x_dtype: 0 = FP16 bits, 1 = BF16 bits.  row_scale (may be NULL) receives
  * scale[r % scale_count] for every row. */
+/* Dynamic per-row quant (codec.py:205-255): scale = max(finite amax,
+ * 1e-12), codes of x / scale with a double-precision quotient. */
+void hif8o_dynamic_quant(const uint16_t *x, int x_dtype, int64_t rows, int64_t k, uint8_t *out,
+                         float *row_scale);
+
 void hif8o_static_quant(const uint16_t *x, int x_dtype, int64_t rows, int64_t k,
                         const float *scale, int64_t scale_count, uint8_t *out,
                         float *row_scale);

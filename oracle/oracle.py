@@ -58,6 +58,7 @@ def lib() -> ctypes.CDLL:
     handle.hif8o_encode_lut4096.argtypes = [p]
     handle.hif8o_encode_tensor.argtypes = [p, i64, p]
     handle.hif8o_static_quant.argtypes = [p, ctypes.c_int, i64, i64, p, i64, p, p]
+    handle.hif8o_dynamic_quant.argtypes = [p, ctypes.c_int, i64, i64, p, p]
     handle.hif8o_scaled_decode.argtypes = [p, i64, i64, i64, p, p]
     handle.hif8o_kv_write.argtypes = [p, ctypes.c_int, i64, i64, i64, p, p, p, i64, i64]
     handle.hif8o_kv_write.restype = i64
@@ -138,6 +139,20 @@ def static_quant(x_bits: np.ndarray, scale: np.ndarray, *, dtype: str = "bf16") 
     row_scale = np.empty(rows, dtype=np.float32)
     lib().hif8o_static_quant(_ptr(x_bits), 1 if dtype == "bf16" else 0, rows, k, _ptr(scale),
                              scale.size, _ptr(out), _ptr(row_scale))
+    return out, row_scale
+
+
+def dynamic_quant(x_bits: np.ndarray, *, dtype: str = "bf16") -> tuple[np.ndarray, np.ndarray]:
+    """HiF8 bytes + per-row scale of the dynamic quant (reference
+    codec.py:205-255, choose_row_scale + quantize_rows; the contract of op
+    hif8_dynamic_quant, csrc/opp/op_kernel/hif8_dynamic_quant.cpp): scale =
+    max(amax of the row's finite |x|, 1e-12), codes of x / scale."""
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    k = x_bits.shape[-1]
+    rows = x_bits.size // k if k else 0
+    out = np.empty(x_bits.shape, dtype=np.uint8)
+    row_scale = np.empty(rows, dtype=np.float32)
+    lib().hif8o_dynamic_quant(_ptr(x_bits), 1 if dtype == "bf16" else 0, rows, k, _ptr(out), _ptr(row_scale))
     return out, row_scale
 
 

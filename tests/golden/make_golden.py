@@ -178,6 +178,7 @@ def main(reference_root: str) -> None:
     payload["wq_src"], payload["wq_data"], payload["wq_scale"] = _bf16_bits(wsrc), wdata.numpy(), wscale.numpy()
     np.savez_compressed(HERE / "linear.npz", **payload)
     write_embedding(codec)
+    write_dynamic(codec)
     print("golden fixtures written to", HERE)
 
 
@@ -217,7 +218,42 @@ def write_embedding(codec) -> None:
     np.savez_compressed(HERE / "embedding.npz", **payload)
 
 
+def write_dynamic(codec) -> None:
+    """Dynamic per-row quant (W8A8HIF8_SOFT activations): codec.quantize_rows
+    (choose_row_scale + encode_ascend of x / scale in double precision), the
+    expectation of the reference's tests/test_npu_ops.py:30-50, on the rows
+    of that test, seeded BF16 / FP16 rows of several magnitudes, a row of
+    values below the 1e-12 scale floor, an all-zero row and rows with
+    NaN / Inf."""
+    g = torch.Generator().manual_seed(11)
+    special = torch.tensor([[0.0, 1.0, -2.0, 4.0] * 12,
+                            [0.25, -0.5, 1.0, -4.0] * 12,
+                            [float("nan"), float("inf"), -float("inf"), 0.0] * 12,
+                            [2.0**-12, -(2.0**-11), 2.0**-10, -(2.0**-9)] * 12])
+    randn = torch.randn(12, 48, generator=g) * torch.tensor([1e-3, 1e-1, 1.0, 30.0, 1e3, 3e4] * 2).reshape(-1, 1)
+    tiny = torch.randn(1, 48, generator=g) * 1e-14
+    zero = torch.zeros(1, 48)
+    mixed = torch.randn(2, 48, generator=g)
+    mixed[0, 5] = float("inf")
+    mixed[1, 17] = float("nan")
+    rows = torch.cat([special, randn, tiny, zero, mixed])
+    payload = {}
+    for name, bits_fn, dtype in (("bf16", _bf16_bits, torch.bfloat16), ("f16", _f16_bits, torch.float16)):
+        src = rows.to(dtype)
+        q = codec.quantize_rows(src.float().tolist())
+        payload[f"{name}_x"] = bits_fn(src)
+        payload[f"{name}_data"] = np.array(q.data, dtype=np.uint8)
+        payload[f"{name}_scale"] = np.array(q.scale, dtype=np.float32)
+    np.savez_compressed(HERE / "dynamic.npz", **payload)
+
+
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        raise SystemExit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
-    main(sys.argv[1])
+    if len(sys.argv) not in (2, 3):
+        raise SystemExit("usage: python tests/golden/make_golden.py <path of the reference checkout> [dynamic]")
+    if len(sys.argv) == 3:  # one fixture only
+        sys.path.insert(0, str(Path(sys.argv[1]) / "src"))
+        from vllm_ascend_hif8 import codec
+
+        {"dynamic": write_dynamic}[sys.argv[2]](codec)
+    else:
+        main(sys.argv[1])

@@ -142,6 +142,18 @@ def test_cabi_rejects_contract_violations_without_device_work():
     assert lib.hif8_embedding_gather(fake, fake, 8, 64, fake, -1, fake, None, None) == 1
     assert lib.hif8_embedding_gather(None, fake, 8, 64, fake, 1, fake, None, None) == 1
     assert lib.hif8_embedding_gather(fake, fake, 8, 64, None, 0, fake, None, None) == cabi.HIF8_OK  # no ids
+    # dynamic quant: FP16/BF16 only, a positive scale stride, pointers for any rows
+    assert lib.hif8_dynamic_quant(fake, 3, 2, 16, fake, fake, 16, None) == 1
+    assert lib.hif8_dynamic_quant(fake, 1, 2, 16, fake, fake, 0, None) == 1
+    assert lib.hif8_dynamic_quant(None, 1, 2, 16, fake, fake, 16, None) == 1
+    assert lib.hif8_dynamic_quant(fake, 1, 2, 0, fake, fake, 16, None) == 1
+    assert lib.hif8_dynamic_quant(None, 1, 0, 16, None, None, 16, None) == cabi.HIF8_OK  # no rows
+    # fused dynamic linear: M <= 2 and a workspace of the reported size
+    ws = lib.soft_hif8_fused_gemm_workspace_size(2, 8, 64)
+    assert ws > 0 and ws % 256 == 0
+    assert lib.soft_hif8_fused_gemm(fake, 1, fake, fake, None, -1, 1, 3, 8, 64, fake, fake, 1 << 20, None) == 1
+    assert lib.soft_hif8_fused_gemm(fake, 1, fake, fake, None, -1, 1, 2, 8, 64, fake, fake, ws - 1, None) == 3
+    assert lib.soft_hif8_fused_gemm(fake, 1, fake, fake, None, -1, 1, 2, 8, 64, fake, None, ws, None) == 3
     assert lib.hif8_status_string(3) == b"workspace missing or too small"
 
 
@@ -212,6 +224,11 @@ def test_meta_shapes():
     assert out.shape == (5, 7) and out.dtype == torch.bfloat16
     dec = torch.ops.vllm_ascend_hif8.hif8_scaled_decode(a, torch.empty(5, device="meta"))
     assert dec.shape == a.shape and dec.dtype == torch.bfloat16
+    data, token_scale = torch.ops.vllm_ascend_hif8.hif8_dynamic_quant(x)
+    assert data.shape == x.shape and data.dtype == torch.uint8 and token_scale.shape == (6,)
+    x2 = torch.empty(2, 64, dtype=torch.float16, device="meta")
+    fused = torch.ops.vllm_ascend_hif8.soft_hif8_fused_gemm(x2, w, torch.empty(7, device="meta"), None, torch.float16)
+    assert fused.shape == (2, 7) and fused.dtype == torch.float16
 
 
 def test_native_wrapper_contracts_raise_before_dispatch():
@@ -233,8 +250,17 @@ def test_native_wrapper_contracts_raise_before_dispatch():
         native.scaled_decode(torch.zeros(2, 4), torch.ones(2))
     with pytest.raises(ValueError):
         native.scaled_decode(torch.zeros(2, 2, 4, dtype=torch.uint8), torch.ones(2))
-    with pytest.raises(native.NativeExtensionUnavailable):
+    with pytest.raises(NotImplementedError):  # the op has no CPU kernel
         native.dynamic_quant(torch.zeros(2, 4, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="M <= 2"):
+        native.soft_fused_linear(torch.zeros(3, 4, dtype=torch.bfloat16), torch.zeros(2, 4, dtype=torch.uint8),
+                                 torch.ones(2), output_dtype=torch.bfloat16)
+    with pytest.raises(TypeError):
+        native.soft_fused_linear(torch.zeros(1, 4), torch.zeros(2, 4, dtype=torch.uint8), torch.ones(2),
+                                 output_dtype=torch.bfloat16)
+    with pytest.raises(TypeError):
+        native.soft_fused_linear(torch.zeros(1, 4, dtype=torch.bfloat16), torch.zeros(2, 4, dtype=torch.uint8),
+                                 torch.ones(3), output_dtype=torch.bfloat16)
     with pytest.raises(TypeError):
         native.soft_static_fused_linear(torch.zeros(1, 4, dtype=torch.bfloat16), torch.zeros(2, 4, dtype=torch.uint8),
                                         torch.ones(2), torch.ones(2), output_dtype=torch.bfloat16)
@@ -319,6 +345,27 @@ def test_static_scheme_parameter_contract():
     no_scale = SimpleNamespace(weight=ok.weight, weight_scale=ok.weight_scale)
     with pytest.raises(ValueError, match="missing input_scale"):
         scheme.process_weights_after_loading(no_scale)
+
+
+def test_dynamic_scheme_parameter_contract(monkeypatch):
+    from types import SimpleNamespace
+
+    from hif8_b200 import scheme
+
+    layer = SimpleNamespace(weight=torch.nn.Parameter(torch.zeros(4, 8, dtype=torch.uint8), requires_grad=False),
+                            weight_scale=torch.nn.Parameter(torch.ones(4, 1, dtype=torch.float64), requires_grad=False))
+    scheme.process_dynamic_weights_after_loading(layer)
+    assert layer.weight_scale.shape == (4,) and layer.weight_scale.dtype == torch.float32
+    bad = SimpleNamespace(weight=torch.nn.Parameter(torch.zeros(4, 8), requires_grad=False),
+                          weight_scale=layer.weight_scale)
+    with pytest.raises(TypeError, match="torch.uint8"):
+        scheme.process_dynamic_weights_after_loading(bad)
+    short = SimpleNamespace(weight=layer.weight, weight_scale=torch.nn.Parameter(torch.ones(3), requires_grad=False))
+    with pytest.raises(ValueError, match="one value per output channel"):
+        scheme.process_dynamic_weights_after_loading(short)
+    monkeypatch.setenv("HIF8_COMPUTE_BACKEND", "other")
+    with pytest.raises(ValueError):
+        scheme.process_dynamic_weights_after_loading(layer)
 
 
 def test_static_scale_factor_env(monkeypatch):

@@ -136,3 +136,15 @@ def assert_bf16_equal_nan_any(actual, expected):
     e_nan = (expected & 0x7FFF) > 0x7F80
     np.testing.assert_array_equal(a_nan, e_nan)
     np.testing.assert_array_equal(np.where(a_nan, 0, actual), np.where(e_nan, 0, expected))
+
+
+def test_dynamic_quant_matches_reference_rows():
+    """Dynamic per-row quant: the oracle against codec.quantize_rows of the
+    reference (tests/golden/dynamic.npz; the expectation of the reference's
+    tests/test_npu_ops.py:30-50), BF16 and FP16 rows, special values and a
+    row below the 1e-12 scale floor included."""
+    d = np.load(GOLDEN / "dynamic.npz")
+    for name in ("bf16", "f16"):
+        data, scale = oracle.dynamic_quant(d[f"{name}_x"], dtype=name)
+        np.testing.assert_array_equal(data, d[f"{name}_data"])
+        np.testing.assert_array_equal(scale, d[f"{name}_scale"])
