@@ -586,6 +586,10 @@ def run_ours(args) -> None:
 
     # -------------------------------------------- e2e: public API, host I/O
     e2e = measure_e2e(calls, args, device, world, tp=world > 1, reduce=reduce if world > 1 else None)
+    serial = measure_e2e(calls, args, device, world, tp=world > 1, reduce=reduce if world > 1 else None,
+                         pipelined=False)
+    e2e["serial"] = {"value": serial["value"], "ms_per_step": serial["ms_per_step"],
+                     "how": "upload, compute and read-back in order on one stream"}
     if world > 1:
         reduce.close()
 
@@ -752,7 +756,8 @@ HBM_KERNEL_CASES = {
     "quant": ("static_quant_vec16", "x [4096, 12288] BF16 (configs[2] prefill, down input), scale = calibration "
                                     "absmax / 32768",
               "x [16, 12288] BF16"),
-    "kv_write": ("kv_write_kernel", "16384 tokens x 4 KV heads x 256, K and V, BF16 source",
+    "kv_write": ("kv_write_warp_kernel", "16384 tokens x 4 KV heads x 256, K and V, BF16 source, per-head scale = "
+                                         "calibration absmax / 32768, random slots",
                  "4 tokens (a batch-4 decode step)"),
     "embedding": ("embedding_gather", "16384 ids of a [248320, 4096] HiF8 table",
                   "4 ids (a batch-4 decode step)"),
@@ -782,8 +787,9 @@ def _hbm_kernel_inputs(name: str, big: bool, device):
         kc, vc = layout.allocate(device)
         key = torch.randn(tokens, heads, d, device=device, generator=g).to(torch.bfloat16)
         val = torch.randn(tokens, heads, d, device=device, generator=g).to(torch.bfloat16)
-        ks = torch.full((heads,), 0.3, device=device)
-        vs = torch.full((heads,), 0.25, device=device)
+        # per-head static scales by the configs' rule: calibration absmax / 32768
+        ks = (key[:64].float().abs().amax(dim=(0, 2)) / 32768.0).contiguous()
+        vs = (val[:64].float().abs().amax(dim=(0, 2)) / 32768.0).contiguous()
         slots = torch.randperm(layout.num_blocks * block, device=device, generator=g)[:tokens].contiguous()
         fn = lambda: torch.ops.hif8_b200.kv_cache_write(key, val, ks, vs, slots, kc, vc, None)
         # per token and plane: heads x (2 D source bytes + D + 4 page bytes); + the 8-byte slot
@@ -1023,53 +1029,86 @@ def gemv_roofline(calls, args, device, world) -> dict:
             "per_launch": per}
 
 
-def measure_e2e(calls, args, device, world, tp: bool = False, reduce=None) -> dict:
+def measure_e2e(calls, args, device, world, tp: bool = False, reduce=None, pipelined: bool = True) -> dict:
     """The same sweep through the public API (hif8_b200.scheme, eager) with
     host buffers inside the timed region: every step copies its 15
     activations from one packed pinned host buffer to the device (one H2D
     transfer), runs the 15 ``scheme.apply`` calls, gathers the 15 outputs
     into one device buffer and reads it back into pinned host memory (one D2H
-    transfer after the step's launches, so the copies do not split the chain
-    of programmatic launches; one transfer instead of 15 saves their host
-    dispatch).  With ``tp`` the calls are this rank's tensor-parallel shards
-    (row-parallel results all-reduced over NCCL inside the step) and value is
-    the sweep's bytes over the slowest rank's time; without it, one
-    independent replica per rank (value aggregates the ranks)."""
+    transfer).  ``pipelined`` (the headline): the copies run on a copy stream
+    and overlap the neighbouring steps' compute, as a serving loop overlaps
+    its transfers -- step i's upload is issued once step i-2 has finished
+    with its input buffer (two buffers), and its read-back as soon as its
+    outputs are gathered; the timed region opens before the first upload and
+    closes after the last read-back.  Without it, every step uploads, computes
+    and reads back in order on one stream.  With ``tp`` the calls are this
+    rank's tensor-parallel shards (row-parallel results all-reduced inside
+    the step) and value is the sweep's bytes over the slowest rank's time;
+    without it, one independent replica per rank (value aggregates the
+    ranks)."""
     import torch
     import torch.distributed as dist
-
-    from hif8_b200 import scheme
 
     sizes = [c["x"].numel() for c in calls]
     offs = [sum(sizes[:i]) for i in range(len(sizes))]
     host_in = torch.cat([c["x"].reshape(-1).cpu() for c in calls]).pin_memory()
-    dev_in = torch.empty(host_in.numel(), dtype=host_in.dtype, device=device)
-    dev_x = [dev_in[o:o + n].view(c["x"].shape) for o, n, c in zip(offs, sizes, calls)]
     out_sizes = [c["m"] * (c["n_loc"] if not c["row_parallel"] else c["n"]) for c in calls]
-    host_out = torch.empty(sum(out_sizes), dtype=torch.bfloat16).pin_memory()
+    slots = 2 if pipelined else 1
+    dev_in = [torch.empty(host_in.numel(), dtype=host_in.dtype, device=device) for _ in range(slots)]
+    dev_x = [[buf[o:o + n].view(c["x"].shape) for o, n, c in zip(offs, sizes, calls)] for buf in dev_in]
+    dev_out = [torch.empty(sum(out_sizes), dtype=torch.bfloat16, device=device) for _ in range(slots)]
+    host_out = [torch.empty(sum(out_sizes), dtype=torch.bfloat16).pin_memory() for _ in range(slots)]
     cur = torch.cuda.current_stream(device)
+    copy = torch.cuda.Stream(device) if pipelined else cur
+    uploaded = [torch.cuda.Event() for _ in range(slots)]
+    computed = [torch.cuda.Event() for _ in range(slots)]
 
-    def step():
-        dev_in.copy_(host_in, non_blocking=True)
+    def compute(slot):
         outs = []
         if tp:
             reduce.begin_step()
-        for c, x in zip(calls, dev_x):
+        for c, x in zip(calls, dev_x[slot]):
             y = tp_apply(c, x, tp)
             if tp and c["row_parallel"]:
                 y = reduce(y)
-            outs.append(y)
-        host_out.copy_(torch.cat([y.reshape(-1) for y in outs]), non_blocking=True)
+            outs.append(y.reshape(-1))
+        torch.cat(outs, out=dev_out[slot])
 
-    for _ in range(max(args.warmup, 1)):
-        step()
+    def run(steps, start=None):
+        if not pipelined:
+            for _ in range(steps):
+                dev_in[0].copy_(host_in, non_blocking=True)
+                compute(0)
+                host_out[0].copy_(dev_out[0], non_blocking=True)
+            return
+        if start is not None:
+            copy.wait_event(start)
+        else:
+            copy.wait_stream(cur)
+        with torch.cuda.stream(copy):
+            for i in range(min(2, steps)):
+                dev_in[i].copy_(host_in, non_blocking=True)
+                uploaded[i].record(copy)
+        for i in range(steps):
+            slot = i % 2
+            cur.wait_event(uploaded[slot])
+            compute(slot)
+            computed[slot].record(cur)
+            copy.wait_event(computed[slot])
+            with torch.cuda.stream(copy):
+                host_out[slot].copy_(dev_out[slot], non_blocking=True)
+                if i + 2 < steps:
+                    dev_in[slot].copy_(host_in, non_blocking=True)
+                    uploaded[slot].record(copy)
+        cur.wait_stream(copy)
+
+    run(max(args.warmup, 1))
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(cur)
-    for _ in range(args.steps):
-        step()
+    run(args.steps, start)
     end.record(cur)
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
@@ -1077,18 +1116,23 @@ def measure_e2e(calls, args, device, world, tp: bool = False, reduce=None) -> di
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    for hy, c in zip(host_out.split(out_sizes), calls):  # the read-back values are the step's results
+    last = (args.steps - 1) % slots
+    if not torch.equal(host_out[last], dev_out[last].cpu()):
+        raise RuntimeError("e2e: the read-back differs from the step's device outputs")
+    for hy, c in zip(host_out[last].split(out_sizes), calls):  # the read-back values are the step's results
         if not torch.isfinite(hy.float()).all():
             raise RuntimeError(f"e2e: non-finite output for {c['name']} M={c['m']}")
     h2d = host_in.numel() * 2
-    d2h = host_out.numel() * 2
+    d2h = host_out[0].numel() * 2
     problems = 1 if tp else world  # TP: one problem split over the ranks; else one per rank
+    how = ("copies on a copy stream overlapping the neighbouring steps' compute (two input buffers)" if pipelined
+           else "upload, compute and read-back in order on one stream")
     return {"value": problems * step_bytes() * args.steps / (ms * 1e-3) / 1e9, "unit": UNIT,
             "h2d_bytes_per_step": world * h2d, "d2h_bytes_per_step": world * d2h, "ms_per_step": ms / args.steps,
             "transfers_per_step": {"h2d": 1, "d2h": 1},
-            "path": "hif8_b200.scheme.apply (eager PyTorch ops -> C ABI), pinned host buffers, outputs gathered on "
-                    "the device and read back in one transfer" + (f", tensor-parallel shards + {reduce.kind} "
-                                                                  "all-reduce" if tp else "")}
+            "path": "hif8_b200.scheme.apply (one hif8_b200::static_linear operator per call -> C ABI), pinned host "
+                    "buffers, outputs gathered on the device and read back in one transfer; " + how +
+                    (f"; tensor-parallel shards + {reduce.kind} all-reduce" if tp else "")}
 
 
 def run_profile_case(spec: str, launches: int) -> None:

@@ -364,8 +364,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
       r = __frcp_rn(ts0);
       r64 = __drcp_rn((double)ts0);
       const uint32_t re = __float_as_uint(r) & 0x7F800000u;
-      exact_only = (re == 0u) | (re == 0x7F800000u) | !(ts0 > 0.f);
+      // the exact FP64 path for every element: zero, negative and non-finite
+      // scales, extreme reciprocals, and scales outside [2^-60, 2^60]
+      exact_only = (re == 0u) | (re == 0x7F800000u) | !(ts0 > 0.f) | !scale_edge_ok(ts0);
     }
+    const float s_half = 0.5f * ts0;
     for (int base = 0; base < real; base += kPro * kThreads) {
       if (base > 0) load_round(base);
 #pragma unroll
@@ -393,9 +396,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_hif8_kernel(const GemvArgs p
             }
             // decode(static code) of the 16 values, bit-identical to
             // hif8_static_quant and a decode of its bytes: the fake-quant
-            // table with its chunk-wide check, else the exact FP64 path
+            // entry of each correctly rounded quotient, or the exact FP64
+            // path (a huge or non-finite product, or a scale that needs it)
             uint32_t r8[8];
-            if (exact_only || !fake_quant16<QSRC>(h8, r, fq, r8)) {
+            if (exact_only || !fake_quant16<QSRC>(h8, ts0, r, s_half, fq, r8)) {
 #pragma unroll
               for (int j = 0; j < 8; ++j)
                 r8[j] = lut[static_code_exact(half_bits_to_f32<QSRC>(h8[j] & 0xFFFFu), r64, mag) * 64 + lane] |
@@ -1035,4 +1039,37 @@ extern "C" int soft_hif8_fused_gemm(const void *x, int x_dtype, const uint8_t *w
   GemvArgs args{codes, weight, scales, channel_scale, bias, out, (int)m, (int)n, (int)k, 0,
                 bias ? bias_dtype : HIF8_DTYPE_NONE, 1};
   return run_linear(args, output_dtype, s);
+}
+
+static size_t round256(size_t bytes) { return (bytes + 255) / 256 * 256; }
+
+extern "C" size_t hif8_static_linear_workspace_size(int64_t m, int64_t n, int64_t k, int fused_max_rows) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  if (m <= fused_max_rows && m <= 4) return 0;
+  return round256((size_t)m * k) + round256((size_t)m * sizeof(float)) + soft_hif8_gemm_workspace_size(m, n, k);
+}
+
+extern "C" int hif8_static_linear(const void *x, int x_dtype, const uint8_t *weight, const float *input_scale,
+                                  const float *channel_scale, const void *bias, int bias_dtype, int output_dtype,
+                                  int64_t m, int64_t n, int64_t k, int fused_max_rows, void *out, void *workspace,
+                                  size_t workspace_bytes, void *stream) {
+  int status = validate_linear(x, weight, input_scale, channel_scale, bias, bias_dtype, output_dtype, m, n, k, out);
+  if (status != HIF8_OK) return status;
+  if (x_dtype != HIF8_DTYPE_F16 && x_dtype != HIF8_DTYPE_BF16) return HIF8_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (m <= fused_max_rows && m <= 4) {
+    GemvArgs args{x, weight, input_scale, channel_scale, bias, out, (int)m, (int)n, (int)k, 0,
+                  bias ? bias_dtype : HIF8_DTYPE_NONE, 0};
+    return run_fused_linear(args, x_dtype, output_dtype, s);
+  }
+  const size_t need = hif8_static_linear_workspace_size(m, n, k, fused_max_rows);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return HIF8_ERR_WORKSPACE;
+  uint8_t *codes = static_cast<uint8_t *>(workspace);
+  float *row_scale = reinterpret_cast<float *>(codes + round256((size_t)m * k));
+  uint8_t *gemm_ws = reinterpret_cast<uint8_t *>(row_scale) + round256((size_t)m * sizeof(float));
+  status = hif8_static_quant(x, x_dtype, m, k, input_scale, 1, codes, row_scale, s);
+  if (status != HIF8_OK) return status;
+  return soft_hif8_gemm(codes, weight, row_scale, channel_scale, bias, bias_dtype, output_dtype, m, n, k, out,
+                        gemm_ws, workspace_bytes - (size_t)(gemm_ws - codes), s);
 }

@@ -264,19 +264,53 @@ __device__ __forceinline__ uint32_t static_code(float f, float r, double r64, bo
   return lo == 0u ? 0u : lo | ((u >> 24) & 0x80u);
 }
 
+// Bits of Q = RN32(x), x = |f| / s, from the product q = RN32(|f| * r),
+// r = RN32(1/s), for a positive scale s in [2^-60, 2^60] (scale_edge_ok)
+// and q below 2^123 -- the quotient that the reference's FP32 division
+// rounds to, without a division.  q is within 1.5 ulp of x (r's relative
+// error is at most 2^-24, the product's rounding adds half an ulp) and Q
+// within half an ulp, so Q is q or one of its neighbours: Q is above q
+// exactly when x exceeds q by more than half the gap to the next float, and
+// below it when x falls short by more than half the gap to the previous one.
+// x is never an FP32 midpoint (a dyadic |f| / s has at most 11 significant
+// bits: s's odd part would have to divide |f|'s), so the comparisons are
+// strict.  They are made on the remainder rho = |f| - q * s (one fused
+// multiply-add) against the half gaps times s (exact: s / 2 times a power of
+// two): rho is an integer multiple of q's and s's unit products, with fewer
+// than 25 significant bits whenever |x - q| <= 1 ulp, so it is exact where it
+// meets a threshold, and where it is not exact (|x - q| > 1 ulp) it lies far
+// from both thresholds.  The sign of a correctly rounded sum is exact, so
+// each test is one more fused multiply-add.  q = 0 gives 0 (its lower gap
+// is NaN; an underflowed nonzero x may step up to the smallest subnormal,
+// whose code is 0 like every value below 2^-23).
+__device__ __forceinline__ uint32_t rn_quotient_bits(float fa, float q, float s, float s_half) {
+  const uint32_t a = __float_as_uint(q);
+  const float rho = __fmaf_rn(-q, s, fa);
+  const float up = __uint_as_float(a + 1u) - q;
+  const float dn = q - __uint_as_float(a - 1u);
+  const uint32_t above = __fmaf_rn(-up, s_half, rho) > 0.f ? 1u : 0u;
+  const uint32_t below = __fmaf_rn(dn, s_half, rho) < 0.f ? 1u : 0u;
+  return a + above - below;
+}
+
+// True when rn_quotient_bits may be used with scale s: 2^-60 <= s <= 2^60.
+__device__ __forceinline__ bool scale_edge_ok(float s) {
+  const uint32_t u = __float_as_uint(s);
+  return u - 0x21800000u <= 0x5D800000u - 0x21800000u;
+}
+
 // Static codes of 16 consecutive FP16/BF16 elements (w: their 8 words,
-// element 2i in the low half of w[i]) by the product with the reciprocal r
-// of a POSITIVE fixed scale, four codes per output word in element order:
-// the rule of static_code with one check for the whole chunk (every
-// element's codes at |q| -+ 4 ulp agree, every |q| below 2^123).  Returns
-// false when any element fails -- the caller then takes static_codes16_exact
-// (a chunk-wide branch keeps a warp's lanes together where a per-element one
-// would not).  Each nonzero code gets its element's sign, read straight from
-// the input words.
+// element 2i in the low half of w[i]) with a POSITIVE fixed scale s in the
+// range of scale_edge_ok (r = RN32(1/s), s_half = s / 2), four codes per
+// output word in element order: the table entry of each element's correctly
+// rounded quotient (rn_quotient_bits).  Returns false when some product
+// reaches 2^123 or is NaN / Inf -- the caller then takes
+// static_codes16_exact for the chunk.  Each nonzero code gets its element's
+// sign, read straight from the input words.
 template <int kDtype>
-__device__ __forceinline__ bool static_codes16(const uint32_t (&w)[8], float r, const uint8_t *__restrict__ mag,
-                                               uint32_t (&out)[4]) {
-  uint32_t diff = 0u, amax = 0u;
+__device__ __forceinline__ bool static_codes16(const uint32_t (&w)[8], float s, float r, float s_half,
+                                               const uint8_t *__restrict__ mag, uint32_t (&out)[4]) {
+  uint32_t amax = 0u;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint32_t c[4];
@@ -286,10 +320,10 @@ __device__ __forceinline__ bool static_codes16(const uint32_t (&w)[8], float r, 
       float f;
       if constexpr (kDtype == HIF8_DTYPE_BF16) f = __uint_as_float((e & 1) ? (word & 0xFFFF0000u) : (word << 16));
       else f = __half2float(__ushort_as_half((unsigned short)((e & 1) ? (word >> 16) : (word & 0xFFFFu))));
-      const uint32_t a = max(__float_as_uint(__fmul_rn(f, r)) & 0x7FFFFFFFu, 4u);
-      amax = max(amax, a);
-      c[e] = mag[(a - 4u) >> 19];
-      diff |= c[e] ^ mag[((a + 4u) >> 19) & 0xFFFu];  // masked: see static_code
+      const float fa = fabsf(f);
+      const float q = __fmul_rn(fa, r);
+      amax = max(amax, __float_as_uint(q));
+      c[e] = mag[(rn_quotient_bits(fa, q, s, s_half) >> 19) & 0xFFFu];
     }
     const uint32_t codes = __byte_perm(__byte_perm(c[0], c[1], 0x0040u), __byte_perm(c[2], c[3], 0x0040u), 0x5410u);
     // bit 7 of every byte: the element's sign (bit 15 of each FP16/BF16)
@@ -297,7 +331,7 @@ __device__ __forceinline__ bool static_codes16(const uint32_t (&w)[8], float r, 
     // codes are below 0x80, so + 0x7F sets bit 7 of exactly the nonzero ones
     out[j] = codes | (signs & (codes + 0x7F7F7F7Fu) & 0x80808080u);
   }
-  return diff == 0u && amax < 0x7D000000u;
+  return amax < 0x7D000000u;
 }
 
 // The 16 codes by static_code_exact.
@@ -317,17 +351,52 @@ __device__ __forceinline__ void static_codes16_exact(const uint32_t (&w)[8], dou
   }
 }
 
-// BF16 payloads of decode(static code) of 16 FP16/BF16 elements (w: their 8
-// words, element 2i in the low half of w[i]) quantised with the reciprocal r
-// of a POSITIVE fixed scale, two per output word in element order -- the
-// rule of static_codes16 with the decoded values looked up directly
-// (`fq`: shared-memory copy of g_fake_quant_bf16); the values at |q| -+ 4 ulp
-// also serve as the check.  Returns false when any element needs the exact
-// path.  A nonzero value takes its element's sign from the input word.
+// True when s is a positive normal power of two: its reciprocal r is then
+// exact, so f * r is the exact quotient f / s rounded once -- RN32(f / s)
+// itself, overflow and underflow included.
+__device__ __forceinline__ bool scale_is_pow2(float s) {
+  const uint32_t u = __float_as_uint(s);
+  return (u & 0x007FFFFFu) == 0u && u - 0x00800000u < 0x7F000000u;
+}
+
+// Static codes of 16 elements for a power-of-two scale (r = 1 / s exact):
+// the product is the correctly rounded quotient, so its table entry is the
+// code, with no check (NaN gives 0x80).
 template <int kDtype>
-__device__ __forceinline__ bool fake_quant16(const uint32_t (&w)[8], float r, const uint16_t *__restrict__ fq,
-                                             uint32_t (&out)[8]) {
-  uint32_t diff = 0u, amax = 0u;
+__device__ __forceinline__ void static_codes16_pow2(const uint32_t (&w)[8], float r, const uint8_t *__restrict__ mag,
+                                                    uint32_t (&out)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t c[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t word = w[2 * j + (e >> 1)];
+      float f;
+      if constexpr (kDtype == HIF8_DTYPE_BF16) f = __uint_as_float((e & 1) ? (word & 0xFFFF0000u) : (word << 16));
+      else f = __half2float(__ushort_as_half((unsigned short)((e & 1) ? (word >> 16) : (word & 0xFFFFu))));
+      const uint32_t a = __float_as_uint(__fmul_rn(f, r)) & 0x7FFFFFFFu;
+      c[e] = a > 0x7F800000u ? 0x80u : (uint32_t)mag[a >> 19];
+    }
+    const uint32_t codes = __byte_perm(__byte_perm(c[0], c[1], 0x0040u), __byte_perm(c[2], c[3], 0x0040u), 0x5410u);
+    const uint32_t signs = __byte_perm(w[2 * j], w[2 * j + 1], 0x7531u);
+    // the NaN code 0x80 keeps bit 7 whatever the sign; other codes are below 0x80
+    out[j] = codes | (signs & (codes + 0x7F7F7F7Fu) & 0x80808080u);
+  }
+}
+
+
+// BF16 payloads of decode(static code) of 16 FP16/BF16 elements (w: their 8
+// words, element 2i in the low half of w[i]) quantised with a POSITIVE
+// fixed scale s (scale_edge_ok; r = RN32(1/s), s_half = s / 2), two per
+// output word in element order -- the rule of static_codes16 with the
+// decoded values looked up directly (`fq`: shared-memory copy of
+// g_fake_quant_bf16).  Returns false when some product reaches 2^123 or is
+// NaN / Inf (the caller takes the exact path).  A nonzero value takes its
+// element's sign from the input word.
+template <int kDtype>
+__device__ __forceinline__ bool fake_quant16(const uint32_t (&w)[8], float s, float r, float s_half,
+                                             const uint16_t *__restrict__ fq, uint32_t (&out)[8]) {
+  uint32_t amax = 0u;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     uint32_t v[2];
@@ -336,16 +405,16 @@ __device__ __forceinline__ bool fake_quant16(const uint32_t (&w)[8], float r, co
       float f;
       if constexpr (kDtype == HIF8_DTYPE_BF16) f = __uint_as_float(e ? (w[j] & 0xFFFF0000u) : (w[j] << 16));
       else f = __half2float(__ushort_as_half((unsigned short)(e ? (w[j] >> 16) : (w[j] & 0xFFFFu))));
-      const uint32_t a = max(__float_as_uint(__fmul_rn(f, r)) & 0x7FFFFFFFu, 4u);
-      amax = max(amax, a);
-      v[e] = fq[(a - 4u) >> 19];
-      diff |= v[e] ^ fq[((a + 4u) >> 19) & 0xFFFu];  // masked: see static_code
+      const float fa = fabsf(f);
+      const float q = __fmul_rn(fa, r);
+      amax = max(amax, __float_as_uint(q));
+      v[e] = fq[(rn_quotient_bits(fa, q, s, s_half) >> 19) & 0xFFFu];
     }
     const uint32_t pair = v[0] | (v[1] << 16);
     // payloads are below 0x8000: + 0x7FFF sets bit 15 of exactly the nonzero ones
     out[j] = pair | (w[j] & (pair + 0x7FFF7FFFu) & 0x80008000u);
   }
-  return diff == 0u && amax < 0x7D000000u;
+  return amax < 0x7D000000u;
 }
 
 // Lane-replicated FP32 decode table in shared memory (32 KB): entry b of

@@ -131,7 +131,8 @@ __global__ void __launch_bounds__(256) kv_write_kernel(const KvWriteArgs p) {
       // the 16-element chunk path (one check per chunk); each element by
       // division-capable static_code where that check fails
       if constexpr (ELEMS == 16) {
-        if (exact_only || !static_codes16<kDtype>(w, r, tbl, o)) static_codes16_exact<kDtype>(w, r64, tbl, o);
+        if (exact_only || !scale_edge_ok(s) || !static_codes16<kDtype>(w, s, r, 0.5f * s, tbl, o))
+          static_codes16_exact<kDtype>(w, r64, tbl, o);
       } else {
         const uint32_t lo = w[0], hi = w[1];
         const uint32_t b0 = kv_quant_one(half_bits_to_f32<kDtype>(lo & 0xFFFFu), r, r64, exact_only, tbl);
@@ -144,6 +145,132 @@ __global__ void __launch_bounds__(256) kv_write_kernel(const KvWriteArgs p) {
       for (int j = 0; j < ELEMS / 4; ++j) dst[j] = o[j];
       if (chunk[u] == upr - 1) *reinterpret_cast<float *>(dst_row + p.d) = s;
     }
+  }
+}
+
+// One warp per (plane, token): the token's heads x D source elements (one
+// contiguous run: head rows are D apart inside a token) are quantised into a
+// shared-memory image of the token's page row group -- heads rows of D codes
+// and the FP32 scale, (D + 4) bytes apart -- and the warp then writes the
+// group (slot * heads * (D + 4) bytes into the cache) with consecutive
+// lanes on consecutive 16-byte words (4-byte words when the group size or
+// base is not a multiple of 16): full, coalesced sectors instead of four
+// 4-byte stores per 16 codes 16 bytes apart.  Chunk c (16 elements) of the
+// token is head c >> kv_shift, offset (c & (D/16 - 1)) * 16: D / 16 is a
+// power of two, so no division.  Scales that are powers of two take the
+// check-free encode.  kKvWarpKeep chunks per lane are loaded before any is
+// encoded.
+constexpr int kKvWarps = 8;      // warps per CTA
+constexpr int kKvWarpKeep = 2;   // 16-element chunks per lane in flight
+constexpr int kKvGroupMax = 8192;  // largest row group (heads * (D + 4) bytes) staged per warp
+
+struct KvWarpArgs {
+  KvWriteArgs p;
+  int shift;           // log2(D / 16)
+  int group;           // heads * (D + 4) bytes
+  int group_stage;     // group rounded up to 16 bytes (per-warp stage stride)
+  int store16;         // the groups of both caches start on 16-byte boundaries
+};
+
+template <int kDtype>
+__global__ void __launch_bounds__(kKvWarps * 32, 3) kv_write_warp_kernel(const KvWarpArgs a) {
+  extern __shared__ __align__(16) uint8_t kv_smem[];
+  uint8_t *tbl = kv_smem;                                  // 4 KB encode table
+  float *sh_s = reinterpret_cast<float *>(kv_smem + 4096);  // [2][kKvScaleSlots]
+  float *sh_r = sh_s + 2 * kKvScaleSlots;
+  uint32_t *sh_mode = reinterpret_cast<uint32_t *>(sh_r + 2 * kKvScaleSlots);  // 0 check, 1 pow2, 2 exact only
+  double *sh_r64 = reinterpret_cast<double *>(sh_mode + 2 * kKvScaleSlots);
+  uint8_t *stage_all = reinterpret_cast<uint8_t *>(sh_r64 + 2 * kKvScaleSlots);
+  const KvWriteArgs &p = a.p;
+  load_encode_mag_table(tbl);  // module data: before the dependency wait
+  pdl_wait();                  // inputs come from the previous kernel of the stream
+  for (int i = threadIdx.x; i < p.planes * p.heads; i += blockDim.x) {
+    const int plane = i / (int)p.heads, h = i - plane * (int)p.heads;
+    const float sc = p.scale[plane][h];
+    bool exact_only, pow2;
+    double r64;
+    const float r = __frcp_rn(sc);
+    const uint32_t re = __float_as_uint(r) & 0x7F800000u;
+    exact_only = (re == 0u) | (re == 0x7F800000u) | !(sc > 0.f);
+    pow2 = scale_is_pow2(sc);
+    r64 = __drcp_rn((double)sc);
+    sh_s[plane * kKvScaleSlots + h] = sc;
+    sh_r[plane * kKvScaleSlots + h] = r;
+    sh_r64[plane * kKvScaleSlots + h] = r64;
+    // 0: quotient from the product, 1: power of two, 2: exact FP64 path
+    sh_mode[plane * kKvScaleSlots + h] = exact_only || !scale_edge_ok(sc) ? 2u : (pow2 ? 1u : 0u);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint8_t *stage = stage_all + warp * a.group_stage;
+  const int d = (int)p.d, width = d + 4;
+  const int nchunks = (int)p.heads << a.shift;  // 16-element chunks per token
+  const int64_t items = (int64_t)p.planes * p.tokens;
+  for (int64_t it = (int64_t)blockIdx.x * kKvWarps + warp; it < items; it += (int64_t)gridDim.x * kKvWarps) {
+    const int plane = it >= p.tokens;
+    const int64_t tok = it - (plane ? p.tokens : 0);
+    const int64_t slot = __ldg(p.slots + tok);  // warp-uniform
+    const uint4 *src = reinterpret_cast<const uint4 *>(p.src[plane] + tok * p.token_stride);
+    // the first source loads go out with the slot load (they do not depend
+    // on it), so the two latencies overlap
+    uint4 va[kKvWarpKeep], vb[kKvWarpKeep];
+#pragma unroll
+    for (int u = 0; u < kKvWarpKeep; ++u) {
+      const int c = u * 32 + lane;
+      if (c < nchunks) {
+        va[u] = __ldcs(src + 2 * c);
+        vb[u] = __ldcs(src + 2 * c + 1);
+      }
+    }
+    if (slot < 0) continue;
+    if (slot >= p.cache_slots) {
+      if (p.bad_slots && plane == 0 && lane == 0) atomicAdd(p.bad_slots, 1);
+      continue;
+    }
+    for (int c0 = 0; c0 < nchunks; c0 += 32 * kKvWarpKeep) {
+      if (c0 > 0) {
+#pragma unroll
+        for (int u = 0; u < kKvWarpKeep; ++u) {
+          const int c = c0 + u * 32 + lane;
+          if (c < nchunks) {
+            va[u] = __ldcs(src + 2 * c);
+            vb[u] = __ldcs(src + 2 * c + 1);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kKvWarpKeep; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c >= nchunks) break;
+        const int h = c >> a.shift;
+        const int slot_h = plane * kKvScaleSlots + h;
+        const float r = sh_r[slot_h];
+        const uint32_t mode = sh_mode[slot_h];
+        const uint32_t w[8] = {va[u].x, va[u].y, va[u].z, va[u].w, vb[u].x, vb[u].y, vb[u].z, vb[u].w};
+        uint32_t o[4];
+        if (mode == 1u) {
+          static_codes16_pow2<kDtype>(w, r, tbl, o);
+        } else if (mode == 2u ||
+                   !static_codes16<kDtype>(w, sh_s[slot_h], r, 0.5f * sh_s[slot_h], tbl, o)) {
+          static_codes16_exact<kDtype>(w, sh_r64[slot_h], tbl, o);
+        }
+        uint32_t *dst = reinterpret_cast<uint32_t *>(stage + h * width + ((c & ((1 << a.shift) - 1)) << 4));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dst[j] = o[j];
+      }
+    }
+    for (int h = lane; h < (int)p.heads; h += 32)
+      *reinterpret_cast<float *>(stage + h * width + d) = sh_s[plane * kKvScaleSlots + h];
+    __syncwarp();
+    uint8_t *dst = p.cache[plane] + slot * (int64_t)a.group;
+    if (a.store16) {
+      for (int i = lane; i < (a.group >> 4); i += 32)
+        __stcs(reinterpret_cast<uint4 *>(dst) + i, reinterpret_cast<const uint4 *>(stage)[i]);
+    } else {
+      for (int i = lane; i < (a.group >> 2); i += 32)
+        __stcs(reinterpret_cast<uint32_t *>(dst) + i, reinterpret_cast<const uint32_t *>(stage)[i]);
+    }
+    __syncwarp();  // the stage is rewritten by the warp's next token
   }
 }
 
@@ -843,12 +970,32 @@ extern "C" int hif8_kv_cache_write(const void *key, const void *value, int src_d
   const bool vec16 = head_size % 16 == 0 && src_token_stride % 8 == 0 &&
                      (reinterpret_cast<uintptr_t>(key) & 15u) == 0 &&
                      (!value || (reinterpret_cast<uintptr_t>(value) & 15u) == 0);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf16 = src_dtype == HIF8_DTYPE_BF16;
+  const int64_t group = kv_heads * (head_size + 4);
+  const int64_t per_head = head_size / 16;
+  if (vec16 && (per_head & (per_head - 1)) == 0 && kv_heads <= kKvScaleSlots && group <= kKvGroupMax) {
+    // the warp-per-token kernel: D / 16 a power of two, the row group staged
+    KvWarpArgs a{};
+    a.p = p;
+    a.shift = 0;
+    while ((1LL << a.shift) < per_head) ++a.shift;
+    a.group = (int)group;
+    a.group_stage = (int)((group + 15) / 16 * 16);
+    a.store16 = group % 16 == 0 && (reinterpret_cast<uintptr_t>(key_cache) & 15u) == 0 &&
+                (!value_cache || (reinterpret_cast<uintptr_t>(value_cache) & 15u) == 0);
+    const size_t smem = 4096 + 2 * kKvScaleSlots * (4 + 4 + 4 + 8) + (size_t)kKvWarps * a.group_stage;
+    const int64_t items = p.planes * tokens;
+    const int grid = attn_grid_cap((items + kKvWarps - 1) / kKvWarps);
+    auto kernel = bf16 ? kv_write_warp_kernel<HIF8_DTYPE_BF16> : kv_write_warp_kernel<HIF8_DTYPE_F16>;
+    const int st = ensure_smem_limit(reinterpret_cast<const void *>(kernel), smem);
+    if (st != HIF8_OK) return st;
+    return launch_pdl(kernel, dim3(grid), dim3(kKvWarps * 32), smem, s, a);
+  }
   const int elems = vec16 ? 16 : 4;
   p.units = p.planes * tokens * kv_heads * (head_size / elems);
   if (p.units > 0x7FFFFFFFLL) return HIF8_ERR_INVALID_ARGUMENT;  // 32-bit unit indices
   const int grid = attn_grid_cap((p.units + 255) / 256);  // one wave at most; then kKvUnroll per step
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool bf16 = src_dtype == HIF8_DTYPE_BF16;
   if (vec16)
     return bf16 ? launch_pdl(kv_write_kernel<HIF8_DTYPE_BF16, 16>, dim3(grid), dim3(256), 0, s, p)
                 : launch_pdl(kv_write_kernel<HIF8_DTYPE_F16, 16>, dim3(grid), dim3(256), 0, s, p);

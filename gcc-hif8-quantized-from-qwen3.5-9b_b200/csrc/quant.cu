@@ -40,21 +40,45 @@ __device__ __forceinline__ void write_row_scale(const float *__restrict__ scale,
 // per thread (kPerRow: once per change of the scale along the thread's
 // chunks), and a chunk's row is a 32-bit division only when scales differ
 // per row (chunks < 2^32, checked by the launcher).
-constexpr int kQuantUnroll = 4;
+constexpr int kQuantUnroll = 2;
+
+// The scale's encode mode: kModeQuotient (the correctly rounded quotient
+// from the product, static_codes16), kModePow2 (power of two: the product is
+// the quotient), kModeExact (every element by the exact FP64 path: zero,
+// negative and non-finite scales, and scales outside [2^-60, 2^60]).
+struct QuantScale {
+  float s, r, s_half;
+  double r64;
+  int mode;
+};
+constexpr int kModeQuotient = 0, kModePow2 = 1, kModeExact = 2;
+
+__device__ __forceinline__ QuantScale quant_scale(float s) {
+  QuantScale q;
+  bool exact_only;
+  q.s = s;
+  q.s_half = 0.5f * s;
+  q.r = reciprocal(s, exact_only, q.r64);
+  q.mode = exact_only || !scale_edge_ok(s) ? kModeExact : (scale_is_pow2(s) ? kModePow2 : kModeQuotient);
+  return q;
+}
 
 template <int kDtype>
-__device__ __forceinline__ uint4 quant_chunk(const uint4 a, const uint4 b, float r, double r64, bool exact_only,
+__device__ __forceinline__ uint4 quant_chunk(const uint4 a, const uint4 b, const QuantScale &q,
                                              const uint8_t *__restrict__ tbl) {
   const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
   uint32_t o[4];
-  // some element within 4 ulp of a code boundary (or zero, or huge): the
-  // whole chunk by the exact FP64 path
-  if (exact_only || !static_codes16<kDtype>(w, r, tbl, o)) static_codes16_exact<kDtype>(w, r64, tbl, o);
+  if (q.mode == kModePow2) {
+    static_codes16_pow2<kDtype>(w, q.r, tbl, o);
+  } else if (q.mode == kModeExact || !static_codes16<kDtype>(w, q.s, q.r, q.s_half, tbl, o)) {
+    // a huge or non-finite product in the chunk (or an extreme scale)
+    static_codes16_exact<kDtype>(w, q.r64, tbl, o);
+  }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 template <int kDtype, bool kPerRow>
-__global__ void __launch_bounds__(256) static_quant_vec16(const uint16_t *__restrict__ x, int64_t k,
+__global__ void __launch_bounds__(256, 4) static_quant_vec16(const uint16_t *__restrict__ x, int64_t k,
                                                           const float *__restrict__ scale,
                                                           int64_t scale_count, uint8_t *__restrict__ out,
                                                           int64_t chunks, float *__restrict__ row_scale,
@@ -71,10 +95,7 @@ __global__ void __launch_bounds__(256) static_quant_vec16(const uint16_t *__rest
   __syncthreads();
   const uint32_t chunks_per_row = (uint32_t)(k >> 4);
   int64_t cur = 0;  // scale index of s / r
-  float s = __ldg(scale);
-  bool exact_only;
-  double r64;
-  float r = reciprocal(s, exact_only, r64);
+  QuantScale qs = quant_scale(__ldg(scale));
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t c0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c0 < chunks; c0 += kQuantUnroll * stride) {
     uint4 a[kQuantUnroll], b[kQuantUnroll];
@@ -95,11 +116,10 @@ __global__ void __launch_bounds__(256) static_quant_vec16(const uint16_t *__rest
         const int64_t sidx = (int64_t)((uint32_t)c / chunks_per_row) % scale_count;
         if (sidx != cur) {
           cur = sidx;
-          s = __ldg(scale + sidx);
-          r = reciprocal(s, exact_only, r64);
+          qs = quant_scale(__ldg(scale + sidx));
         }
       }
-      __stcs(reinterpret_cast<uint4 *>(out + (c << 4)), quant_chunk<kDtype>(a[u], b[u], r, r64, exact_only, tbl));
+      __stcs(reinterpret_cast<uint4 *>(out + (c << 4)), quant_chunk<kDtype>(a[u], b[u], qs, tbl));
     }
   }
 }
@@ -227,21 +247,19 @@ __global__ void __launch_bounds__(kDynThreads) dynamic_quant_vec16(const uint16_
     const bool floor_row = !(amax > kDynFloorScaleF);
     const float s = floor_row ? kDynFloorScaleF : amax;
     if (tid == 0 && row_scale) row_scale[row * scale_stride] = s;
-    bool exact_only;
-    double r64;
-    const float r = reciprocal(s, exact_only, r64);
+    const QuantScale qs = quant_scale(s);
     uint4 *orow = reinterpret_cast<uint4 *>(out + row * k);
 #pragma unroll
     for (int u = 0; u < kDynKeep; ++u) {
       const int64_t c = tid + (int64_t)u * kDynThreads;
       if (c < chunks)
         __stcs(orow + c, floor_row ? floor_chunk<kDtype>(a[u], b[u], tbl)
-                                   : quant_chunk<kDtype>(a[u], b[u], r, r64, exact_only, tbl));
+                                   : quant_chunk<kDtype>(a[u], b[u], qs, tbl));
     }
     for (int64_t c = tid + (int64_t)kDynKeep * kDynThreads; c < chunks; c += kDynThreads) {
       const uint4 a1 = __ldg(xr + 2 * c), b1 = __ldg(xr + 2 * c + 1);
       __stcs(orow + c, floor_row ? floor_chunk<kDtype>(a1, b1, tbl)
-                                 : quant_chunk<kDtype>(a1, b1, r, r64, exact_only, tbl));
+                                 : quant_chunk<kDtype>(a1, b1, qs, tbl));
     }
     __syncthreads();  // warp_max is rewritten by the next row
   }

@@ -642,6 +642,70 @@ at::Tensor Hif8LinearPartialF32(const at::Tensor &x_in, const at::Tensor &weight
   return out;
 }
 
+// The static scheme's apply (reference scheme.py:174-211) as one operator:
+// the routing between the fused quant + linear (rows <= fused_max_rows) and
+// quant then linear happens here, so a projection costs one dispatch.  The
+// checks are the ones the two reference operators make, with their messages.
+at::Tensor Hif8StaticLinear(const at::Tensor &x_in, const at::Tensor &weight, const at::Tensor &input_scale,
+                            const at::Tensor &weight_scale, const std::optional<at::Tensor> &bias,
+                            int64_t fused_max_rows) {
+  TORCH_CHECK(x_in.defined() && x_in.is_cuda(), "x must be a CUDA tensor");
+  TORCH_CHECK(x_in.scalar_type() == at::ScalarType::Half || x_in.scalar_type() == at::ScalarType::BFloat16,
+              "x must have dtype torch.float16 or torch.bfloat16");
+  TORCH_CHECK(x_in.dim() >= 2, "x must have shape [..., K]");
+  // a contiguous view at any 16-byte aligned offset is used in place; any
+  // other layout is copied (to an aligned allocation, so the kernels take
+  // the same vector paths -- and give the same bits -- as for an owned tensor)
+  const bool in_place = x_in.is_contiguous() && (reinterpret_cast<uintptr_t>(x_in.data_ptr()) & 15u) == 0;
+  const at::Tensor x = in_place ? x_in : x_in.contiguous().clone();
+  CheckCudaTensor(weight, "weight");
+  CheckCudaTensor(input_scale, "fixed_scale");
+  CheckCudaTensor(weight_scale, "channel_scale");
+  TORCH_CHECK(weight.scalar_type() == at::ScalarType::Byte, "weight must have dtype torch.uint8");
+  TORCH_CHECK(weight.dim() == 2, "weight must have shape [N, K]");
+  TORCH_CHECK(input_scale.scalar_type() == at::ScalarType::Float, "fixed_scale must have dtype torch.float32");
+  TORCH_CHECK(input_scale.numel() == 1, "fixed_scale must have shape [1]");
+  TORCH_CHECK(weight_scale.scalar_type() == at::ScalarType::Float, "channel_scale must have dtype torch.float32");
+  CheckPositiveDimensions(x, "activation");
+  CheckPositiveDimensions(weight, "weight");
+  const int64_t k = x.size(-1), m = x.numel() / k, n = weight.size(0);
+  TORCH_CHECK(weight.size(1) == k, "activation and weight K dimensions differ: ", k, " != ", weight.size(1));
+  TORCH_CHECK(weight_scale.numel() == n, "channel_scale must contain one value per output channel");
+  CheckFitsUint32(m, "M");
+  CheckFitsUint32(n, "N");
+  CheckFitsUint32(k, "K");
+  const auto device = x.device();
+  CheckSameDevice(weight, device, "weight");
+  CheckSameDevice(input_scale, device, "fixed_scale");
+  CheckSameDevice(weight_scale, device, "channel_scale");
+  const void *bias_ptr = nullptr;
+  int bias_dtype = HIF8_DTYPE_NONE;
+  if (bias.has_value()) {
+    CheckCudaTensor(*bias, "bias");
+    CheckSameDevice(*bias, device, "bias");
+    TORCH_CHECK(bias->dim() == 1, "bias must have shape [N]");
+    TORCH_CHECK(bias->numel() == n, "bias must contain N values");
+    TORCH_CHECK(bias->scalar_type() == at::ScalarType::Half || bias->scalar_type() == at::ScalarType::BFloat16,
+                "bias must have dtype torch.float16 or torch.bfloat16");
+    bias_ptr = bias->data_ptr();
+    bias_dtype = DtypeCode(bias->scalar_type());
+  }
+  c10::cuda::CUDAGuard guard(device);
+  std::vector<int64_t> out_shape(x.sizes().begin(), x.sizes().end());
+  out_shape.back() = n;
+  auto out = at::empty(out_shape, x.options());
+  const int fused = (int)std::max<int64_t>(0, std::min<int64_t>(fused_max_rows, 4));
+  const size_t ws_bytes = hif8_static_linear_workspace_size(m, n, k, fused);
+  at::Tensor ws;
+  if (ws_bytes) ws = at::empty({(int64_t)ws_bytes}, x.options().dtype(at::kByte));
+  const int dtype = DtypeCode(x.scalar_type());
+  CheckStatus(hif8_static_linear(x.data_ptr(), dtype, weight.data_ptr<uint8_t>(), input_scale.data_ptr<float>(),
+                                 weight_scale.data_ptr<float>(), bias_ptr, bias_dtype, dtype, m, n, k, fused,
+                                 out.data_ptr(), ws_bytes ? ws.data_ptr() : nullptr, ws_bytes, Stream(x)),
+              "hif8_static_linear");
+  return out;
+}
+
 std::tuple<at::Tensor, at::Tensor> ModelPeerAllreduceRmsnorm(const at::Tensor &local,
                                                              const std::optional<at::Tensor> &residual,
                                                              const at::Tensor &weight, const at::Tensor &peer_buf,
@@ -820,6 +884,17 @@ TORCH_LIBRARY(hif8_b200, m) {
   m.def("peer_allreduce(Tensor local, Tensor peer_buf, Tensor(a!) counter, Tensor(b!) error, int max_rows, int rank, "
         "int world, int slot, int timeout_ns) -> Tensor");
   m.def("linear_partial_f32(Tensor x, Tensor weight, Tensor input_scale, Tensor weight_scale) -> Tensor");
+  m.def("static_linear(Tensor x, Tensor weight, Tensor input_scale, Tensor weight_scale, Tensor? bias=None, "
+        "int fused_max_rows=4) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(hif8_b200, Meta, m) {
+  m.impl("static_linear", [](const at::Tensor &x, const at::Tensor &weight, const at::Tensor &, const at::Tensor &,
+                             const std::optional<at::Tensor> &, int64_t) -> at::Tensor {
+    std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end());
+    shape.back() = weight.size(0);
+    return at::empty(shape, x.options());
+  });
 }
 
 TORCH_LIBRARY_IMPL(hif8_b200, CUDA, m) {
@@ -836,4 +911,5 @@ TORCH_LIBRARY_IMPL(hif8_b200, CUDA, m) {
   m.impl("peer_allreduce_rmsnorm", &ModelPeerAllreduceRmsnorm);
   m.impl("peer_allreduce", &ModelPeerAllreduce);
   m.impl("linear_partial_f32", &Hif8LinearPartialF32);
+  m.impl("static_linear", &Hif8StaticLinear);
 }

@@ -43,6 +43,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hif8_dynamic_quant": (_INT, [_P, _INT, _I64, _I64, _P, _P, _I64, _P]),
     "soft_hif8_fused_gemm_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "soft_hif8_fused_gemm": (_INT, [_P, _INT, _P, _P, _P, _INT, _INT, _I64, _I64, _I64, _P, _P, _SZ, _P]),
+    "hif8_static_linear_workspace_size": (_SZ, [_I64, _I64, _I64, _INT]),
+    "hif8_static_linear": (_INT, [_P, _INT, _P, _P, _P, _P, _INT, _INT, _I64, _I64, _I64, _INT, _P, _P, _SZ, _P]),
     "hif8_static_fused_linear_partial_f32": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soft_hif8_static_fused_gemm": (_INT, [_P, _INT, _P, _P, _P, _P, _INT, _INT, _I64, _I64, _I64, _P, _P]),
     "hif8_kv_cache_write": (_INT, [_P, _P, _INT, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _P]),
@@ -147,6 +149,25 @@ def gemm(activation, weight, token_scale, channel_scale, bias, out, workspace=No
         _ptr(activation), _ptr(weight), _ptr(token_scale), _ptr(channel_scale), _ptr(bias),
         HIF8_DTYPE_NONE if bias is None else _dtype_code(bias.dtype), _dtype_code(out.dtype), m, n, k, _ptr(out),
         _ptr(workspace), ws_bytes, _stream(out)))
+
+
+def static_linear(x, weight, input_scale, channel_scale, bias, out, fused_max_rows: int = 4, workspace=None) -> None:
+    """The static scheme's quant + linear pair in one C-ABI call."""
+    k = x.shape[-1]
+    m = x.numel() // k
+    n = weight.shape[0]
+    lib = library()
+    need = lib.hif8_static_linear_workspace_size(m, n, k, fused_max_rows)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    if need and workspace is None:
+        import torch
+
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+        ws_bytes = need
+    check("hif8_static_linear", lib.hif8_static_linear(
+        _ptr(x), _dtype_code(x.dtype), _ptr(weight), _ptr(input_scale), _ptr(channel_scale), _ptr(bias),
+        HIF8_DTYPE_NONE if bias is None else _dtype_code(bias.dtype), _dtype_code(out.dtype), m, n, k,
+        fused_max_rows, _ptr(out), _ptr(workspace), ws_bytes, _stream(out)))
 
 
 def gemv(activation, weight, token_scale, channel_scale, bias, out) -> None:

@@ -93,9 +93,11 @@ def is_available() -> bool:
 
 def reset_extension_cache() -> None:
     """Reset loader state for isolated tests."""
-    global _extension, _load_error
+    global _extension, _load_error, _static_linear_op
     _extension = None
     _load_error = None
+    _static_linear_op = None
+    _OPS.clear()
     _reset_loader()
 
 
@@ -297,6 +299,24 @@ def soft_static_fused_linear(
     channel_scale = _as_native_operand(_flat1d(weight_scale))
     output = _op("soft_hif8_static_fused_gemm")(flattened, weight, fixed, channel_scale, bias, output_dtype)
     return output if x.dim() == 2 else output.reshape(*x.shape[:-1], weight.shape[0])
+
+
+_static_linear_op = None
+
+
+def static_linear(x, weight, input_scale, weight_scale, bias=None, fused_max_rows: int = 4):
+    """Static quant + HiF8 linear as ONE operator (hif8_b200::static_linear),
+    output in x's dtype: the pair of calls the static scheme's apply makes,
+    routed in the operator.  The operator checks its arguments with the
+    messages of the two reference operators it replaces."""
+    global _static_linear_op
+    op = _static_linear_op
+    if op is None:
+        import torch
+
+        load_extension()
+        op = _static_linear_op = torch.ops.hif8_b200.static_linear.default
+    return op(x, weight, input_scale, weight_scale, bias, fused_max_rows)
 
 
 def _validate_quantized_activation(source, data, scale, *, operation: str = "hif8_static_quant") -> None:

@@ -34,9 +34,17 @@ _FUSED_MAX_ROWS = 4
 _SOFT_FUSED_MAX_ROWS = 2
 
 
+# (raw environment string, parsed factor) of the last valid read: apply
+# re-reads the variable on every call, and parses it only when it changed
+_factor_cache: tuple = (None, 1.0)
+
+
 def static_scale_factor() -> float:
     """Optional constant multiplier of calibrated input scales (scheme.py:26-40)."""
+    global _factor_cache
     raw = os.environ.get(_STATIC_SCALE_FACTOR_ENV)
+    if raw == _factor_cache[0]:
+        return _factor_cache[1]
     if raw is None or raw == "":
         return 1.0
     try:
@@ -45,6 +53,7 @@ def static_scale_factor() -> float:
         raise ValueError(f"{_STATIC_SCALE_FACTOR_ENV} must be a positive finite float") from exc
     if not math.isfinite(value) or value <= 0.0:
         raise ValueError(f"{_STATIC_SCALE_FACTOR_ENV} must be a positive finite float")
+    _factor_cache = (raw, value)
     return value
 
 
@@ -79,19 +88,19 @@ def process_weights_after_loading(layer) -> None:
 
 
 def apply(layer, x, bias=None):
-    """Static activation quant + HiF8 linear (scheme.py:174-211)."""
-    token_rows = x.numel() // x.shape[-1]
-    fused_env = os.environ.get(_STATIC_FUSED_GENERATION_ENV)
-    use_fused = token_rows <= _FUSED_MAX_ROWS and fused_env != "0"
+    """Static activation quant + HiF8 linear (scheme.py:174-211) in one
+    operator call: the operator takes the fused quant + linear for rows <= 4
+    (unless HIF8_STATIC_FUSED_GENERATION=0), else the static quant and then
+    the linear -- the kernels of native.soft_static_fused_linear /
+    native.static_quant + native.soft_linear, with the same bytes -- so the
+    routing costs no extra dispatch.  The layer's parameters were validated
+    when it was loaded (process_weights_after_loading)."""
+    fused_rows = 0 if os.environ.get(_STATIC_FUSED_GENERATION_ENV) == "0" else _FUSED_MAX_ROWS
     fixed_scale = layer.input_scale
     factor = static_scale_factor()
     if factor != 1.0:
         fixed_scale = fixed_scale * factor
-    if use_fused:
-        return native.soft_static_fused_linear(x, layer.weight, fixed_scale, layer.weight_scale, bias,
-                                               output_dtype=x.dtype)
-    activation, row_scale = native.static_quant(x, fixed_scale)
-    return native.soft_linear(activation, layer.weight, row_scale, layer.weight_scale, bias, output_dtype=x.dtype)
+    return native.static_linear(x, layer.weight, fixed_scale, layer.weight_scale, bias, fused_rows)
 
 
 def process_dynamic_weights_after_loading(layer) -> None:

@@ -147,6 +147,23 @@ int soft_hif8_fused_gemm(const void *x, int x_dtype, const uint8_t *weight, cons
                          const void *bias, int bias_dtype, int output_dtype, int64_t m, int64_t n,
                          int64_t k, void *out, void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- the static scheme's apply in one call ---------------------------
+ * hif8_static_linear replaces the pair of operator calls that the static
+ * scheme's apply makes per projection (reference src/vllm_ascend_hif8/
+ * scheme.py:174-211): for m <= fused_max_rows (at most 4) the fused quant +
+ * linear of soft_hif8_static_fused_gemm, otherwise hif8_static_quant of x
+ * with the one input_scale into the workspace followed by soft_hif8_gemm --
+ * the same kernels and bytes as the two separate calls.  x: [m, k]
+ * FP16/BF16 (x_dtype); input_scale: one float (device); bias optional;
+ * out: [m, n] of output_dtype.  workspace: hif8_static_linear_workspace_size()
+ * bytes, 256-byte aligned (0 bytes, and NULL allowed, on the fused path). */
+size_t hif8_static_linear_workspace_size(int64_t m, int64_t n, int64_t k, int fused_max_rows);
+
+int hif8_static_linear(const void *x, int x_dtype, const uint8_t *weight, const float *input_scale,
+                       const float *channel_scale, const void *bias, int bias_dtype, int output_dtype, int64_t m,
+                       int64_t n, int64_t k, int fused_max_rows, void *out, void *workspace, size_t workspace_bytes,
+                       void *stream);
+
 /* ---- tensor-parallel partial products ---------------------------------
  * No counterpart in the reference, which runs a projection on one device.
  * When a row-parallel projection is split over ranks by its input columns,

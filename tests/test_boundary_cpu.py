@@ -154,6 +154,14 @@ def test_cabi_rejects_contract_violations_without_device_work():
     assert lib.soft_hif8_fused_gemm(fake, 1, fake, fake, None, -1, 1, 3, 8, 64, fake, fake, 1 << 20, None) == 1
     assert lib.soft_hif8_fused_gemm(fake, 1, fake, fake, None, -1, 1, 2, 8, 64, fake, fake, ws - 1, None) == 3
     assert lib.soft_hif8_fused_gemm(fake, 1, fake, fake, None, -1, 1, 2, 8, 64, fake, None, ws, None) == 3
+    # the scheme's single call: the fused route needs no workspace, the other one does
+    assert lib.hif8_static_linear_workspace_size(4, 8, 64, 4) == 0
+    assert lib.hif8_static_linear_workspace_size(4, 8, 64, 0) == 256 + 256
+    assert lib.hif8_static_linear_workspace_size(64, 4096, 4096, 4) == (
+        64 * 4096 + 256 + lib.soft_hif8_gemm_workspace_size(64, 4096, 4096))
+    assert lib.hif8_static_linear(fake, 3, fake, fake, fake, None, -1, 1, 2, 8, 64, 4, fake, None, 0, None) == 1
+    assert lib.hif8_static_linear(fake, 1, fake, fake, fake, None, -1, 1, 5, 8, 64, 4, fake, None, 0, None) == 3
+    assert lib.hif8_static_linear(fake, 1, fake, None, fake, None, -1, 1, 2, 8, 64, 4, fake, None, 0, None) == 1
     assert lib.hif8_status_string(3) == b"workspace missing or too small"
 
 
@@ -226,6 +234,8 @@ def test_meta_shapes():
     assert dec.shape == a.shape and dec.dtype == torch.bfloat16
     data, token_scale = torch.ops.vllm_ascend_hif8.hif8_dynamic_quant(x)
     assert data.shape == x.shape and data.dtype == torch.uint8 and token_scale.shape == (6,)
+    lin = torch.ops.hif8_b200.static_linear(x, w, torch.empty(1, device="meta"), torch.empty(7, device="meta"))
+    assert lin.shape == (2, 3, 7) and lin.dtype == torch.bfloat16
     x2 = torch.empty(2, 64, dtype=torch.float16, device="meta")
     fused = torch.ops.vllm_ascend_hif8.soft_hif8_fused_gemm(x2, w, torch.empty(7, device="meta"), None, torch.float16)
     assert fused.shape == (2, 7) and fused.dtype == torch.float16

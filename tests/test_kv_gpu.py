@@ -253,3 +253,48 @@ def test_paged_decode_head_size_128():
     out = kv.paged_attention(torch.from_numpy(q).to(torch.bfloat16).to(DEV), torch.from_numpy(kc).to(DEV),
                              torch.from_numpy(vc).to(DEV), torch.from_numpy(table).to(DEV), ctx, scale=scale)
     _check_attention(out, expected)
+
+
+@pytest.mark.parametrize("heads,d", [(1, 256), (2, 256), (4, 256), (8, 128), (4, 64), (3, 16), (2, 96), (5, 48)])
+@pytest.mark.parametrize("scales", ["calibrated", "pow2", "special"])
+def test_kv_write_head_layouts_scales_and_strided_source(heads, d, scales):
+    """Every page-row-group size (the warp-per-token write stores 16-byte
+    words when heads * (D + 4) is a multiple of 16, 4-byte words otherwise;
+    D / 16 not a power of two takes the per-chunk kernel), power-of-two
+    scales (the check-free encode), calibrated ones and non-positive /
+    non-finite ones (the exact path), K and V read from a fused qkv row
+    (token stride > heads * D): byte-exact with the oracle."""
+    kv = _kv()
+    tokens, block, nblocks = 77, 16, 8
+    gen = torch.Generator().manual_seed(heads * 1000 + d + len(scales))
+    qkv = (torch.randn(tokens, 3 * heads * d + 8, generator=gen) * 2.5).to(torch.bfloat16)
+    qkv[0, heads * d:heads * d + 8] = torch.tensor([float("nan"), float("inf"), -float("inf"), 0.0, -0.0, 1e30,
+                                                     -1e-30, 65504.0])
+    key = qkv[:, heads * d:2 * heads * d].view(tokens, heads, d)
+    value = qkv[:, 2 * heads * d:3 * heads * d].view(tokens, heads, d)
+    if scales == "calibrated":
+        ks = (key.float().abs().amax(dim=(0, 2)) / 448.0).numpy().astype(np.float32)
+        vs = (value.float().abs().amax(dim=(0, 2)) / 32768.0).numpy().astype(np.float32)
+    elif scales == "pow2":
+        ks = (2.0 ** np.arange(-3, -3 + heads)).astype(np.float32)
+        vs = (2.0 ** -np.arange(1, heads + 1)).astype(np.float32)
+    else:
+        ks = np.array([0.0, -0.5, float("inf"), 3.0e-39, 0.125, 1e30, 0.3, 2.0][:heads] * 2, np.float32)[:heads]
+        vs = np.array([float("nan"), 1e-40, 0.25, -2.0, 7.0, 0.5, 1.0, 3.0][:heads] * 2, np.float32)[:heads]
+    slots = np.random.default_rng(heads + d).permutation(nblocks * block)[:tokens].astype(np.int64)
+    slots[[2, 40]] = -1
+    kc = torch.zeros((nblocks, block, heads, d + 4), dtype=torch.uint8, device=DEV)
+    vc = torch.zeros_like(kc)
+    qkv_dev = qkv.to(DEV)
+    kd = qkv_dev[:, heads * d:2 * heads * d].view(tokens, heads, d)
+    vd = qkv_dev[:, 2 * heads * d:3 * heads * d].view(tokens, heads, d)
+    assert kd.stride(0) == 3 * heads * d + 8
+    kv.write_static(kd, vd, kc, vc, torch.from_numpy(slots).to(DEV), torch.from_numpy(ks).to(DEV),
+                    torch.from_numpy(vs).to(DEV), validate=True)
+    torch.cuda.synchronize()
+    kref = np.zeros(kc.shape, np.uint8)
+    vref = np.zeros_like(kref)
+    oracle.kv_write(key.contiguous().view(torch.int16).numpy().view(np.uint16), ks, slots, kref)
+    oracle.kv_write(value.contiguous().view(torch.int16).numpy().view(np.uint16), vs, slots, vref)
+    np.testing.assert_array_equal(kc.cpu().numpy(), kref)
+    np.testing.assert_array_equal(vc.cpu().numpy(), vref)

@@ -345,3 +345,51 @@ def test_tensor_parallel_partial_products_fp32(m):
     assert max_rel(summed.float().cpu().numpy(), unsharded.float().cpu().numpy()) <= 2.0**-8, f"m={m}"
     ulps = (summed.view(torch.int16).int() - unsharded.view(torch.int16).int()).abs()
     assert float((ulps > 1).float().mean()) <= 1e-3, f"m={m}: split partials differ by more than one BF16 ulp"
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_static_linear_op_equals_the_two_call_path(dtype):
+    """hif8_b200::static_linear (scheme.apply's single operator) is the
+    reference's pair of calls bit for bit: soft_hif8_static_fused_gemm for
+    rows <= fused_max_rows, static quant + soft_hif8_gemm beyond (GEMV and
+    tcgen05 routes), with and without bias, for 3-D and strided inputs, and
+    through the C ABI."""
+    from hif8_b200 import cabi
+
+    native = _native()
+    ext = native.load_extension()
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
+    g = torch.Generator().manual_seed(77)
+    n, k = 1544, 4096
+    w = torch.randint(0, 111, (n, k), generator=g, dtype=torch.uint8).to(DEV)
+    cs = (torch.rand(n, generator=g) * 1e-3 + 1e-4).to(DEV)
+    fixed = torch.tensor([3.0 / 32768.0], device=DEV)
+    bias = torch.randn(n, generator=g).to(tdt).to(DEV)
+    for m in (1, 2, 3, 4, 5, 8, 16, 17, 33, 64, 512):
+        x = (torch.randn(m, k, generator=g) * 2).to(tdt).to(DEV)
+        for fused_rows in (4, 0):
+            for b in (None, bias):
+                got = torch.ops.hif8_b200.static_linear(x, w, fixed, cs, b, fused_rows)
+                if m <= fused_rows:
+                    expected = ext.soft_hif8_static_fused_gemm(x, w, fixed, cs, b, tdt)
+                else:
+                    data, row_scale = native.static_quant(x, fixed)
+                    expected = ext.soft_hif8_gemm(data, w, row_scale, cs, b, tdt)
+                assert torch.equal(got, expected), (m, fused_rows, b is None)
+        via_abi = torch.empty(m, n, dtype=tdt, device=DEV)
+        cabi.static_linear(x, w, fixed, cs, bias, via_abi)
+        assert torch.equal(via_abi, torch.ops.hif8_b200.static_linear(x, w, fixed, cs, bias, 4)), m
+    x3 = (torch.randn(2, 3, 2 * k, generator=g)).to(tdt).to(DEV)[:, :, ::2]  # strided [2, 3, K]
+    got = torch.ops.hif8_b200.static_linear(x3, w, fixed, cs, None, 4)
+    data, row_scale = native.static_quant(x3.contiguous(), fixed)
+    expected = ext.soft_hif8_gemm(data.reshape(6, k), w, row_scale, cs, None, tdt)
+    assert got.shape == (2, 3, n) and torch.equal(got.reshape(6, n), expected)
+    with pytest.raises(RuntimeError, match="K dimensions differ"):
+        torch.ops.hif8_b200.static_linear(x3[..., :-8], w, fixed, cs, None, 4)
+    # contiguous views at an aligned and at an unaligned offset of a packed buffer
+    for m in (2, 16):
+        buf = (torch.randn(m * k + 16, generator=g) * 2).to(tdt).to(DEV)
+        for off in (8, 3):
+            xv = buf[off:off + m * k].view(m, k)
+            got = torch.ops.hif8_b200.static_linear(xv, w, fixed, cs, bias, 4)
+            assert torch.equal(got, torch.ops.hif8_b200.static_linear(xv.clone(), w, fixed, cs, bias, 4)), (m, off)
