@@ -691,20 +691,30 @@ def measure_prefill_gemm(device) -> dict:
         w.view(-1)[idx] = sign * 20 * 0.02
         wq, ws = scheme.quantize_weight_rows(w.to(torch.bfloat16))
         del w
+        lin = scheme.Hif8StaticLinear(wq, ws.reshape(-1, 1), torch.tensor([4.5 / 32768.0], device=device))
         for m in (512, 4096):
             x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
             a, ts = native.static_quant(x, torch.tensor([4.5 / 32768.0], device=device))
             ext.soft_hif8_gemm(a, wq, ts, ws, None, torch.bfloat16)
             t = _timed_alone(lambda: ext.soft_hif8_gemm(a, wq, ts, ws, None, torch.bfloat16), device)
+            # the projection as scheme.apply runs it from BF16 input: the static
+            # quant fused into the GEMM's operand pass (beside: quant + GEMM)
+            scheme.apply(lin, x)
+            t_apply = _timed_alone(lambda: scheme.apply(lin, x), device)
+            t_pair = _timed_alone(lambda: ext.soft_hif8_gemm(*native.static_quant(x, lin.input_scale)[:1], wq,
+                                                             ts, ws, None, torch.bfloat16), device)
             flops = 2.0 * m * n * k
             per.append({"m": m, "shape": name, "us": round(t * 1e3, 1), "tflops": round(flops / (t * 1e-3) / 1e12, 1),
-                        "frac": round(flops / (t * 1e-3) / 1e12 / peak, 3)})
+                        "frac": round(flops / (t * 1e-3) / 1e12 / peak, 3),
+                        "apply_us": round(t_apply * 1e3, 1), "quant_then_gemm_us": round(t_pair * 1e3, 1)})
             flops_total += flops
             ms_total += t
     achieved = flops_total / (ms_total * 1e-3) / 1e12
     return {"bound": "tensor", "kernel": "gemm_hif8_tc_kernel (tcgen05, TMEM A operand) + decode_to_bf16",
             "achieved": round(achieved, 1), "peak": peak, "unit": "TF/s", "frac": round(achieved / peak, 3),
             "peak_kind": kind, "algorithmic": "2*M*N*K FLOPs per call", "per_call": per,
+            "apply": "apply_us: scheme.apply from BF16 input (static quant fused into the GEMM's BF16 operand pass); "
+                     "quant_then_gemm_us: hif8_static_quant then soft_hif8_gemm",
             "timing": "median of 5 calls per config, each after a read-based L2 eviction, CUDA events"}
 
 

@@ -383,6 +383,48 @@ __global__ void __launch_bounds__(256) decode_to_bf16(const uint8_t *__restrict_
   }
 }
 
+// Static quantisation of FP16/BF16 activations with the fixed scale *scale
+// fused with the decode: the unscaled BF16 value of each element's static
+// code, written straight into the GEMM's BF16 operand (bit-identical to
+// hif8_static_quant followed by decode_to_bf16, without the byte round
+// trip).  The fake-quant table gives each correctly rounded quotient's value
+// (fake_quant16); a chunk with a huge or non-finite product, or a scale that
+// needs it, takes the exact FP64 path.
+template <int kDtype>
+__global__ void __launch_bounds__(256) fake_quant_to_bf16(const uint16_t *__restrict__ x,
+                                                          const float *__restrict__ scale,
+                                                          uint16_t *__restrict__ out, int64_t chunks) {
+  __shared__ __align__(16) uint16_t fq[4096];
+  __shared__ __align__(16) uint8_t mag[4096];
+  __shared__ uint32_t dec[256];
+  for (int i = threadIdx.x; i < 4096 / 8; i += blockDim.x)
+    reinterpret_cast<uint4 *>(fq)[i] = reinterpret_cast<const uint4 *>(g_fake_quant_bf16.v)[i];
+  load_encode_mag_table(mag);
+  dec[threadIdx.x] = g_decode_f32.v[threadIdx.x];
+  __syncthreads();
+  const float s = __ldg(scale);
+  const float r = __frcp_rn(s);
+  const double r64 = __drcp_rn((double)s);
+  const uint32_t re = __float_as_uint(r) & 0x7F800000u;
+  const bool exact_only = (re == 0u) | (re == 0x7F800000u) | !(s > 0.f) | !scale_edge_ok(s);
+  const float s_half = 0.5f * s;
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks; c += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 a = __ldcs(reinterpret_cast<const uint4 *>(x) + 2 * c);
+    const uint4 b = __ldcs(reinterpret_cast<const uint4 *>(x) + 2 * c + 1);
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint32_t o[8];
+    if (exact_only || !fake_quant16<kDtype>(w, s, r, s_half, fq, o)) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        o[j] = (dec[static_code_exact(half_bits_to_f32<kDtype>(w[j] & 0xFFFFu), r64, mag)] >> 16) |
+               (dec[static_code_exact(half_bits_to_f32<kDtype>(w[j] >> 16), r64, mag)] & 0xFFFF0000u);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(out) + 2 * c;
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
 // ------------------------------------------------------------------ host --
 
 static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -432,7 +474,7 @@ static int launch_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const CUt
 }
 
 int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t workspace_bytes,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, int a_dtype) {
   const int64_t m = args.m, n = args.n, k = args.k;
   if (workspace_bytes < hif8_gemm_tc_workspace(m, n, k)) return HIF8_ERR_WORKSPACE;
   auto encode = tensor_map_encoder();
@@ -444,11 +486,20 @@ int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t
     set_last_error(e);
     return HIF8_ERR_CUDA;
   }
-  // 1. activation -> BF16 (exact), 16 bytes per thread (k % 64 == 0)
+  // 1. activation -> BF16 (exact), 16 elements per thread (k % 64 == 0):
+  // the decode of HiF8 bytes, or the static quant + decode of FP16/BF16
+  // input with the fixed scale args.ts[0]
   const int64_t chunks = m * k / 16;
   int64_t blocks = (chunks + 255) / 256;
   if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
-  decode_to_bf16<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint8_t *>(args.a), xb, chunks);
+  if (a_dtype == HIF8_DTYPE_BF16)
+    fake_quant_to_bf16<HIF8_DTYPE_BF16><<<(unsigned)blocks, 256, 0, stream>>>(
+        static_cast<const uint16_t *>(args.a), args.ts, xb, chunks);
+  else if (a_dtype == HIF8_DTYPE_F16)
+    fake_quant_to_bf16<HIF8_DTYPE_F16><<<(unsigned)blocks, 256, 0, stream>>>(
+        static_cast<const uint16_t *>(args.a), args.ts, xb, chunks);
+  else
+    decode_to_bf16<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint8_t *>(args.a), xb, chunks);
   int status = check_launch();
   if (status != HIF8_OK) return status;
 

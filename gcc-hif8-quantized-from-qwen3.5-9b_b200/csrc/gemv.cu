@@ -1065,6 +1065,13 @@ extern "C" int hif8_static_linear(const void *x, int x_dtype, const uint8_t *wei
   const size_t need = hif8_static_linear_workspace_size(m, n, k, fused_max_rows);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return HIF8_ERR_WORKSPACE;
+  if (hif8_gemm_tc_supported(m, n, k) && aligned16(x) && aligned16(weight) && aligned16(out)) {
+    // prefill: the static quant happens in the GEMM's operand pass (FP16/BF16
+    // -> decoded static code as BF16), the bytes never reach memory
+    GemvArgs args{x, weight, input_scale, channel_scale, bias, out, (int)m, (int)n, (int)k, 0,
+                  bias ? bias_dtype : HIF8_DTYPE_NONE, 0};
+    return hif8_gemm_tc(args, output_dtype, workspace, workspace_bytes, s, x_dtype);
+  }
   uint8_t *codes = static_cast<uint8_t *>(workspace);
   float *row_scale = reinterpret_cast<float *>(codes + round256((size_t)m * k));
   uint8_t *gemm_ws = reinterpret_cast<uint8_t *>(row_scale) + round256((size_t)m * sizeof(float));

@@ -38,7 +38,10 @@ struct GemvArgs {
 
 bool hif8_gemm_tc_supported(int64_t m, int64_t n, int64_t k);
 size_t hif8_gemm_tc_workspace(int64_t m, int64_t n, int64_t k);
+// a_dtype: HIF8_DTYPE_NONE for HiF8 activation bytes (args.ts per row), or
+// HIF8_DTYPE_BF16 / HIF8_DTYPE_F16 for activations statically quantised in
+// the GEMM's operand pass with the fixed scale args.ts[0] (ts_stride 0).
 int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t workspace_bytes,
-                 cudaStream_t stream);
+                 cudaStream_t stream, int a_dtype = HIF8_DTYPE_NONE);
 
 }  // namespace hif8

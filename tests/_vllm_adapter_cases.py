@@ -83,8 +83,8 @@ def main(mode: str) -> None:
         pre = "language_model.model.layers"  # vLLM's module tree of Qwen3.5
 
         def weights(n, k):
-            return (torch.randint(0, 111, (n, k), dtype=torch.uint8, generator=g),
-                    (torch.rand(n, 1, generator=g) * 1e-3 + 1e-4))
+            return (torch.randint(0, 111, (n, k), dtype=torch.uint8, generator=g, device="cpu"),
+                    (torch.rand(n, 1, generator=g, device="cpu") * 1e-3 + 1e-4))
 
         # q/k/v fused, static, one input scale stored under q_proj only
         qkv = QKVParallelLinear(HIDDEN, HEAD, HEADS, KV_HEADS, bias=False, params_dtype=torch.bfloat16,
@@ -174,12 +174,12 @@ def _forward_checks(qkv, o, qkvz, emb, table, tscale, scheme):
     dev = qkv.weight.device
     g = torch.Generator().manual_seed(11)
     for rows in (1, 3, 40):
-        x = (torch.randn(rows, HIDDEN, generator=g) * 2).to(torch.bfloat16).to(dev)
+        x = (torch.randn(rows, HIDDEN, generator=g, device="cpu") * 2).to(torch.bfloat16).to(dev)
         ref = scheme.Hif8StaticLinear(qkv.weight.clone(), qkv.weight_scale.reshape(-1, 1).clone(),
                                       qkv.input_scale.clone())
         y, _ = qkv(x)
         assert torch.equal(y, ref(x)), f"qkv forward differs from scheme.apply at {rows} rows"
-        xo = (torch.randn(rows, HEADS * HEAD, generator=g)).to(torch.bfloat16).to(dev)
+        xo = (torch.randn(rows, HEADS * HEAD, generator=g, device="cpu")).to(torch.bfloat16).to(dev)
         ref_o = scheme.Hif8StaticLinear(o.weight.clone(), o.weight_scale.reshape(-1, 1).clone(), o.input_scale.clone())
         yo, _ = o(xo)
         assert torch.equal(yo, ref_o(xo)), f"o_proj forward differs at {rows} rows"

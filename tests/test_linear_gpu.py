@@ -386,6 +386,22 @@ def test_static_linear_op_equals_the_two_call_path(dtype):
     assert got.shape == (2, 3, n) and torch.equal(got.reshape(6, n), expected)
     with pytest.raises(RuntimeError, match="K dimensions differ"):
         torch.ops.hif8_b200.static_linear(x3[..., :-8], w, fixed, cs, None, 4)
+    # prefill rows holding specials (NaN, Inf, huge and tiny values, zeros): the
+    # GEMM's fused operand pass takes the exact path for their chunks
+    xs = (torch.randn(64, k, generator=g) * 2).to(tdt)
+    xs[3, :6] = torch.tensor([float("nan"), float("inf"), -float("inf"), 6.0e4, -1e-7, 0.0]).to(tdt)
+    xs[40] = 0
+    xs = xs.to(DEV)
+    data, row_scale = native.static_quant(xs, fixed)
+    expected = ext.soft_hif8_gemm(data, w, row_scale, cs, bias, tdt)
+    got = torch.ops.hif8_b200.static_linear(xs, w, fixed, cs, bias, 4)
+    assert torch.equal(got.isnan(), expected.isnan())
+    assert torch.equal(torch.nan_to_num(got), torch.nan_to_num(expected))
+    for odd in (torch.tensor([2.0 ** -70], device=DEV), torch.tensor([0.25], device=DEV)):  # exact-only / power of two
+        data, row_scale = native.static_quant(xs, odd)
+        expected = ext.soft_hif8_gemm(data, w, row_scale, cs, None, tdt)
+        got = torch.ops.hif8_b200.static_linear(xs, w, odd, cs, None, 4)
+        assert torch.equal(torch.nan_to_num(got), torch.nan_to_num(expected)), float(odd)
     # contiguous views at an aligned and at an unaligned offset of a packed buffer
     for m in (2, 16):
         buf = (torch.randn(m * k + 16, generator=g) * 2).to(tdt).to(DEV)
