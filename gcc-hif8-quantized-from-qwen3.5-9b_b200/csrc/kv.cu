@@ -624,9 +624,14 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArg
   if (q_len <= 0 || chunk0 >= seq) return;  // the merge reads only chunks that hold keys
   const int64_t width = D + 4;
   const int32_t *table = p.tables + (int64_t)b * p.max_blocks;
+  const int bsz = (int)p.block_size;  // < 2^31 (checked by the launcher): 32-bit division
   auto row_of = [&](int key) -> int64_t {  // -1: absent
-    const int64_t blk = key < seq ? page_of(table, key, p.block_size, p.max_blocks, p.num_blocks) : -1;
-    return blk >= 0 ? ((blk * p.block_size + key % p.block_size) * p.kv_heads + h) * width : -1;
+    if (key >= seq) return -1;
+    const int col = key / bsz;
+    if (col >= p.max_blocks) return -1;
+    const int64_t blk = table[col];
+    if (blk < 0 || blk >= p.num_blocks) return -1;
+    return ((blk * p.block_size + (key - col * bsz)) * p.kv_heads + h) * width;
   };
   for (int i = tid; i < 256; i += kDecThreads) lut[i] = __uint_as_float(g_decode_f32.v[i]);
   // the chunk's reference scales (NaN: no table) and whether every row of
@@ -769,7 +774,9 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArg
         if (nb < nblk) mine_n = row_pre(nb, att_n);
         // ---- scores of keys 0..7 of the block (B fragment = K^T: bytes 0,1 ->
         // k-slots 2t, 2t+1; bytes 2,3 -> 2t+8, 2t+9)
-        float sa[4] = {0.f, 0.f, 0.f, 0.f};
+        // two accumulators (even and odd k-steps): two dependent MMA chains of
+        // 8 instead of one of 16
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int ks = 0; ks < 16; ++ks) {
           const uint32_t w = kr[ks];
@@ -777,8 +784,10 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArg
                                           kv_dec<TAB>(kvlut, lut, w, 1, lane, ksc, false), 0x7632u);
           const uint32_t b1 = __byte_perm(kv_dec<TAB>(kvlut, lut, w, 2, lane, ksc, false),
                                           kv_dec<TAB>(kvlut, lut, w, 3, lane, ksc, false), 0x7632u);
-          attn_mma16816(sa, qa[ks][0], qa[ks][1], b0, b1);
+          attn_mma16816((ks & 1) ? sb : sa, qa[ks][0], qa[ks][1], b0, b1);
         }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sa[q] += sb[q];
         if (nb < nblk) stage(nb, mine_n, att_n);
         cp_async_commit();
         // ---- online softmax of head g over keys 2t, 2t+1
@@ -1071,7 +1080,7 @@ int paged_attention_args_status(const void *query, const void *key_cache, const 
                                 int64_t max_blocks, int64_t max_seq_len) {
   if (batch <= 0 || num_tokens < 0 || num_heads <= 0 || kv_heads <= 0 || num_heads % kv_heads != 0 ||
       head_size <= 0 || head_size % 4 != 0 || head_size > 1024 || num_blocks <= 0 || block_size <= 0 ||
-      max_blocks <= 0 || max_seq_len < 0)
+      block_size > 0x7FFFFFFFLL || max_blocks <= 0 || max_seq_len < 0)
     return HIF8_ERR_INVALID_ARGUMENT;
   if (!query || !key_cache || !value_cache || !block_tables || !seq_lens || !query_start || !out)
     return HIF8_ERR_INVALID_ARGUMENT;
