@@ -163,6 +163,7 @@ struct TcParams {
   void *out;
   int *err;
   int m, n, k, bias_dtype, ts_stride;
+  int kb_per;  // K blocks per split (blockIdx.z): all of them without split-K
 };
 
 template <int OUT>
@@ -194,7 +195,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // and the weight crosses HBM once while the BF16 activation stays in L2
   const int m0 = blockIdx.x * BN, n0 = blockIdx.y * kTcBM;
   constexpr uint32_t kTmemCols = BN + 4 * 32 <= 256 ? 256 : 512;
-  const int nkb = p.k / kTcBK;
+  // split-K: CTA z takes K blocks [kb0, kb0 + nkb) and stores its FP32
+  // partial tile into slice z of a [splits][M][N] buffer
+  const int kb0 = blockIdx.z * p.kb_per;
+  const int nkb = min(p.k / kTcBK - kb0, p.kb_per);
 
   // ---- set-up: barriers, TMEM, decode table --------------------------------
   if (tid == 0) {
@@ -235,8 +239,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int s = kb % kTcStages;
         if (kb >= kTcStages && !mbar_wait(&empty[s], ((kb / kTcStages) - 1) & 1, abort)) atomicAdd(p.err, 1);
         mbar_expect_tx(&full_b[s], kBBytes + kWBytes);
-        tma_load_2d(b_stages + s * kBBytes, &xmap, kb * kTcBK, m0, &full_b[s]);
-        tma_load_2d(w_stages + s * kWBytes, &wmap, kb * kTcBK, n0, &full_b[s]);
+        tma_load_2d(b_stages + s * kBBytes, &xmap, (kb0 + kb) * kTcBK, m0, &full_b[s]);
+        tma_load_2d(w_stages + s * kWBytes, &wmap, (kb0 + kb) * kTcBK, n0, &full_b[s]);
       }
     }
   } else if (warp == 1) {
@@ -346,9 +350,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("bar.sync 1, %0;" ::"n"(kDecoderWarps * 32) : "memory");
     if (warp == 2 && lane == 0) {
-      asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
-                   ::"l"(&ymap), "r"(n0), "r"(m0), "r"(smem_addr(stage_out))
-                   : "memory");
+      if (gridDim.z > 1)  // split-K partial: slice blockIdx.z of the [splits][M][N] buffer
+        asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                     ::"l"(&ymap), "r"(n0), "r"(m0), "r"((int)blockIdx.z), "r"(smem_addr(stage_out))
+                     : "memory");
+      else
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                     ::"l"(&ymap), "r"(n0), "r"(m0), "r"(smem_addr(stage_out))
+                     : "memory");
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // smem read before the CTA exits
     }
@@ -425,6 +434,39 @@ __global__ void __launch_bounds__(256) fake_quant_to_bf16(const uint16_t *__rest
   }
 }
 
+// Split-K epilogue: out[m, n] = sum over the splits in order of the FP32
+// partials (each (acc * cs[n]) * ts[m] of its K range) + bias[n], rounded
+// once to the output type.  Four outputs per thread.
+template <int OUT>
+__global__ void __launch_bounds__(256) splitk_reduce(const float *__restrict__ part, int splits, int64_t mn,
+                                                     int n, const void *__restrict__ bias, int bias_dtype,
+                                                     void *__restrict__ out) {
+  for (int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) * 4; i < mn;
+       i += (int64_t)gridDim.x * blockDim.x * 4) {
+    float4 v = *reinterpret_cast<const float4 *>(part + i);
+    for (int z = 1; z < splits; ++z) {
+      const float4 w = *reinterpret_cast<const float4 *>(part + (int64_t)z * mn + i);
+      v.x += w.x, v.y += w.y, v.z += w.z, v.w += w.w;
+    }
+    float r[4] = {v.x, v.y, v.z, v.w};
+    if (bias) {
+      const int c = (int)(i % n);  // n % 8 == 0: the four outputs share a row
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint16_t h = static_cast<const uint16_t *>(bias)[c + q];
+        r[q] += bias_dtype == HIF8_DTYPE_BF16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
+      }
+    }
+    if constexpr (OUT == HIF8_DTYPE_F32) {
+      *reinterpret_cast<float4 *>(static_cast<float *>(out) + i) = make_float4(r[0], r[1], r[2], r[3]);
+    } else {
+      const uint32_t lo = to_out_bits<OUT>(r[0]) | (to_out_bits<OUT>(r[1]) << 16);
+      const uint32_t hi = to_out_bits<OUT>(r[2]) | (to_out_bits<OUT>(r[3]) << 16);
+      *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(out) + i) = make_uint2(lo, hi);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ host --
 
 static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -451,9 +493,52 @@ bool hif8_gemm_tc_supported(int64_t m, int64_t n, int64_t k) {
 
 static size_t err_offset(int64_t m, int64_t k) { return ((size_t)m * k * 2 + 255) & ~size_t(255); }
 
+// Tile width BN (tokens per CTA) and split-K count of a call, by the estimated
+// time: waves of tiles over the SMs x the cost of a tile, whose weight decode
+// dominates and grows with the tile's K blocks (measured on B200: 0.53-0.57
+// us per 64-wide K block at BN 256, a little less at BN 128 / 64, about 3 us
+// of set-up per tile), plus for split-K the FP32 partial round trip and the
+// reduce launch.  Splitting K pays where the token x channel tiles alone
+// leave SMs idle (configs[2] down, M = 512: 64 tiles for 148 SMs).
+struct TcPlan {
+  int bn, splits, kb_per;
+};
+
+static TcPlan tc_plan(int64_t m, int64_t n, int64_t k) {
+  const int sms = num_sms();
+  const int64_t nkb = k / kTcBK;
+  const int bns[3] = {256, 128, 64};
+  const double per_kb[3] = {0.55, 0.49, 0.46};
+  TcPlan best{64, 1, (int)nkb};
+  double best_t = -1.0;
+  for (int i = 0; i < 3; ++i) {
+    if (bns[i] > 64 && m < bns[i] / 2) continue;
+    const int64_t tiles = ((m + bns[i] - 1) / bns[i]) * ((n + kTcBM - 1) / kTcBM);
+    for (int splits = 1; splits <= 4; ++splits) {
+      const int64_t kb_per = (nkb + splits - 1) / splits;
+      if (splits > 1 && (kb_per < 2 * kTcStages || (splits - 1) * kb_per >= nkb)) break;
+      const int64_t waves = (tiles * splits + sms - 1) / sms;
+      double t = (double)waves * (3.0 + per_kb[i] * (double)kb_per);
+      // FP32 partials written by the GEMM and read back by the reduce (~5 TB/s
+      // achieved), one more launch (measured: configs[2] down, M = 4096, two
+      // splits 446 us against 430 unsplit; M = 512 108 -> 76 us)
+      if (splits > 1) t += (double)(2 * splits + 1) * (double)m * (double)n * 4.0 / 5.0e6 + 5.0;
+      if (best_t < 0 || t < best_t) {
+        best_t = t;
+        best = TcPlan{bns[i], splits, (int)kb_per};
+      }
+    }
+  }
+  return best;
+}
+
+static size_t part_offset(int64_t m, int64_t k) { return err_offset(m, k) + 256; }
+
 size_t hif8_gemm_tc_workspace(int64_t m, int64_t n, int64_t k) {
-  (void)n;
-  return err_offset(m, k) + 256;  // BF16 activation copy + error word
+  // BF16 activation copy + error word (+ FP32 split-K partials)
+  const TcPlan plan = tc_plan(m, n, k);
+  const size_t part = plan.splits > 1 ? (size_t)plan.splits * m * n * sizeof(float) : 0;
+  return part_offset(m, k) + (part + 255) / 256 * 256;
 }
 
 template <int BN>
@@ -463,12 +548,12 @@ static constexpr size_t tc_smem_bytes() {
 
 template <int BN, int OUT>
 static int launch_tc(const CUtensorMap &xmap, const CUtensorMap &wmap, const CUtensorMap &ymap, const TcParams &p,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, int splits) {
   auto kernel = gemm_hif8_tc_kernel<BN, OUT>;
   const size_t smem = tc_smem_bytes<BN>();
   const int st = ensure_smem_limit(reinterpret_cast<const void *>(kernel), smem);
   if (st != HIF8_OK) return st;
-  dim3 grid((unsigned)((p.m + BN - 1) / BN), (unsigned)((p.n + kTcBM - 1) / kTcBM), 1);
+  dim3 grid((unsigned)((p.m + BN - 1) / BN), (unsigned)((p.n + kTcBM - 1) / kTcBM), (unsigned)splits);
   kernel<<<grid, kTcThreads, smem, stream>>>(xmap, wmap, ymap, p);
   return check_launch();
 }
@@ -503,28 +588,10 @@ int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t
   int status = check_launch();
   if (status != HIF8_OK) return status;
 
-  // 2. the tcgen05 GEMM; BN = tokens per tile, chosen by the estimated time
-  // of the launch: waves of tiles over the SMs times the cost of a tile.  The
-  // weight decode dominates a tile and does not shrink with BN (measured on
-  // B200, K = 4096: 37 us per tile at BN 256, 33 us at 128, 31 us at 64), so
-  // narrower tiles pay only where they fill SMs that would otherwise idle.
-  int bn = 64;
-  {
-    const double tile_cost[3] = {37.0, 33.0, 31.0};  // BN 256, 128, 64
-    const int bns[3] = {256, 128, 64};
-    double best = 0;
-    for (int i = 0; i < 3; ++i) {
-      if (bns[i] > 64 && m < bns[i] / 2) continue;
-      const int64_t tiles = ((m + bns[i] - 1) / bns[i]) * ((n + kTcBM - 1) / kTcBM);
-      const int64_t waves = (tiles + num_sms() - 1) / num_sms();
-      const double t = (double)waves * tile_cost[i];
-      if (best == 0 || t < best) {
-        best = t;
-        bn = bns[i];
-      }
-    }
-  }
-  const cuuint32_t estr[2] = {1, 1};
+  // 2. the tcgen05 GEMM, BN (tokens per tile) and split-K by tc_plan
+  const TcPlan plan = tc_plan(m, n, k);
+  const int bn = plan.bn, splits = plan.splits;
+  const cuuint32_t estr[3] = {1, 1, 1};
   CUtensorMap xmap, wmap, ymap;
   {  // BF16 activation [M, K]: BN x 64 boxes, 128-byte swizzle (UMMA SW128 K-major)
     const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
@@ -544,32 +611,58 @@ int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return HIF8_ERR_CUDA;
   }
-  const bool f32 = output_dtype == HIF8_DTYPE_F32;
-  {  // output [M, N] (BF16 / FP16 bits, or FP32 partials): 128-channel x BN-token boxes for the TMA store
+  float *part = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + part_offset(m, k));
+  const bool f32 = output_dtype == HIF8_DTYPE_F32 || splits > 1;
+  if (splits > 1) {  // FP32 partials [splits][M][N]: 128-channel x BN-token x 1 boxes
+    const cuuint64_t dims[3] = {(cuuint64_t)n, (cuuint64_t)m, (cuuint64_t)splits};
+    const cuuint64_t strides[2] = {(cuuint64_t)n * 4, (cuuint64_t)m * n * 4};
+    const cuuint32_t box[3] = {(cuuint32_t)kTcBM, (cuuint32_t)bn, 1};
+    if (encode(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, part, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return HIF8_ERR_CUDA;
+  } else {  // output [M, N] (BF16 / FP16 bits, or FP32 partials): 128-channel x BN-token boxes for the TMA store
     const cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)m};
     const cuuint64_t strides[1] = {(cuuint64_t)n * (f32 ? 4 : 2)};
     const cuuint32_t box[2] = {(cuuint32_t)kTcBM, (cuuint32_t)bn};
     if (encode(&ymap, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, args.out, dims,
-               strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return HIF8_ERR_CUDA;
   }
-  TcParams p{args.w, args.ts, args.cs, args.bias, args.out, err, args.m, args.n, args.k, args.bias_dtype, args.ts_stride};
+  // split-K partials carry no bias: the reduce adds it once
+  TcParams p{args.w, args.ts, args.cs, splits > 1 ? nullptr : args.bias, splits > 1 ? (void *)part : args.out, err,
+             args.m, args.n, args.k, args.bias_dtype, args.ts_stride, plan.kb_per};
   const bool bf16 = output_dtype == HIF8_DTYPE_BF16;
   if (f32) {
-    if (bn == 256) return launch_tc<256, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream);
-    if (bn == 128) return launch_tc<128, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream);
-    return launch_tc<64, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream);
+    if (bn == 256) status = launch_tc<256, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream, splits);
+    else if (bn == 128) status = launch_tc<128, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream, splits);
+    else status = launch_tc<64, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream, splits);
+  } else if (bn == 256) {
+    status = bf16 ? launch_tc<256, HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream, 1)
+                  : launch_tc<256, HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream, 1);
+  } else if (bn == 128) {
+    status = bf16 ? launch_tc<128, HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream, 1)
+                  : launch_tc<128, HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream, 1);
+  } else {
+    status = bf16 ? launch_tc<64, HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream, 1)
+                  : launch_tc<64, HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream, 1);
   }
-  if (bn == 256)
-    return bf16 ? launch_tc<256, HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream)
-                : launch_tc<256, HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream);
-  if (bn == 128)
-    return bf16 ? launch_tc<128, HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream)
-                : launch_tc<128, HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream);
-  return bf16 ? launch_tc<64, HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream)
-              : launch_tc<64, HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream);
+  if (status != HIF8_OK || splits == 1) return status;
+  // 3. split-K: sum the partials in split order, add the bias, round once
+  const int64_t mn = m * n;
+  int64_t rblocks = (mn / 4 + 255) / 256;
+  if (rblocks > (int64_t)num_sms() * 8) rblocks = (int64_t)num_sms() * 8;
+  if (output_dtype == HIF8_DTYPE_F32)
+    splitk_reduce<HIF8_DTYPE_F32><<<(unsigned)rblocks, 256, 0, stream>>>(part, splits, mn, (int)n, args.bias,
+                                                                          args.bias_dtype, args.out);
+  else if (bf16)
+    splitk_reduce<HIF8_DTYPE_BF16><<<(unsigned)rblocks, 256, 0, stream>>>(part, splits, mn, (int)n, args.bias,
+                                                                           args.bias_dtype, args.out);
+  else
+    splitk_reduce<HIF8_DTYPE_F16><<<(unsigned)rblocks, 256, 0, stream>>>(part, splits, mn, (int)n, args.bias,
+                                                                          args.bias_dtype, args.out);
+  return check_launch();
 }
 
 }  // namespace hif8

@@ -145,3 +145,50 @@ def test_prefill_gemm_workspace_contract():
     cabi.gemm(a, w, ts, cs, None, out, big[:need])
     torch.cuda.synchronize()
     assert torch.equal(out.float().cpu(), torch.zeros(m, n))
+
+
+def test_prefill_gemm_split_k():
+    """Shapes whose token x channel tiles leave most SMs idle take split-K
+    (FP32 partial tiles of K ranges summed in split order by a second kernel,
+    bias added once): against the FP64 oracle with BF16/FP16 output and bias,
+    FP32 output through the tensor-parallel partial operator, bit-exact on
+    small-integer operands, deterministic, and NaN codes still reach their
+    rows."""
+    from hif8_b200 import cabi
+
+    ext = _native().load_extension()
+    lib = cabi.library()
+    m, n, k = 96, 512, 8192
+    # the plan splits K here: the workspace holds FP32 partials beyond the BF16 copy
+    assert lib.soft_hif8_gemm_workspace_size(m, n, k) > (m * k * 2 + 255) // 256 * 256 + 256 + m * n * 4
+    w, w_s = _hif8_weights(n, k, seed=5, outlier_frac=1e-3)
+    _, a, a_s, _ = _activations(m, k, seed=6)
+    bias = (np.random.default_rng(3).random(n).astype(np.float32) - 0.5)
+    for out_dtype in (torch.float16, torch.bfloat16):
+        b = _to(bias, torch.bfloat16)
+        out = ext.soft_hif8_gemm(_to(a), _to(w), _to(a_s), _to(w_s), b, out_dtype)
+        expected = oracle.linear(a, w, a_s, w_s, b.float().cpu().numpy())
+        got = out.float().cpu().numpy()
+        assert max_rel(got, expected) <= MAX_REL, out_dtype
+        assert channel_rel(got, expected) <= CHANNEL_REL, out_dtype
+        assert row_cosine_min(got, expected) >= MIN_COSINE, out_dtype
+        again = ext.soft_hif8_gemm(_to(a), _to(w), _to(a_s), _to(w_s), b, out_dtype)
+        assert torch.equal(out, again), "split-K run-twice determinism"
+    # FP32 partial products (the tensor-parallel operator) through the same split
+    x_bits, _, _, scale = _activations(m, k, seed=6)
+    x = _to(x_bits.view(np.int16)).view(torch.bfloat16)
+    part = torch.ops.hif8_b200.linear_partial_f32(x, _to(w), _to(scale), _to(w_s))
+    data, rows = oracle.static_quant(x_bits, scale)
+    assert max_rel(part.cpu().numpy(), oracle.linear(data, w, rows, w_s)) <= 1e-4
+    # small integers: every partial and their sum exact in FP32
+    rng = np.random.default_rng(9)
+    values = np.array([-2.0, -1.0, -0.5, 0.0, 0.5, 1.0, 2.0], np.float32)
+    ai = np.vectorize(oracle.encode_value)(values[rng.integers(0, 7, (m, k))]).astype(np.uint8)
+    wi = np.vectorize(oracle.encode_value)(values[rng.integers(0, 7, (n, k))]).astype(np.uint8)
+    ai[7, 100] = 0x80  # NaN code in row 7
+    ones_m, ones_n = np.ones(m, np.float32), np.ones(n, np.float32)
+    out = ext.soft_hif8_gemm(_to(ai), _to(wi), _to(ones_m), _to(ones_n), None, torch.float16)
+    exp = oracle.linear(ai, wi, ones_m, ones_n).astype(np.float16)
+    got = out.cpu().numpy()
+    assert np.isnan(got[7]).all()
+    np.testing.assert_array_equal(np.delete(got, 7, axis=0), np.delete(exp, 7, axis=0))
