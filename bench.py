@@ -50,8 +50,11 @@ METRIC = "HiF8 GEMV HBM GB/s vs peak (M=1-16); W8A8KV8 decode tok/s at 1/2/4/8 B
 UNIT = "GB/s"
 FALLBACK_HBM_GBS = 6650.0
 TP_SWEEP_TOL = 1e-2    # north-star tolerance of a TP split (only the summation order changes)
-DECODER_TP_COS_BF16 = 0.995  # logits cosine vs TP-1 after 32 random-init layers (rounding-level differences)
-DECODER_TP_COS_HIF8 = 0.9     # idem with static HiF8 codes that a one-ulp difference can move by a step
+# logits cosine vs TP-1 after 32 random-init layers: measured at TP 2, 0.9985-0.9989 for the BF16 twin
+# (rounding-level differences amplified layer by layer) and 0.95-0.97 for HiF8 (a one-ulp difference can
+# move a static code by a whole step); the bounds leave margin for other TP degrees
+DECODER_TP_COS_BF16 = 0.99
+DECODER_TP_COS_HIF8 = 0.85
 
 
 def call_bytes(m: int, n: int, k: int) -> int:
@@ -416,8 +419,9 @@ def decoder_tp_parity(device, world: int, rank: int, calib: dict, steps: int = 8
     whole code step (cosine 0.95-0.97).  The exact per-projection check is
     the sweep parity, and the 4-layer decoder is held to 2e-2 and identical
     tokens in tests/test_tp_gpu.py; here the pass criteria are cosine >=
-    0.995 (twin) and >= 0.9 (HiF8) at every step, and every step's max-rel,
-    cosine and greedy-token agreement is reported."""
+    DECODER_TP_COS_BF16 (twin) and >= DECODER_TP_COS_HIF8 (HiF8) at every
+    step, and every step's max-rel, cosine and greedy-token agreement is
+    reported."""
     import torch
     import torch.distributed as dist
 
