@@ -291,7 +291,6 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_kernel(const Hif8GdnArgs p) {
 }
 
 // ------------------------------ TP all-reduce + residual + RMSNorm (peer) --
-constexpr int kPeerThreads = 1024;
 
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -307,40 +306,76 @@ __device__ __forceinline__ uint64_t gtimer_ns() {
   return t;
 }
 
-// Bytes of one rank's peer buffer: two slots of `world` partials
-// (max_rows x dim FP32 each, one per source rank), then `world` flags.
+// One rank's peer buffer: two slots of `world` partials (max_rows x dim
+// FP32 each, one per source rank); the flags, one per (source rank, CTA);
+// then this rank's own scratch (never written by peers): the CTAs' row sums
+// of squares and two counters (the CTAs' barrier and completion).
+constexpr int kPeerMaxCtas = 16;
+constexpr int kPeerCtaThreads = 256;
+
 __host__ __device__ inline size_t peer_part_bytes(int64_t max_rows, int64_t dim) {
   return (size_t)max_rows * dim * sizeof(float);
 }
+__host__ __device__ inline size_t peer_flags_off(int64_t world, int64_t max_rows, int64_t dim) {
+  return 2 * (size_t)world * peer_part_bytes(max_rows, dim);
+}
+__host__ __device__ inline size_t peer_scratch_off(int64_t world, int64_t max_rows, int64_t dim) {
+  return peer_flags_off(world, max_rows, dim) + ((size_t)world * kPeerMaxCtas * sizeof(uint32_t) + 15) / 16 * 16;
+}
+constexpr size_t kPeerScratchBytes = (size_t)kPeerMaxCtas * 8 * sizeof(float) + 16;
 
-// Push all-reduce of one decode step's row-parallel FP32 partials, optionally
-// fused with the following residual add + RMSNorm (weight != null).  One CTA
-// per rank (decode sizes: rows x dim <= 4 x 1024 x 8 values):
-//   1. this rank's partial is stored into slot [rank] of every rank's buffer
-//      (its own first, then the peers after it in rank order) -- one-way
-//      NVLink stores, no remote read on the critical path;
-//   2. a system-scope fence, then epoch into flag[rank] of every rank's
-//      buffer (st.release.sys), and a bounded wait on this rank's own flags;
-//   3. the `world` partials are summed in FP32 from local memory in rank
-//      order, the same order on every rank, so every rank computes identical
-//      bits, and the sum is rounded to BF16 once -- as the unsharded
-//      projection rounds its FP32 accumulator once.
-// The CTA signals its dependents as soon as its inputs are visible: the
-// following linear's CTAs launch on the SMs this single CTA leaves idle and
-// build their tables while the exchange runs.
-__global__ void __launch_bounds__(kPeerThreads) peer_allreduce_rmsnorm_kernel(const Hif8PeerArgs p) {
+// CTAs of an exchange: column slices of at least 128 values (dim % 256 == 0).
+__host__ __device__ inline int peer_ctas(int64_t dim) {
+  return dim / 128 < kPeerMaxCtas ? (int)(dim / 128) : kPeerMaxCtas;
+}
+
+__device__ __forceinline__ bool wait_at_least(const uint32_t *flag, uint32_t target, uint64_t t0, uint64_t limit) {
+  while ((int32_t)(ld_acquire_sys(flag) - target) < 0)
+    if (gtimer_ns() - t0 > limit) return false;
+  return true;
+}
+
+// Push all-reduce of row-parallel partials, optionally fused with the
+// following residual add + RMSNorm (weight != null).  CTA c of the grid owns
+// the column slice [c * cw, (c + 1) * cw) of every row, so the stores to the
+// peers leave from several SMs:
+//   1. the slice of this rank's partial is stored into slot [rank] of every
+//      rank's buffer (its own first): one-way NVLink stores;
+//   2. a system-scope fence, then epoch into flag[rank][c] of every rank's
+//      buffer (st.release.sys), and a bounded wait for flag[q][c] of every
+//      rank q in its own buffer;
+//   3. the `world` partials of the slice are summed in FP32 from local memory
+//      in rank order (identical bits on every rank) and rounded to BF16
+//      once.  With the norm, each CTA's row sums of squares (warps in order)
+//      go to the scratch, a bounded barrier of the grid's CTAs follows, and
+//      every CTA adds the CTAs' sums in CTA order -- the same row norm on every
+//      CTA and every rank -- before it writes its normalised slice.
+// The last CTA to finish advances the epoch counter and resets the scratch
+// counters (the next exchange on this stream starts after this grid ends).
+// Every CTA signals its dependents at its start: the following linear's CTAs
+// take the SMs this small grid leaves idle and build their tables.
+__global__ void __launch_bounds__(kPeerCtaThreads, 1) peer_allreduce_rmsnorm_kernel(const Hif8PeerArgs p) {
   pdl_wait();  // inputs come from the previous kernel of the stream
   pdl_launch_dependents();
-  __shared__ float rowsum[8];
-  const int tid = threadIdx.x;
-  const int64_t n = p.rows * p.dim;
+  constexpr int kWarps = kPeerCtaThreads / 32;
+  __shared__ float warp_ss[kWarps][8];
+  __shared__ float row_inv[8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = blockIdx.x, ctas = gridDim.x;
+  const int64_t cw = p.dim / ctas, col0 = (int64_t)c * cw;
+  const int per_row = (int)(cw / 8);                 // 8-value chunks of a row in this slice
+  const int items = (int)p.rows * per_row;
   const size_t part_bytes = peer_part_bytes(p.max_rows, p.dim);
   const size_t slot_bytes = (size_t)p.world * part_bytes;
-  const size_t flags_off = 2 * slot_bytes;
-  if (tid < 8) rowsum[tid] = 0.f;
-  constexpr int kMaxChunks = 4;  // with the norm: rows x dim <= 4 x 1024 x 8
-  // 1. push: every 8-value chunk of the partial to every rank's buffer
-  for (int64_t i = (int64_t)tid * 8; i < n; i += (int64_t)kPeerThreads * 8) {
+  const size_t flags_off = peer_flags_off(p.world, p.max_rows, p.dim);
+  float *scratch = reinterpret_cast<float *>(p.peer_buf[p.rank] + peer_scratch_off(p.world, p.max_rows, p.dim));
+  uint32_t *bar = reinterpret_cast<uint32_t *>(scratch + kPeerMaxCtas * 8);
+  uint32_t *done = bar + 1;
+  const uint32_t epoch = *p.epoch_counter + 1;  // advanced by the last CTA, after every CTA read it
+  auto index = [&](int it) -> int64_t { return (int64_t)(it / per_row) * p.dim + col0 + (int64_t)(it % per_row) * 8; };
+  // 1. push the slice to every rank's buffer
+  for (int it = tid; it < items; it += kPeerCtaThreads) {
+    const int64_t i = index(it);
     uint4 x0, x1;
     if (p.local_dtype == HIF8_DTYPE_F32) {
       x0 = *reinterpret_cast<const uint4 *>(static_cast<const float *>(p.local) + i);
@@ -359,33 +394,21 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_rmsnorm_kernel(co
   }
   __threadfence_system();
   __syncthreads();
-  // 2. signal every rank, wait for every rank (bounded)
+  // 2. signal every rank for this slice, wait for every rank's slice (bounded)
   if (tid == 0) {
-    const uint32_t epoch = *p.epoch_counter + 1;
     for (int d = 0; d < p.world; ++d) {
       const int q = (p.rank + d) % p.world;
-      st_release_sys(reinterpret_cast<uint32_t *>(p.peer_buf[q] + flags_off) + p.rank, epoch);
+      st_release_sys(reinterpret_cast<uint32_t *>(p.peer_buf[q] + flags_off) + p.rank * kPeerMaxCtas + c, epoch);
     }
     const uint32_t *flags = reinterpret_cast<const uint32_t *>(p.peer_buf[p.rank] + flags_off);
     const uint64_t t0 = gtimer_ns();
     bool ok = true;
-    for (int q = 0; q < p.world && ok; ++q) {
-      while ((int32_t)(ld_acquire_sys(flags + q) - epoch) < 0) {
-        if (gtimer_ns() - t0 > p.timeout_ns) {
-          ok = false;
-          break;
-        }
-      }
-    }
+    for (int q = 0; q < p.world && ok; ++q) ok = wait_at_least(flags + q * kPeerMaxCtas + c, epoch, t0, p.timeout_ns);
     if (!ok) atomicExch(p.error, 1);
-    *p.epoch_counter = epoch;
   }
   __syncthreads();
-  // 3. sum in rank order from local memory, then (optional) residual + RMSNorm
+  // 3. sum in rank order from local memory
   const uint8_t *own = p.peer_buf[p.rank] + (size_t)p.slot * slot_bytes;
-  const bool norm = p.weight != nullptr;
-  // rank q's FP32 values i .. i + 7, written by the peers over NVLink: read
-  // past L1, summed in rank order
   auto sum8 = [&](int64_t i, float (&acc)[8]) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.f;
@@ -397,24 +420,8 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_rmsnorm_kernel(co
       acc[4] += b.x, acc[5] += b.y, acc[6] += b.z, acc[7] += b.w;
     }
   };
-  if (!norm) {  // the sum alone: stream the chunks
-    for (int64_t i = (int64_t)tid * 8; i < n; i += (int64_t)kPeerThreads * 8) {
-      float acc[8];
-      sum8(i, acc);
-      uint32_t o[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[e] = to_bf(acc[2 * e]) | ((uint32_t)to_bf(acc[2 * e + 1]) << 16);
-      *reinterpret_cast<uint4 *>(p.out + i) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-    return;
-  }
-  float v[kMaxChunks][8];
-  int row_of[kMaxChunks];
-#pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int64_t i = ((int64_t)tid + (int64_t)c * kPeerThreads) * 8;
-    row_of[c] = -1;
-    if (i >= n) continue;
+  // sum + residual as the BF16 values the norm sees (the sum rounded once)
+  auto value8 = [&](int64_t i, float (&v)[8]) {
     float acc[8];
     sum8(i, acc);
     uint32_t rr[4] = {0, 0, 0, 0};
@@ -422,44 +429,105 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_rmsnorm_kernel(co
       const uint4 r = *reinterpret_cast<const uint4 *>(p.residual + i);
       rr[0] = r.x, rr[1] = r.y, rr[2] = r.z, rr[3] = r.w;
     }
-    uint32_t o[4];
-    float ss = 0.f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float lo = bf(to_bf(acc[2 * e])), hi = bf(to_bf(acc[2 * e + 1]));  // the all-reduced sum, one BF16 rounding
+      float lo = bf(to_bf(acc[2 * e])), hi = bf(to_bf(acc[2 * e + 1]));
       if (p.residual) {
         lo = bf(to_bf(lo + bf(rr[e] & 0xFFFFu)));
         hi = bf(to_bf(hi + bf(rr[e] >> 16)));
       }
-      v[c][2 * e] = lo;
-      v[c][2 * e + 1] = hi;
-      o[e] = to_bf(lo) | ((uint32_t)to_bf(hi) << 16);
-      ss += lo * lo + hi * hi;
+      v[2 * e] = lo;
+      v[2 * e + 1] = hi;
     }
-    *reinterpret_cast<uint4 *>(p.residual_out + i) = make_uint4(o[0], o[1], o[2], o[3]);
-    row_of[c] = (int)(i / p.dim);
-    // a warp's 32 chunks lie in one row: reduce and add once per warp
+  };
+  const bool norm = p.weight != nullptr;
+  if (!norm) {
+    for (int it = tid; it < items; it += kPeerCtaThreads) {
+      const int64_t i = index(it);
+      float acc[8];
+      sum8(i, acc);
+      uint32_t o[4];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
-    if ((tid & 31) == 0) atomicAdd(&rowsum[row_of[c]], ss);
+      for (int e = 0; e < 4; ++e) o[e] = to_bf(acc[2 * e]) | ((uint32_t)to_bf(acc[2 * e + 1]) << 16);
+      *reinterpret_cast<uint4 *>(p.out + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  } else {
+    float ss[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int it = tid; it < items; it += kPeerCtaThreads) {
+      const int64_t i = index(it);
+      float v[8];
+      value8(i, v);
+      uint32_t o[4];
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        o[e] = to_bf(v[2 * e]) | ((uint32_t)to_bf(v[2 * e + 1]) << 16);
+        s += v[2 * e] * v[2 * e] + v[2 * e + 1] * v[2 * e + 1];
+      }
+      *reinterpret_cast<uint4 *>(p.residual_out + i) = make_uint4(o[0], o[1], o[2], o[3]);
+      const int row = it / per_row;
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r == row) ss[r] += s;
+    }
+    // this CTA's row sums: lanes, then warps in order
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      float x = ss[r];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xFFFFFFFFu, x, off);
+      if (lane == 0) warp_ss[warp][r] = x;
+    }
+    __syncthreads();
+    if (tid < p.rows) {
+      float x = 0.f;
+      for (int w = 0; w < kWarps; ++w) x += warp_ss[w][tid];
+      __stcg(scratch + c * 8 + tid, x);
+    }
+    __threadfence();
+    __syncthreads();
+    // barrier of the grid's CTAs (all resident: a few CTAs of 256 threads,
+    // launched after the previous kernel finished), bounded
+    if (tid == 0) {
+      atomicAdd(bar, 1u);
+      if (!wait_at_least(bar, (uint32_t)ctas, gtimer_ns(), p.timeout_ns)) atomicExch(p.error, 1);
+      __threadfence();
+    }
+    __syncthreads();
+    if (tid < p.rows) {
+      float x = 0.f;
+      for (int k = 0; k < ctas; ++k) x += __ldcg(scratch + k * 8 + tid);  // CTA order: identical everywhere
+      row_inv[tid] = rsqrtf(x / (float)p.dim + p.eps);
+    }
+    __syncthreads();
+    for (int it = tid; it < items; it += kPeerCtaThreads) {
+      const int64_t i = index(it);
+      const int row = it / per_row;
+      float v[8];
+      value8(i, v);
+      const float inv = row_inv[row];
+      const uint4 wv = *reinterpret_cast<const uint4 *>(p.weight + (i - (int64_t)row * p.dim));
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float w0 = bf(ww[e] & 0xFFFFu), w1 = bf(ww[e] >> 16);
+        if (p.one_plus) w0 += 1.f, w1 += 1.f;
+        o[e] = to_bf(v[2 * e] * inv * w0) | ((uint32_t)to_bf(v[2 * e + 1] * inv * w1) << 16);
+      }
+      *reinterpret_cast<uint4 *>(p.out + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
+  // the last CTA out advances the epoch and resets the counters
   __syncthreads();
-#pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    if (row_of[c] < 0) continue;
-    const int64_t i = ((int64_t)tid + (int64_t)c * kPeerThreads) * 8;
-    const float inv = rsqrtf(rowsum[row_of[c]] / (float)p.dim + p.eps);
-    const int64_t col = i - (int64_t)row_of[c] * p.dim;
-    const uint4 wv = *reinterpret_cast<const uint4 *>(p.weight + col);
-    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float w0 = bf(ww[e] & 0xFFFFu), w1 = bf(ww[e] >> 16);
-      if (p.one_plus) w0 += 1.f, w1 += 1.f;
-      o[e] = to_bf(v[c][2 * e] * inv * w0) | ((uint32_t)to_bf(v[c][2 * e + 1] * inv * w1) << 16);
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(done, 1u) == (uint32_t)ctas - 1) {
+      *bar = 0u;
+      *done = 0u;
+      *p.epoch_counter = epoch;
+      __threadfence();
     }
-    *reinterpret_cast<uint4 *>(p.out + i) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -477,16 +545,16 @@ extern "C" int hif8_model_peer_allreduce_rmsnorm(const Hif8PeerArgs *args, void 
       p.rows > p.max_rows || p.dim <= 0 || p.dim % 256 != 0 ||
       (p.local_dtype != HIF8_DTYPE_F32 && p.local_dtype != HIF8_DTYPE_BF16))
     return HIF8_ERR_INVALID_ARGUMENT;
-  // the fused norm keeps each thread's values in registers: rows x dim <=
-  // 4 x 8 x threads, at most 8 rows
-  if (p.weight && (p.rows * p.dim > (int64_t)kPeerThreads * 8 * 4 || p.rows > 8)) return HIF8_ERR_INVALID_ARGUMENT;
+  // the fused norm: at most 8 rows (one row sum of squares per CTA and row)
+  if (p.weight && p.rows > 8) return HIF8_ERR_INVALID_ARGUMENT;
   if (p.rows == 0) return HIF8_OK;
-  return launch_pdl(peer_allreduce_rmsnorm_kernel, dim3(1), dim3(kPeerThreads), 0, static_cast<cudaStream_t>(stream), p);
+  return launch_pdl(peer_allreduce_rmsnorm_kernel, dim3(peer_ctas(p.dim)), dim3(kPeerCtaThreads), 0,
+                    static_cast<cudaStream_t>(stream), p);
 }
 
 extern "C" size_t hif8_peer_buffer_bytes(int64_t world, int64_t max_rows, int64_t dim) {
   if (world < 1 || max_rows < 1 || dim < 1) return 0;
-  const size_t bytes = 2 * (size_t)world * peer_part_bytes(max_rows, dim) + (size_t)world * sizeof(uint32_t);
+  const size_t bytes = peer_scratch_off(world, max_rows, dim) + kPeerScratchBytes;
   return (bytes + 255) / 256 * 256;
 }
 

@@ -116,28 +116,34 @@ int hif8_model_glue_linear(const uint16_t *x, const Hif8GlueArgs *glue, int64_t 
  * hif8_peer_buffer_bytes(world, max_rows, dim) bytes that its peers map over
  * NVLink (hif8_peer_open of the exchanged 64-byte IPC handle).  Layout of a
  * rank's buffer: two slots, each holding `world` partials of max_rows x dim
- * FP32 (partial q = rank q's), then `world` uint32 flags.  One launch (one
- * CTA) per rank:
- *   1. stores this rank's partial `local` (rows x dim; FP32, the unrounded
- *      output of hif8_linear_partial_f32 / hif8_static_fused_linear_partial_f32,
- *      or BF16, widened) as FP32 into partial [rank] of
- *      the slot in every rank's buffer (its own first): one-way peer stores;
- *   2. system-scope fence, then writes epoch into flag[rank] of every rank's
- *      buffer, and waits (bounded by timeout_ns of %globaltimer; on time-out
- *      *error = 1 and the kernel finishes) until every flag of its own
- *      buffer has reached epoch;
- *   3. sums the ranks' partials in FP32 from its own buffer in rank order
- *      (identical on every rank) and rounds the sum to BF16 once; with
- *      `weight` it adds the residual (BF16) and
- *      normalises: out = RMSNorm(sum + residual) * (one_plus ? 1 + w : w),
- *      residual_out = sum + residual; with weight == NULL, out = the sum.
- * dim % 256 == 0; with weight, rows <= 8 and rows x dim <= 32768.
+ * FP32 (partial q = rank q's), then one uint32 flag per (source rank, CTA)
+ * for up to 16 CTAs, then the rank's own scratch (row sums of squares and
+ * two counters, never written by peers).  One launch per rank, of C CTAs
+ * (C = min(16, dim / 128)); CTA c owns the column slice [c dim / C,
+ * (c + 1) dim / C) of every row:
+ *   1. stores the slice of this rank's partial `local` (rows x dim; FP32,
+ *      the unrounded output of hif8_linear_partial_f32 /
+ *      hif8_static_fused_linear_partial_f32, or BF16, widened) as FP32 into
+ *      partial [rank] of the slot in every rank's buffer (its own first):
+ *      one-way peer stores, from C SMs;
+ *   2. system-scope fence, then writes epoch into flag[rank][c] of every
+ *      rank's buffer, and waits (bounded by timeout_ns of %globaltimer; on
+ *      time-out *error = 1 and the kernel finishes) until flag[q][c] of its
+ *      own buffer has reached epoch for every rank q;
+ *   3. sums the ranks' partials of the slice in FP32 from its own buffer in
+ *      rank order (identical on every rank) and rounds the sum to BF16
+ *      once; with `weight` it adds the residual (BF16) and normalises: out =
+ *      RMSNorm(sum + residual) * (one_plus ? 1 + w : w), residual_out = sum
+ *      + residual, the row norm from the CTAs' row sums of squares added in
+ *      CTA order after a bounded barrier of the grid (identical on every
+ *      CTA and rank); with weight == NULL, out = the sum.
+ * dim % 256 == 0; with weight, rows <= 8.
  * epoch = *epoch_counter + 1 (a per-rank device counter, advanced by the
- * launch), so the launch can live in a CUDA graph.  Two slots (alternate
- * call sites) keep a rank from overwriting partials a slower peer still
- * reads.  Plain peer loads and stores only (no multicast).  The kernel
- * signals programmatic dependents once its inputs are visible (see
- * hif8_b200.h on the ordering contract). */
+ * launch's last CTA), so the launch can live in a CUDA graph.  Two slots
+ * (alternate call sites) keep a rank from overwriting partials a slower
+ * peer still reads.  Plain peer loads and stores only (no multicast).  The
+ * CTAs signal programmatic dependents at their start (see hif8_b200.h on
+ * the ordering contract). */
 size_t hif8_peer_buffer_bytes(int64_t world, int64_t max_rows, int64_t dim);
 
 typedef struct Hif8PeerArgs {

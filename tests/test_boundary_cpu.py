@@ -67,8 +67,10 @@ def test_model_glue_header_symbols_are_exported():
 
     fn = cabi.library().hif8_peer_buffer_bytes
     fn.restype, fn.argtypes = ctypes.c_size_t, [ctypes.c_int64] * 3
-    # two slots of `world` FP32 partials (max_rows x dim), world flags, 256-byte multiple
-    assert fn(2, 4, 4096) == 2 * 2 * 4 * 4096 * 4 + 256
+    # two slots of `world` FP32 partials (max_rows x dim), one flag per (rank, CTA) for up to
+    # 16 CTAs, the rank's own scratch (16 CTAs x 8 row sums + two counters), a 256-byte multiple
+    want = 2 * 2 * 4 * 4096 * 4 + 2 * 16 * 4 + 16 * 8 * 4 + 16
+    assert fn(2, 4, 4096) == (want + 255) // 256 * 256
     assert fn(0, 4, 4096) == 0
     lib = cabi.library()
     for name in names:
