@@ -324,9 +324,17 @@ __host__ __device__ inline size_t peer_scratch_off(int64_t world, int64_t max_ro
 }
 constexpr size_t kPeerScratchBytes = (size_t)kPeerMaxCtas * 8 * sizeof(float) + 16;
 
-// CTAs of an exchange: column slices of at least 128 values (dim % 256 == 0).
-__host__ __device__ inline int peer_ctas(int64_t dim) {
-  return dim / 128 < kPeerMaxCtas ? (int)(dim / 128) : kPeerMaxCtas;
+// CTAs of an exchange: one per 128 KB that a rank pushes to the ranks (rows
+// x dim x 4 bytes x world), in column slices of at least 128 values (dim %
+// 256 == 0).  Small exchanges (a decode step at TP 2, or batch 1 at TP 8)
+// are latency-bound and run as one CTA without the grid barrier: measured at
+// TP 2, 16 CTAs for them cost ~10 us per exchange (decode 331 -> 269 tok/s).
+__host__ __device__ inline int peer_ctas(int64_t rows, int64_t dim, int world) {
+  const int64_t bytes = rows * dim * (int64_t)sizeof(float) * world;
+  int64_t c = (bytes + (128 << 10) - 1) >> 17;
+  if (c > dim / 128) c = dim / 128;
+  if (c > kPeerMaxCtas) c = kPeerMaxCtas;
+  return c < 1 ? 1 : (int)c;
 }
 
 __device__ __forceinline__ bool wait_at_least(const uint32_t *flag, uint32_t target, uint64_t t0, uint64_t limit) {
@@ -479,25 +487,33 @@ __global__ void __launch_bounds__(kPeerCtaThreads, 1) peer_allreduce_rmsnorm_ker
       if (lane == 0) warp_ss[warp][r] = x;
     }
     __syncthreads();
-    if (tid < p.rows) {
-      float x = 0.f;
-      for (int w = 0; w < kWarps; ++w) x += warp_ss[w][tid];
-      __stcg(scratch + c * 8 + tid, x);
-    }
-    __threadfence();
-    __syncthreads();
-    // barrier of the grid's CTAs (all resident: a few CTAs of 256 threads,
-    // launched after the previous kernel finished), bounded
-    if (tid == 0) {
-      atomicAdd(bar, 1u);
-      if (!wait_at_least(bar, (uint32_t)ctas, gtimer_ns(), p.timeout_ns)) atomicExch(p.error, 1);
+    if (ctas == 1) {  // the whole row in this CTA: no barrier
+      if (tid < p.rows) {
+        float x = 0.f;
+        for (int w = 0; w < kWarps; ++w) x += warp_ss[w][tid];
+        row_inv[tid] = rsqrtf(x / (float)p.dim + p.eps);
+      }
+    } else {
+      if (tid < p.rows) {
+        float x = 0.f;
+        for (int w = 0; w < kWarps; ++w) x += warp_ss[w][tid];
+        __stcg(scratch + c * 8 + tid, x);
+      }
       __threadfence();
-    }
-    __syncthreads();
-    if (tid < p.rows) {
-      float x = 0.f;
-      for (int k = 0; k < ctas; ++k) x += __ldcg(scratch + k * 8 + tid);  // CTA order: identical everywhere
-      row_inv[tid] = rsqrtf(x / (float)p.dim + p.eps);
+      __syncthreads();
+      // barrier of the grid's CTAs (all resident: a few CTAs of 256 threads,
+      // launched after the previous kernel finished), bounded
+      if (tid == 0) {
+        atomicAdd(bar, 1u);
+        if (!wait_at_least(bar, (uint32_t)ctas, gtimer_ns(), p.timeout_ns)) atomicExch(p.error, 1);
+        __threadfence();
+      }
+      __syncthreads();
+      if (tid < p.rows) {
+        float x = 0.f;
+        for (int k = 0; k < ctas; ++k) x += __ldcg(scratch + k * 8 + tid);  // CTA order: identical everywhere
+        row_inv[tid] = rsqrtf(x / (float)p.dim + p.eps);
+      }
     }
     __syncthreads();
     for (int it = tid; it < items; it += kPeerCtaThreads) {
@@ -548,7 +564,7 @@ extern "C" int hif8_model_peer_allreduce_rmsnorm(const Hif8PeerArgs *args, void 
   // the fused norm: at most 8 rows (one row sum of squares per CTA and row)
   if (p.weight && p.rows > 8) return HIF8_ERR_INVALID_ARGUMENT;
   if (p.rows == 0) return HIF8_OK;
-  return launch_pdl(peer_allreduce_rmsnorm_kernel, dim3(peer_ctas(p.dim)), dim3(kPeerCtaThreads), 0,
+  return launch_pdl(peer_allreduce_rmsnorm_kernel, dim3(peer_ctas(p.rows, p.dim, p.world)), dim3(kPeerCtaThreads), 0,
                     static_cast<cudaStream_t>(stream), p);
 }
 

@@ -119,7 +119,8 @@ int hif8_model_glue_linear(const uint16_t *x, const Hif8GlueArgs *glue, int64_t 
  * FP32 (partial q = rank q's), then one uint32 flag per (source rank, CTA)
  * for up to 16 CTAs, then the rank's own scratch (row sums of squares and
  * two counters, never written by peers).  One launch per rank, of C CTAs
- * (C = min(16, dim / 128)); CTA c owns the column slice [c dim / C,
+ * (one per 128 KB that the rank pushes, rows x dim x 4 x world bytes, at
+ * most 16 and at most dim / 128); CTA c owns the column slice [c dim / C,
  * (c + 1) dim / C) of every row:
  *   1. stores the slice of this rank's partial `local` (rows x dim; FP32,
  *      the unrounded output of hif8_linear_partial_f32 /

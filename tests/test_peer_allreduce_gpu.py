@@ -1,7 +1,8 @@
 """The peer all-reduce kernel (hif8_b200::peer_allreduce_rmsnorm /
-peer_allreduce) on one GPU with a world of one rank: the multi-CTA exchange
-(column slices, per-(rank, CTA) flags, the grid barrier of the fused norm,
-the epoch counter advanced by the last CTA) against a torch reference of the
+peer_allreduce) on one GPU with a world of one rank: the exchange over one or
+several CTAs (column slices, per-(rank, CTA) flags, the grid barrier of the
+fused norm, the epoch counter advanced by the last CTA) against a torch
+reference of the
 same arithmetic -- the partial rounded to BF16 once, the residual added in
 BF16, RMSNorm with (1 + w) or w.  residual_out and the plain sum are
 bit-exact; the normalised output within one BF16 unit (the reference sums
