@@ -1011,16 +1011,13 @@ def gemv_roofline(calls, args, device, world) -> dict:
         iso.append(statistics.median(times))
     del flush
 
+    # compact rows (one short list per launch) so the whole JSON line stays short
     per = []
     total_b = sum(algo_bytes(c) for c in calls)
     for i, c in enumerate(calls):
         b = algo_bytes(c)
-        row = {"m": c["m"], "shape": c["name"], "bytes": b,
-               "isolated_us": round(iso[i] * 1e3, 2), "isolated_gbs": round(b / (iso[i] * 1e-3) / 1e9, 1)}
-        if in_graph is not None:
-            row["event_us"] = round(in_graph[i] * 1e3, 2)
-            row["event_gbs"] = round(b / (in_graph[i] * 1e-3) / 1e9, 1)
-        per.append(row)
+        per.append([c["m"], c["name"], b, round(iso[i] * 1e3, 2),
+                    round(in_graph[i] * 1e3, 2) if in_graph is not None else None])
     peak, kind = load_peak_hbm()
     achieved = total_b / (stream_ms * 1e-3) / 1e9
     iso_achieved = total_b / (sum(iso) * 1e-3) / 1e9
@@ -1040,6 +1037,7 @@ def gemv_roofline(calls, args, device, world) -> dict:
             "event_timing": "per_launch event_us: events recorded around each launch inside a graph (serialising)",
             "isolated": {"achieved": iso_achieved, "frac": iso_achieved / peak,
                          "timing": "median of 5 launches per config, each after a read-based L2 eviction"},
+            "per_launch_fields": ["m", "shape", "algorithmic bytes", "isolated_us", "event_us"],
             "per_launch": per}
 
 
