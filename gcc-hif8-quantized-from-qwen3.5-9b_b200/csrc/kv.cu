@@ -4,6 +4,9 @@
 // Page layout (reference src/vllm_ascend_hif8/kv_cache.py:26-88): a cache is
 // [num_blocks, block_size, kv_heads, head_size + 4] bytes; each row holds
 // head_size HiF8 codes followed by the row's little-endian FP32 scale.
+// Consecutive blocks of a cache may sit further apart than one block's
+// bytes (block_stride): vLLM's block-major page holds a block's K rows and
+// then its V rows, so each plane's blocks are two block images apart.
 #include <math_constants.h>
 
 #include <atomic>
@@ -29,10 +32,20 @@ struct KvWriteArgs {
   const int64_t *slots;
   int32_t *bad_slots;
   int64_t tokens, heads, d, token_stride, num_blocks, block_size;
+  int64_t block_stride;  // bytes between consecutive blocks of a cache
   int64_t cache_slots;  // num_blocks * block_size: slots at or above are out of range
   int64_t units;        // planes * tokens * heads * (d / elements per unit), < 2^32
   int planes;           // 1 = K only, 2 = K and V
 };
+
+// Byte offset of the row group (every head's row) of slot `slot` in a
+// cache: slot * group for dense blocks, otherwise block * block_stride +
+// offset * group (one division, once per row group).
+__device__ __forceinline__ int64_t kv_slot_offset(const KvWriteArgs &p, int64_t slot, int64_t group) {
+  if (p.block_stride == p.block_size * group) return slot * group;
+  const int64_t blk = slot / p.block_size;
+  return blk * p.block_stride + (slot - blk * p.block_size) * group;
+}
 
 constexpr int kKvUnroll = 4;      // units in flight per thread
 constexpr int kKvScaleSlots = 64;  // heads whose scale / reciprocal a CTA stages in shared memory
@@ -41,9 +54,10 @@ constexpr int kKvScaleSlots = 64;  // heads whose scale / reciprocal a CTA stage
 // unit (ELEMS = 16: two 16-byte loads; 4: one 8-byte load) and store them
 // into the row's page slot with 4-byte stores (a page row is D + 4 bytes,
 // so rows are only 4-byte aligned).  A page row starts at
-// (slot * heads + head) * (D + 4): slot = block * block_size + offset, so no
-// division is needed; a slot at or beyond num_blocks * block_size is out of
-// range (counted once per token), a negative slot is skipped.  The unit
+// (slot * heads + head) * (D + 4) in dense blocks (slot = block * block_size
+// + offset, so no division is needed; kv_slot_offset otherwise); a slot at
+// or beyond num_blocks * block_size is out of range (counted once per
+// token), a negative slot is skipped.  The unit
 // holding a row's last elements also writes the row's FP32 scale.  Every
 // thread keeps kKvUnroll units in flight (slot and source loads of all of
 // them first), and the per-head reciprocals are formed once per CTA.
@@ -124,7 +138,7 @@ __global__ void __launch_bounds__(256) kv_write_kernel(const KvWriteArgs p) {
         const uint32_t re = __float_as_uint(r) & 0x7F800000u;
         exact_only = (re == 0u) | (re == 0x7F800000u) | !(s > 0.f);
       }
-      uint8_t *dst_row = p.cache[plane[u]] + (slot[u] * (int64_t)heads + h) * width;
+      uint8_t *dst_row = p.cache[plane[u]] + kv_slot_offset(p, slot[u], (int64_t)heads * width) + h * width;
       uint32_t *dst = reinterpret_cast<uint32_t *>(dst_row + (int64_t)chunk[u] * ELEMS);
       const uint32_t w[8] = {a[u].x, a[u].y, a[u].z, a[u].w, b[u].x, b[u].y, b[u].z, b[u].w};
       uint32_t o[4];
@@ -152,7 +166,7 @@ __global__ void __launch_bounds__(256) kv_write_kernel(const KvWriteArgs p) {
 // contiguous run: head rows are D apart inside a token) are quantised into a
 // shared-memory image of the token's page row group -- heads rows of D codes
 // and the FP32 scale, (D + 4) bytes apart -- and the warp then writes the
-// group (slot * heads * (D + 4) bytes into the cache) with consecutive
+// group (kv_slot_offset: slot * heads * (D + 4) bytes into dense blocks) with consecutive
 // lanes on consecutive 16-byte words (4-byte words when the group size or
 // base is not a multiple of 16): full, coalesced sectors instead of four
 // 4-byte stores per 16 codes 16 bytes apart.  Chunk c (16 elements) of the
@@ -262,7 +276,7 @@ __global__ void __launch_bounds__(kKvWarps * 32, 3) kv_write_warp_kernel(const K
     for (int h = lane; h < (int)p.heads; h += 32)
       *reinterpret_cast<float *>(stage + h * width + d) = sh_s[plane * kKvScaleSlots + h];
     __syncwarp();
-    uint8_t *dst = p.cache[plane] + slot * (int64_t)a.group;
+    uint8_t *dst = p.cache[plane] + kv_slot_offset(p, slot, a.group);
     if (a.store16) {
       for (int i = lane; i < (a.group >> 4); i += 32)
         __stcs(reinterpret_cast<uint4 *>(dst) + i, reinterpret_cast<const uint4 *>(stage)[i]);
@@ -288,6 +302,7 @@ struct AttnArgs {
   uint16_t *out;              // [tokens, heads, D] BF16
   float *part;                // split partials (null when splits == 1)
   int64_t heads, kv_heads, d, block_size, max_blocks, num_blocks;
+  int64_t block_stride;       // bytes between consecutive blocks of a cache
   int splits;                 // KV chunks per request (grid.y)
   int chunk;                  // keys per chunk (decode kernel)
   int q_rows_per_cta;         // query rows handled per CTA (grid.z groups)
@@ -359,7 +374,7 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attention_kernel(const Att
   const int64_t kblk = key < seq ? page_of(table, key, p.block_size, p.max_blocks, p.num_blocks) : -1;
   if (kblk >= 0) {
     const int64_t blk = kblk;
-    const uint8_t *row = p.kc + ((blk * p.block_size + key % p.block_size) * p.kv_heads) * width + head_off;
+    const uint8_t *row = p.kc + blk * p.block_stride + ((key % p.block_size) * p.kv_heads) * width + head_off;
     const float ks = *reinterpret_cast<const float *>(row + D);
     float acc[NQ];
 #pragma unroll
@@ -418,7 +433,7 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attention_kernel(const Att
       const int kk = chunk0 + j;
       const int64_t blk = page_of(table, kk, p.block_size, p.max_blocks, p.num_blocks);
       if (blk < 0) continue;  // its probability is zero as well
-      const uint8_t *row = p.vc + ((blk * p.block_size + kk % p.block_size) * p.kv_heads) * width + head_off;
+      const uint8_t *row = p.vc + blk * p.block_stride + ((kk % p.block_size) * p.kv_heads) * width + head_off;
       const float vs = *reinterpret_cast<const float *>(row + D);
       const float vv = bf16_bits_to_f32(f32_to_bf16_bits(lut[row[c]] * vs));
 #pragma unroll
@@ -631,7 +646,7 @@ __global__ void __launch_bounds__(kDecThreads) paged_decode_kernel(const AttnArg
     if (col >= p.max_blocks) return -1;
     const int64_t blk = table[col];
     if (blk < 0 || blk >= p.num_blocks) return -1;
-    return ((blk * p.block_size + (key - col * bsz)) * p.kv_heads + h) * width;
+    return blk * p.block_stride + ((int64_t)(key - col * bsz) * p.kv_heads + h) * width;
   };
   for (int i = tid; i < 256; i += kDecThreads) lut[i] = __uint_as_float(g_decode_f32.v[i]);
   // the chunk's reference scales (NaN: no table) and whether every row of
@@ -941,14 +956,46 @@ static int attn_grid_cap(int64_t work) {
 
 using namespace hif8;
 
+// Smallest legal block stride of a cache (one block's bytes), or -1 when the
+// block does not fit int64.
+static int64_t dense_block_stride(int64_t block_size, int64_t kv_heads, int64_t head_size) {
+  int64_t v = 0;
+  if (__builtin_mul_overflow(block_size, kv_heads, &v) || __builtin_mul_overflow(v, head_size + 4, &v)) return -1;
+  return v;
+}
+
+// A block stride the kernels accept: at least one block's bytes, 4-byte
+// rows, and every block's last byte addressable in int64.
+static bool block_stride_ok(int64_t block_stride, int64_t num_blocks, int64_t block_size, int64_t kv_heads,
+                            int64_t head_size) {
+  const int64_t dense = dense_block_stride(block_size, kv_heads, head_size);
+  int64_t span = 0;
+  return dense > 0 && block_stride >= dense && block_stride % 4 == 0 &&
+         !__builtin_mul_overflow(num_blocks, block_stride, &span);
+}
+
 extern "C" int hif8_kv_cache_write(const void *key, const void *value, int src_dtype, int64_t tokens,
                                    int64_t kv_heads, int64_t head_size, int64_t src_token_stride,
                                    const float *key_scale, const float *value_scale,
                                    const int64_t *slot_mapping, uint8_t *key_cache, uint8_t *value_cache,
                                    int64_t num_blocks, int64_t block_size, int32_t *bad_slots, void *stream) {
+  const int64_t dense = dense_block_stride(block_size > 0 ? block_size : 1, kv_heads > 0 ? kv_heads : 1,
+                                           head_size > 0 ? head_size : 0);
+  return hif8_kv_cache_write_strided(key, value, src_dtype, tokens, kv_heads, head_size, src_token_stride,
+                                     key_scale, value_scale, slot_mapping, key_cache, value_cache, num_blocks,
+                                     block_size, dense, bad_slots, stream);
+}
+
+extern "C" int hif8_kv_cache_write_strided(const void *key, const void *value, int src_dtype, int64_t tokens,
+                                           int64_t kv_heads, int64_t head_size, int64_t src_token_stride,
+                                           const float *key_scale, const float *value_scale,
+                                           const int64_t *slot_mapping, uint8_t *key_cache, uint8_t *value_cache,
+                                           int64_t num_blocks, int64_t block_size, int64_t block_stride,
+                                           int32_t *bad_slots, void *stream) {
   if (tokens < 0 || kv_heads <= 0 || head_size <= 0 || head_size % 4 != 0 || num_blocks <= 0 ||
       block_size <= 0 || src_token_stride < kv_heads * head_size || src_token_stride % 4 != 0)
     return HIF8_ERR_INVALID_ARGUMENT;
+  if (!block_stride_ok(block_stride, num_blocks, block_size, kv_heads, head_size)) return HIF8_ERR_INVALID_ARGUMENT;
   if (src_dtype != HIF8_DTYPE_F16 && src_dtype != HIF8_DTYPE_BF16) return HIF8_ERR_INVALID_ARGUMENT;
   if (!key || !key_scale || !key_cache || (tokens > 0 && !slot_mapping)) return HIF8_ERR_INVALID_ARGUMENT;
   // 8-byte source loads and 4-byte page stores
@@ -973,6 +1020,7 @@ extern "C" int hif8_kv_cache_write(const void *key, const void *value, int src_d
   p.token_stride = src_token_stride;
   p.num_blocks = num_blocks;
   p.block_size = block_size;
+  p.block_stride = block_stride;
   p.planes = with_v ? 2 : 1;
   p.cache_slots = num_blocks * block_size;
   // 16-element units where the source rows allow 16-byte loads
@@ -991,7 +1039,7 @@ extern "C" int hif8_kv_cache_write(const void *key, const void *value, int src_d
     while ((1LL << a.shift) < per_head) ++a.shift;
     a.group = (int)group;
     a.group_stage = (int)((group + 15) / 16 * 16);
-    a.store16 = group % 16 == 0 && (reinterpret_cast<uintptr_t>(key_cache) & 15u) == 0 &&
+    a.store16 = group % 16 == 0 && block_stride % 16 == 0 && (reinterpret_cast<uintptr_t>(key_cache) & 15u) == 0 &&
                 (!value_cache || (reinterpret_cast<uintptr_t>(value_cache) & 15u) == 0);
     const size_t smem = 4096 + 2 * kKvScaleSlots * (4 + 4 + 4 + 8) + (size_t)kKvWarps * a.group_stage;
     const int64_t items = p.planes * tokens;
@@ -1108,11 +1156,28 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
                                     int64_t block_size, int64_t max_blocks, int64_t max_seq_len,
                                     float softmax_scale, int causal,
                                     uint16_t *out, void *workspace, size_t workspace_bytes, void *stream) {
+  const int64_t dense = dense_block_stride(block_size > 0 ? block_size : 1, kv_heads > 0 ? kv_heads : 1,
+                                           head_size > 0 ? head_size : 0);
+  return hif8_paged_attention_strided(query, key_cache, value_cache, block_tables, seq_lens, query_start, batch,
+                                      num_tokens, num_heads, kv_heads, head_size, num_blocks, block_size, dense,
+                                      max_blocks, max_seq_len, softmax_scale, causal, out, workspace,
+                                      workspace_bytes, stream);
+}
+
+extern "C" int hif8_paged_attention_strided(const uint16_t *query, const uint8_t *key_cache,
+                                            const uint8_t *value_cache, const int32_t *block_tables,
+                                            const int32_t *seq_lens, const int32_t *query_start, int64_t batch,
+                                            int64_t num_tokens, int64_t num_heads, int64_t kv_heads,
+                                            int64_t head_size, int64_t num_blocks, int64_t block_size,
+                                            int64_t block_stride, int64_t max_blocks, int64_t max_seq_len,
+                                            float softmax_scale, int causal, uint16_t *out, void *workspace,
+                                            size_t workspace_bytes, void *stream) {
   const int args_status =
       paged_attention_args_status(query, key_cache, value_cache, block_tables, seq_lens, query_start, out, batch,
                                   num_tokens, num_heads, kv_heads, head_size, num_blocks, block_size, max_blocks,
                                   max_seq_len);
   if (args_status != HIF8_OK) return args_status;
+  if (!block_stride_ok(block_stride, num_blocks, block_size, kv_heads, head_size)) return HIF8_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return HIF8_OK;
   const int64_t group = num_heads / kv_heads;
   const size_t need = hif8_paged_attention_workspace_size(num_tokens, num_heads, head_size, max_seq_len);
@@ -1137,6 +1202,7 @@ extern "C" int hif8_paged_attention(const uint16_t *query, const uint8_t *key_ca
   p.kv_heads = kv_heads;
   p.d = head_size;
   p.block_size = block_size;
+  p.block_stride = block_stride;
   p.max_blocks = max_blocks;
   p.num_blocks = num_blocks;
   p.splits = (int)splits;

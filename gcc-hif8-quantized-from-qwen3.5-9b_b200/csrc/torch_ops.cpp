@@ -340,6 +340,23 @@ at::Tensor Hif8EmbeddingGather(const at::Tensor &weight, const at::Tensor &weigh
 
 // --------------------------------------------------------------- KV ops --
 
+// A cache plane: uint8 [num_blocks, block_size, heads, head_size + 4] with
+// dense rows and row groups, whose blocks may sit further apart (one plane
+// of vLLM's block-major page [num_blocks, 2, block_size, heads, width]).
+// Returns the block stride in bytes.
+int64_t CacheBlockStride(const at::Tensor &t, const char *name) {
+  TORCH_CHECK(t.defined() && t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kByte && t.dim() == 4,
+              name, " must be uint8 [num_blocks, block_size, heads, head_size + 4]");
+  auto dense_dim = [&](int dim, int64_t want) { return t.size(dim) == 1 || t.stride(dim) == want; };
+  const int64_t group = t.size(2) * t.size(3), block = t.size(1) * group;
+  TORCH_CHECK(dense_dim(3, 1) && dense_dim(2, t.size(3)) && dense_dim(1, group),
+              name, " must have dense rows and row groups");
+  const int64_t stride = t.size(0) == 1 ? block : t.stride(0);
+  TORCH_CHECK(stride >= block, name, " blocks must not overlap");
+  return stride;
+}
+
 void Hif8KvCacheWrite(const at::Tensor &key, const at::Tensor &value, const at::Tensor &key_scale,
                       const at::Tensor &value_scale, const at::Tensor &slot_mapping, at::Tensor key_cache,
                       at::Tensor value_cache, const std::optional<at::Tensor> &bad_slots) {
@@ -354,8 +371,9 @@ void Hif8KvCacheWrite(const at::Tensor &key, const at::Tensor &value, const at::
   CheckCudaTensor(key_scale, "key_scale");
   CheckCudaTensor(value_scale, "value_scale");
   CheckCudaTensor(slot_mapping, "slot_mapping");
-  CheckCudaTensor(key_cache, "key_cache");
-  CheckCudaTensor(value_cache, "value_cache");
+  const int64_t block_stride = CacheBlockStride(key_cache, "key_cache");
+  TORCH_CHECK(CacheBlockStride(value_cache, "value_cache") == block_stride,
+              "key_cache and value_cache must have the same block stride");
   TORCH_CHECK(slot_mapping.scalar_type() == at::kLong && slot_mapping.dim() == 1 &&
                   slot_mapping.numel() >= key.size(0),
               "slot_mapping must be int64 with one slot per token");
@@ -373,11 +391,12 @@ void Hif8KvCacheWrite(const at::Tensor &key, const at::Tensor &value, const at::
     bad = bad_slots->data_ptr<int32_t>();
   }
   c10::cuda::CUDAGuard guard(key.device());
-  CheckStatus(hif8_kv_cache_write(key.data_ptr(), value.data_ptr(), DtypeCode(key.scalar_type()), key.size(0),
-                                  key.size(1), key.size(2), key.stride(0), key_scale.data_ptr<float>(),
-                                  value_scale.data_ptr<float>(), slot_mapping.data_ptr<int64_t>(),
-                                  key_cache.data_ptr<uint8_t>(), value_cache.data_ptr<uint8_t>(), key_cache.size(0),
-                                  key_cache.size(1), bad, Stream(key)),
+  CheckStatus(hif8_kv_cache_write_strided(key.data_ptr(), value.data_ptr(), DtypeCode(key.scalar_type()),
+                                          key.size(0), key.size(1), key.size(2), key.stride(0),
+                                          key_scale.data_ptr<float>(), value_scale.data_ptr<float>(),
+                                          slot_mapping.data_ptr<int64_t>(), key_cache.data_ptr<uint8_t>(),
+                                          value_cache.data_ptr<uint8_t>(), key_cache.size(0), key_cache.size(1),
+                                          block_stride, bad, Stream(key)),
               "hif8_kv_cache_write");
 }
 
@@ -386,8 +405,9 @@ at::Tensor Hif8PagedAttention(const at::Tensor &query, const at::Tensor &key_cac
                               const at::Tensor &query_start, int64_t max_seq_len, double softmax_scale,
                               bool causal) {
   CheckCudaTensor(query, "query");
-  CheckCudaTensor(key_cache, "key_cache");
-  CheckCudaTensor(value_cache, "value_cache");
+  const int64_t block_stride = CacheBlockStride(key_cache, "key_cache");
+  TORCH_CHECK(CacheBlockStride(value_cache, "value_cache") == block_stride,
+              "key_cache and value_cache must have the same block stride");
   CheckCudaTensor(block_tables, "block_tables");
   CheckCudaTensor(seq_lens, "seq_lens");
   CheckCudaTensor(query_start, "query_start");
@@ -405,13 +425,13 @@ at::Tensor Hif8PagedAttention(const at::Tensor &query, const at::Tensor &key_cac
   const size_t ws_bytes = hif8_paged_attention_workspace_size(tokens, heads, d, max_seq_len);
   at::Tensor ws;
   if (ws_bytes > 0) ws = at::empty({(int64_t)ws_bytes}, query.options().dtype(at::kByte));
-  CheckStatus(hif8_paged_attention(reinterpret_cast<const uint16_t *>(query.data_ptr()), key_cache.data_ptr<uint8_t>(),
-                                   value_cache.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(),
-                                   seq_lens.data_ptr<int32_t>(), query_start.data_ptr<int32_t>(),
-                                   block_tables.size(0), tokens, heads, key_cache.size(2), d, key_cache.size(0),
-                                   key_cache.size(1), block_tables.size(1), max_seq_len, (float)softmax_scale, causal ? 1 : 0,
-                                   reinterpret_cast<uint16_t *>(out.data_ptr()), ws_bytes ? ws.data_ptr() : nullptr,
-                                   ws_bytes, Stream(query)),
+  CheckStatus(hif8_paged_attention_strided(
+                  reinterpret_cast<const uint16_t *>(query.data_ptr()), key_cache.data_ptr<uint8_t>(),
+                  value_cache.data_ptr<uint8_t>(), block_tables.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
+                  query_start.data_ptr<int32_t>(), block_tables.size(0), tokens, heads, key_cache.size(2), d,
+                  key_cache.size(0), key_cache.size(1), block_stride, block_tables.size(1), max_seq_len,
+                  (float)softmax_scale, causal ? 1 : 0, reinterpret_cast<uint16_t *>(out.data_ptr()),
+                  ws_bytes ? ws.data_ptr() : nullptr, ws_bytes, Stream(query)),
               "hif8_paged_attention");
   return out;
 }

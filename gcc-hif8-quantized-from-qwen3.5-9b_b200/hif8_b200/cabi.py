@@ -48,9 +48,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "hif8_static_fused_linear_partial_f32": (_INT, [_P, _INT, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soft_hif8_static_fused_gemm": (_INT, [_P, _INT, _P, _P, _P, _P, _INT, _INT, _I64, _I64, _I64, _P, _P]),
     "hif8_kv_cache_write": (_INT, [_P, _P, _INT, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _P]),
+    "hif8_kv_cache_write_strided": (_INT, [_P, _P, _INT, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64,
+                                           _P, _P]),
     "hif8_paged_attention_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
     "hif8_paged_attention": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                     ctypes.c_float, _INT, _P, _P, _SZ, _P]),
+    "hif8_paged_attention_strided": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                            _I64, _I64, ctypes.c_float, _INT, _P, _P, _SZ, _P]),
     "hif8_paged_attention_noalloc": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                             _I64, ctypes.c_float, _INT, _P, _P]),
     "hif8_kv_gather_decode": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P]),
@@ -190,6 +194,12 @@ def static_fused_gemm(x, weight, fixed_scale, channel_scale, bias, out) -> None:
 
 def kv_cache_write(key, value, key_scale, value_scale, slot_mapping, key_cache, value_cache, bad_slots=None) -> None:
     tokens, heads, d = key.shape
+    if key_cache.stride(0) != key_cache[0].numel() and key_cache.shape[0] > 1:
+        check("hif8_kv_cache_write_strided", library().hif8_kv_cache_write_strided(
+            _ptr(key), _ptr(value), _dtype_code(key.dtype), tokens, heads, d, key.stride(0), _ptr(key_scale),
+            _ptr(value_scale), _ptr(slot_mapping), _ptr(key_cache), _ptr(value_cache), key_cache.shape[0],
+            key_cache.shape[1], key_cache.stride(0), _ptr(bad_slots), _stream(key)))
+        return
     check("hif8_kv_cache_write", library().hif8_kv_cache_write(
         _ptr(key), _ptr(value), _dtype_code(key.dtype), tokens, heads, d, key.stride(0), _ptr(key_scale),
         _ptr(value_scale), _ptr(slot_mapping), _ptr(key_cache), _ptr(value_cache), key_cache.shape[0],
@@ -206,6 +216,13 @@ def paged_attention(query, key_cache, value_cache, block_tables, seq_lens, query
     if need and workspace is None:
         workspace = torch.empty(need, dtype=torch.uint8, device=query.device)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    if key_cache.stride(0) != key_cache[0].numel() and key_cache.shape[0] > 1:
+        check("hif8_paged_attention_strided", lib.hif8_paged_attention_strided(
+            _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables), _ptr(seq_lens), _ptr(query_start),
+            block_tables.shape[0], tokens, heads, key_cache.shape[2], d, key_cache.shape[0], key_cache.shape[1],
+            key_cache.stride(0), block_tables.shape[1], max_seq_len, float(scale), 1 if causal else 0, _ptr(out),
+            _ptr(workspace), ws_bytes, _stream(query)))
+        return
     check("hif8_paged_attention", lib.hif8_paged_attention(
         _ptr(query), _ptr(key_cache), _ptr(value_cache), _ptr(block_tables), _ptr(seq_lens), _ptr(query_start),
         block_tables.shape[0], tokens, heads, key_cache.shape[2], d, key_cache.shape[0], key_cache.shape[1],

@@ -21,8 +21,8 @@ vLLM fuses q/k/v, gate/up and the gated-delta-net input projections into one
 module; its components must share one quant type, and the static input scale
 of a fused module is the components' shared one (the exporter stores it
 under the first component, exporter.py:84-89).  The HiF8 KV cache and its
-attention are not routed through vLLM here: vLLM keeps its own KV cache
-(the kernels are reachable through ``hif8_b200.kv_cache``).
+attention are the ``CUSTOM`` attention backend of ``hif8_b200.vllm_attention``,
+installed by ``register()`` when ``HIF8_KV_CACHE=1``.
 
 ``register()`` is the ``vllm.general_plugins`` entry point; call it before
 building an engine in the same process.
@@ -276,4 +276,7 @@ def register() -> None:
         return
     if QUANT_METHOD_NAME not in QUANTIZATION_METHODS:
         register_quantization_config(QUANT_METHOD_NAME)(Hif8Config)
+    from .vllm_attention import install_hif8_kv_cache_adapter
+
+    install_hif8_kv_cache_adapter()  # the HiF8 KV cache, when HIF8_KV_CACHE=1
     _registered = True

@@ -218,6 +218,22 @@ int hif8_kv_cache_write(const void *key, const void *value, int src_dtype, int64
                         int64_t num_blocks, int64_t block_size, int32_t *bad_slots,
                         void *stream);
 
+/* hif8_kv_cache_write for caches whose consecutive blocks are block_stride
+ * bytes apart (hif8_kv_cache_write is this with the dense stride
+ * block_size * kv_heads * (head_size + 4)).  block_stride >= that, a
+ * multiple of 4, and num_blocks * block_stride must fit int64_t.  vLLM's
+ * block-major page [num_blocks][2][block_size][kv_heads][head_size + 4]
+ * (K rows, then V rows) is key_cache = page base, value_cache = base + one
+ * block image, block_stride = its page size.  Replaces the same reference
+ * write path as hif8_kv_cache_write, for the cache tensors vLLM binds
+ * (kv_runtime.py:533-571 _bind_hif8_cache_tensors). */
+int hif8_kv_cache_write_strided(const void *key, const void *value, int src_dtype, int64_t tokens,
+                                int64_t kv_heads, int64_t head_size, int64_t src_token_stride,
+                                const float *key_scale, const float *value_scale,
+                                const int64_t *slot_mapping, uint8_t *key_cache, uint8_t *value_cache,
+                                int64_t num_blocks, int64_t block_size, int64_t block_stride,
+                                int32_t *bad_slots, void *stream);
+
 /* Paged attention over HiF8 pages; replaces _gather_dense_hif8 + scaled
  * decode + the fused-infer-attention call of kv_runtime.py:1375-1563 (and the
  * oracle kv_cache.paged_attention_reference, kv_cache.py:314-372).  Only the
@@ -242,6 +258,18 @@ int hif8_paged_attention(const uint16_t *query, const uint8_t *key_cache,
                          int64_t head_size, int64_t num_blocks, int64_t block_size,
                          int64_t max_blocks, int64_t max_seq_len, float softmax_scale, int causal,
                          uint16_t *out, void *workspace, size_t workspace_bytes, void *stream);
+
+/* hif8_paged_attention over caches whose consecutive blocks are
+ * block_stride bytes apart (same rule as hif8_kv_cache_write_strided; K and
+ * V share the stride).  hif8_paged_attention is this with the dense stride. */
+int hif8_paged_attention_strided(const uint16_t *query, const uint8_t *key_cache,
+                                 const uint8_t *value_cache, const int32_t *block_tables,
+                                 const int32_t *seq_lens, const int32_t *query_start, int64_t batch,
+                                 int64_t num_tokens, int64_t num_heads, int64_t kv_heads,
+                                 int64_t head_size, int64_t num_blocks, int64_t block_size,
+                                 int64_t block_stride, int64_t max_blocks, int64_t max_seq_len,
+                                 float softmax_scale, int causal, uint16_t *out, void *workspace,
+                                 size_t workspace_bytes, void *stream);
 
 /* hif8_paged_attention without a caller workspace.  No counterpart in the
  * reference (its attention scratch comes from the framework allocator).

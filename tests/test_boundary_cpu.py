@@ -135,6 +135,15 @@ def test_cabi_rejects_contract_violations_without_device_work():
     assert lib.soft_hif8_static_fused_gemm(fake, 1, fake, fake, fake, None, -1, 1, 5, 8, 64, fake, None) == 1
     # KV: head_size must keep the FP32 sidecar aligned
     assert lib.hif8_kv_cache_write(fake, fake, 1, 1, 1, 6, 6, fake, fake, fake, fake, fake, 1, 1, None, None) == 1
+    # strided pages: the block stride holds a whole block, 4-byte rows, int64 span
+    dense = 16 * 2 * (64 + 4)
+    for stride in (dense - 4, dense + 2, 1 << 62):
+        assert lib.hif8_kv_cache_write_strided(fake, fake, 1, 1, 2, 64, 128, fake, fake, fake, fake, fake, 8, 16,
+                                               stride, None, None) == 1
+        assert lib.hif8_paged_attention_strided(fake, fake, fake, fake, fake, fake, 1, 1, 4, 2, 64, 8, 16, stride,
+                                                1, 16, 1.0, 1, fake, None, 0, None) == 1
+    assert lib.hif8_kv_cache_write_strided(fake, fake, 1, 0, 2, 64, 128, fake, fake, fake, fake, fake, 8, 16,
+                                           2 * dense, None, None) == cabi.HIF8_OK  # no tokens: nothing enqueued
     # attention: heads must be a multiple of kv heads
     assert lib.hif8_paged_attention(fake, fake, fake, fake, fake, fake, 1, 1, 6, 4, 256, 8, 128, 1, 1, 1.0, 1,
                                     fake, None, 0, None) == 1

@@ -298,3 +298,44 @@ def test_kv_write_head_layouts_scales_and_strided_source(heads, d, scales):
     oracle.kv_write(value.contiguous().view(torch.int16).numpy().view(np.uint16), vs, slots, vref)
     np.testing.assert_array_equal(kc.cpu().numpy(), kref)
     np.testing.assert_array_equal(vc.cpu().numpy(), vref)
+
+
+@pytest.mark.parametrize("pad_bytes", [0, 4096])
+def test_block_major_pages_through_the_strided_c_abi(pad_bytes):
+    """vLLM's block-major page [num_blocks, 2, block_size, kv_heads, D + 4]
+    (K rows then V rows, optionally padded pages): hif8_kv_cache_write_strided
+    writes each plane byte-identical to the dense write of the same rows, and
+    hif8_paged_attention_strided (decode and prefill batches) returns the
+    dense caches' output bit for bit."""
+    from hif8_b200 import cabi
+
+    kv = _kv()
+    nb, bs, kvh, d, heads = 24, 16, 2, 256, 8
+    w = d + 4
+    page = 2 * bs * kvh * w
+    raw = torch.zeros(nb * (page + pad_bytes), dtype=torch.uint8, device=DEV)
+    pages = torch.as_strided(raw, (nb, 2, bs, kvh, w), (page + pad_bytes, bs * kvh * w, kvh * w, w, 1))
+    kc = torch.zeros((nb, bs, kvh, w), dtype=torch.uint8, device=DEV)
+    vc = torch.zeros_like(kc)
+    gen = torch.Generator().manual_seed(77 + pad_bytes)
+    table = torch.tensor([[3, 11, 5, 0], [20, 2, 0, 0], [7, 0, 0, 0]], dtype=torch.int32)
+    lens = [50, 23, 9]
+    slots = torch.tensor([int(table[r, p // bs]) * bs + p % bs for r, n in enumerate(lens) for p in range(n)],
+                         dtype=torch.int64)
+    key = (torch.randn(len(slots), kvh, d, generator=gen) * 2).to(torch.bfloat16).to(DEV)
+    value = torch.randn(len(slots), kvh, d, generator=gen).to(torch.bfloat16).to(DEV)
+    ks = torch.tensor([5.0 / 32768, 3.0 / 32768], device=DEV)
+    vs = torch.tensor([2.0 / 32768, 4.0 / 32768], device=DEV)
+    cabi.kv_cache_write(key, value, ks, vs, slots.to(DEV), pages[:, 0], pages[:, 1])
+    kv.write_static(key, value, kc, vc, slots.to(DEV), ks, vs)
+    torch.cuda.synchronize()
+    assert torch.equal(pages[:, 0], kc) and torch.equal(pages[:, 1], vc)
+    table_d, lens_d = table.to(DEV), torch.tensor(lens, dtype=torch.int32, device=DEV)
+    for q_lens in ([1, 1, 1], [7, 1, 4]):
+        starts = torch.tensor(np.concatenate([[0], np.cumsum(q_lens)]), dtype=torch.int32, device=DEV)
+        q = torch.randn(sum(q_lens), heads, d, generator=gen).to(torch.bfloat16).to(DEV)
+        out = torch.empty_like(q)
+        cabi.paged_attention(q, pages[:, 0], pages[:, 1], table_d, lens_d, starts, max(lens), 1.0 / math.sqrt(d), out)
+        want = kv.paged_attention(q, kc, vc, table_d, lens, query_lens=q_lens, scale=1.0 / math.sqrt(d))
+        torch.cuda.synchronize()
+        assert torch.equal(out, want), f"strided pages changed the attention output ({q_lens})"
