@@ -28,6 +28,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "linear.cuh"
@@ -371,6 +373,286 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ---------------------------------------------------- CTA-pair variant ---
+//
+// The same pipeline on a pair of CTAs (a 2-CTA cluster on two SMs) issuing
+// tcgen05.mma.cta_group::2 with M = 256: the pair computes 256 weight rows x
+// 256 tokens.  Each CTA decodes its own 128 weight rows into its own tensor
+// memory (the A operand of its half) and stages its own 128 of the 256 tokens
+// of the BF16 activation (the B operand is split between the two CTAs'
+// shared memory at the same offset); each CTA's tensor memory receives its
+// 128 rows x 256 tokens of the accumulator.  Per CTA and K block this moves
+// 8 KB of weights and 16 KB of activations from L2 for the same 128 x 256 x
+// 64 MMA that the single-CTA kernel feeds with 8 + 32 KB.
+//
+// Barriers (every wait bounded as in the single-CTA kernel):
+//   * w_full[s] (each CTA): its weight tile of stage s has landed (TMA);
+//   * full_b[s] (leader CTA 0): both CTAs' activation halves have landed --
+//     the leader's producer expects both halves' bytes, each CTA's TMA
+//     (.cta_group::2) completes its bytes on the leader's barrier;
+//   * full_a[s] (leader): all 16 decoding warps of both CTAs have stored
+//     their rows of stage s into tensor memory (CTA 1's warps arrive
+//     remotely);
+//   * empty[s] (each CTA): the MMAs of stage s have completed -- the leader's
+//     MMA thread commits to its own and to the peer's barrier;
+//   * accum_full (each CTA): every MMA of the tile has completed.
+// Both CTAs allocate tensor memory with cta_group::2 from the same warp, and
+// a cluster barrier at the end keeps either CTA from exiting (or freeing its
+// tensor memory) while the other may still touch its shared memory.
+constexpr int kTc2Stages = 6;
+constexpr int kTc2BN = 256;           // tokens per pair tile
+constexpr int kTc2Half = kTc2BN / 2;  // tokens staged per CTA
+constexpr int kTc2Rows = 2 * kTcBM;   // weight rows per pair tile
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared-memory location in CTA `rank`
+__device__ __forceinline__ uint32_t map_to_rank(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+  return r;
+}
+
+// Arrive on a barrier of either CTA of the pair (a shared::cluster address).
+// Default (CTA-scope release) semantics, like the local arrivals: what the
+// waiting side consumes is tensor memory, ordered by the tcgen05 fences and
+// tcgen05.wait::st around the arrive, not shared-memory data.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// arrive on the barrier at a shared::cluster address once the pair's prior
+// MMAs have completed
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+// TMA load into this CTA's shared memory whose bytes complete on the
+// leader's barrier (a shared::cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int x, int y,
+                                                 uint32_t leader_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];"
+      ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(leader_bar)
+      : "memory");
+}
+
+__device__ __forceinline__ constexpr uint32_t instr_desc_bf16_pair() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTc2BN >> 3) << 17) | ((uint32_t)(kTc2Rows >> 4) << 24);
+}
+
+template <int OUT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_hif8_tc_pair_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                             const __grid_constant__ CUtensorMap ymap, const TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kBBytes = kTc2Half * 128;  // this CTA's 128 tokens x 64 K of BF16
+  constexpr int kWBytes = kTcBM * kTcBK;   // this CTA's 128 weight rows x 64 bytes
+  uint8_t *b_stages = smem;                // [stages][128][128 B], 128-byte swizzle
+  uint8_t *w_stages = b_stages + kTc2Stages * kBBytes;
+  uint8_t *lut = w_stages + kTc2Stages * kWBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(lut + kTcLut);
+  uint64_t *full_a = bars, *full_b = bars + kTc2Stages, *w_full = bars + 2 * kTc2Stages;
+  uint64_t *empty = bars + 3 * kTc2Stages, *accum_full = bars + 4 * kTc2Stages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum_full + 1);
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the MMAs
+  const int m0 = (int)(blockIdx.x >> 1) * kTc2BN;                 // the pair's first token
+  const int n0 = (int)blockIdx.y * kTc2Rows + (int)rank * kTcBM;  // this CTA's first weight row
+  const int kb0 = blockIdx.z * p.kb_per;
+  const int nkb = min(p.k / kTcBK - kb0, p.kb_per);
+  constexpr uint32_t kTmemCols = 512;  // 256 accumulator columns + 6 stages x 32 A columns
+
+  if (tid == 0) {
+    for (int s = 0; s < kTc2Stages; ++s) {
+      mbar_init(&full_a[s], 2 * kDecoderWarps);  // decoding warps of both CTAs (used on the leader)
+      mbar_init(&full_b[s], 1);                  // the leader's expect_tx of both halves
+      mbar_init(&w_full[s], 1);                  // this CTA's weight tile
+      mbar_init(&empty[s], 1);                   // the leader's commit
+    }
+    mbar_init(accum_full, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // the same warp in both CTAs allocates the pair's columns
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  for (int b0 = warp * 16; b0 < 256; b0 += (kTcThreads / 32) * 16) {
+    const uint32_t mine = g_decode_f32.v[b0 + (lane & 15)] >> 16;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      reinterpret_cast<uint32_t *>(lut)[(b0 + j) * 64 + lane] = __shfl_sync(0xFFFFFFFFu, mine, j);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_barrier();  // both CTAs' barriers are initialised before any remote arrive or TMA
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t d_tmem = tmem;                      // columns [0, 256)
+  const uint32_t a_tmem0 = tmem + (uint32_t)kTc2BN;  // stage s: columns 256 + 32 s
+
+  if (warp == 0) {
+    // ---- TMA producer: this CTA's weight tile and activation half ------------
+    if (lane == 0) {
+      const uint32_t leader_full_b0 = map_to_rank(&full_b[0], 0);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kTc2Stages;
+        if (kb >= kTc2Stages && !mbar_wait(&empty[s], ((kb / kTc2Stages) - 1) & 1, abort))
+          atomicAdd(p.err, 1);
+        mbar_expect_tx(&w_full[s], kWBytes);
+        tma_load_2d(w_stages + s * kWBytes, &wmap, (kb0 + kb) * kTcBK, n0, &w_full[s]);
+        if (rank == 0) mbar_expect_tx(&full_b[s], 2 * kBBytes);
+        tma_load_2d_pair(b_stages + s * kBBytes, &xmap, (kb0 + kb) * kTcBK, m0 + (int)rank * kTc2Half,
+                         leader_full_b0 + (uint32_t)(s * sizeof(uint64_t)));
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer (leader only) ---------------------------------------------
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = instr_desc_bf16_pair();
+      const uint32_t own_empty0 = map_to_rank(&empty[0], 0), peer_empty0 = map_to_rank(&empty[0], 1);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kTc2Stages;
+        const uint32_t parity = (kb / kTc2Stages) & 1;
+        bool ok = mbar_wait(&full_a[s], parity, abort);
+        ok = mbar_wait(&full_b[s], parity, abort) && ok;
+        if (!ok) atomicAdd(p.err, 1);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint64_t bdesc = smem_desc_sw128(b_stages + s * kBBytes);
+#pragma unroll
+        for (int j = 0; j < kTcBK / 16; ++j)
+          mma_ts_pair(d_tmem, a_tmem0 + s * 32 + j * 8, bdesc + (uint64_t)(j * 2), idesc, (kb | j) != 0);
+        mma_commit_pair(own_empty0 + (uint32_t)(s * sizeof(uint64_t)));
+        mma_commit_pair(peer_empty0 + (uint32_t)(s * sizeof(uint64_t)));
+      }
+      mma_commit_pair(map_to_rank(accum_full, 0));
+      mma_commit_pair(map_to_rank(accum_full, 1));
+    }
+  } else {
+    // ---- weight decoders (warps 2..9 of each CTA), then the epilogue ---------
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const int n = n0 + row;
+    const uint32_t lane4 = (uint32_t)lane << 2;
+    const uint32_t a_lane = (uint32_t)(quarter * 32) << 16;
+    const int sw = (row >> 1) & 3;
+    const int off0 = row * kTcBK + ((2 * half) ^ sw) * 16;
+    const int off1 = row * kTcBK + ((2 * half + 1) ^ sw) * 16;
+    const uint32_t leader_full_a0 = map_to_rank(&full_a[0], 0);
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % kTc2Stages;
+      const uint32_t parity = (kb / kTc2Stages) & 1;
+      // this CTA's weight tile has landed; the MMAs that read A stage s one
+      // ring ago have completed
+      if (!mbar_wait(&w_full[s], parity, abort)) atomicAdd(p.err, 1);
+      if (kb >= kTc2Stages && !mbar_wait(&empty[s], parity ^ 1, abort)) atomicAdd(p.err, 1);
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint8_t *ws = w_stages + s * kWBytes;
+      const uint4 x0 = *reinterpret_cast<const uint4 *>(ws + off0);
+      const uint4 x1 = *reinterpret_cast<const uint4 *>(ws + off1);
+      const uint32_t words[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      uint32_t v[16];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        v[q * 2] = lut_pair(lut, words[q], lane4, false);
+        v[q * 2 + 1] = lut_pair(lut, words[q], lane4, true);
+      }
+      tmem_st16(a_tmem0 + s * 32 + half * 16 + a_lane, v);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(leader_full_a0 + (uint32_t)(s * sizeof(uint64_t)));
+    }
+
+    // epilogue: as in the single-CTA kernel, over this CTA's 128 rows x the
+    // pair's 256 tokens, staged in the (idle) activation and weight rings
+    const bool n_ok = n < p.n;
+    const float cs = n_ok ? p.cs[n] : 0.f;
+    float bias = 0.f;
+    if (n_ok && p.bias) {
+      const uint16_t h = static_cast<const uint16_t *>(p.bias)[n];
+      bias = p.bias_dtype == HIF8_DTYPE_BF16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
+    }
+    constexpr int kChunks = kTc2BN / 64;
+    const int c0 = half * (kTc2BN / 2);
+    float tsr[kChunks];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      const int m = m0 + c0 + c * 32 + lane;
+      tsr[c] = m < p.m ? p.ts[(int64_t)m * p.ts_stride] : 0.f;
+    }
+    if (!mbar_wait(accum_full, 0, abort)) atomicAdd(p.err, 1);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    static_assert(kTc2Stages * (kBBytes + kWBytes) >= kTc2BN * kTcBM * 4, "the FP32 output tile fits the rings");
+    uint16_t *stage_out = reinterpret_cast<uint16_t *>(b_stages);
+    float *stage_out32 = reinterpret_cast<float *>(b_stages);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      uint32_t acc[32];
+      tmem_ld32(d_tmem + (uint32_t)(c0 + c * 32) + a_lane, acc);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int q = 0; q < 32; ++q) {
+        const float ts = __shfl_sync(0xFFFFFFFFu, tsr[c], q);
+        float val = __uint_as_float(acc[q]) * cs;
+        val = val * ts;
+        val += bias;
+        if constexpr (OUT == HIF8_DTYPE_F32) stage_out32[(c0 + c * 32 + q) * kTcBM + row] = val;
+        else stage_out[(c0 + c * 32 + q) * kTcBM + row] = (uint16_t)to_out_bits<OUT>(val);
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(kDecoderWarps * 32) : "memory");
+    if (warp == 2 && lane == 0 && n0 < p.n) {  // a pair's second row block may lie past N
+      if (gridDim.z > 1)
+        asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                     ::"l"(&ymap), "r"(n0), "r"(m0), "r"((int)blockIdx.z), "r"(smem_addr(stage_out))
+                     : "memory");
+      else
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                     ::"l"(&ymap), "r"(n0), "r"(m0), "r"(smem_addr(stage_out))
+                     : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_barrier();  // neither CTA leaves while the pair's MMAs or arrivals may touch it
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
 // Decode HiF8 activation bytes to unscaled BF16 (exact) for the TMA B operand.
 __global__ void __launch_bounds__(256) decode_to_bf16(const uint8_t *__restrict__ a, uint16_t *__restrict__ out,
                                                       int64_t chunks) {
@@ -502,30 +784,86 @@ static size_t err_offset(int64_t m, int64_t k) { return ((size_t)m * k * 2 + 255
 // leave SMs idle (configs[2] down, M = 512: 64 tiles for 148 SMs).
 struct TcPlan {
   int bn, splits, kb_per;
+  bool pair;  // the CTA-pair kernel (256 weight rows x 256 tokens per pair)
 };
+
+template <int OUT>
+static const void *tc_pair_kernel_ptr() {
+  return reinterpret_cast<const void *>(gemm_hif8_tc_pair_kernel<OUT>);
+}
+
+static constexpr size_t tc_pair_smem_bytes() {
+  return 1024 + (size_t)kTc2Stages * (kTc2Half * 128 + kTcBM * kTcBK) + kTcLut + (4 * kTc2Stages + 1) * 8 + 16;
+}
+
+// Resident CTA pairs of the pair kernel on this device (cached per device).
+static int tc_pair_slots() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
+    const void *k = tc_pair_kernel_ptr<HIF8_DTYPE_BF16>();
+    v = -1;
+    if (ensure_smem_limit(k, tc_pair_smem_bytes()) == HIF8_OK) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2, 1, 1);
+      cfg.blockDim = dim3(kTcThreads, 1, 1);
+      cfg.dynamicSmemBytes = tc_pair_smem_bytes();
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) == cudaSuccess && clusters > 0) v = clusters;
+    }
+    cudaGetLastError();
+    cache[dev].store(v, std::memory_order_relaxed);
+  }
+  return v > 0 ? v : 0;
+}
+
+// The CTA-pair kernel runs only when HIF8_GEMM_PAIR=1 (measured slower than
+// the single-CTA kernel on the configs[2] shapes); with it set, every call
+// of at least 256 tokens takes the pair kernel.
+static bool tc_pair_requested() {
+  const char *v = std::getenv("HIF8_GEMM_PAIR");
+  return v != nullptr && v[0] == '1';
+}
 
 static TcPlan tc_plan(int64_t m, int64_t n, int64_t k) {
   const int sms = num_sms();
   const int64_t nkb = k / kTcBK;
   const int bns[3] = {256, 128, 64};
   const double per_kb[3] = {0.55, 0.49, 0.46};
-  TcPlan best{64, 1, (int)nkb};
+  TcPlan best{64, 1, (int)nkb, false};
   double best_t = -1.0;
-  for (int i = 0; i < 3; ++i) {
-    if (bns[i] > 64 && m < bns[i] / 2) continue;
-    const int64_t tiles = ((m + bns[i] - 1) / bns[i]) * ((n + kTcBM - 1) / kTcBM);
+  const int pair_slots = m >= kTc2BN && tc_pair_requested() ? tc_pair_slots() : 0;
+  for (int i = 0; i < 4; ++i) {
+    const bool pair = i == 3;  // candidate 3: the CTA pair, only where requested
+    if (pair != (pair_slots > 0)) continue;
+    const int bn = pair ? kTc2BN : bns[i];
+    if (!pair && bn > 64 && m < bn / 2) continue;
+    const int rows = pair ? kTc2Rows : kTcBM;
+    const int slots = pair ? pair_slots : sms;
+    const int stages = pair ? kTc2Stages : kTcStages;
+    const double kb_cost = pair ? 0.55 : per_kb[i];
+    const int64_t tiles = ((m + bn - 1) / bn) * ((n + rows - 1) / rows);
     for (int splits = 1; splits <= 4; ++splits) {
       const int64_t kb_per = (nkb + splits - 1) / splits;
-      if (splits > 1 && (kb_per < 2 * kTcStages || (splits - 1) * kb_per >= nkb)) break;
-      const int64_t waves = (tiles * splits + sms - 1) / sms;
-      double t = (double)waves * (3.0 + per_kb[i] * (double)kb_per);
+      if (splits > 1 && (kb_per < 2 * stages || (splits - 1) * kb_per >= nkb)) break;
+      const int64_t waves = (tiles * splits + slots - 1) / slots;
+      double t = (double)waves * (3.0 + kb_cost * (double)kb_per);
       // FP32 partials written by the GEMM and read back by the reduce (~5 TB/s
       // achieved), one more launch (measured: configs[2] down, M = 4096, two
       // splits 446 us against 430 unsplit; M = 512 108 -> 76 us)
       if (splits > 1) t += (double)(2 * splits + 1) * (double)m * (double)n * 4.0 / 5.0e6 + 5.0;
       if (best_t < 0 || t < best_t) {
         best_t = t;
-        best = TcPlan{bns[i], splits, (int)kb_per};
+        best = TcPlan{bn, splits, (int)kb_per, pair};
       }
     }
   }
@@ -544,6 +882,34 @@ size_t hif8_gemm_tc_workspace(int64_t m, int64_t n, int64_t k) {
 template <int BN>
 static constexpr size_t tc_smem_bytes() {
   return 1024 + (size_t)kTcStages * (BN * 128 + kTcBM * kTcBK) + kTcLut + (3 * kTcStages + 1) * 8 + 16;
+}
+
+template <int OUT>
+static int launch_tc_pair(const CUtensorMap &xmap, const CUtensorMap &wmap, const CUtensorMap &ymap,
+                          const TcParams &p, cudaStream_t stream, int splits) {
+  const void *kernel = tc_pair_kernel_ptr<OUT>();
+  const size_t smem = tc_pair_smem_bytes();
+  const int st = ensure_smem_limit(kernel, smem);
+  if (st != HIF8_OK) return st;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * ((p.m + kTc2BN - 1) / kTc2BN)), (unsigned)((p.n + kTc2Rows - 1) / kTc2Rows),
+                     (unsigned)splits);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, gemm_hif8_tc_pair_kernel<OUT>, xmap, wmap, ymap, p);
+  if (err != cudaSuccess) {
+    set_last_error(err);
+    return HIF8_ERR_CUDA;
+  }
+  return check_launch();
 }
 
 template <int BN, int OUT>
@@ -593,10 +959,10 @@ int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t
   const int bn = plan.bn, splits = plan.splits;
   const cuuint32_t estr[3] = {1, 1, 1};
   CUtensorMap xmap, wmap, ymap;
-  {  // BF16 activation [M, K]: BN x 64 boxes, 128-byte swizzle (UMMA SW128 K-major)
+  {  // BF16 activation [M, K]: (tokens per CTA) x 64 boxes, 128-byte swizzle (UMMA SW128 K-major)
     const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
     const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)bn};
+    const cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)(plan.pair ? kTc2Half : bn)};
     if (encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -634,7 +1000,11 @@ int hif8_gemm_tc(const GemvArgs &args, int output_dtype, void *workspace, size_t
   TcParams p{args.w, args.ts, args.cs, splits > 1 ? nullptr : args.bias, splits > 1 ? (void *)part : args.out, err,
              args.m, args.n, args.k, args.bias_dtype, args.ts_stride, plan.kb_per};
   const bool bf16 = output_dtype == HIF8_DTYPE_BF16;
-  if (f32) {
+  if (plan.pair) {
+    if (f32) status = launch_tc_pair<HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream, splits);
+    else if (bf16) status = launch_tc_pair<HIF8_DTYPE_BF16>(xmap, wmap, ymap, p, stream, splits);
+    else status = launch_tc_pair<HIF8_DTYPE_F16>(xmap, wmap, ymap, p, stream, splits);
+  } else if (f32) {
     if (bn == 256) status = launch_tc<256, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream, splits);
     else if (bn == 128) status = launch_tc<128, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream, splits);
     else status = launch_tc<64, HIF8_DTYPE_F32>(xmap, wmap, ymap, p, stream, splits);

@@ -192,3 +192,48 @@ def test_prefill_gemm_split_k():
     got = out.cpu().numpy()
     assert np.isnan(got[7]).all()
     np.testing.assert_array_equal(np.delete(got, 7, axis=0), np.delete(exp, 7, axis=0))
+
+
+@pytest.mark.parametrize("m,n,k", [(4096, 6144, 4096), (512, 4096, 12288), (300, 1000, 640), (257, 136, 256),
+                                   (256, 64, 128)])
+def test_prefill_gemm_cta_pair(m, n, k, monkeypatch):
+    """The CTA-pair kernel (tcgen05.mma.cta_group::2, 256 weight rows x 256
+    tokens per pair; taken with HIF8_GEMM_PAIR=1): projection shapes with and
+    without split-K, ragged token and channel tails (a pair whose second CTA
+    holds only rows past N, a token tile of one row) against the FP64 oracle
+    and the single-CTA kernel; run-twice determinism; bit-exact on
+    small-integer operands."""
+    from hif8_b200 import cabi
+
+    ext = _native().load_extension()
+    w, w_s = _hif8_weights(n, k, seed=m + n, outlier_frac=1e-3)
+    _, a, a_s, _ = _activations(m, k, seed=k)
+    args = (_to(a), _to(w), _to(a_s), _to(w_s))
+    monkeypatch.setenv("HIF8_GEMM_PAIR", "0")
+    single = ext.soft_hif8_gemm(*args, None, torch.bfloat16)
+    monkeypatch.setenv("HIF8_GEMM_PAIR", "1")
+    lib = cabi.library()
+    need = lib.soft_hif8_gemm_workspace_size(m, n, k)
+    workspace = torch.full((need,), 0xAB, dtype=torch.uint8, device=DEV)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+    cabi.gemm(*args, None, out, workspace)
+    torch.cuda.synchronize()
+    assert _err_word(workspace, m, k) == 0, "a pipeline wait timed out"
+    got = out.float().cpu().numpy()
+    rows = np.arange(m) if m <= 512 else np.sort(np.random.default_rng(m).choice(m, size=256, replace=False))
+    cols = np.arange(n) if n <= 1000 else np.sort(np.random.default_rng(n).choice(n, size=256, replace=False))
+    expected = oracle.linear(a[rows], w[cols], a_s[rows], w_s[cols])
+    assert max_rel(got[np.ix_(rows, cols)], expected) <= MAX_REL
+    assert channel_rel(got[np.ix_(rows, cols)], expected) <= CHANNEL_REL
+    assert row_cosine_min(got[np.ix_(rows, cols)], expected) >= MIN_COSINE
+    assert max_rel(got, single.float().cpu().numpy()) <= MAX_REL
+    again = torch.empty_like(out)
+    cabi.gemm(*args, None, again, workspace)
+    assert torch.equal(out, again), "run-twice determinism"
+    rng = np.random.default_rng(m)
+    values = np.array([-2.0, -1.0, -0.5, 0.0, 0.5, 1.0, 2.0], np.float32)
+    ai = np.vectorize(oracle.encode_value)(values[rng.integers(0, 7, (m, k))]).astype(np.uint8)
+    wi = np.vectorize(oracle.encode_value)(values[rng.integers(0, 7, (n, k))]).astype(np.uint8)
+    ones_m, ones_n = np.ones(m, np.float32), np.ones(n, np.float32)
+    exact = ext.soft_hif8_gemm(_to(ai), _to(wi), _to(ones_m), _to(ones_n), None, torch.float16)
+    np.testing.assert_array_equal(exact.cpu().numpy(), oracle.linear(ai, wi, ones_m, ones_n).astype(np.float16))

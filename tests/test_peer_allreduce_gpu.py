@@ -33,7 +33,7 @@ def _buffer(max_rows, dim):
     return buf, table
 
 
-@pytest.mark.parametrize("dim", [256, 4096, 12288])
+@pytest.mark.parametrize("dim", [256, 4096, 12288, 65536])  # 65536 x 8 rows: the 16-CTA maximum
 @pytest.mark.parametrize("rows", [1, 4, 8])
 def test_peer_allreduce_rmsnorm_world_one(rows, dim):
     from hif8_b200 import kv_cache
