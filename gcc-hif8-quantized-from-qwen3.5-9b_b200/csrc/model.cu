@@ -311,7 +311,7 @@ __device__ __forceinline__ uint64_t gtimer_ns() {
 // then this rank's own scratch (never written by peers): the CTAs' row sums
 // of squares and two counters (the CTAs' barrier and completion).
 constexpr int kPeerMaxCtas = 16;
-constexpr int kPeerCtaThreads = 256;
+constexpr int kPeerCtaThreads = 1024;  // a one-CTA exchange sums and normalises with all of them
 
 __host__ __device__ inline size_t peer_part_bytes(int64_t max_rows, int64_t dim) {
   return (size_t)max_rows * dim * sizeof(float);
