@@ -501,8 +501,9 @@ __global__ void __launch_bounds__(kPeerCtaThreads, 1) peer_allreduce_rmsnorm_ker
       }
       __threadfence();
       __syncthreads();
-      // barrier of the grid's CTAs (all resident: a few CTAs of 256 threads,
-      // launched after the previous kernel finished), bounded
+      // barrier of the grid's CTAs (all resident: at most 16 CTAs, one per
+      // SM, and the dependent grid starts only after every CTA of this one
+      // has signalled at its start), bounded
       if (tid == 0) {
         atomicAdd(bar, 1u);
         if (!wait_at_least(bar, (uint32_t)ctas, gtimer_ns(), p.timeout_ns)) atomicExch(p.error, 1);
