@@ -403,6 +403,12 @@ constexpr int kTc2Stages = 6;
 constexpr int kTc2BN = 256;           // tokens per pair tile
 constexpr int kTc2Half = kTc2BN / 2;  // tokens staged per CTA
 constexpr int kTc2Rows = 2 * kTcBM;   // weight rows per pair tile
+// Two sets of 8 decoding warps take alternate K blocks (set j the blocks kb
+// with kb % 2 == j), so each warp's per-stage chain (table lookups, tensor
+// memory store, its wait, the arrive) has two MMA steps of time; set 0 also
+// runs the epilogue.
+constexpr int kTc2DecSets = 2;
+constexpr int kTc2Threads = 32 * (2 + kTc2DecSets * kDecoderWarps);
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -462,7 +468,7 @@ __device__ __forceinline__ constexpr uint32_t instr_desc_bf16_pair() {
 }
 
 template <int OUT>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTc2Threads, 1)
     gemm_hif8_tc_pair_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                              const __grid_constant__ CUtensorMap ymap, const TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -488,7 +494,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < kTc2Stages; ++s) {
-      mbar_init(&full_a[s], 2 * kDecoderWarps);  // decoding warps of both CTAs (used on the leader)
+      mbar_init(&full_a[s], 2 * kDecoderWarps);  // the stage's decoding set in both CTAs (used on the leader)
       mbar_init(&full_b[s], 1);                  // the leader's expect_tx of both halves
       mbar_init(&w_full[s], 1);                  // this CTA's weight tile
       mbar_init(&empty[s], 1);                   // the leader's commit
@@ -503,7 +509,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
-  for (int b0 = warp * 16; b0 < 256; b0 += (kTcThreads / 32) * 16) {
+  for (int b0 = warp * 16; b0 < 256; b0 += (kTc2Threads / 32) * 16) {
     const uint32_t mine = g_decode_f32.v[b0 + (lane & 15)] >> 16;
 #pragma unroll
     for (int j = 0; j < 16; ++j)
@@ -557,7 +563,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else {
     // ---- weight decoders (warps 2..9 of each CTA), then the epilogue ---------
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int half = ((warp - 2) >> 2) & 1;
+    const int set = (warp - 2) / kDecoderWarps;  // K blocks kb % 2 == set
     const int row = quarter * 32 + lane;
     const int n = n0 + row;
     const uint32_t lane4 = (uint32_t)lane << 2;
@@ -566,7 +573,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int off0 = row * kTcBK + ((2 * half) ^ sw) * 16;
     const int off1 = row * kTcBK + ((2 * half + 1) ^ sw) * 16;
     const uint32_t leader_full_a0 = map_to_rank(&full_a[0], 0);
-    for (int kb = 0; kb < nkb; ++kb) {
+    static_assert(kTc2Stages % kTc2DecSets == 0, "each ring slot belongs to one decoding set");
+    for (int kb = set; kb < nkb; kb += kTc2DecSets) {
       const int s = kb % kTc2Stages;
       const uint32_t parity = (kb / kTc2Stages) & 1;
       // this CTA's weight tile has landed; the MMAs that read A stage s one
@@ -591,8 +599,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive_remote(leader_full_a0 + (uint32_t)(s * sizeof(uint64_t)));
     }
 
-    // epilogue: as in the single-CTA kernel, over this CTA's 128 rows x the
-    // pair's 256 tokens, staged in the (idle) activation and weight rings
+    if (set == 0) {
+    // epilogue (set 0): as in the single-CTA kernel, over this CTA's 128 rows
+    // x the pair's 256 tokens, staged in the (idle) activation and weight rings
     const bool n_ok = n < p.n;
     const float cs = n_ok ? p.cs[n] : 0.f;
     float bias = 0.f;
@@ -641,6 +650,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                      : "memory");
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    }
     }
   }
 
@@ -808,7 +818,7 @@ static int tc_pair_slots() {
     if (ensure_smem_limit(k, tc_pair_smem_bytes()) == HIF8_OK) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2, 1, 1);
-      cfg.blockDim = dim3(kTcThreads, 1, 1);
+      cfg.blockDim = dim3(kTc2Threads, 1, 1);
       cfg.dynamicSmemBytes = tc_pair_smem_bytes();
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -894,7 +904,7 @@ static int launch_tc_pair(const CUtensorMap &xmap, const CUtensorMap &wmap, cons
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * ((p.m + kTc2BN - 1) / kTc2BN)), (unsigned)((p.n + kTc2Rows - 1) / kTc2Rows),
                      (unsigned)splits);
-  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.blockDim = dim3(kTc2Threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
